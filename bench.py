@@ -1,0 +1,411 @@
+#!/usr/bin/env python
+"""Benchmark of the log-space hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
+
+One JSON line on rank 0.  Default workload (the headline metric): the batched
+log-space contraction 'bik,bkj->bij', b=128, i=k=j=512, fp32 log-values drawn
+N(0, 8^2) from seed 1, logspace_max mode — "log-space einsum TFLOP/s" over
+algorithmic FLOPs (2*b*i*j*k per step).  A step is one pass of the hot path
+over the whole batch: the shift pre-pass and the fused contraction kernel.
+The line also carries the folded-circuit throughput (samples/s) of the 32x32
+quad-tree circuit, batch 8192 per GPU, as `secondary`.
+
+Multi-GPU (torchrun, one process per GPU, NCCL): the batch is sharded by
+construction — every rank processes its own batch of the same size (weak
+scaling) with no data-path collective; the circuit gathers its per-sample
+log-likelihoods with one all_gather per step.  Times are CUDA-event times,
+the max over ranks.
+
+``--impl reference`` times the reference's CPU path (its torch executor call
+sequence, oracle/torch_port.py) on the host cores, on rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+SPLIT_TF32_NOTE = "split-TF32 (3 TF32 products per multiply-add): peak = measured bf16 / 2 (TF32 rate) / 3"
+
+
+# ---------------------------------------------------------------------------
+# environment
+
+
+def measured_peaks() -> dict:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return {"hbm_gbs": data.get("hbm_gbs", 6650.0), "bf16_tflops": data.get("bf16_tflops", 1590.0), "basis": "of measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "basis": "of fallback"}
+
+
+def profiled_traffic() -> dict:
+    path = ROOT / "profiles" / "traffic.json"
+    return json.loads(path.read_text()) if path.exists() else {}
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML during the timed region."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+        0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+        0x100: "display_clock_setting",
+    }
+
+    def __init__(self, device_index: int) -> None:
+        self.samples: list[int] = []
+        self.reasons = 0
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            uuid = torch.cuda.get_device_properties(device_index).uuid
+            handle = None
+            for i in range(pynvml.nvmlDeviceGetCount()):
+                h = pynvml.nvmlDeviceGetHandleByIndex(i)
+                raw = pynvml.nvmlDeviceGetUUID(h)
+                raw = raw.decode() if isinstance(raw, bytes) else raw
+                if raw.replace("GPU-", "") == str(uuid):
+                    handle = h
+            self._handle = handle or pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._handle, pynvml.NVML_CLOCK_SM)
+        except Exception:  # noqa: BLE001 - clocks are reported as unavailable
+            self._nvml = None
+
+    def _run(self) -> None:
+        nv = self._nvml
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._handle, nv.NVML_CLOCK_SM))
+                self.reasons |= nv.nvmlDeviceGetCurrentClocksEventReasons(self._handle)
+            except Exception:  # noqa: BLE001
+                break
+            time.sleep(0.002)
+
+    def __enter__(self):
+        if self._nvml is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def report(self) -> dict | None:
+        if self._nvml is None or not self.samples:
+            return None
+        reasons = [name for bit, name in self.REASONS.items() if self.reasons & bit]
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz, "reasons": reasons, "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------
+# workloads
+
+
+class LogspaceBmm:
+    """'bik,bkj->bij', b=128, i=k=j=512, N(0, 8^2) log-values, logspace_max."""
+
+    metric = "log-space einsum TFLOP/s"
+    unit = "TFLOP/s"
+    batch, m, n, k = 128, 512, 512, 512
+    launches_per_step = 3  # shift of A, shift of B, contraction kernel
+
+    def __init__(self, device: torch.device, rank: int) -> None:
+        gen = torch.Generator().manual_seed(1 + 1000 * rank)
+        self.a_host = (8.0 * torch.randn(self.batch, self.m, self.k, generator=gen)).pin_memory()
+        self.b_host = (8.0 * torch.randn(self.batch, self.k, self.n, generator=gen)).pin_memory()
+        self.a = self.a_host.to(device)
+        self.b = self.b_host.to(device)
+        self.out_host = torch.empty(self.batch, self.m, self.n).pin_memory()
+        self.device = device
+        self.kernel_events: list[tuple[torch.cuda.Event, torch.cuda.Event]] = []
+
+    @property
+    def flops_per_step(self) -> float:
+        return 2.0 * self.batch * self.m * self.n * self.k
+
+    def config(self) -> dict:
+        return {
+            "workload": "logspace einsum 'bik,bkj->bij' b=128 i=k=j=512, fp32 N(0,8^2) log-values seed 1, logspace_max",
+            "global_batch": self.batch, "seq_len": None, "parallelism": None,
+            "l2": "inputs (268 MB) larger than L2 (126 MB); no flush",
+        }
+
+    def step(self, record: bool) -> None:
+        from extended_einsum_b200 import ops
+
+        sa = ops.logspace_shift(self.a, shift="max")
+        sb = ops.logspace_shift(self.b.transpose(1, 2), shift="max")
+        if record:
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+        ops.logspace_gemm_shifted(self.a, self.b, sa, sb)
+        if record:
+            e.record()
+            self.kernel_events.append((s, e))
+
+    def kernel_ms(self) -> float:
+        return statistics.mean(s.elapsed_time(e) for s, e in self.kernel_events)
+
+    def e2e_step(self) -> None:
+        """Public API with host buffers: H2D of both operands, materialize, D2H of the result."""
+        import extended_einsum_b200 as xb
+
+        a = self.a_host.to(self.device, non_blocking=True)
+        b = self.b_host.to(self.device, non_blocking=True)
+        result = xb.log(xb.einsum("bik,bkj->bij", xb.exp(xb.array(a)), xb.exp(xb.array(b)))).materialize("logspace_max")
+        self.out_host.copy_(result.backend_array, non_blocking=True)
+
+    @property
+    def e2e_bytes(self) -> tuple[int, int]:
+        return self.a_host.numel() * 4 + self.b_host.numel() * 4, self.out_host.numel() * 4
+
+    def roofline(self, kernel_ms: float, peaks: dict, traffic: dict) -> dict:
+        peak = peaks["bf16_tflops"] / 2.0 / 3.0
+        achieved = self.flops_per_step / (kernel_ms * 1e-3) / 1e12
+        return {
+            "bound": "tensor", "kernel": "xe::gemm::lse_gemm_kernel", "achieved": round(achieved, 2), "peak": round(peak, 1),
+            "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "traffic": traffic.get("lse_bmm"),
+            "peak_basis": f"{SPLIT_TF32_NOTE} ({peaks['basis']})", "kernel_ms": round(kernel_ms, 4),
+        }
+
+    @staticmethod
+    def cpu_sample(threads_budget_s: float = 10.0) -> dict:
+        """The reference's torch CPU path on a sample of 4 of the 128 batches, repeated for ~10 s."""
+        from oracle import torch_port
+
+        gen = torch.Generator().manual_seed(1)
+        a = 8.0 * torch.randn(4, 512, 512, generator=gen)
+        b = 8.0 * torch.randn(4, 512, 512, generator=gen)
+        torch_port.logspace_bmm(a, b)
+        t0 = time.perf_counter()
+        reps = 0
+        while time.perf_counter() - t0 < threads_budget_s:
+            torch_port.logspace_bmm(a, b)
+            reps += 1
+        dt = (time.perf_counter() - t0) / reps
+        return {
+            "value": round(2.0 * 4 * 512**3 / dt / 1e12, 5), "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+            "kind": "port", "sample": f"4 of 128 batches of 512^3 per call, {reps} calls, torch CPU executor sequence (oracle/torch_port.py)",
+        }
+
+
+class Circuit:
+    """32x32 quad-tree CP circuit, K=64, 256 states, batch 8192 per GPU, log-likelihood output."""
+
+    metric = "circuit samples/s"
+    unit = "samples/s"
+
+    def __init__(self, device: torch.device, rank: int, batch: int = 8192) -> None:
+        from extended_einsum_b200.circuit import CircuitForward, QuadTreeCircuit
+
+        self.circuit = QuadTreeCircuit(32, 32, 64, 256)
+        gen = torch.Generator().manual_seed(3)
+        params = self.circuit.init_parameters(gen)
+        self.params = params
+        self.batch = batch
+        pixel_gen = torch.Generator().manual_seed(3 + 1000 * rank)
+        self.pixels_host = torch.randint(256, (batch, self.circuit.variables), generator=pixel_gen, dtype=torch.uint8).pin_memory()
+        self.pixels = self.pixels_host.to(device)
+        dev = {k: (v.to(device) if isinstance(v, torch.Tensor) else [t.to(device) for t in v]) for k, v in params.items()}
+        self.forward = CircuitForward(self.circuit, dev)
+        self.ll_host = torch.empty(batch, 1).pin_memory()
+        self.device = device
+
+    def step(self) -> torch.Tensor:
+        return self.forward(self.pixels)
+
+    def e2e_step(self) -> None:
+        ll = self.forward(self.pixels_host.to(self.device, non_blocking=True))
+        self.ll_host.copy_(ll, non_blocking=True)
+
+    def launches_per_step(self) -> int:
+        levels = len(self.circuit.fold_counts)
+        return 2 + 2 * levels + 2
+
+
+# ---------------------------------------------------------------------------
+
+
+def time_region(fn, steps: int, warmup: int, dist_on: bool) -> float:
+    for _ in range(warmup):
+        fn(False)
+    torch.cuda.synchronize()
+    if dist_on:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        fn(True)
+    end.record()
+    end.synchronize()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    if dist_on:
+        t = torch.tensor([ms], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+        torch.distributed.barrier()
+    return ms
+
+
+def run_ours(args, rank: int, world: int, device: torch.device, dist_on: bool) -> dict | None:
+    from extended_einsum_b200 import _lib
+
+    _lib.load()
+    peaks = measured_peaks()
+    work = LogspaceBmm(device, rank)
+    # the headline (device-resident) measurement
+    sampler = ClockSampler(device.index or 0)
+    with sampler:
+        ms = time_region(work.step, args.steps, args.warmup, dist_on)
+    kernel_ms = work.kernel_ms()
+    if dist_on:
+        t = torch.tensor([kernel_ms], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        kernel_ms = float(t.item())
+    ms_per_step = ms / args.steps
+    value = world * work.flops_per_step / (ms_per_step * 1e-3) / 1e12
+    # end to end through the public API with host buffers
+    e2e_ms = time_region(lambda record: work.e2e_step(), max(3, args.steps // 4), 2, dist_on) / max(3, args.steps // 4)
+    e2e_value = world * work.flops_per_step / (e2e_ms * 1e-3) / 1e12
+    h2d, d2h = work.e2e_bytes
+
+    # secondary: the folded circuit, batch-sharded
+    circ = Circuit(device, rank)
+
+    def circuit_step(record: bool) -> None:
+        ll = circ.step()
+        if dist_on:
+            gathered = torch.empty(world * circ.batch, 1, device=device)
+            torch.distributed.all_gather_into_tensor(gathered, ll)
+
+    c_steps = max(3, args.steps // 2)
+    c_ms = time_region(circuit_step, c_steps, max(3, args.warmup), dist_on) / c_steps
+    c_e2e_ms = time_region(lambda record: circ.e2e_step(), max(3, c_steps // 2), 2, dist_on) / max(3, c_steps // 2)
+    flops_sample = circ.circuit.flops_per_sample()
+    bytes_sample = circ.circuit.hbm_bytes_per_sample()
+    c_value = world * circ.batch / (c_ms * 1e-3)
+    del circ
+    torch.cuda.empty_cache()
+
+    if rank != 0:
+        return None
+    line = {
+        "metric": work.metric, "value": round(value, 3), "unit": work.unit, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32 (split-TF32 tensor-core products, fp32 accumulation)", "data": "synthetic",
+        "config": {**work.config(), "parallelism": f"batch-sharded x{world} (weak)"},
+        "gpu_launches": work.launches_per_step * args.steps,
+        "roofline": work.roofline(kernel_ms, peaks, profiled_traffic()),
+        "e2e": {"value": round(e2e_value, 3), "unit": work.unit, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "clocks": sampler.report(),
+        "secondary": {
+            "metric": "circuit samples/s", "value": round(c_value, 1), "unit": "samples/s",
+            "workload": "folded 32x32 quad-tree CP circuit, K=64, 256 states, batch 8192 per GPU, uint8 pixels seed 3",
+            "ms_per_step": round(c_ms, 4),
+            "hbm_frac": round(bytes_sample * c_value / world / 1e9 / peaks["hbm_gbs"], 4),
+            "hbm_gbs_algorithmic": round(bytes_sample * c_value / world / 1e9, 1),
+            "tflops_algorithmic": round(flops_sample * c_value / world / 1e12, 2),
+            "e2e_samples_per_s": round(world * circ_batch(world) / (c_e2e_ms * 1e-3), 1),
+        },
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = LogspaceBmm.cpu_sample()
+    return line
+
+
+def circ_batch(world: int) -> int:
+    return 8192
+
+
+def run_reference(args, rank: int) -> dict | None:
+    """The reference's CPU path (torch executor sequence) on the host cores, rank 0 only."""
+    if rank != 0:
+        return None
+    from oracle import torch_port
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    gen = torch.Generator().manual_seed(1)
+    sample_batches = 4
+    a = 8.0 * torch.randn(sample_batches, 512, 512, generator=gen)
+    b = 8.0 * torch.randn(sample_batches, 512, 512, generator=gen)
+    for _ in range(args.warmup):
+        torch_port.logspace_bmm(a, b)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        torch_port.logspace_bmm(a, b)
+    dt = (time.perf_counter() - t0) / args.steps
+    value = 2.0 * sample_batches * 512**3 / dt / 1e12
+    sample = f"{sample_batches} of the 128 batches of 512^3 per step (the per-batch work is identical), torch CPU executor sequence (oracle/torch_port.py)"
+    return {
+        "impl": "reference", "metric": LogspaceBmm.metric, "value": round(value, 5), "unit": "TFLOP/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "logspace einsum 'bik,bkj->bij' b=128 i=k=j=512, fp32 N(0,8^2) log-values seed 1, logspace_max"},
+        "cpu_baseline": {"value": round(value, 5), "unit": "TFLOP/s", "cores": torch.get_num_threads(), "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=50)
+    parser.add_argument("--warmup", type=int, default=5)
+    parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    args = parser.parse_args()
+    if args.warmup < 3:
+        parser.error("--warmup must be at least 3")
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        line = run_reference(args, rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+
+    dist_on = world > 1
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if dist_on:
+        import datetime
+
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    try:
+        line = run_ours(args, rank, world, device, dist_on)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        if dist_on:
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,154 @@
+"""Folded quad-tree probabilistic circuit executed on the B200 kernels.
+
+This is the circuit that the reference's cirkit demo builds (categorical
+inputs, alternating Hadamard products and CP sum layers, demo/cirkit.py:131-187)
+in the form FoldSameShapedOperations gives it (preprocess.py:1310-1393): one
+folded sum layer per tree level, 'dac,dbc->dab' over (F, B, K) x (F, K, K),
+with the folded Hadamard product of the two halves of the previous level in
+between (slices + 'cab,cab->cab', see the folded program of a quad-tree
+circuit), and a root sum 'ab,cb->ac'.
+
+Per forward pass the launches are:
+  1  log-softmax of the categorical logits over the states      (xe_softmax, log output)
+  1  categorical gather of the per-pixel log-probabilities        (xe_categorical_gather)
+  L  softmax of each level's sum-layer logits                     (xe_softmax)
+  L  CP sum layers, the Hadamard product fused into the A operand (xe_logspace_gemm, a2)
+  1  root softmax + 1 root sum layer                              (xe_softmax, xe_logspace_gemm)
+and the whole sequence can be captured in one CUDA graph.
+
+Layout in HBM (fp32, contiguous): level output (F, B, K) with the batch
+inner to the fold, so that the two Hadamard halves of level l+1 are the two
+contiguous halves [0, F/2) and [F/2, F) of level l's output.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from . import ops
+
+
+def quad_tree_leaf_order(height: int, width: int) -> list[int]:
+    """Pixel variable of each leaf fold.
+
+    The region of fold f at level l+1 is the union of folds f and f + F_{l+1}
+    of level l, so the bits of a leaf index, from the lowest, choose the
+    half at each split from the root down.  Splits alternate between rows
+    and columns (the quad-tree region graph), each halving the region.
+    """
+    variables = height * width
+    if variables & (variables - 1) or height & (height - 1) or width & (width - 1):
+        raise ValueError("the quad-tree circuit needs power-of-two height and width")
+    levels = int(math.log2(variables))
+    order = []
+    for leaf in range(variables):
+        r0, r1, c0, c1 = 0, height, 0, width
+        split_rows = height >= width
+        for bit in range(levels):
+            choose_second = (leaf >> bit) & 1
+            if split_rows and r1 - r0 > 1 or c1 - c0 == 1:
+                mid = (r0 + r1) // 2
+                r0, r1 = (mid, r1) if choose_second else (r0, mid)
+            else:
+                mid = (c0 + c1) // 2
+                c0, c1 = (mid, c1) if choose_second else (c0, mid)
+            split_rows = not split_rows
+        order.append(r0 * width + c0)
+    return order
+
+
+@dataclass(frozen=True)
+class QuadTreeCircuit:
+    height: int = 32
+    width: int = 32
+    units: int = 64
+    states: int = 256
+
+    @property
+    def variables(self) -> int:
+        return self.height * self.width
+
+    @property
+    def fold_counts(self) -> list[int]:
+        """Folds of each sum level: V, V/2, ..., 2."""
+        counts, f = [], self.variables
+        while f >= 2:
+            counts.append(f)
+            f //= 2
+        return counts
+
+    def parameter_shapes(self) -> dict[str, list[tuple[int, ...]]]:
+        k = self.units
+        return {
+            "categorical": [(self.variables, self.states, k)],
+            "levels": [(f, k, k) for f in self.fold_counts],
+            "root": [(1, k)],
+        }
+
+    def init_parameters(self, generator: torch.Generator, device: torch.device | str = "cpu") -> dict[str, object]:
+        """N(0, 1) logits for every parameter, drawn in a fixed order."""
+        shapes = self.parameter_shapes()
+        categorical = torch.randn(shapes["categorical"][0], generator=generator)
+        levels = [torch.randn(s, generator=generator) for s in shapes["levels"]]
+        root = torch.randn(shapes["root"][0], generator=generator)
+        return {
+            "categorical": categorical.to(device),
+            "levels": [t.to(device) for t in levels],
+            "root": root.to(device),
+            "var_of_fold": torch.tensor(quad_tree_leaf_order(self.height, self.width), dtype=torch.int32).to(device),
+        }
+
+    def flops_per_sample(self) -> int:
+        """Algorithmic FLOPs of the sum layers per sample (2 per multiply-add)."""
+        k = self.units
+        return 2 * k * k * sum(self.fold_counts) + 2 * k
+
+    def hbm_bytes_per_sample(self) -> int:
+        """Algorithmic HBM bytes per sample with the Hadamard fused into the next sum layer.
+
+        Level 0 reads its (V, K) input and writes (V, K); level l >= 1 reads
+        the previous output (2F_l, K) and writes (F_l, K); the root reads
+        (2, K) and writes one value.  The gathered input is written once.
+        """
+        k = self.units
+        counts = self.fold_counts
+        elements = counts[0] * k  # gather output
+        elements += counts[0] * k + counts[0] * k  # level 0
+        for f in counts[1:]:
+            elements += 2 * f * k + f * k
+        elements += 2 * k + 1
+        return 4 * elements
+
+
+class CircuitForward:
+    """Forward pass of a QuadTreeCircuit on the current CUDA device."""
+
+    def __init__(self, circuit: QuadTreeCircuit, parameters: dict[str, object], shift: str = "max") -> None:
+        self.circuit = circuit
+        self.shift = shift
+        self.categorical = parameters["categorical"]
+        self.levels = list(parameters["levels"])
+        self.root = parameters["root"]
+        self.var_of_fold = parameters["var_of_fold"]
+        ops._check_tensors("CircuitForward", self.categorical, *self.levels, self.root)
+
+    def __call__(self, pixels: torch.Tensor) -> torch.Tensor:
+        """Log-likelihoods (B, 1) of uint8 pixels (B, variables)."""
+        table = ops.softmax(self.categorical, 1, log_output=True)
+        x = ops.categorical_gather(table, pixels, self.var_of_fold)
+        y = None
+        for level, logits in enumerate(self.levels):
+            w = ops.softmax(logits, 2)  # (F, O, K) linear weights
+            b_op = w.permute(0, 2, 1)  # (F, K, O), k contiguous
+            if level == 0:
+                y = ops.logspace_gemm(x, b_op, b_linear=True, shift=self.shift)
+            else:
+                half = y.shape[0] // 2
+                y = ops.logspace_gemm(y[:half], b_op, a2=y[half:], b_linear=True, shift=self.shift)
+        w_root = ops.softmax(self.root, 1)  # (1, K)
+        b_root = w_root.t().unsqueeze(0)  # (1, K, 1)
+        ll = ops.logspace_gemm(y[0:1], b_root, a2=y[1:2], b_linear=True, shift=self.shift)
+        return ll[0]

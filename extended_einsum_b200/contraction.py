@@ -1,0 +1,158 @@
+"""Maps one stable einsum onto one kernel call.
+
+_append_logspace_einsum (backend_translation/translate.py:686-750) lowers an
+einsum whose operands are log-space values (or linear parameter-derived
+values) into max / exp / einsum / log / shift-add backend calls.  Here the
+same arithmetic is one launch:
+
+* one operand            -> xe_logspace_reduce (log-sum-exp over the reduced labels)
+* two operands           -> xe_logspace_gemm with the labels grouped into
+                            batch (both operands and output), M (first operand
+                            and output), N (second operand and output) and K
+                            (both operands, not output)
+* 'bfi,bfj,foij->bfo'    -> xe_logspace_tucker (the fused Tucker layer,
+                            preprocess.py:1095-1106)
+* contraction-free       -> xe_log_add (translate.py:706-718)
+
+Grouped labels are flattened with ``reshape``, which is a view for the
+layouts that reach this path; a layout that cannot be viewed is copied.
+"""
+
+from __future__ import annotations
+
+import math
+from collections.abc import Sequence
+
+import torch
+
+from . import ops
+from .frontend import parse_format_string
+
+
+def _check_labels(input_strings: list[str], output_string: str) -> None:
+    for s in input_strings + [output_string]:
+        if len(set(s)) != len(s):
+            raise NotImplementedError(f"einsum: repeated labels in {s!r} (diagonals) are not supported on this path")
+
+
+def _sizes(input_strings: list[str], operands: Sequence[torch.Tensor]) -> dict[str, int]:
+    sizes: dict[str, int] = {}
+    for labels, operand in zip(input_strings, operands, strict=True):
+        if len(labels) != operand.dim():
+            raise ValueError(f"einsum: operand of rank {operand.dim()} for labels {labels!r}")
+        for label, size in zip(labels, operand.shape):
+            if sizes.setdefault(label, size) != size:
+                raise RuntimeError(f"Incompatible axis sizes for index {label}: {sizes[label]} and {size}.")
+    return sizes
+
+
+def _group(t: torch.Tensor, labels: str, groups: Sequence[str], sizes: dict[str, int]) -> torch.Tensor:
+    """Permutes ``t`` (labelled ``labels``) into ``groups`` order and flattens each group.
+
+    Labels of a group that ``t`` lacks get size 1.
+    """
+    order = [labels.index(label) for group in groups for label in group if label in labels]
+    shape = [math.prod(sizes[label] for label in group if label in labels) for group in groups]
+    return t.permute(order).reshape(shape)
+
+
+def log_broadcast_product(format_string: str, *log_operands: torch.Tensor) -> torch.Tensor:
+    """Contraction-free einsum in log space: the broadcast sum of the operands."""
+    input_strings, output_string = parse_format_string(format_string)
+    _check_labels(input_strings, output_string)
+    sizes = _sizes(input_strings, log_operands)
+    aligned = []
+    for labels, operand in zip(input_strings, log_operands, strict=True):
+        order = [labels.index(label) for label in output_string if label in labels]
+        view = operand.permute(order) if order else operand
+        shape = [sizes[label] if label in labels else 1 for label in output_string]
+        aligned.append(view.reshape(shape))
+    result = aligned[0]
+    for operand in aligned[1:]:
+        result = ops.log_add(result, operand)
+    return result
+
+
+def logspace_einsum(
+    format_string: str, linear: Sequence[bool], shift: str, *operands: torch.Tensor
+) -> torch.Tensor:
+    """The log of the einsum of exp(log operands) and linear operands, shifted per operand.
+
+    ``linear[i]`` marks operand i as a raw (parameter-derived) value; the
+    others are log-space values.  Returns the log-space result.
+    """
+    input_strings, output_string = parse_format_string(format_string)
+    if len(input_strings) != len(operands):
+        raise ValueError(f"The einsum format string has {len(input_strings)} inputs, but the instruction has {len(operands)} arguments.")
+    _check_labels(input_strings, output_string)
+    sizes = _sizes(input_strings, operands)
+    out_shape = [sizes[label] for label in output_string]
+    if len(operands) == 1:
+        return _reduce(input_strings[0], output_string, operands[0], linear[0], shift, sizes)
+    if len(operands) == 2:
+        return _binary(input_strings, output_string, operands, linear, shift, sizes)
+    if len(operands) == 3:
+        tucker = _match_tucker(input_strings, output_string, linear)
+        if tucker is not None:
+            left, right, weights = (operands[i] for i in tucker)
+            return _tucker(input_strings, output_string, tucker, left, right, weights, shift, sizes, out_shape)
+    raise NotImplementedError(
+        f"einsum {format_string!r} with {len(operands)} operands has no fused log-space kernel on this path"
+    )
+
+
+def _reduce(labels: str, output_string: str, x: torch.Tensor, linear: bool, shift: str, sizes) -> torch.Tensor:
+    reduced = "".join(label for label in labels if label not in output_string)
+    if linear:
+        # log(sum(x)) of a positive linear operand = log-sum-exp of log(x)
+        x = ops.log(x)
+    if not reduced:
+        return log_broadcast_product(f"{labels}->{output_string}", x)
+    view = _group(x, labels, ["", output_string, reduced], sizes)
+    y = ops.logspace_reduce(view, shift=shift)
+    return y.reshape([sizes[label] for label in output_string])
+
+
+def _binary(input_strings, output_string, operands, linear, shift, sizes) -> torch.Tensor:
+    la, lb = input_strings
+    batch = "".join(label for label in output_string if label in la and label in lb)
+    m_labels = "".join(label for label in output_string if label in la and label not in lb)
+    n_labels = "".join(label for label in output_string if label in lb and label not in la)
+    k_labels = "".join(label for label in la if label in lb and label not in output_string)
+    private = [label for s in (la, lb) for label in s if label not in output_string and label not in k_labels]
+    if private:
+        raise NotImplementedError(
+            f"einsum {la},{lb}->{output_string}: labels {''.join(private)!r} are summed within one operand only"
+        )
+    a = _group(operands[0], la, [batch, m_labels, k_labels], sizes)
+    b = _group(operands[1], lb, [batch, k_labels, n_labels], sizes)
+    c = ops.logspace_gemm(a, b, a_linear=linear[0], b_linear=linear[1], shift=shift)
+    grouped = batch + m_labels + n_labels
+    c = c.reshape([sizes[label] for label in grouped])
+    return c.permute([grouped.index(label) for label in output_string])
+
+
+def _match_tucker(input_strings, output_string, linear):
+    """Index order (left, right, weights) if the einsum is a Tucker layer 'bfi,bfj,foij->bfo'."""
+    for w in range(3):
+        if not linear[w]:
+            continue
+        others = [i for i in range(3) if i != w]
+        if linear[others[0]] or linear[others[1]]:
+            continue
+        l_lab, r_lab, w_lab = input_strings[others[0]], input_strings[others[1]], input_strings[w]
+        if len(l_lab) != 3 or len(r_lab) != 3 or len(w_lab) != 4 or len(output_string) != 3:
+            continue
+        b, f, i = l_lab
+        b2, f2, j = r_lab
+        o = next((x for x in output_string if x not in (b, f)), None)
+        if (b, f) != (b2, f2) or o is None or output_string != b + f + o:
+            continue
+        if w_lab != f + o + i + j:
+            continue
+        return (others[0], others[1], w)
+    return None
+
+
+def _tucker(input_strings, output_string, order, left, right, weights, shift, sizes, out_shape) -> torch.Tensor:
+    return ops.logspace_tucker(left, right, weights, shift=shift)

@@ -1,0 +1,474 @@
+// Memory-bound kernels of the log-space path: per-operand shift reduction,
+// softmax, log-space broadcast addition, categorical gather.  All of them
+// stream fp32 with 16-byte accesses where the layout allows it.
+#pragma once
+
+#include "xe_common.cuh"
+
+namespace xe {
+
+// torch.amax / torch.amin propagate NaN; so does PTX max.NaN / min.NaN.
+template <bool MAXMODE>
+__device__ __forceinline__ float nan_extreme(float a, float b) {
+  float r;
+  if (MAXMODE)
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  else
+    asm("min.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+
+template <bool MAXMODE>
+__device__ __forceinline__ float extreme_identity() {
+  return MAXMODE ? -INFINITY : INFINITY;
+}
+
+// ---------------------------------------------------------------------------
+// Shift reduction over k, rows gathered per warp (k contiguous or general
+// stride).  out[b*rows + r] = extreme_k x[b,r,k] (+ x2).
+template <bool MAXMODE, bool VEC>
+__global__ void __launch_bounds__(256) shift_rows_warp(const float* __restrict__ x, const float* __restrict__ x2,
+                                                       int64_t sb, int64_t sr, int64_t sk, int64_t batch,
+                                                       int64_t rows, int64_t k, float* __restrict__ out) {
+  const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (gw >= batch * rows) return;
+  const int64_t b = gw / rows, r = gw - b * rows;
+  const int64_t base = b * sb + r * sr;
+  const float* p = x + base;
+  const float* p2 = x2 ? x2 + base : nullptr;
+  float acc = extreme_identity<MAXMODE>();
+  if (VEC) {
+    for (int64_t kk = 4 * lane; kk < k; kk += 128) {
+      float4 v = ldg_nc_v4(p + kk);
+      if (p2) {
+        float4 w = ldg_nc_v4(p2 + kk);
+        v.x += w.x; v.y += w.y; v.z += w.z; v.w += w.w;
+      }
+      acc = nan_extreme<MAXMODE>(acc, nan_extreme<MAXMODE>(nan_extreme<MAXMODE>(v.x, v.y), nan_extreme<MAXMODE>(v.z, v.w)));
+    }
+  } else {
+    for (int64_t kk = lane; kk < k; kk += 32) {
+      float v = ldg_nc(p + kk * sk);
+      if (p2) v += ldg_nc(p2 + kk * sk);
+      acc = nan_extreme<MAXMODE>(acc, v);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc = nan_extreme<MAXMODE>(acc, __shfl_xor_sync(0xffffffffu, acc, o));
+  if (lane == 0) out[gw] = acc;
+}
+
+// Shift reduction over k when the rows are the contiguous axis (sr == 1):
+// block = 32 row-quads x 8 k-slices; grid = (ceil(rows/128), batch).
+template <bool MAXMODE, bool VEC>
+__global__ void __launch_bounds__(256) shift_rows_colwise(const float* __restrict__ x, const float* __restrict__ x2,
+                                                          int64_t sb, int64_t sk, int64_t rows, int64_t k,
+                                                          float* __restrict__ out) {
+  __shared__ float4 red[8][32];
+  const int64_t b = blockIdx.y;
+  const int64_t r0 = ((int64_t)blockIdx.x * 32 + threadIdx.x) * 4;
+  const int ks = threadIdx.y;
+  const float* p = x + b * sb + r0;
+  const float* p2 = x2 ? x2 + b * sb + r0 : nullptr;
+  const float id = extreme_identity<MAXMODE>();
+  float4 acc = make_float4(id, id, id, id);
+  const int64_t valid = rows - r0;
+  if (valid > 0) {
+    for (int64_t kk = ks; kk < k; kk += 8) {
+      float4 v;
+      if (VEC) {
+        v = ldg_nc_v4(p + kk * sk);
+        if (p2) {
+          float4 w = ldg_nc_v4(p2 + kk * sk);
+          v.x += w.x; v.y += w.y; v.z += w.z; v.w += w.w;
+        }
+      } else {
+        const float* q = p + kk * sk;
+        const float* q2 = p2 ? p2 + kk * sk : nullptr;
+        v.x = ldg_nc(q) + (q2 ? ldg_nc(q2) : 0.0f);
+        v.y = valid > 1 ? ldg_nc(q + 1) + (q2 ? ldg_nc(q2 + 1) : 0.0f) : id;
+        v.z = valid > 2 ? ldg_nc(q + 2) + (q2 ? ldg_nc(q2 + 2) : 0.0f) : id;
+        v.w = valid > 3 ? ldg_nc(q + 3) + (q2 ? ldg_nc(q2 + 3) : 0.0f) : id;
+      }
+      acc.x = nan_extreme<MAXMODE>(acc.x, v.x);
+      acc.y = nan_extreme<MAXMODE>(acc.y, v.y);
+      acc.z = nan_extreme<MAXMODE>(acc.z, v.z);
+      acc.w = nan_extreme<MAXMODE>(acc.w, v.w);
+    }
+  }
+  red[ks][threadIdx.x] = acc;
+  __syncthreads();
+  if (ks == 0 && valid > 0) {
+#pragma unroll
+    for (int j = 1; j < 8; ++j) {
+      float4 v = red[j][threadIdx.x];
+      acc.x = nan_extreme<MAXMODE>(acc.x, v.x);
+      acc.y = nan_extreme<MAXMODE>(acc.y, v.y);
+      acc.z = nan_extreme<MAXMODE>(acc.z, v.z);
+      acc.w = nan_extreme<MAXMODE>(acc.w, v.w);
+    }
+    float* o = out + b * rows + r0;
+    o[0] = acc.x;
+    if (valid > 1) o[1] = acc.y;
+    if (valid > 2) o[2] = acc.z;
+    if (valid > 3) o[3] = acc.w;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Softmax.  torch's CPU softmax (the reference executor) computes
+// exp(x - max) * (1 / sum); the same formula is used here.
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = nan_extreme<true>(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Block-wide reduction for blocks of kThreads (multiple of 32).
+template <int kThreads, bool IS_MAX>
+__device__ __forceinline__ float block_reduce(float v, float* scratch) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  v = IS_MAX ? warp_max(v) : warp_sum(v);
+  if (kThreads == 32) return v;
+  __syncthreads();
+  if (lane == 0) scratch[warp] = v;
+  __syncthreads();
+  float r = (lane < kThreads / 32) ? scratch[lane] : (IS_MAX ? -INFINITY : 0.0f);
+  r = IS_MAX ? warp_max(r) : warp_sum(r);
+  return r;
+}
+
+// Row softmax with the whole row in registers: kThreads threads per row,
+// each holding kQ float4 (row length <= kThreads*kQ*4; tail masked).
+// kThreads == 32 processes blockDim.x/32 rows per block (one per warp).
+template <int kThreads, int kQ, bool VEC>
+__global__ void __launch_bounds__(kThreads == 32 ? 256 : kThreads)
+    softmax_rows_reg(const float* __restrict__ x, float* __restrict__ y, int64_t rows, int64_t len, int log_out) {
+  __shared__ float scratch[32];
+  int64_t row;
+  int tid;
+  if (kThreads == 32) {
+    row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    tid = threadIdx.x & 31;
+    if (row >= rows) return;
+  } else {
+    row = blockIdx.x;
+    tid = threadIdx.x;
+  }
+  const float* px = x + row * len;
+  float* py = y + row * len;
+  float4 v[kQ];
+  float m = -INFINITY;
+#pragma unroll
+  for (int q = 0; q < kQ; ++q) {
+    const int64_t i = 4 * ((int64_t)q * kThreads + tid);
+    if (VEC) {
+      v[q] = (i < len) ? ldg_nc_v4(px + i) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+    } else {
+      v[q].x = (i < len) ? ldg_nc(px + i) : -INFINITY;
+      v[q].y = (i + 1 < len) ? ldg_nc(px + i + 1) : -INFINITY;
+      v[q].z = (i + 2 < len) ? ldg_nc(px + i + 2) : -INFINITY;
+      v[q].w = (i + 3 < len) ? ldg_nc(px + i + 3) : -INFINITY;
+    }
+    m = nan_extreme<true>(m, nan_extreme<true>(nan_extreme<true>(v[q].x, v[q].y), nan_extreme<true>(v[q].z, v[q].w)));
+  }
+  m = block_reduce<kThreads, true>(m, scratch);
+  float s = 0.0f;
+#pragma unroll
+  for (int q = 0; q < kQ; ++q) {
+    const int64_t i = 4 * ((int64_t)q * kThreads + tid);
+    // masked lanes are skipped (they hold -inf)
+    const float ex = (i < len) ? expf(v[q].x - m) : 0.0f;
+    const float ey = (i + 1 < len) ? expf(v[q].y - m) : 0.0f;
+    const float ez = (i + 2 < len) ? expf(v[q].z - m) : 0.0f;
+    const float ew = (i + 3 < len) ? expf(v[q].w - m) : 0.0f;
+    s += (ex + ey) + (ez + ew);
+  }
+  if (kThreads != 32) __syncthreads();
+  s = block_reduce<kThreads, false>(s, scratch);
+  const float inv = 1.0f / s;
+  // log softmax = x - (max + log(sum))
+  const float lse = m + logf(s);
+#pragma unroll
+  for (int q = 0; q < kQ; ++q) {
+    const int64_t i = 4 * ((int64_t)q * kThreads + tid);
+    float4 o;
+    if (log_out) {
+      o = make_float4(v[q].x - lse, v[q].y - lse, v[q].z - lse, v[q].w - lse);
+    } else {
+      o = make_float4(expf(v[q].x - m) * inv, expf(v[q].y - m) * inv, expf(v[q].z - m) * inv,
+                      expf(v[q].w - m) * inv);
+    }
+    if (VEC) {
+      if (i < len) stg_v4(py + i, o);
+    } else {
+      if (i < len) py[i] = o.x;
+      if (i + 1 < len) py[i + 1] = o.y;
+      if (i + 2 < len) py[i + 2] = o.z;
+      if (i + 3 < len) py[i + 3] = o.w;
+    }
+  }
+}
+
+// Softmax of rows too long for registers: one block per row, three streaming
+// passes (max, sum, write).
+__global__ void __launch_bounds__(1024) softmax_rows_stream(const float* __restrict__ x, float* __restrict__ y,
+                                                            int64_t len, int log_out) {
+  __shared__ float scratch[32];
+  const float* px = x + (int64_t)blockIdx.x * len;
+  float* py = y + (int64_t)blockIdx.x * len;
+  float m = -INFINITY;
+  for (int64_t i = threadIdx.x; i < len; i += 1024) m = nan_extreme<true>(m, ldg_nc(px + i));
+  m = block_reduce<1024, true>(m, scratch);
+  float s = 0.0f;
+  for (int64_t i = threadIdx.x; i < len; i += 1024) s += expf(ldg_nc(px + i) - m);
+  __syncthreads();
+  s = block_reduce<1024, false>(s, scratch);
+  const float inv = 1.0f / s, lse = m + logf(s);
+  for (int64_t i = threadIdx.x; i < len; i += 1024) {
+    const float v = ldg_nc(px + i);
+    py[i] = log_out ? v - lse : expf(v - m) * inv;
+  }
+}
+
+// Softmax over a strided middle axis: one thread per (outer, inner) fibre,
+// consecutive threads on consecutive inner positions (coalesced).
+__global__ void __launch_bounds__(256) softmax_strided(const float* __restrict__ x, float* __restrict__ y,
+                                                       int64_t outer, int64_t len, int64_t inner, int log_out) {
+  const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (g >= outer * inner) return;
+  const int64_t o = g / inner, in = g - o * inner;
+  const float* px = x + o * len * inner + in;
+  float* py = y + o * len * inner + in;
+  float m = -INFINITY;
+  for (int64_t a = 0; a < len; ++a) m = nan_extreme<true>(m, ldg_nc(px + a * inner));
+  float s = 0.0f;
+  for (int64_t a = 0; a < len; ++a) s += expf(ldg_nc(px + a * inner) - m);
+  const float inv = 1.0f / s, lse = m + logf(s);
+  for (int64_t a = 0; a < len; ++a) {
+    const float v = ldg_nc(px + a * inner);
+    py[a * inner] = log_out ? v - lse : expf(v - m) * inv;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Log-space broadcast addition (contraction-free einsum / multiply).
+struct NdShape {
+  int64_t shape[6];
+  int64_t as[6];
+  int64_t bs[6];
+  int ndim;
+};
+
+__global__ void __launch_bounds__(256) log_add_nd(const float* __restrict__ a, const float* __restrict__ b,
+                                                  float* __restrict__ y, NdShape s, int64_t total, float sign) {
+  for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < total; g += (int64_t)gridDim.x * blockDim.x) {
+    int64_t rem = g, oa = 0, ob = 0;
+    for (int d = s.ndim - 1; d >= 0; --d) {
+      const int64_t idx = rem % s.shape[d];
+      rem /= s.shape[d];
+      oa += idx * s.as[d];
+      ob += idx * s.bs[d];
+    }
+    y[g] = a[oa] + sign * b[ob];
+  }
+}
+
+__global__ void __launch_bounds__(256) log_add_contig4(const float4* __restrict__ a, const float4* __restrict__ b,
+                                                       float4* __restrict__ y, int64_t n4, float sign) {
+  for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < n4; g += (int64_t)gridDim.x * blockDim.x) {
+    float4 u, v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(u.x), "=f"(u.y), "=f"(u.z), "=f"(u.w)
+                 : "l"(a + g));
+    asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(b + g));
+    y[g] = make_float4(u.x + sign * v.x, u.y + sign * v.y, u.z + sign * v.z, u.w + sign * v.w);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Categorical gather: y[f,b,:] = table[f, pixels[b*ps + var[f]], :].
+// One thread per float4 of an output row (units % 4 == 0 on this path).
+__global__ void __launch_bounds__(256) categorical_gather4(const float* __restrict__ table,
+                                                           const uint8_t* __restrict__ pixels, int64_t ps,
+                                                           const int32_t* __restrict__ var_of_fold,
+                                                           float* __restrict__ y, int64_t folds, int64_t states,
+                                                           int64_t units, int64_t batch) {
+  const int64_t uq = units >> 2;
+  const int64_t total = folds * batch * uq;
+  for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < total; g += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t q = g % uq;
+    const int64_t row = g / uq;  // f*batch + b
+    const int64_t f = row / batch, b = row - f * batch;
+    const int64_t v = var_of_fold ? (int64_t)__ldg(var_of_fold + f) : f;
+    const int64_t s = (int64_t)__ldg(pixels + b * ps + v);
+    const float4 t = ldg_nc_v4(table + (f * states + s) * units + 4 * q);
+    stg_v4(y + row * units + 4 * q, t);
+  }
+}
+
+__global__ void __launch_bounds__(256) categorical_gather1(const float* __restrict__ table,
+                                                           const uint8_t* __restrict__ pixels, int64_t ps,
+                                                           const int32_t* __restrict__ var_of_fold,
+                                                           float* __restrict__ y, int64_t folds, int64_t states,
+                                                           int64_t units, int64_t batch) {
+  const int64_t total = folds * batch * units;
+  for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < total; g += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t u = g % units;
+    const int64_t row = g / units;
+    const int64_t f = row / batch, b = row - f * batch;
+    const int64_t v = var_of_fold ? (int64_t)__ldg(var_of_fold + f) : f;
+    const int64_t s = (int64_t)__ldg(pixels + b * ps + v);
+    y[g] = __ldg(table + (f * states + s) * units + u);
+  }
+}
+
+
+// ---------------------------------------------------------------------------
+// Log-space reduction of one operand: y = log(sum_k exp(x - s)) + s with
+// s = extreme_k x (two passes over the row; the second hits L1/L2).
+template <bool MAXMODE, bool VEC>
+__global__ void __launch_bounds__(256) lse_rows_warp(const float* __restrict__ x, int64_t sb, int64_t sr, int64_t sk,
+                                                     int64_t batch, int64_t rows, int64_t k, float* __restrict__ y) {
+  const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (gw >= batch * rows) return;
+  const int64_t b = gw / rows, r = gw - b * rows;
+  const float* p = x + b * sb + r * sr;
+  float m = extreme_identity<MAXMODE>();
+  if (VEC) {
+    for (int64_t kk = 4 * lane; kk < k; kk += 128) {
+      const float4 v = ldg_nc_v4(p + kk);
+      m = nan_extreme<MAXMODE>(m, nan_extreme<MAXMODE>(nan_extreme<MAXMODE>(v.x, v.y), nan_extreme<MAXMODE>(v.z, v.w)));
+    }
+  } else {
+    for (int64_t kk = lane; kk < k; kk += 32) m = nan_extreme<MAXMODE>(m, ldg_nc(p + kk * sk));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = nan_extreme<MAXMODE>(m, __shfl_xor_sync(0xffffffffu, m, o));
+  float s = 0.0f;
+  if (VEC) {
+    for (int64_t kk = 4 * lane; kk < k; kk += 128) {
+      const float4 v = ldg_nc_v4(p + kk);
+      s += (expf(v.x - m) + expf(v.y - m)) + (expf(v.z - m) + expf(v.w - m));
+    }
+  } else {
+    for (int64_t kk = lane; kk < k; kk += 32) s += expf(ldg_nc(p + kk * sk) - m);
+  }
+  s = warp_sum(s);
+  if (lane == 0) y[gw] = logf(s) + m;
+}
+
+// Same reduction when the rows are the unit-stride axis (sr == 1).
+template <bool MAXMODE>
+__global__ void __launch_bounds__(256) lse_rows_colwise(const float* __restrict__ x, int64_t sb, int64_t sk,
+                                                        int64_t rows, int64_t k, float* __restrict__ y) {
+  __shared__ float red[8][32];
+  const int64_t b = blockIdx.y;
+  const int64_t r = (int64_t)blockIdx.x * 32 + threadIdx.x;
+  const int ks = threadIdx.y;
+  const bool valid = r < rows;
+  const float* p = x + b * sb + r;
+  float m = extreme_identity<MAXMODE>();
+  if (valid)
+    for (int64_t kk = ks; kk < k; kk += 8) m = nan_extreme<MAXMODE>(m, ldg_nc(p + kk * sk));
+  red[ks][threadIdx.x] = m;
+  __syncthreads();
+  m = red[0][threadIdx.x];
+#pragma unroll
+  for (int j = 1; j < 8; ++j) m = nan_extreme<MAXMODE>(m, red[j][threadIdx.x]);
+  __syncthreads();
+  float s = 0.0f;
+  if (valid)
+    for (int64_t kk = ks; kk < k; kk += 8) s += expf(ldg_nc(p + kk * sk) - m);
+  red[ks][threadIdx.x] = s;
+  __syncthreads();
+  if (ks == 0 && valid) {
+    float t = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) t += red[j][threadIdx.x];
+    y[b * rows + r] = logf(t) + m;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Scalar extreme of one or two contiguous arrays (single block; these are the
+// small tensors of log-space +/-), combined as extreme(extreme(a), extreme(b)).
+template <bool MAXMODE>
+__global__ void __launch_bounds__(1024) global_extreme2(const float* __restrict__ a, int64_t na,
+                                                        const float* __restrict__ b, int64_t nb,
+                                                        float* __restrict__ out) {
+  __shared__ float scratch[32];
+  float ma = extreme_identity<MAXMODE>(), mb = extreme_identity<MAXMODE>();
+  for (int64_t i = threadIdx.x; i < na; i += 1024) ma = nan_extreme<MAXMODE>(ma, ldg_nc(a + i));
+  for (int64_t i = threadIdx.x; i < nb; i += 1024) mb = nan_extreme<MAXMODE>(mb, ldg_nc(b + i));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    ma = nan_extreme<MAXMODE>(ma, __shfl_xor_sync(0xffffffffu, ma, o));
+    mb = nan_extreme<MAXMODE>(mb, __shfl_xor_sync(0xffffffffu, mb, o));
+  }
+  __shared__ float scratch_b[32];
+  if (lane == 0) {
+    scratch[warp] = ma;
+    scratch_b[warp] = mb;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    ma = scratch[lane];
+    mb = scratch_b[lane];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      ma = nan_extreme<MAXMODE>(ma, __shfl_xor_sync(0xffffffffu, ma, o));
+      mb = nan_extreme<MAXMODE>(mb, __shfl_xor_sync(0xffffffffu, mb, o));
+    }
+    if (lane == 0) out[0] = nan_extreme<MAXMODE>(ma, mb);
+  }
+}
+
+// y = log(exp(a - m) +/- exp(b - m)) + m with m = *shift, broadcast strides.
+__global__ void __launch_bounds__(256) log_add_exp_nd(const float* __restrict__ a, const float* __restrict__ b,
+                                                      float* __restrict__ y, NdShape s, int64_t total,
+                                                      const float* __restrict__ shift, int subtract) {
+  const float m = __ldg(shift);
+  for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < total; g += (int64_t)gridDim.x * blockDim.x) {
+    int64_t rem = g, oa = 0, ob = 0;
+    for (int d = s.ndim - 1; d >= 0; --d) {
+      const int64_t idx = rem % s.shape[d];
+      rem /= s.shape[d];
+      oa += idx * s.as[d];
+      ob += idx * s.bs[d];
+    }
+    const float ea = expf(a[oa] - m), eb = expf(b[ob] - m);
+    y[g] = logf(subtract ? ea - eb : ea + eb) + m;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Domain conversions.
+template <int OP>
+__global__ void __launch_bounds__(256) unary_map(const float* __restrict__ x, float* __restrict__ y, int64_t n) {
+  for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < n; g += (int64_t)gridDim.x * blockDim.x) {
+    const float v = x[g];
+    y[g] = OP == 0 ? expf(v) : logf(v);
+  }
+}
+
+template <int OP>
+__global__ void __launch_bounds__(256) unary_map4(const float4* __restrict__ x, float4* __restrict__ y, int64_t n4) {
+  for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < n4; g += (int64_t)gridDim.x * blockDim.x) {
+    const float4 v = x[g];
+    y[g] = OP == 0 ? make_float4(expf(v.x), expf(v.y), expf(v.z), expf(v.w))
+                   : make_float4(logf(v.x), logf(v.y), logf(v.z), logf(v.w));
+  }
+}
+
+}  // namespace xe

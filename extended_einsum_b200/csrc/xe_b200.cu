@@ -1,0 +1,497 @@
+// C ABI of the sm_100a kernels (declared in include/xe_b200.h).  One
+// translation unit so that the device status word is shared by all kernels.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+
+#include "../../include/xe_b200.h"
+#include "lse_gemm.cuh"
+#include "pointwise.cuh"
+#include "tucker.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+xe_status fail(xe_status code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+xe_status check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(XE_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return XE_OK;
+}
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int current_device_sms() {
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms > 0 ? sms : 148;
+}
+
+int64_t grid_for(int64_t work, int64_t per_block, int64_t cap) {
+  int64_t g = (work + per_block - 1) / per_block;
+  return std::max<int64_t>(1, std::min<int64_t>(g, cap));
+}
+
+constexpr size_t kAlign = 256;
+inline size_t round_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
+
+// ------------------------------------------------------------------ GEMM
+using xe::gemm::Params;
+
+// Per-device "max dynamic shared memory" attribute, set once per kernel.
+// `done_mask` must be distinct for every kernel (the callers pass a static of
+// their own template instantiation).
+template <typename K>
+cudaError_t prepare_kernel(K kernel, int smem_bytes, std::atomic<uint32_t>& done_mask) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint32_t bit = 1u << (dev & 31);
+  if (done_mask.load() & bit) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+  if (e == cudaSuccess) done_mask.fetch_or(bit);
+  return e;
+}
+
+template <int BN, bool AK, bool BK, bool VEC, bool SPLIT>
+xe_status launch_gemm_t(const Params& p, cudaStream_t stream) {
+  using C = xe::gemm::Cfg<BN, SPLIT>;
+  auto kernel = xe::gemm::lse_gemm_kernel<BN, AK, BK, VEC, SPLIT>;
+  static std::atomic<uint32_t> attribute_set{0};
+  cudaError_t e = prepare_kernel(kernel, C::kSmemBytes, attribute_set);
+  if (e != cudaSuccess) return fail(XE_ERR_CUDA, "xe_logspace_gemm: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  const int grid = (int)std::min<int64_t>(p.num_tiles, current_device_sms());
+  kernel<<<grid, xe::gemm::kThreads, C::kSmemBytes, stream>>>(p);
+  return check_launch("xe_logspace_gemm");
+}
+
+template <int BN, bool SPLIT>
+xe_status launch_gemm_layout(const Params& p, bool ak, bool bk, bool vec, cudaStream_t s) {
+  if (ak) {
+    if (bk) return vec ? launch_gemm_t<BN, true, true, true, SPLIT>(p, s) : launch_gemm_t<BN, true, true, false, SPLIT>(p, s);
+    return vec ? launch_gemm_t<BN, true, false, true, SPLIT>(p, s) : launch_gemm_t<BN, true, false, false, SPLIT>(p, s);
+  }
+  if (bk) return vec ? launch_gemm_t<BN, false, true, true, SPLIT>(p, s) : launch_gemm_t<BN, false, true, false, SPLIT>(p, s);
+  return vec ? launch_gemm_t<BN, false, false, true, SPLIT>(p, s) : launch_gemm_t<BN, false, false, false, SPLIT>(p, s);
+}
+
+int env_int(const char* name, int dflt) {
+  const char* v = std::getenv(name);
+  return (v && *v) ? std::atoi(v) : dflt;
+}
+
+int pick_bn(int64_t n) {
+  const int forced = env_int("XE_GEMM_BN", 0);
+  if (forced == 32 || forced == 64 || forced == 128 || forced == 256) return forced;
+  if (n <= 32) return 32;
+  if (n <= 64) return 64;
+  if (n <= 128) return 128;
+  return 256;
+}
+
+xe_status launch_gemm(const Params& p, bool ak, bool bk, bool vec, cudaStream_t s) {
+  const int bn = pick_bn(p.N);
+  const bool split = env_int("XE_GEMM_SPLIT_ACC", 1) != 0;
+  Params q = p;
+  q.tiles_m = (int)((p.M + xe::gemm::kBM - 1) / xe::gemm::kBM);
+  q.tiles_n = (int)((p.N + bn - 1) / bn);
+  q.num_tiles = q.tiles_m * q.tiles_n * p.batch;
+  q.num_kb = (p.K + xe::gemm::kBK - 1) / xe::gemm::kBK;
+  switch (bn) {
+    case 32: return split ? launch_gemm_layout<32, true>(q, ak, bk, vec, s) : launch_gemm_layout<32, false>(q, ak, bk, vec, s);
+    case 64: return split ? launch_gemm_layout<64, true>(q, ak, bk, vec, s) : launch_gemm_layout<64, false>(q, ak, bk, vec, s);
+    case 128: return split ? launch_gemm_layout<128, true>(q, ak, bk, vec, s) : launch_gemm_layout<128, false>(q, ak, bk, vec, s);
+    default: return split ? launch_gemm_layout<256, true>(q, ak, bk, vec, s) : launch_gemm_layout<256, false>(q, ak, bk, vec, s);
+  }
+}
+
+xe_status shift_impl(const float* x, const float* x2, int64_t sb, int64_t sr, int64_t sk, int64_t batch, int64_t rows,
+                     int64_t k, bool maxmode, float* out, cudaStream_t stream) {
+  if (batch == 0 || rows == 0) return XE_OK;
+  const bool al = aligned16(x) && (x2 == nullptr || aligned16(x2));
+  if (sr == 1 && sk != 1) {
+    const bool vec = al && rows % 4 == 0 && sk % 4 == 0 && sb % 4 == 0;
+    dim3 block(32, 8), grid((unsigned)((rows + 127) / 128), (unsigned)batch);
+    if (maxmode) {
+      if (vec) xe::shift_rows_colwise<true, true><<<grid, block, 0, stream>>>(x, x2, sb, sk, rows, k, out);
+      else xe::shift_rows_colwise<true, false><<<grid, block, 0, stream>>>(x, x2, sb, sk, rows, k, out);
+    } else {
+      if (vec) xe::shift_rows_colwise<false, true><<<grid, block, 0, stream>>>(x, x2, sb, sk, rows, k, out);
+      else xe::shift_rows_colwise<false, false><<<grid, block, 0, stream>>>(x, x2, sb, sk, rows, k, out);
+    }
+  } else {
+    const bool vec = al && sk == 1 && k % 4 == 0 && sr % 4 == 0 && sb % 4 == 0;
+    const int64_t warps = batch * rows;
+    const int64_t blocks = (warps + 7) / 8;
+    if (maxmode) {
+      if (vec) xe::shift_rows_warp<true, true><<<(unsigned)blocks, 256, 0, stream>>>(x, x2, sb, sr, sk, batch, rows, k, out);
+      else xe::shift_rows_warp<true, false><<<(unsigned)blocks, 256, 0, stream>>>(x, x2, sb, sr, sk, batch, rows, k, out);
+    } else {
+      if (vec) xe::shift_rows_warp<false, true><<<(unsigned)blocks, 256, 0, stream>>>(x, x2, sb, sr, sk, batch, rows, k, out);
+      else xe::shift_rows_warp<false, false><<<(unsigned)blocks, 256, 0, stream>>>(x, x2, sb, sr, sk, batch, rows, k, out);
+    }
+  }
+  return check_launch("xe_logspace_shift");
+}
+
+bool make_nd(const int64_t* shape, const int64_t* as, const int64_t* bs, int ndim, xe::NdShape& sh, int64_t& total,
+             bool& contig) {
+  sh = xe::NdShape{};
+  sh.ndim = ndim;
+  total = 1;
+  contig = true;
+  int64_t expect = 1;
+  for (int d = ndim - 1; d >= 0; --d) {
+    if (shape[d] < 0) return false;
+    sh.shape[d] = shape[d];
+    sh.as[d] = as[d];
+    sh.bs[d] = bs[d];
+    if (shape[d] != 1 && (as[d] != expect || bs[d] != expect)) contig = false;
+    expect *= shape[d];
+    total *= shape[d];
+  }
+  if (ndim == 0) {
+    sh.ndim = 1;
+    sh.shape[0] = 1;
+    sh.as[0] = sh.bs[0] = 0;
+  }
+  return true;
+}
+
+}  // namespace
+
+extern "C" {
+
+int xe_version(void) { return 100; }
+
+const char* xe_last_error_string(void) { return g_last_error.c_str(); }
+
+int xe_device_status(int clear) {
+  int v = 0;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    fail(XE_ERR_CUDA, "xe_device_status: %s", cudaGetErrorString(e));
+    return XE_ERR_CUDA << 16;
+  }
+  e = cudaMemcpyFromSymbol(&v, xe::g_device_status, sizeof(int));
+  if (e != cudaSuccess) {
+    fail(XE_ERR_CUDA, "xe_device_status: %s", cudaGetErrorString(e));
+    return XE_ERR_CUDA << 16;
+  }
+  if (clear && v != 0) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(xe::g_device_status, &zero, sizeof(int));
+  }
+  return v;
+}
+
+size_t xe_logspace_gemm_workspace_size(int64_t batch, int64_t m, int64_t n, int64_t k, int32_t a_linear,
+                                       int32_t b_linear) {
+  (void)k;
+  size_t bytes = 0;
+  if (!a_linear) bytes += round_up((size_t)batch * (size_t)m * sizeof(float));
+  if (!b_linear) bytes += round_up((size_t)batch * (size_t)n * sizeof(float));
+  return bytes;
+}
+
+xe_status xe_logspace_shift(const float* x, const float* x2, int64_t sb, int64_t sr, int64_t sk, int64_t batch,
+                            int64_t rows, int64_t k, int32_t shift_mode, float* out, void* stream) {
+  if (!x || !out) return fail(XE_ERR_INVALID_ARGUMENT, "xe_logspace_shift: null pointer");
+  if (batch < 0 || rows < 0 || k <= 0)
+    return fail(XE_ERR_INVALID_ARGUMENT, "xe_logspace_shift: the reduced axis must be non-empty (k=%lld)", (long long)k);
+  if (shift_mode != XE_SHIFT_MAX && shift_mode != XE_SHIFT_MIN)
+    return fail(XE_ERR_INVALID_ARGUMENT, "xe_logspace_shift: unknown shift mode %d", shift_mode);
+  return shift_impl(x, x2, sb, sr, sk, batch, rows, k, shift_mode == XE_SHIFT_MAX, out, as_stream(stream));
+}
+
+}  // extern "C"
+
+namespace {
+
+xe_status gemm_launch(const float* a, const float* a2, int64_t a_sb, int64_t a_sm, int64_t a_sk, const float* shift_a,
+                      const float* b, int64_t b_sb, int64_t b_sk, int64_t b_sn, const float* shift_b, float* c,
+                      int64_t c_sb, int64_t c_sm, int64_t c_sn, int64_t batch, int64_t m, int64_t n, int64_t k,
+                      cudaStream_t s) {
+  Params p{};
+  p.a = a;
+  p.a2 = a2;
+  p.a_sb = a_sb;
+  p.a_sm = a_sm;
+  p.a_sk = a_sk;
+  p.b = b;
+  p.b_sb = b_sb;
+  p.b_sk = b_sk;
+  p.b_sn = b_sn;
+  p.c = c;
+  p.c_sb = c_sb;
+  p.c_sm = c_sm;
+  p.c_sn = c_sn;
+  p.shift_a = shift_a;
+  p.shift_b = shift_b;
+  p.batch = (int)batch;
+  p.M = (int)m;
+  p.N = (int)n;
+  p.K = (int)k;
+  p.c_vec = (c_sn == 1 && n % 4 == 0 && c_sm % 4 == 0 && c_sb % 4 == 0 && aligned16(c)) ? 1 : 0;
+
+  // Operand staging layout: K-major unless the M (resp. N) axis is the
+  // unit-stride one.  16-byte loads need the unit-stride axis, every other
+  // stride and the base pointers to be multiples of four elements.
+  const bool ak = !(a_sm == 1 && a_sk != 1);
+  const bool bk = !(b_sn == 1) && b_sk == 1;
+  const bool a_al = aligned16(a) && (a2 == nullptr || aligned16(a2));
+  const bool a_vec = a_al && a_sb % 4 == 0 &&
+                     (ak ? (a_sk == 1 && k % 4 == 0 && a_sm % 4 == 0) : (a_sm == 1 && m % 4 == 0 && a_sk % 4 == 0));
+  const bool b_vec = aligned16(b) && b_sb % 4 == 0 &&
+                     (bk ? (b_sk == 1 && k % 4 == 0 && b_sn % 4 == 0) : (b_sn == 1 && n % 4 == 0 && b_sk % 4 == 0));
+  return launch_gemm(p, ak, bk, a_vec && b_vec, s);
+}
+
+xe_status gemm_check(const char* who, const float* a, const float* b, const float* c, int64_t batch, int64_t m,
+                     int64_t n, int64_t k) {
+  if (!a || !b || !c) return fail(XE_ERR_INVALID_ARGUMENT, "%s: null operand pointer", who);
+  if (batch < 0 || m < 0 || n < 0 || k < 0) return fail(XE_ERR_INVALID_ARGUMENT, "%s: negative extent", who);
+  if (k == 0)
+    return fail(XE_ERR_INVALID_ARGUMENT, "%s: the contracted extent is empty (reduction over size 0)", who);
+  if (batch > INT32_MAX || m > INT32_MAX || n > INT32_MAX || k > INT32_MAX)
+    return fail(XE_ERR_NOT_SUPPORTED, "%s: extents above 2^31-1 are not supported", who);
+  return XE_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+xe_status xe_logspace_gemm(const float* a, const float* a2, int64_t a_sb, int64_t a_sm, int64_t a_sk, int32_t a_linear,
+                           const float* b, int64_t b_sb, int64_t b_sk, int64_t b_sn, int32_t b_linear, float* c,
+                           int64_t c_sb, int64_t c_sm, int64_t c_sn, int64_t batch, int64_t m, int64_t n, int64_t k,
+                           int32_t shift_mode, void* workspace, size_t workspace_bytes, void* stream) {
+  xe_status st = gemm_check("xe_logspace_gemm", a, b, c, batch, m, n, k);
+  if (st != XE_OK) return st;
+  if (shift_mode != XE_SHIFT_MAX && shift_mode != XE_SHIFT_MIN)
+    return fail(XE_ERR_INVALID_ARGUMENT, "xe_logspace_gemm: unknown shift mode %d", shift_mode);
+  if (a2 && a_linear)
+    return fail(XE_ERR_INVALID_ARGUMENT, "xe_logspace_gemm: a fused addend requires a log-domain A operand");
+  if (batch == 0 || m == 0 || n == 0) return XE_OK;
+  const size_t need = xe_logspace_gemm_workspace_size(batch, m, n, k, a_linear, b_linear);
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need))
+    return fail(XE_ERR_INVALID_ARGUMENT, "xe_logspace_gemm: workspace of %zu bytes required, %zu given", need,
+                workspace_bytes);
+  if ((reinterpret_cast<uintptr_t>(workspace) & (kAlign - 1)) != 0)
+    return fail(XE_ERR_INVALID_ARGUMENT, "xe_logspace_gemm: workspace must be 256-byte aligned");
+
+  cudaStream_t s = as_stream(stream);
+  const bool maxmode = shift_mode == XE_SHIFT_MAX;
+  float* ws = static_cast<float*>(workspace);
+  float* shift_a = nullptr;
+  float* shift_b = nullptr;
+  if (!a_linear) {
+    shift_a = ws;
+    ws = reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + round_up((size_t)batch * m * sizeof(float)));
+    st = shift_impl(a, a2, a_sb, a_sm, a_sk, batch, m, k, maxmode, shift_a, s);
+    if (st != XE_OK) return st;
+  }
+  if (!b_linear) {
+    shift_b = ws;
+    st = shift_impl(b, nullptr, b_sb, b_sn, b_sk, batch, n, k, maxmode, shift_b, s);
+    if (st != XE_OK) return st;
+  }
+  return gemm_launch(a, a2, a_sb, a_sm, a_sk, shift_a, b, b_sb, b_sk, b_sn, shift_b, c, c_sb, c_sm, c_sn, batch, m, n,
+                     k, s);
+}
+
+xe_status xe_logspace_gemm_shifted(const float* a, const float* a2, int64_t a_sb, int64_t a_sm, int64_t a_sk,
+                                   const float* shift_a, const float* b, int64_t b_sb, int64_t b_sk, int64_t b_sn,
+                                   const float* shift_b, float* c, int64_t c_sb, int64_t c_sm, int64_t c_sn,
+                                   int64_t batch, int64_t m, int64_t n, int64_t k, void* stream) {
+  xe_status st = gemm_check("xe_logspace_gemm_shifted", a, b, c, batch, m, n, k);
+  if (st != XE_OK) return st;
+  if (a2 && !shift_a)
+    return fail(XE_ERR_INVALID_ARGUMENT, "xe_logspace_gemm_shifted: a fused addend requires a log-domain A operand");
+  if (batch == 0 || m == 0 || n == 0) return XE_OK;
+  return gemm_launch(a, a2, a_sb, a_sm, a_sk, shift_a, b, b_sb, b_sk, b_sn, shift_b, c, c_sb, c_sm, c_sn, batch, m, n,
+                     k, as_stream(stream));
+}
+
+xe_status xe_softmax(const float* x, float* y, int64_t outer, int64_t axis_len, int64_t inner, int32_t log_output,
+                     void* stream) {
+  if (!x || !y) return fail(XE_ERR_INVALID_ARGUMENT, "xe_softmax: null pointer");
+  if (outer < 0 || axis_len < 0 || inner < 0) return fail(XE_ERR_INVALID_ARGUMENT, "xe_softmax: negative extent");
+  if (outer == 0 || axis_len == 0 || inner == 0) return XE_OK;
+  cudaStream_t s = as_stream(stream);
+  const int lo = log_output ? 1 : 0;
+  if (inner > 1) {
+    const int64_t fibres = outer * inner;
+    xe::softmax_strided<<<(unsigned)((fibres + 255) / 256), 256, 0, s>>>(x, y, outer, axis_len, inner, lo);
+    return check_launch("xe_softmax");
+  }
+  const bool vec = aligned16(x) && aligned16(y) && axis_len % 4 == 0;
+  const int64_t rows = outer, len = axis_len;
+#define XE_SOFTMAX_WARP(Q)                                                                                   \
+  do {                                                                                                       \
+    const unsigned blocks = (unsigned)((rows + 7) / 8);                                                      \
+    if (vec) xe::softmax_rows_reg<32, Q, true><<<blocks, 256, 0, s>>>(x, y, rows, len, lo);                   \
+    else xe::softmax_rows_reg<32, Q, false><<<blocks, 256, 0, s>>>(x, y, rows, len, lo);                      \
+  } while (0)
+#define XE_SOFTMAX_BLOCK(T, Q)                                                                               \
+  do {                                                                                                       \
+    if (vec) xe::softmax_rows_reg<T, Q, true><<<(unsigned)rows, T, 0, s>>>(x, y, rows, len, lo);              \
+    else xe::softmax_rows_reg<T, Q, false><<<(unsigned)rows, T, 0, s>>>(x, y, rows, len, lo);                 \
+  } while (0)
+  if (len <= 128) XE_SOFTMAX_WARP(1);
+  else if (len <= 512) XE_SOFTMAX_WARP(4);
+  else if (len <= 1024) XE_SOFTMAX_WARP(8);
+  else if (len <= 4096) XE_SOFTMAX_BLOCK(256, 4);
+  else if (len <= 16384) XE_SOFTMAX_BLOCK(1024, 4);
+  else if (len <= 32768) XE_SOFTMAX_BLOCK(1024, 8);
+  else if (len <= 65536) XE_SOFTMAX_BLOCK(1024, 16);
+  else xe::softmax_rows_stream<<<(unsigned)rows, 1024, 0, s>>>(x, y, len, lo);
+#undef XE_SOFTMAX_WARP
+#undef XE_SOFTMAX_BLOCK
+  return check_launch("xe_softmax");
+}
+
+xe_status xe_log_add(const float* a, const int64_t* a_strides, const float* b, const int64_t* b_strides, float* y,
+                     const int64_t* shape, int32_t ndim, int32_t negate_b, void* stream) {
+  if (!a || !b || !y || !shape || !a_strides || !b_strides) return fail(XE_ERR_INVALID_ARGUMENT, "xe_log_add: null pointer");
+  if (ndim < 0 || ndim > 6) return fail(XE_ERR_NOT_SUPPORTED, "xe_log_add: rank %d above 6 is not supported", ndim);
+  xe::NdShape sh{};
+  int64_t total = 0;
+  bool contig = false;
+  if (!make_nd(shape, a_strides, b_strides, ndim, sh, total, contig)) return fail(XE_ERR_INVALID_ARGUMENT, "xe_log_add: negative extent");
+  if (total == 0) return XE_OK;
+  const float sign = negate_b ? -1.0f : 1.0f;
+  cudaStream_t s = as_stream(stream);
+  const int cap = current_device_sms() * 8;
+  if (contig && total % 4 == 0 && aligned16(a) && aligned16(b) && aligned16(y)) {
+    const int64_t n4 = total / 4;
+    xe::log_add_contig4<<<(unsigned)grid_for(n4, 256, cap), 256, 0, s>>>(
+        reinterpret_cast<const float4*>(a), reinterpret_cast<const float4*>(b), reinterpret_cast<float4*>(y), n4, sign);
+  } else {
+    xe::log_add_nd<<<(unsigned)grid_for(total, 256, cap), 256, 0, s>>>(a, b, y, sh, total, sign);
+  }
+  return check_launch("xe_log_add");
+}
+
+xe_status xe_categorical_gather(const float* table, const uint8_t* pixels, int64_t pixel_stride,
+                                const int32_t* var_of_fold, float* y, int64_t folds, int64_t states, int64_t units,
+                                int64_t batch, void* stream) {
+  if (!table || !pixels || !y) return fail(XE_ERR_INVALID_ARGUMENT, "xe_categorical_gather: null pointer");
+  if (folds < 0 || states <= 0 || units < 0 || batch < 0)
+    return fail(XE_ERR_INVALID_ARGUMENT, "xe_categorical_gather: invalid extents");
+  if (states > 256) return fail(XE_ERR_INVALID_ARGUMENT, "xe_categorical_gather: uint8 pixels address at most 256 states");
+  if (folds == 0 || units == 0 || batch == 0) return XE_OK;
+  cudaStream_t s = as_stream(stream);
+  const int cap = current_device_sms() * 8;
+  if (units % 4 == 0 && aligned16(table) && aligned16(y)) {
+    const int64_t total = folds * batch * (units / 4);
+    xe::categorical_gather4<<<(unsigned)grid_for(total, 256, cap), 256, 0, s>>>(table, pixels, pixel_stride, var_of_fold,
+                                                                                y, folds, states, units, batch);
+  } else {
+    const int64_t total = folds * batch * units;
+    xe::categorical_gather1<<<(unsigned)grid_for(total, 256, cap), 256, 0, s>>>(table, pixels, pixel_stride, var_of_fold,
+                                                                                y, folds, states, units, batch);
+  }
+  return check_launch("xe_categorical_gather");
+}
+
+xe_status xe_logspace_reduce(const float* x, int64_t sb, int64_t sr, int64_t sk, int64_t batch, int64_t rows, int64_t k,
+                             int32_t shift_mode, float* y, void* stream) {
+  if (!x || !y) return fail(XE_ERR_INVALID_ARGUMENT, "xe_logspace_reduce: null pointer");
+  if (batch < 0 || rows < 0 || k <= 0)
+    return fail(XE_ERR_INVALID_ARGUMENT, "xe_logspace_reduce: the reduced axes must be non-empty (k=%lld)", (long long)k);
+  if (shift_mode != XE_SHIFT_MAX && shift_mode != XE_SHIFT_MIN)
+    return fail(XE_ERR_INVALID_ARGUMENT, "xe_logspace_reduce: unknown shift mode %d", shift_mode);
+  if (batch == 0 || rows == 0) return XE_OK;
+  cudaStream_t s = as_stream(stream);
+  const bool mx = shift_mode == XE_SHIFT_MAX;
+  if (sr == 1 && sk != 1) {
+    dim3 block(32, 8), grid((unsigned)((rows + 31) / 32), (unsigned)batch);
+    if (mx) xe::lse_rows_colwise<true><<<grid, block, 0, s>>>(x, sb, sk, rows, k, y);
+    else xe::lse_rows_colwise<false><<<grid, block, 0, s>>>(x, sb, sk, rows, k, y);
+  } else {
+    const bool vec = aligned16(x) && sk == 1 && k % 4 == 0 && sr % 4 == 0 && sb % 4 == 0;
+    const unsigned blocks = (unsigned)((batch * rows + 7) / 8);
+    if (mx) {
+      if (vec) xe::lse_rows_warp<true, true><<<blocks, 256, 0, s>>>(x, sb, sr, sk, batch, rows, k, y);
+      else xe::lse_rows_warp<true, false><<<blocks, 256, 0, s>>>(x, sb, sr, sk, batch, rows, k, y);
+    } else {
+      if (vec) xe::lse_rows_warp<false, true><<<blocks, 256, 0, s>>>(x, sb, sr, sk, batch, rows, k, y);
+      else xe::lse_rows_warp<false, false><<<blocks, 256, 0, s>>>(x, sb, sr, sk, batch, rows, k, y);
+    }
+  }
+  return check_launch("xe_logspace_reduce");
+}
+
+xe_status xe_log_add_exp(const float* a, const int64_t* a_strides, int64_t a_numel, const float* b,
+                         const int64_t* b_strides, int64_t b_numel, float* y, const int64_t* shape, int32_t ndim,
+                         int32_t subtract, int32_t shift_mode, float* scratch, void* stream) {
+  if (!a || !b || !y || !shape || !a_strides || !b_strides || !scratch)
+    return fail(XE_ERR_INVALID_ARGUMENT, "xe_log_add_exp: null pointer");
+  if (ndim < 0 || ndim > 6) return fail(XE_ERR_NOT_SUPPORTED, "xe_log_add_exp: rank %d above 6 is not supported", ndim);
+  if (a_numel <= 0 || b_numel <= 0) return fail(XE_ERR_INVALID_ARGUMENT, "xe_log_add_exp: empty operand");
+  if (shift_mode != XE_SHIFT_MAX && shift_mode != XE_SHIFT_MIN)
+    return fail(XE_ERR_INVALID_ARGUMENT, "xe_log_add_exp: unknown shift mode %d", shift_mode);
+  xe::NdShape sh{};
+  int64_t total = 0;
+  bool contig = false;
+  if (!make_nd(shape, a_strides, b_strides, ndim, sh, total, contig))
+    return fail(XE_ERR_INVALID_ARGUMENT, "xe_log_add_exp: negative extent");
+  if (total == 0) return XE_OK;
+  cudaStream_t s = as_stream(stream);
+  if (shift_mode == XE_SHIFT_MAX) xe::global_extreme2<true><<<1, 1024, 0, s>>>(a, a_numel, b, b_numel, scratch);
+  else xe::global_extreme2<false><<<1, 1024, 0, s>>>(a, a_numel, b, b_numel, scratch);
+  const int cap = current_device_sms() * 8;
+  xe::log_add_exp_nd<<<(unsigned)grid_for(total, 256, cap), 256, 0, s>>>(a, b, y, sh, total, scratch, subtract ? 1 : 0);
+  return check_launch("xe_log_add_exp");
+}
+
+xe_status xe_unary(const float* x, float* y, int64_t n, int32_t op, void* stream) {
+  if (!x || !y) return fail(XE_ERR_INVALID_ARGUMENT, "xe_unary: null pointer");
+  if (op != 0 && op != 1) return fail(XE_ERR_INVALID_ARGUMENT, "xe_unary: unknown op %d", op);
+  if (n < 0) return fail(XE_ERR_INVALID_ARGUMENT, "xe_unary: negative extent");
+  if (n == 0) return XE_OK;
+  cudaStream_t s = as_stream(stream);
+  const int cap = current_device_sms() * 8;
+  if (n % 4 == 0 && aligned16(x) && aligned16(y)) {
+    const int64_t n4 = n / 4;
+    const unsigned g = (unsigned)grid_for(n4, 256, cap);
+    if (op == 0) xe::unary_map4<0><<<g, 256, 0, s>>>(reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(y), n4);
+    else xe::unary_map4<1><<<g, 256, 0, s>>>(reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(y), n4);
+  } else {
+    const unsigned g = (unsigned)grid_for(n, 256, cap);
+    if (op == 0) xe::unary_map<0><<<g, 256, 0, s>>>(x, y, n);
+    else xe::unary_map<1><<<g, 256, 0, s>>>(x, y, n);
+  }
+  return check_launch("xe_unary");
+}
+
+xe_status xe_logspace_tucker(const float* l, const float* r, const float* w, float* y, int64_t batch, int64_t folds,
+                             int64_t i_dim, int64_t j_dim, int64_t o_dim, int32_t shift_mode, void* stream) {
+  return xe_tucker_impl(l, r, w, y, batch, folds, i_dim, j_dim, o_dim, shift_mode, as_stream(stream));
+}
+
+}  // extern "C"
+
+static xe_status xe_tucker_impl(const float*, const float*, const float*, float*, int64_t, int64_t, int64_t, int64_t,
+                                int64_t, int32_t, cudaStream_t) {
+  return fail(XE_ERR_NOT_SUPPORTED, "xe_logspace_tucker: not built yet");
+}

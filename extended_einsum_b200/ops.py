@@ -1,0 +1,323 @@
+"""Torch-tensor entry points over the sm_100a C ABI.
+
+Each function validates its operands (CUDA, float32, one device), allocates
+the outputs and the scratch buffers with torch's caching allocator, and calls
+one entry point of libxe_b200.so on torch's current stream.  There is no CPU
+path: a CPU tensor is a ValueError, exactly like an unsupported shape in the
+reference raises instead of silently switching implementations.
+"""
+
+from __future__ import annotations
+
+import math
+from collections.abc import Sequence
+
+import torch
+
+from . import _lib
+
+SHIFT_MODES = {"max": _lib.XE_SHIFT_MAX, "min": _lib.XE_SHIFT_MIN}
+
+
+def _check_tensors(what: str, *tensors: torch.Tensor) -> torch.device:
+    device = None
+    for t in tensors:
+        if not isinstance(t, torch.Tensor):
+            raise TypeError(f"{what}: expected torch.Tensor, got {type(t).__name__}")
+        if t.device.type != "cuda":
+            raise ValueError(f"{what}: the B200 kernels take CUDA tensors, got a tensor on {t.device}")
+        if t.dtype != torch.float32:
+            raise NotImplementedError(f"{what}: only float32 is implemented, got {t.dtype}")
+        if device is None:
+            device = t.device
+        elif t.device != device:
+            raise ValueError(f"{what}: tensors on different devices ({device} and {t.device})")
+    assert device is not None
+    return device
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _shift(mode: str) -> int:
+    try:
+        return SHIFT_MODES[mode]
+    except KeyError:
+        raise ValueError(f"unknown shift mode {mode!r}; expected 'max' or 'min'") from None
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+# ---------------------------------------------------------------------------
+# log-space contraction
+
+
+def logspace_gemm(
+    a: torch.Tensor,
+    b: torch.Tensor,
+    *,
+    a2: torch.Tensor | None = None,
+    a_linear: bool = False,
+    b_linear: bool = False,
+    shift: str = "max",
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """C[t,m,n] = log(sum_k A'[t,m,k] B'[t,k,n]) + shifts (xe_logspace_gemm).
+
+    ``a`` is (batch, M, K) and ``b`` (batch, K, N), any strides; a log-domain
+    operand X enters as exp(X - shift) with shift = max (or min) over k and the
+    shift is added back, a linear operand enters as is.  ``a2`` (same shape
+    and strides as ``a``) is added to ``a`` in the log domain first.
+    """
+    tensors = [a, b] + ([a2] if a2 is not None else []) + ([out] if out is not None else [])
+    device = _check_tensors("logspace_gemm", *tensors)
+    if a.dim() != 3 or b.dim() != 3:
+        raise ValueError("logspace_gemm: operands must be 3-D (batch, M, K) and (batch, K, N)")
+    batch, m, k = a.shape
+    if b.shape[0] != batch or b.shape[1] != k:
+        raise ValueError(f"logspace_gemm: incompatible shapes {tuple(a.shape)} and {tuple(b.shape)}")
+    n = b.shape[2]
+    if a2 is not None and (a2.shape != a.shape or a2.stride() != a.stride()):
+        raise ValueError("logspace_gemm: the fused addend must have the shape and strides of A")
+    if out is None:
+        out = torch.empty((batch, m, n), device=device, dtype=torch.float32)
+    elif out.shape != (batch, m, n):
+        raise ValueError(f"logspace_gemm: out has shape {tuple(out.shape)}, expected {(batch, m, n)}")
+    lib = _lib.load()
+    ws_bytes = lib.xe_logspace_gemm_workspace_size(batch, m, n, k, int(a_linear), int(b_linear))
+    ws = torch.empty(ws_bytes, device=device, dtype=torch.uint8) if ws_bytes else None
+    status = lib.xe_logspace_gemm(
+        a.data_ptr(), _ptr(a2), a.stride(0), a.stride(1), a.stride(2), int(a_linear),
+        b.data_ptr(), b.stride(0), b.stride(1), b.stride(2), int(b_linear),
+        out.data_ptr(), out.stride(0), out.stride(1), out.stride(2),
+        batch, m, n, k, _shift(shift), _ptr(ws), ws_bytes, _stream(device),
+    )
+    _lib.check(status, "xe_logspace_gemm")
+    return out
+
+
+def logspace_gemm_shifted(
+    a: torch.Tensor,
+    b: torch.Tensor,
+    shift_a: torch.Tensor | None,
+    shift_b: torch.Tensor | None,
+    *,
+    a2: torch.Tensor | None = None,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """The contraction kernel alone with given shifts (None = linear operand), xe_logspace_gemm_shifted."""
+    extra = [t for t in (a2, out, shift_a, shift_b) if t is not None]
+    device = _check_tensors("logspace_gemm_shifted", a, b, *extra)
+    batch, m, k = a.shape
+    n = b.shape[2]
+    if b.shape[:2] != (batch, k):
+        raise ValueError(f"logspace_gemm_shifted: incompatible shapes {tuple(a.shape)} and {tuple(b.shape)}")
+    for s, size in ((shift_a, m), (shift_b, n)):
+        if s is not None and (not s.is_contiguous() or s.numel() != batch * size):
+            raise ValueError("logspace_gemm_shifted: shifts must be contiguous (batch, rows) vectors")
+    if out is None:
+        out = torch.empty((batch, m, n), device=device, dtype=torch.float32)
+    status = _lib.load().xe_logspace_gemm_shifted(
+        a.data_ptr(), _ptr(a2), a.stride(0), a.stride(1), a.stride(2), _ptr(shift_a),
+        b.data_ptr(), b.stride(0), b.stride(1), b.stride(2), _ptr(shift_b),
+        out.data_ptr(), out.stride(0), out.stride(1), out.stride(2),
+        batch, m, n, k, _stream(device),
+    )
+    _lib.check(status, "xe_logspace_gemm_shifted")
+    return out
+
+
+def logspace_shift(x: torch.Tensor, *, shift: str = "max", x2: torch.Tensor | None = None) -> torch.Tensor:
+    """Per-row max (or min) over the last axis of a (batch, rows, k) view."""
+    device = _check_tensors("logspace_shift", x, *([x2] if x2 is not None else []))
+    if x.dim() != 3:
+        raise ValueError("logspace_shift: expected a (batch, rows, k) tensor")
+    batch, rows, k = x.shape
+    out = torch.empty((batch, rows), device=device, dtype=torch.float32)
+    status = _lib.load().xe_logspace_shift(
+        x.data_ptr(), _ptr(x2), x.stride(0), x.stride(1), x.stride(2), batch, rows, k, _shift(shift),
+        out.data_ptr(), _stream(device),
+    )
+    _lib.check(status, "xe_logspace_shift")
+    return out
+
+
+def logspace_reduce(x: torch.Tensor, *, shift: str = "max") -> torch.Tensor:
+    """y[t,r] = log(sum_k exp(x[t,r,k] - s)) + s over a (batch, rows, k) view."""
+    device = _check_tensors("logspace_reduce", x)
+    if x.dim() != 3:
+        raise ValueError("logspace_reduce: expected a (batch, rows, k) tensor")
+    batch, rows, k = x.shape
+    out = torch.empty((batch, rows), device=device, dtype=torch.float32)
+    status = _lib.load().xe_logspace_reduce(
+        x.data_ptr(), x.stride(0), x.stride(1), x.stride(2), batch, rows, k, _shift(shift), out.data_ptr(),
+        _stream(device),
+    )
+    _lib.check(status, "xe_logspace_reduce")
+    return out
+
+
+# ---------------------------------------------------------------------------
+# softmax
+
+
+def softmax(x: torch.Tensor, axis: int | Sequence[int], *, log_output: bool = False) -> torch.Tensor:
+    """Softmax over one axis or a set of axes (TorchBackendFunctions.softmax semantics).
+
+    A consecutive block of axes is flattened into one reduced axis (as
+    backends/torch.py:107-110 does for a trailing block); other axis sets are
+    moved to the end first.
+    """
+    device = _check_tensors("softmax", x)
+    if x.dim() == 0:
+        raise ValueError("softmax requires an input tensor with at least one axis")
+    axes = (axis,) if isinstance(axis, int) else tuple(axis)
+    if not axes:
+        raise ValueError("softmax requires at least one axis")
+    nd = x.dim()
+    axes = tuple(sorted(a + nd if a < 0 else a for a in axes))
+    if any(not 0 <= a < nd for a in axes) or len(set(axes)) != len(axes):
+        raise ValueError(f"softmax axes {axis} are invalid for a {nd}-D tensor")
+    permuted = None
+    if axes != tuple(range(axes[0], axes[-1] + 1)):
+        keep = [d for d in range(nd) if d not in axes]
+        permuted = keep + list(axes)
+        x = x.permute(permuted)
+        axes = tuple(range(nd - len(axes), nd))
+    x = x.contiguous()
+    shape = x.shape
+    outer = math.prod(shape[: axes[0]])
+    length = math.prod(shape[axes[0] : axes[-1] + 1])
+    inner = math.prod(shape[axes[-1] + 1 :])
+    y = torch.empty_like(x)
+    status = _lib.load().xe_softmax(x.data_ptr(), y.data_ptr(), outer, length, inner, int(log_output), _stream(device))
+    _lib.check(status, "xe_softmax")
+    if permuted is not None:
+        inverse = [0] * nd
+        for i, d in enumerate(permuted):
+            inverse[d] = i
+        y = y.permute(inverse)
+    return y
+
+
+# ---------------------------------------------------------------------------
+# elementwise log-space arithmetic
+
+
+def _broadcast_strides(t: torch.Tensor, shape: torch.Size) -> list[int]:
+    return list(t.expand(shape).stride())
+
+
+def log_add(a: torch.Tensor, b: torch.Tensor, *, negate_b: bool = False) -> torch.Tensor:
+    """y = a + b (or a - b) with numpy broadcasting: a log-space product (quotient)."""
+    device = _check_tensors("log_add", a, b)
+    shape = torch.broadcast_shapes(a.shape, b.shape)
+    if len(shape) > 6:
+        raise NotImplementedError(f"log_add: rank {len(shape)} above 6 is not supported")
+    y = torch.empty(shape, device=device, dtype=torch.float32)
+    status = _lib.load().xe_log_add(
+        a.data_ptr(), _lib.int64_array(_broadcast_strides(a, shape)),
+        b.data_ptr(), _lib.int64_array(_broadcast_strides(b, shape)),
+        y.data_ptr(), _lib.int64_array(shape), len(shape), int(negate_b), _stream(device),
+    )
+    _lib.check(status, "xe_log_add")
+    return y
+
+
+def log_add_exp(a: torch.Tensor, b: torch.Tensor, *, subtract: bool = False, shift: str = "max") -> torch.Tensor:
+    """y = log(exp(a - m) +/- exp(b - m)) + m with the scalar m = extreme of a and b."""
+    device = _check_tensors("log_add_exp", a, b)
+    a = a.contiguous()
+    b = b.contiguous()
+    shape = torch.broadcast_shapes(a.shape, b.shape)
+    if len(shape) > 6:
+        raise NotImplementedError(f"log_add_exp: rank {len(shape)} above 6 is not supported")
+    y = torch.empty(shape, device=device, dtype=torch.float32)
+    scratch = torch.empty(1, device=device, dtype=torch.float32)
+    status = _lib.load().xe_log_add_exp(
+        a.data_ptr(), _lib.int64_array(_broadcast_strides(a, shape)), a.numel(),
+        b.data_ptr(), _lib.int64_array(_broadcast_strides(b, shape)), b.numel(),
+        y.data_ptr(), _lib.int64_array(shape), len(shape), int(subtract), _shift(shift), scratch.data_ptr(),
+        _stream(device),
+    )
+    _lib.check(status, "xe_log_add_exp")
+    return y
+
+
+def _unary(x: torch.Tensor, op: int, what: str) -> torch.Tensor:
+    device = _check_tensors(what, x)
+    x = x.contiguous()
+    y = torch.empty_like(x)
+    _lib.check(_lib.load().xe_unary(x.data_ptr(), y.data_ptr(), x.numel(), op, _stream(device)), what)
+    return y
+
+
+def exp(x: torch.Tensor) -> torch.Tensor:
+    """Log space -> raw (translate.py:631-636)."""
+    return _unary(x, 0, "exp")
+
+
+def log(x: torch.Tensor) -> torch.Tensor:
+    """Raw -> log space (translate.py:639-644)."""
+    return _unary(x, 1, "log")
+
+
+# ---------------------------------------------------------------------------
+# circuit inputs
+
+
+def categorical_gather(
+    log_table: torch.Tensor, pixels: torch.Tensor, var_of_fold: torch.Tensor | None = None
+) -> torch.Tensor:
+    """y[f,b,:] = log_table[f, pixels[b, var_of_fold[f]], :] for uint8 pixels (batch, variables)."""
+    device = _check_tensors("categorical_gather", log_table)
+    if pixels.device != device or pixels.dtype != torch.uint8 or pixels.dim() != 2:
+        raise ValueError("categorical_gather: pixels must be a (batch, variables) uint8 tensor on the table's device")
+    if pixels.stride(1) != 1:
+        pixels = pixels.contiguous()
+    folds, states, units = log_table.shape
+    log_table = log_table.contiguous()
+    batch = pixels.shape[0]
+    if var_of_fold is not None:
+        if var_of_fold.dtype != torch.int32 or var_of_fold.device != device or var_of_fold.numel() != folds:
+            raise ValueError("categorical_gather: var_of_fold must be int32 with one entry per fold")
+        var_of_fold = var_of_fold.contiguous()
+    elif pixels.shape[1] < folds:
+        raise ValueError("categorical_gather: fewer pixel variables than folds")
+    y = torch.empty((folds, batch, units), device=device, dtype=torch.float32)
+    status = _lib.load().xe_categorical_gather(
+        log_table.data_ptr(), pixels.data_ptr(), pixels.stride(0), _ptr(var_of_fold), y.data_ptr(),
+        folds, states, units, batch, _stream(device),
+    )
+    _lib.check(status, "xe_categorical_gather")
+    return y
+
+
+def logspace_tucker(
+    left: torch.Tensor, right: torch.Tensor, weights: torch.Tensor, *, shift: str = "max"
+) -> torch.Tensor:
+    """y[b,f,o] = log(sum_ij exp(l-sl) exp(r-sr) w[f,o,i,j]) + sl + sr (xe_logspace_tucker)."""
+    device = _check_tensors("logspace_tucker", left, right, weights)
+    if left.dim() != 3 or right.dim() != 3 or weights.dim() != 4:
+        raise ValueError("logspace_tucker: expected (B,F,I), (B,F,J) and (F,O,I,J) tensors")
+    batch, folds, i_dim = left.shape
+    j_dim = right.shape[2]
+    o_dim = weights.shape[1]
+    if right.shape[:2] != (batch, folds) or weights.shape != (folds, o_dim, i_dim, j_dim):
+        raise ValueError("logspace_tucker: incompatible shapes")
+    left, right, weights = left.contiguous(), right.contiguous(), weights.contiguous()
+    y = torch.empty((batch, folds, o_dim), device=device, dtype=torch.float32)
+    status = _lib.load().xe_logspace_tucker(
+        left.data_ptr(), right.data_ptr(), weights.data_ptr(), y.data_ptr(), batch, folds, i_dim, j_dim, o_dim,
+        _shift(shift), _stream(device),
+    )
+    _lib.check(status, "xe_logspace_tucker")
+    return y
+
+
+def device_status(clear: bool = True) -> int:
+    """The device-side status word (non-zero after a bounded wait ran out)."""
+    return int(_lib.load().xe_device_status(int(clear)))

@@ -1,0 +1,181 @@
+/*
+ * xe_b200.h — C ABI of the B200 (sm_100a) kernels behind extended_einsum's
+ * stable-materialization hot path.
+ *
+ * Every entry point takes plain device pointers, element strides and sizes,
+ * and a CUDA stream passed as `void*` (a `cudaStream_t`; NULL = legacy default
+ * stream).  Nothing here allocates device memory: outputs and scratch buffers
+ * are allocated by the caller.  All calls are stream-ordered and asynchronous;
+ * a non-OK status means nothing was launched (argument errors) or the launch
+ * itself failed.  Device-side waits are bounded: a wait that runs out records
+ * a code that xe_device_status() reports.
+ *
+ * Status codes map onto the exceptions the reference raises on this path:
+ *   XE_ERR_INVALID_ARGUMENT -> ValueError          (backend_translation/runtime.py:13-14)
+ *   XE_ERR_NOT_SUPPORTED    -> NotImplementedError (backend_translation/translate.py:41, 585, 810)
+ *   XE_ERR_CUDA, XE_ERR_DEVICE_TIMEOUT -> RuntimeError
+ *
+ * Reference paths below are relative to the extended_einsum project root.
+ */
+#ifndef XE_B200_H
+#define XE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  XE_OK = 0,
+  XE_ERR_INVALID_ARGUMENT = 1,
+  XE_ERR_NOT_SUPPORTED = 2,
+  XE_ERR_CUDA = 3,
+  XE_ERR_DEVICE_TIMEOUT = 4
+} xe_status;
+
+/* Which per-operand shift the log-space lowering uses
+ * (translate.py:698: max for logspace_max, min for logspace_min). */
+typedef enum { XE_SHIFT_MAX = 0, XE_SHIFT_MIN = 1 } xe_shift_mode;
+
+/* Library version as MAJOR*10000 + MINOR*100 + PATCH. */
+int xe_version(void);
+
+/* Human-readable message of the most recent failing call on this host thread. */
+const char* xe_last_error_string(void);
+
+/* Reads (and with `clear` != 0 resets) the device-side status word of the
+ * current device: 0 when no bounded wait ran out since the last clear,
+ * otherwise an XE_ERR_DEVICE_TIMEOUT-class code with the site in the low bits.
+ * Synchronises the current device. */
+int xe_device_status(int clear);
+
+/* ------------------------------------------------------------------------ */
+/* Log-space batched contraction (the GEMM-shaped stable einsum).
+ *
+ * Replaces the call sequence that _append_logspace_einsum
+ * (backend_translation/translate.py:686-750) emits for a binary einsum whose
+ * contracted labels appear in both operands:
+ *   max/min over the contracted axis, stop_gradient, subtract, exp  (:727-740)
+ *   einsum                                                          (:743)
+ *   log, shift reduction + reshape + add per operand                (:744-749)
+ * as executed by TorchBackendFunctions (backends/torch.py:37-118).
+ *
+ *   C[b,m,n] = log( sum_k  A'[b,m,k] * B'[b,k,n] ) (+ sA[b,m]) (+ sB[b,n])
+ *
+ * A log-domain operand X becomes X' = exp(X - sX) with sX its max (or min)
+ * over k; a linear operand (a parameter-derived value, translate.py:723-725)
+ * is used as is and adds no shift.  If `a2` is not NULL the A operand is the
+ * log-domain sum a + a2 (a fused log-space Hadamard product,
+ * translate.py:706-718), read with the strides of `a`.
+ * Element (b,m,k) of A is a[b*a_sb + m*a_sm + k*a_sk]; B (b,k,n) and C (b,m,n)
+ * likewise.  Arithmetic: fp32 in, split-TF32 (3 passes) tensor-core products,
+ * fp32 accumulation, fp32 out.
+ *
+ * `workspace` must hold xe_logspace_gemm_workspace_size(...) bytes of device
+ * memory (the shift vectors); it may be NULL when that size is 0.
+ */
+size_t xe_logspace_gemm_workspace_size(int64_t batch, int64_t m, int64_t n, int64_t k,
+                                       int32_t a_linear, int32_t b_linear);
+
+xe_status xe_logspace_gemm(const float* a, const float* a2, int64_t a_sb, int64_t a_sm, int64_t a_sk,
+                           int32_t a_linear,
+                           const float* b, int64_t b_sb, int64_t b_sk, int64_t b_sn, int32_t b_linear,
+                           float* c, int64_t c_sb, int64_t c_sm, int64_t c_sn,
+                           int64_t batch, int64_t m, int64_t n, int64_t k, int32_t shift_mode,
+                           void* workspace, size_t workspace_bytes, void* stream);
+
+/* The contraction kernel of xe_logspace_gemm alone, with caller-provided
+ * shift vectors: `shift_a` (batch*m floats) for a log-domain A, NULL for a
+ * linear A; `shift_b` (batch*n floats) likewise.  xe_logspace_gemm is
+ * xe_logspace_shift for each log-domain operand followed by this call. */
+xe_status xe_logspace_gemm_shifted(const float* a, const float* a2, int64_t a_sb, int64_t a_sm, int64_t a_sk,
+                                   const float* shift_a,
+                                   const float* b, int64_t b_sb, int64_t b_sk, int64_t b_sn, const float* shift_b,
+                                   float* c, int64_t c_sb, int64_t c_sm, int64_t c_sn,
+                                   int64_t batch, int64_t m, int64_t n, int64_t k, void* stream);
+
+/* Per-row shift of a strided 3-D operand: out[b*R + r] = max_k (or min_k) of
+ * x[b*sb + r*sr + k*sk] (+ x2[...] when x2 is not NULL).  This is the
+ * `max(x, axis=reduction_axes, keepdims=True)` call of translate.py:733
+ * (TorchBackendFunctions.max -> torch.amax, backends/torch.py:37-48). */
+xe_status xe_logspace_shift(const float* x, const float* x2, int64_t sb, int64_t sr, int64_t sk,
+                            int64_t batch, int64_t rows, int64_t k, int32_t shift_mode,
+                            float* out, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Softmax over the middle axis of a contiguous (outer, axis, inner) view:
+ *   y[o,a,i] = exp(x[o,a,i] - max_a x[o,:,i]) / sum_a exp(x[o,:,i] - max)
+ * Replaces TorchBackendFunctions.softmax (backends/torch.py:102-113), reached
+ * raw-in/raw-out from translate.py:770-773; a trailing block of axes is
+ * flattened into one axis by the caller exactly as torch.py:107-110 does.
+ * `log_output` != 0 writes log(softmax) instead (used for categorical inputs,
+ * whose log is taken next by the log-space lowering, translate.py:639-644). */
+xe_status xe_softmax(const float* x, float* y, int64_t outer, int64_t axis_len, int64_t inner,
+                     int32_t log_output, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Log-space reduction of one operand (an einsum with a single operand, e.g.
+ * 'ij->' or 'ij->i'), as _append_logspace_einsum lowers it
+ * (translate.py:727-749 with one operand: max over the reduced axes, exp,
+ * einsum, log, + shift):
+ *   y[b*R + r] = log( sum_k exp(x[b,r,k] - s) ) + s,   s = max_k (or min_k)
+ * Element (b,r,k) is x[b*sb + r*sr + k*sk]; y is contiguous (batch, rows). */
+xe_status xe_logspace_reduce(const float* x, int64_t sb, int64_t sr, int64_t sk, int64_t batch, int64_t rows,
+                             int64_t k, int32_t shift_mode, float* y, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Log-space product / quotient of up to 6-D broadcast operands:
+ * y = a + b (negate_b == 0) or y = a - b (negate_b != 0).
+ * The contraction-free einsum of translate.py:706-718 (Hadamard / Kronecker
+ * product, lowered by the reference to `add` after _broadcast_einsum_operand),
+ * the log-space multiply of translate.py:790-793 and divide of :794-797.
+ * Shapes/strides are in elements; a broadcast axis has stride 0.  y is
+ * written contiguously in `shape` order. */
+xe_status xe_log_add(const float* a, const int64_t* a_strides, const float* b, const int64_t* b_strides,
+                     float* y, const int64_t* shape, int32_t ndim, int32_t negate_b, void* stream);
+
+/* Log-space sum / difference with a common scalar shift (translate.py:774-789
+ * with _append_shifted, :647-664):
+ *   m = max (or min) over all elements of a and b
+ *   y = log( exp(a - m) + exp(b - m) ) + m      (subtract == 0)
+ *   y = log( exp(a - m) - exp(b - m) ) + m      (subtract != 0)
+ * a, b broadcast as in xe_log_add.  `scratch` is device memory for one float
+ * (the shift m). */
+xe_status xe_log_add_exp(const float* a, const int64_t* a_strides, int64_t a_numel, const float* b,
+                         const int64_t* b_strides, int64_t b_numel, float* y, const int64_t* shape, int32_t ndim,
+                         int32_t subtract, int32_t shift_mode, float* scratch, void* stream);
+
+/* Elementwise domain conversion of a contiguous array (translate.py:631-644):
+ * op 0: y = exp(x) (log space -> raw), op 1: y = log(x) (raw -> log space). */
+xe_status xe_unary(const float* x, float* y, int64_t n, int32_t op, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Categorical input units of the circuit (demo/cirkit.py:525-527 builds
+ * softmax(logits, dim=1)[v, x[b,v], :] in torch; the log-space lowering then
+ * takes its log, translate.py:639-644):
+ *   y[f,b,:] = table[f, pixels[b*pixel_stride + var_of_fold[f]], :]
+ * table is (folds, states, units) and already in the log domain (see
+ * xe_softmax with log_output).  var_of_fold may be NULL for the identity. */
+xe_status xe_categorical_gather(const float* table, const uint8_t* pixels, int64_t pixel_stride,
+                                const int32_t* var_of_fold, float* y, int64_t folds, int64_t states,
+                                int64_t units, int64_t batch, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Log-space Tucker layer 'bfi,bfj,foij->bfo' (the ternary einsum that
+ * OptimizeContractionPaths fuses for Tucker circuits, preprocess.py:1095-1106,
+ * lowered by _append_logspace_einsum, translate.py:686-750):
+ *   y[b,f,o] = log( sum_ij exp(l[b,f,i]-sl) exp(r[b,f,j]-sr) w[f,o,i,j] ) + sl[b,f] + sr[b,f]
+ * with sl = max_i (or min_i) l[b,f,:], sr likewise, and w linear.
+ * l, r are (batch, folds, I) / (batch, folds, J) contiguous, w is
+ * (folds, O, I, J) contiguous, y is (batch, folds, O) contiguous. */
+xe_status xe_logspace_tucker(const float* l, const float* r, const float* w, float* y, int64_t batch,
+                             int64_t folds, int64_t i_dim, int64_t j_dim, int64_t o_dim, int32_t shift_mode,
+                             void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* XE_B200_H */

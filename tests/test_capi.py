@@ -1,0 +1,77 @@
+"""The C-ABI library: it loads, exports every entry point that include/xe_b200.h
+declares, and rejects invalid arguments before touching the device (no GPU)."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from extended_einsum_b200 import _lib
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "xe_b200.h"
+
+
+def header_functions() -> set[str]:
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    return set(re.findall(r"\b(xe_\w+)\s*\(", text))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    declared = header_functions()
+    assert len(declared) >= 12
+    for name in declared:
+        assert hasattr(lib, name), f"{name} declared in xe_b200.h but not exported"
+
+
+def test_binding_covers_the_header():
+    assert set(_lib.SIGNATURES) == header_functions()
+
+
+def test_version_and_error_string():
+    lib = _lib.load()
+    assert lib.xe_version() == 100
+    assert isinstance(_lib.last_error(), str)
+
+
+def test_workspace_size():
+    lib = _lib.load()
+    assert lib.xe_logspace_gemm_workspace_size(2, 100, 30, 8, 0, 0) == 1024 + 256
+    assert lib.xe_logspace_gemm_workspace_size(2, 100, 30, 8, 1, 1) == 0
+    assert lib.xe_logspace_gemm_workspace_size(1, 64, 64, 8, 1, 0) == 256
+
+
+def _gemm(lib, a=1, b=1, c=1, k=4, mode=0, a2=None, a_linear=0, ws=0, ws_bytes=0):
+    return lib.xe_logspace_gemm(a, a2, 0, 4, 1, a_linear, b, 0, 4, 1, 0, c, 0, 4, 1, 1, 4, 4, k, mode, ws, ws_bytes, None)
+
+
+def test_invalid_arguments_are_rejected_without_launch():
+    lib = _lib.load()
+    assert _gemm(lib, a=None) == _lib.XE_ERR_INVALID_ARGUMENT
+    assert "null" in _lib.last_error()
+    assert _gemm(lib, k=0) == _lib.XE_ERR_INVALID_ARGUMENT
+    assert _gemm(lib, mode=7) == _lib.XE_ERR_INVALID_ARGUMENT
+    assert _gemm(lib, a2=1, a_linear=1) == _lib.XE_ERR_INVALID_ARGUMENT
+    assert _gemm(lib, ws=0, ws_bytes=0) == _lib.XE_ERR_INVALID_ARGUMENT  # shifts need a workspace
+    assert "workspace" in _lib.last_error()
+    assert lib.xe_softmax(None, None, 1, 1, 1, 0, None) == _lib.XE_ERR_INVALID_ARGUMENT
+    shape = _lib.int64_array([1] * 7)
+    assert lib.xe_log_add(1, shape, 1, shape, 1, shape, 7, 0, None) == _lib.XE_ERR_NOT_SUPPORTED
+    assert lib.xe_unary(1, 1, 4, 9, None) == _lib.XE_ERR_INVALID_ARGUMENT
+    assert lib.xe_categorical_gather(1, 1, 1, None, 1, 1, 300, 4, 1, None) == _lib.XE_ERR_INVALID_ARGUMENT
+    assert lib.xe_logspace_reduce(1, 0, 1, 1, 1, 1, 0, 0, 1, None) == _lib.XE_ERR_INVALID_ARGUMENT
+
+
+def test_status_maps_to_reference_exceptions():
+    with pytest.raises(ValueError):
+        _lib.check(_lib.XE_ERR_INVALID_ARGUMENT, "x")
+    with pytest.raises(NotImplementedError):
+        _lib.check(_lib.XE_ERR_NOT_SUPPORTED, "x")
+    with pytest.raises(RuntimeError):
+        _lib.check(_lib.XE_ERR_CUDA, "x")
+    with pytest.raises(RuntimeError):
+        _lib.check(_lib.XE_ERR_DEVICE_TIMEOUT, "x")
+    _lib.check(_lib.XE_OK, "x")

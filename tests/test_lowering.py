@@ -1,0 +1,131 @@
+"""Host-side lowering (no GPU): program structure, error behaviour, and
+agreement of the front end with the reference's IR where it is importable."""
+
+from __future__ import annotations
+
+import sys
+from pathlib import Path
+
+import pytest
+import torch
+
+import extended_einsum_b200 as xb
+from conftest import build_program
+from extended_einsum_b200 import frontend as fe
+from extended_einsum_b200.circuit import QuadTreeCircuit, quad_tree_leaf_order
+
+
+def _fns(program):
+    return [getattr(call, "fn", call) for call in program.backend_calls]
+
+
+def test_logspace_matmul_lowers_to_one_call():
+    a = xb.array(torch.zeros(4, 3))
+    b = xb.array(torch.zeros(3, 5))
+    program, inputs = xb.extract_program(xb.log(xb.einsum("ik,kj->ij", xb.exp(a), xb.exp(b))), "logspace_max")
+    lowered = xb.lower(program)
+    # the reference's translation emits 16 calls for this expression (max, detach, subtract,
+    # exp for each operand, einsum, log, and a reduce + reshape + add per shift)
+    assert len(lowered.backend_calls) == 1
+    assert lowered.call_arguments == [(0, 1)]
+
+
+def test_exp_log_roundtrip_is_free():
+    program = fe.dense_program([fe.RichInstruction(fe.OperatorExp(), (0,)), fe.RichInstruction(fe.OperatorLog(), (1,))], 1, "logspace_max")
+    assert len(xb.lower(program).backend_calls) == 0
+
+
+def test_softmax_parameters_stay_linear():
+    instructions = [
+        fe.RichInstruction(fe.OperatorSoftmax(axis=0), (1,)),
+        fe.RichInstruction(fe.OperatorExp(), (0,)),
+        fe.RichInstruction(fe.OperatorEinsum("bi, io -> bo"), (3, 2)),
+        fe.RichInstruction(fe.OperatorLog(), (4,)),
+    ]
+    program = fe.dense_program(instructions, 2, "logspace_max", parameter_indices=frozenset({1}))
+    lowered = xb.lower(program)
+    # softmax + one fused einsum (the reference needs 10 calls)
+    assert len(lowered.backend_calls) == 2
+    einsum_call = lowered.backend_calls[1].fn
+    assert einsum_call.args[1] == (False, True)  # data operand log-space, weights linear
+
+
+def test_unsupported_mode_and_operator_raise_like_the_reference():
+    program = fe.dense_program([fe.RichInstruction(fe.OperatorExp(), (0,))], 1, "unstable")
+    with pytest.raises(NotImplementedError):
+        xb.lower(program)
+
+    class OperatorSin:
+        name = "sin"
+
+    program = fe.dense_program([fe.RichInstruction(OperatorSin(), (0,))], 1, "logspace_max")
+    with pytest.raises(NotImplementedError, match="has no logspace backend translation"):
+        xb.lower(program)
+
+
+def test_run_program_checks_input_count():
+    program = xb.BackendProgram([], [], 2)
+    with pytest.raises(ValueError):
+        xb.run_program(program, [torch.zeros(1)])
+
+
+def test_circuit_program_lowering(golden_programs):
+    program = build_program(golden_programs["circuit_4x4"], "logspace_max")
+    lowered = xb.lower(program)
+    # one log of the raw categorical data input; per level: softmax + fused CP einsum,
+    # plus 2 slices + 1 log-add for levels >= 1; top: 2 selects, 1 log-add, softmax,
+    # root einsum.  The reference's translation of the same program has 63 calls.
+    levels = 4
+    assert len(lowered.backend_calls) == 1 + 2 + 5 * (levels - 1) + 5
+    names = [getattr(f, "func", f) for f in _fns(lowered)]
+    assert names.count(xb.ops.log) == 1 and xb.ops.exp not in names
+
+
+def test_quad_tree_leaf_order_is_a_permutation():
+    for h, w in ((2, 2), (4, 4), (8, 4), (32, 32)):
+        order = quad_tree_leaf_order(h, w)
+        assert sorted(order) == list(range(h * w))
+
+
+def test_quad_tree_regions_are_rectangles():
+    h = w = 8
+    order = quad_tree_leaf_order(h, w)
+    f = h * w
+    regions = [{order[i]} for i in range(f)]
+    while f > 1:
+        f //= 2
+        regions = [regions[i] | regions[i + f] for i in range(f)]
+        for region in regions:
+            rows = {v // w for v in region}
+            cols = {v % w for v in region}
+            assert len(rows) * len(cols) == len(region)
+
+
+def test_circuit_cost_model():
+    c = QuadTreeCircuit(32, 32, 64, 256)
+    assert c.fold_counts == [1024 >> l for l in range(10)]
+    assert c.flops_per_sample() == 2 * 64 * 64 * 2046 + 2 * 64
+    assert c.hbm_bytes_per_sample() == 4 * 64 * (1024 * 3 + 3 * (512 + 256 + 128 + 64 + 32 + 16 + 8 + 4 + 2)) + 4 * (2 * 64 + 1)
+
+
+REFERENCE_SRC = Path("/root/reference/src")
+
+
+@pytest.mark.skipif(not REFERENCE_SRC.exists(), reason="reference source tree not present")
+def test_front_end_matches_reference_extract_program():
+    sys.path.insert(0, str(REFERENCE_SRC))
+    try:
+        import extended_einsum as ref
+        from extended_einsum.interface.tensor_expression import Parameter as RefParameter
+    finally:
+        sys.path.remove(str(REFERENCE_SRC))
+    x = torch.zeros(4, 6, 8)
+    w = torch.zeros(4, 5, 8)
+    ours, _ = xb.extract_program(xb.log(xb.einsum("dac,dbc->dab", xb.exp(xb.array(x)), xb.softmax(xb.Parameter(xb.array(w)), axis=2))), "logspace_max")
+    theirs, _ = ref.extract_program(ref.log(ref.einsum("dac,dbc->dab", ref.exp(ref.array(x)), ref.softmax(RefParameter(ref.array(w)), axis=2))), "logspace_max")
+    assert ours.n_inputs == theirs.n_inputs
+    assert ours.parameter_indices == theirs.parameter_indices
+    assert list(map(tuple, ours.shapes)) == list(map(tuple, theirs.shapes))
+    assert [(i.operator.name, i.argument_ssa_ids) for i in ours.instructions] == [(i.operator.name, i.argument_ssa_ids) for i in theirs.instructions]
+    # the lowering accepts the reference's own program object
+    assert len(xb.lower(theirs).backend_calls) == len(xb.lower(ours).backend_calls) == 2
