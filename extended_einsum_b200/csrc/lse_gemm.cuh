@@ -4,20 +4,25 @@
 //
 // This is the arithmetic that _append_logspace_einsum
 // (backend_translation/translate.py:686-750) spreads over ~16 backend calls
-// for a binary contraction, fused into one persistent kernel:
+// for a binary contraction, fused into one persistent kernel.  Roles (warps):
 //
-//   transform warps (8)  global fp32 tile -> exp(x - shift) (or the linear
-//                        value) -> TF32 hi/lo split -> 128B-swizzled UMMA
-//                        tiles in shared memory (generic-proxy stores)
-//   MMA warp (1 thread)  three tcgen05.mma kind::tf32 per k-step:
-//                        hi*hi into the main TMEM accumulator and
-//                        hi*lo + lo*hi into a separate correction accumulator
-//   epilogue warps (4)   tcgen05.ld -> log(main + corr) + shifts -> global
+//   A transform (0-3)  one thread per tile row: global fp32 -> exp(x - shift)
+//                      (or the linear value, or the Tucker outer product) ->
+//                      TF32 hi/lo split -> tcgen05.st into a TMEM stage
+//   B transform (4-7)  global fp32 -> exp / split -> 128B-swizzled smem stage
+//   MMA (8, 1 thread)  per 8-wide k-step: main += A_hi*B_hi,
+//                      corr += A_hi*B_lo + A_lo*B_hi  (tcgen05.mma, A in TMEM)
+//   drain (9-12)       one thread per row: adds each finished main-accumulator
+//                      chunk into an fp32 running sum in smem (round to
+//                      nearest), then log(running + corr) + shifts -> global
 //
-// Stages are handed over with mbarriers (full: transform -> MMA, empty:
-// tcgen05.commit -> transform); accumulators are double-buffered in TMEM when
-// they fit, so the epilogue of one tile overlaps the main loop of the next.
-// Every wait is bounded (xe_common.cuh).
+// The tensor core accumulates in fp32 with truncation, a bias that grows
+// linearly with the number of accumulating instructions; the main
+// accumulator is therefore restarted every kChunkKB k-blocks (two chunk
+// buffers, so the MMA continues while the previous chunk is drained).  The
+// correction products are ~2^-10 of the main ones and accumulate over the
+// whole tile.  Stages and chunks are handed over with mbarriers; every wait is
+// bounded (xe_common.cuh).
 #pragma once
 
 #include "xe_common.cuh"
@@ -25,14 +30,19 @@
 namespace xe {
 namespace gemm {
 
-constexpr int kBM = 128;  // UMMA M (cta_group::1)
-constexpr int kBK = 32;   // fp32 elements per 128-byte swizzle row
-constexpr int kTransformWarps = 8;
-constexpr int kTransformThreads = kTransformWarps * 32;
-constexpr int kMmaWarp = kTransformWarps;  // warp 8
-constexpr int kEpiWarp0 = kMmaWarp + 1;    // warps 9..12
-constexpr int kEpiWarps = 4;
-constexpr int kThreads = (kTransformWarps + 1 + kEpiWarps) * 32;  // 416
+constexpr int kBM = 128;  // UMMA M (cta_group::1) = TMEM lanes
+constexpr int kBK = 32;   // k per stage
+constexpr int kAWarps = 4;
+constexpr int kBWarps = 4;
+constexpr int kMmaWarp = kAWarps + kBWarps;  // 8
+constexpr int kDrainWarp0 = kMmaWarp + 1;    // 9..12
+constexpr int kDrainWarps = 4;
+constexpr int kThreads = (kMmaWarp + 1 + kDrainWarps) * 32;  // 416
+constexpr int kStages = 2;
+constexpr int kChunkKB = 4;         // 128 k per main-accumulator chunk
+constexpr int kInlineShiftK = 128;  // A row shifts computed in-kernel up to this K
+
+enum AMode : int { kALog = 0, kALinear = 1, kATucker = 2 };
 
 struct Params {
   const float* a;
@@ -42,11 +52,16 @@ struct Params {
   int64_t b_sb, b_sk, b_sn;
   float* c;
   int64_t c_sb, c_sm, c_sn;
-  const float* shift_a;  // [batch*M]; nullptr when A is linear
-  const float* shift_b;  // [batch*N]; nullptr when B is linear
+  const float* shift_a;  // [batch*M] (log A with K > kInlineShiftK); else nullptr
+  const float* shift_b;  // [batch*N] for a log-domain B; nullptr when B is linear
   int batch, M, N, K;
   int tiles_m, tiles_n, num_tiles, num_kb;
-  int c_vec;  // output rows may be written with 16-byte stores
+  int c_vec;      // output rows may be written with 16-byte stores
+  int shift_min;  // row extremes computed in-kernel use min instead of max
+  // Tucker layer: l (rows, folds, I), r (rows, folds, J) contiguous; batch = fold
+  const float* tl;
+  const float* tr;
+  int t_folds, t_i;
 };
 
 __host__ __device__ constexpr int pow2_at_least(int x) {
@@ -55,20 +70,20 @@ __host__ __device__ constexpr int pow2_at_least(int x) {
   return p;
 }
 
-template <int BN, bool SPLIT_ACC>
+template <int BN>
 struct Cfg {
-  static constexpr int kATile = kBM * kBK * 4;  // bytes, one of hi/lo
-  static constexpr int kBTile = BN * kBK * 4;
-  static constexpr int kStageBytes = 2 * kATile + 2 * kBTile;
-  static constexpr int kStages = (BN >= 256) ? 2 : (BN >= 128 ? 3 : 4);
-  static constexpr int kAccCols = SPLIT_ACC ? 2 * BN : BN;
-  static constexpr int kNumAcc = (2 * kAccCols <= 512) ? 2 : 1;
-  static constexpr int kTmemCols = pow2_at_least(kNumAcc * kAccCols);
-  // shared memory: [1024 alignment slack][stages][barriers]
+  static_assert(BN == 32 || BN == 64 || BN == 128, "BN");
+  static constexpr int kBTile = BN * kBK * 4;  // bytes, one of hi/lo
+  static constexpr int kStageBytes = 2 * kBTile;
+  static constexpr int kRunningBytes = BN * kBM * 4;
+  // TMEM columns: A stages (hi 32 + lo 32 each), two main chunks, correction
+  static constexpr int kTmemA = 0;
+  static constexpr int kTmemMain = 64 * kStages;
+  static constexpr int kTmemCorr = kTmemMain + 2 * BN;
+  static constexpr int kTmemCols = pow2_at_least(kTmemCorr + BN);
   static constexpr int kBarrierBytes = 256;
-  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kBarrierBytes;
-  static_assert(kTmemCols <= 512, "accumulators exceed TMEM");
-  static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
+  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kRunningBytes + kBarrierBytes;
+  static_assert(kTmemCorr + BN <= 512, "TMEM");
 };
 
 // Byte offset of the 16-byte chunk holding elements (row, 4q..4q+3) of a
@@ -77,214 +92,323 @@ __device__ __forceinline__ uint32_t kmajor_off(int row, int q) {
   return (uint32_t)((row >> 3) * 1024 + (row & 7) * 128 + ((q ^ (row & 7)) << 4));
 }
 // Byte offset of the 16-byte chunk holding elements (k, 4q..4q+3) of an
-// MN-major tile (32 k-rows x MN, 32-element swizzle atoms stacked every 4096 B).
+// MN-major tile (32 k-rows x MN): 32-element MN blocks every 4096 B, inside a
+// block 4-row k-groups of 512 B, 32-byte chunks swizzled with (k & 3).
 __device__ __forceinline__ uint32_t mnmajor_off(int k, int q) {
-  return (uint32_t)((q >> 3) * 4096 + (k >> 3) * 1024 + (k & 7) * 128 + (((q & 7) ^ (k & 7)) << 4));
+  return (uint32_t)((q >> 3) * 4096 + (k >> 2) * 512 + (k & 3) * 128 + ((((q >> 1) & 3) ^ (k & 3)) << 5) +
+                    ((q & 1) << 4));
 }
 
-__device__ __forceinline__ float lse_prologue(float x, float s, bool linear) {
-  return linear ? x : expf(x - s);
+// exp(x - s) as 2^((x - s) * log2 e): x - s is exact for the terms that
+// dominate a row (Sterbenz), the product adds one rounding, ex2.approx ~2 ulp.
+__device__ __forceinline__ float exp_shifted(float x, float s) {
+  const float y = (x - s) * 1.4426950408889634f;
+  float e;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(y));
+  return e;
 }
 
-__device__ __forceinline__ void split_store(uint32_t hi_addr, uint32_t lo_addr, float4 e) {
-  float4 h, l;
-  split_tf32(e.x, h.x, l.x);
-  split_tf32(e.y, h.y, l.y);
-  split_tf32(e.z, h.z, l.z);
-  split_tf32(e.w, h.w, l.w);
-  sts_v4(hi_addr, h);
-  sts_v4(lo_addr, l);
+// hi = e rounded to the nearest TF32 (10 explicit mantissa bits, ties away),
+// lo = e - hi exactly; the tensor core reads lo's top 10 mantissa bits.
+__device__ __forceinline__ void split_rn(float e, float& hi, float& lo) {
+  hi = __uint_as_float((__float_as_uint(e) + 0x1000u) & 0xFFFFE000u);
+  lo = e - hi;
 }
 
-// Loads four elements p[0], p[s], p[2s], p[3s] with per-element masks.
-template <bool VEC>
-__device__ __forceinline__ float4 load_quad(const float* p, int64_t s, int valid, float fill) {
+__device__ __forceinline__ float4 ldg_v4(const float* p) {
   float4 v;
-  if (VEC) {
-    if (valid >= 4) {
-      v = ldg_nc_v4(p);
-    } else {
-      v = make_float4(fill, fill, fill, fill);
-    }
-  } else {
-    v.x = valid > 0 ? ldg_nc(p) : fill;
-    v.y = valid > 1 ? ldg_nc(p + s) : fill;
-    v.z = valid > 2 ? ldg_nc(p + 2 * s) : fill;
-    v.w = valid > 3 ? ldg_nc(p + 3 * s) : fill;
-  }
+  asm volatile("ld.global.nc.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
   return v;
 }
 
-__device__ __forceinline__ float4 add4(float4 a, float4 b) {
-  return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]), "f"(v[8]), "f"(v[9]),
+      "f"(v[10]), "f"(v[11]), "f"(v[12]), "f"(v[13]), "f"(v[14]), "f"(v[15]), "f"(v[16]), "f"(v[17]), "f"(v[18]),
+      "f"(v[19]), "f"(v[20]), "f"(v[21]), "f"(v[22]), "f"(v[23]), "f"(v[24]), "f"(v[25]), "f"(v[26]), "f"(v[27]),
+      "f"(v[28]), "f"(v[29]), "f"(v[30]), "f"(v[31])
+      : "memory");
 }
 
-// Number of valid elements among idx, idx+1, idx+2, idx+3 (clamped to 0..4).
-__device__ __forceinline__ int quad_valid(int idx, int limit) {
-  int v = limit - idx;
-  return v < 0 ? 0 : (v > 4 ? 4 : v);
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]), "f"(v[8]), "f"(v[9]),
+      "f"(v[10]), "f"(v[11]), "f"(v[12]), "f"(v[13]), "f"(v[14]), "f"(v[15])
+      : "memory");
 }
 
-template <int BN, bool A_KMAJ, bool B_KMAJ, bool VEC>
-struct Loader {
-  // A fragment: 4 float4 per transform thread; B fragment: BN/32 float4.
-  static constexpr int kAQ = 4;
-  static constexpr int kBQ = BN / 32;
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-  // ---- A ----
-  // K-major: thread t covers k-quad t%8 of rows t/8 + 32*i.
-  // MN-major: thread t covers m-quad t%32 of k-rows t/32 + 8*i.
-  __device__ static void load_a(const Params& p, int bb, int m0, int k0, int t, float4 (&ra)[kAQ]) {
-    const bool lin = p.shift_a == nullptr;
-    const float fill = lin ? 0.0f : -INFINITY;
-    const float* base = p.a + (int64_t)bb * p.a_sb;
-    const float* base2 = p.a2 ? p.a2 + (int64_t)bb * p.a_sb : nullptr;
-#pragma unroll
-    for (int i = 0; i < kAQ; ++i) {
-      int m, k, valid;
-      int64_t off, step;
-      if (A_KMAJ) {
-        m = m0 + (t >> 3) + 32 * i;
-        k = k0 + 4 * (t & 7);
-        valid = (m < p.M) ? quad_valid(k, p.K) : 0;
-        off = (int64_t)m * p.a_sm + (int64_t)k * p.a_sk;
-        step = p.a_sk;
-      } else {
-        k = k0 + (t >> 5) + 8 * i;
-        m = m0 + 4 * (t & 31);
-        valid = (k < p.K) ? quad_valid(m, p.M) : 0;
-        off = (int64_t)k * p.a_sk + (int64_t)m * p.a_sm;
-        step = p.a_sm;
-      }
-      float4 v = load_quad<VEC>(base + off, step, valid, fill);
-      if (base2) v = add4(v, load_quad<VEC>(base2 + off, step, valid, 0.0f));
-      ra[i] = v;
-    }
-  }
+// D[tmem] (+)= A[tmem] * B[smem], kind::tf32, one CTA.
+__device__ __forceinline__ void umma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 
-  __device__ static void load_a_shift(const Params& p, int bb, int m0, int t, float (&sa)[4]) {
-    if (p.shift_a == nullptr) {
-#pragma unroll
-      for (int i = 0; i < 4; ++i) sa[i] = 0.0f;
-      return;
-    }
-    const float* s = p.shift_a + (int64_t)bb * p.M;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      int m = A_KMAJ ? m0 + (t >> 3) + 32 * i : m0 + 4 * (t & 31) + i;
-      sa[i] = (m < p.M) ? __ldg(s + m) : 0.0f;
-    }
-  }
-
-  __device__ static void store_a(const Params& p, uint32_t hi, uint32_t lo, int t, const float4 (&ra)[kAQ],
-                                 const float (&sa)[4]) {
-    const bool lin = p.shift_a == nullptr;
-#pragma unroll
-    for (int i = 0; i < kAQ; ++i) {
-      float4 e;
-      uint32_t off;
-      if (A_KMAJ) {
-        const float s = sa[i];
-        e = make_float4(lse_prologue(ra[i].x, s, lin), lse_prologue(ra[i].y, s, lin), lse_prologue(ra[i].z, s, lin),
-                        lse_prologue(ra[i].w, s, lin));
-        off = kmajor_off((t >> 3) + 32 * i, t & 7);
-      } else {
-        e = make_float4(lse_prologue(ra[i].x, sa[0], lin), lse_prologue(ra[i].y, sa[1], lin),
-                        lse_prologue(ra[i].z, sa[2], lin), lse_prologue(ra[i].w, sa[3], lin));
-        off = mnmajor_off((t >> 5) + 8 * i, t & 31);
-      }
-      split_store(hi + off, lo + off, e);
-    }
-  }
-
-  // ---- B ----
-  // MN-major: thread t covers n-quad t%(BN/4) of k-rows t/(BN/4) + (1024/BN)*i.
-  // K-major: thread t covers k-quad t%8 of n-rows t/8 + 32*i.
-  static constexpr int kQPR = BN / 4;
-  static constexpr int kRPP = kTransformThreads / kQPR;
-
-  __device__ static void load_b(const Params& p, int bb, int n0, int k0, int t, float4 (&rb)[kBQ]) {
-    const bool lin = p.shift_b == nullptr;
-    const float fill = lin ? 0.0f : -INFINITY;
-    const float* base = p.b + (int64_t)bb * p.b_sb;
-#pragma unroll
-    for (int i = 0; i < kBQ; ++i) {
-      int n, k, valid;
-      int64_t off, step;
-      if (B_KMAJ) {
-        n = n0 + (t >> 3) + 32 * i;
-        k = k0 + 4 * (t & 7);
-        valid = (n < p.N) ? quad_valid(k, p.K) : 0;
-        off = (int64_t)n * p.b_sn + (int64_t)k * p.b_sk;
-        step = p.b_sk;
-      } else {
-        k = k0 + t / kQPR + kRPP * i;
-        n = n0 + 4 * (t % kQPR);
-        valid = (k < p.K) ? quad_valid(n, p.N) : 0;
-        off = (int64_t)k * p.b_sk + (int64_t)n * p.b_sn;
-        step = p.b_sn;
-      }
-      rb[i] = load_quad<VEC>(base + off, step, valid, fill);
-    }
-  }
-
-  // B shifts: K-major -> one per n-row (kBQ values); MN-major -> 4 per quad.
-  static constexpr int kBS = B_KMAJ ? kBQ : 4;
-  __device__ static void load_b_shift(const Params& p, int bb, int n0, int t, float (&sb)[kBS]) {
-    if (p.shift_b == nullptr) {
-#pragma unroll
-      for (int i = 0; i < kBS; ++i) sb[i] = 0.0f;
-      return;
-    }
-    const float* s = p.shift_b + (int64_t)bb * p.N;
-#pragma unroll
-    for (int i = 0; i < kBS; ++i) {
-      int n = B_KMAJ ? n0 + (t >> 3) + 32 * i : n0 + 4 * (t % kQPR) + i;
-      sb[i] = (n < p.N) ? __ldg(s + n) : 0.0f;
-    }
-  }
-
-  __device__ static void store_b(const Params& p, uint32_t hi, uint32_t lo, int t, const float4 (&rb)[kBQ],
-                                 const float (&sb)[kBS]) {
-    const bool lin = p.shift_b == nullptr;
-#pragma unroll
-    for (int i = 0; i < kBQ; ++i) {
-      float4 e;
-      uint32_t off;
-      if (B_KMAJ) {
-        const float s = sb[i];
-        e = make_float4(lse_prologue(rb[i].x, s, lin), lse_prologue(rb[i].y, s, lin), lse_prologue(rb[i].z, s, lin),
-                        lse_prologue(rb[i].w, s, lin));
-        off = kmajor_off((t >> 3) + 32 * i, t & 7);
-      } else {
-        e = make_float4(lse_prologue(rb[i].x, sb[0], lin), lse_prologue(rb[i].y, sb[1], lin),
-                        lse_prologue(rb[i].z, sb[2], lin), lse_prologue(rb[i].w, sb[3], lin));
-        off = mnmajor_off(t / kQPR + kRPP * i, t % kQPR);
-      }
-      split_store(hi + off, lo + off, e);
-    }
-  }
-};
+__device__ __forceinline__ float extreme(float a, float b, bool is_min) {
+  float r;
+  if (is_min)
+    asm("min.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  else
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
 
 __device__ __forceinline__ void decode_tile(const Params& p, int tile, int& bb, int& mt, int& nt) {
   nt = tile % p.tiles_n;
-  int rest = tile / p.tiles_n;
+  const int rest = tile / p.tiles_n;
   mt = rest % p.tiles_m;
   bb = rest / p.tiles_m;
 }
 
-template <int BN, bool A_KMAJ, bool B_KMAJ, bool VEC, bool SPLIT_ACC>
+// ---------------------------------------------------------------------------
+// A operand, one thread per tile row.
+
+template <int AMODE, bool A_KMAJ, bool VEC, int TJ>
+struct ARow {
+  static constexpr int kTJ = TJ > 0 ? TJ : 1;
+  const float* row = nullptr;   // element (m, 0) of this row (log / linear)
+  const float* row2 = nullptr;  // fused addend
+  int64_t step = 1;             // element stride along k
+  bool valid = false;
+  float shift = 0.0f;  // exp(x - shift); 0 for linear rows; sr for Tucker
+  // Tucker
+  const float* lrow = nullptr;
+  float sl = 0.0f;
+  float er[kTJ];
+
+  // Row extreme of the (possibly fused) operand over all k, for small K.
+  __device__ float scan_extreme(const Params& p, bool is_min) const {
+    float e = is_min ? INFINITY : -INFINITY;
+    for (int k = 0; k < p.K; ++k) {
+      float v = __ldg(row + k * step);
+      if (row2) v += __ldg(row2 + k * step);
+      e = extreme(e, v, is_min);
+    }
+    return e;
+  }
+
+  __device__ void begin_tile(const Params& p, int bb, int m, bool want_er) {
+    valid = m < p.M;
+    const int mm = valid ? m : 0;
+    const bool is_min = p.shift_min != 0;
+    if (AMODE == kATucker) {
+      const int64_t r = (int64_t)mm * p.t_folds + bb;
+      lrow = p.tl + r * p.t_i;
+      const float* rrow = p.tr + r * kTJ;
+      float e1 = is_min ? INFINITY : -INFINITY, e2 = e1;
+      for (int i = 0; i < p.t_i; ++i) e1 = extreme(e1, __ldg(lrow + i), is_min);
+#pragma unroll
+      for (int j = 0; j < kTJ; j += 4) {
+        const float4 v = ldg_v4(rrow + j);
+        e2 = extreme(extreme(e2, v.x, is_min), extreme(v.y, extreme(v.z, v.w, is_min), is_min), is_min);
+      }
+      sl = e1;
+      shift = e2;
+      if (want_er) {
+#pragma unroll
+        for (int j = 0; j < kTJ; j += 4) {
+          const float4 v = ldg_v4(rrow + j);
+          er[j] = valid ? exp_shifted(v.x, e2) : 0.0f;
+          er[j + 1] = valid ? exp_shifted(v.y, e2) : 0.0f;
+          er[j + 2] = valid ? exp_shifted(v.z, e2) : 0.0f;
+          er[j + 3] = valid ? exp_shifted(v.w, e2) : 0.0f;
+        }
+      }
+      return;
+    }
+    const int64_t base = (int64_t)bb * p.a_sb + (int64_t)mm * p.a_sm;
+    row = p.a + base;
+    row2 = p.a2 ? p.a2 + base : nullptr;
+    step = p.a_sk;
+    if (AMODE == kALinear) {
+      shift = 0.0f;
+    } else if (p.shift_a) {
+      shift = valid ? __ldg(p.shift_a + (int64_t)bb * p.M + m) : 0.0f;
+    } else {
+      shift = valid ? scan_extreme(p, is_min) : 0.0f;
+    }
+  }
+
+  // Raw values of k0 .. k0+31 (with the fused addend) into v.
+  __device__ void load(const Params& p, int k0, float (&v)[32]) const {
+    if (AMODE == kATucker) {
+      v[0] = valid ? __ldg(lrow + k0 / kTJ) : -INFINITY;  // one l value per k-block
+      return;
+    }
+    const float fill = (AMODE == kALinear) ? 0.0f : -INFINITY;
+    if (VEC && A_KMAJ) {
+      if (valid && k0 + 32 <= p.K) {
+        const float* r = row + k0;
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          float4 x = ldg_v4(r + j);
+          if (row2) {
+            const float4 y = ldg_v4(row2 + k0 + j);
+            x.x += y.x;
+            x.y += y.y;
+            x.z += y.z;
+            x.w += y.w;
+          }
+          v[j] = x.x;
+          v[j + 1] = x.y;
+          v[j + 2] = x.z;
+          v[j + 3] = x.w;
+        }
+        return;
+      }
+    }
+    const float* r = row + (int64_t)k0 * step;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const bool ok = valid && k0 + j < p.K;
+      float x = ok ? __ldg(r + j * step) : fill;
+      if (row2 && ok) x += __ldg(row2 + (int64_t)(k0 + j) * step);
+      v[j] = x;
+    }
+  }
+
+  // exp / split of loaded values 16*H .. 16*H+15 -> hi, lo
+  template <int H>
+  __device__ void transform_half(const float (&v)[32], int k0, float (&hi)[16], float (&lo)[16]) const {
+    if (AMODE == kATucker) {
+      const float el = exp_shifted(v[0], sl);
+      // J = 64 spans two k-blocks per i: the odd ones use er[32..63]
+      const bool second = kTJ == 64 && ((k0 >> 5) & 1);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        float r = er[(16 * H + j) % kTJ];
+        if (kTJ == 64) r = second ? er[(32 + 16 * H + j) % kTJ] : r;
+        split_rn(el * r, hi[j], lo[j]);
+      }
+      return;
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float x = v[16 * H + j];
+      const float e = (AMODE == kALinear) ? x : exp_shifted(x, shift);
+      split_rn(e, hi[j], lo[j]);
+    }
+  }
+};
+
+// ---------------------------------------------------------------------------
+// B operand: 128 threads, 16-byte chunks.  MN-major: thread t covers n-quad
+// t % (BN/4) of k-rows t / (BN/4) + (512/BN)*i; K-major: k-quad t % 8 of
+// n-rows t / 8 + 16*i.
+template <int BN, bool B_KMAJ, bool VEC>
+struct BTile {
+  static constexpr int kQ = BN / 16;  // float4 per thread
+  static constexpr int kQPR = BN / 4;
+  static constexpr int kRPP = 128 / kQPR;
+  static constexpr int kS = B_KMAJ ? kQ : 4;
+  float shift[kS];
+
+  __device__ static void coords(int t, int i, int& n_local, int& k_local) {
+    if (B_KMAJ) {
+      n_local = (t >> 3) + 16 * i;
+      k_local = 4 * (t & 7);
+    } else {
+      k_local = t / kQPR + kRPP * i;
+      n_local = 4 * (t % kQPR);
+    }
+  }
+
+  __device__ void begin_tile(const Params& p, int bb, int n0, int t) {
+#pragma unroll
+    for (int i = 0; i < kS; ++i) {
+      const int n = B_KMAJ ? n0 + (t >> 3) + 16 * i : n0 + 4 * (t % kQPR) + i;
+      shift[i] = (p.shift_b && n < p.N) ? __ldg(p.shift_b + (int64_t)bb * p.N + n) : 0.0f;
+    }
+  }
+
+  __device__ void load(const Params& p, int bb, int n0, int k0, int t, float4 (&v)[kQ]) const {
+    const bool lin = p.shift_b == nullptr;
+    const float fill = lin ? 0.0f : -INFINITY;
+    const float* base = p.b + (int64_t)bb * p.b_sb;
+#pragma unroll
+    for (int i = 0; i < kQ; ++i) {
+      int nl, kl;
+      coords(t, i, nl, kl);
+      const int n = n0 + nl, k = k0 + kl;
+      const float* q = base + (int64_t)n * p.b_sn + (int64_t)k * p.b_sk;
+      if (B_KMAJ) {
+        const bool nv = n < p.N;
+        if (VEC) {
+          v[i] = (nv && k + 4 <= p.K) ? ldg_v4(q) : make_float4(fill, fill, fill, fill);
+        } else {
+          v[i].x = (nv && k < p.K) ? __ldg(q) : fill;
+          v[i].y = (nv && k + 1 < p.K) ? __ldg(q + p.b_sk) : fill;
+          v[i].z = (nv && k + 2 < p.K) ? __ldg(q + 2 * p.b_sk) : fill;
+          v[i].w = (nv && k + 3 < p.K) ? __ldg(q + 3 * p.b_sk) : fill;
+        }
+      } else {
+        const bool kv = k < p.K;
+        if (VEC) {
+          v[i] = (kv && n + 4 <= p.N) ? ldg_v4(q) : make_float4(fill, fill, fill, fill);
+        } else {
+          v[i].x = (kv && n < p.N) ? __ldg(q) : fill;
+          v[i].y = (kv && n + 1 < p.N) ? __ldg(q + p.b_sn) : fill;
+          v[i].z = (kv && n + 2 < p.N) ? __ldg(q + 2 * p.b_sn) : fill;
+          v[i].w = (kv && n + 3 < p.N) ? __ldg(q + 3 * p.b_sn) : fill;
+        }
+      }
+    }
+  }
+
+  __device__ void store(const Params& p, uint32_t hi, uint32_t lo, int t, const float4 (&v)[kQ]) const {
+    const bool lin = p.shift_b == nullptr;
+#pragma unroll
+    for (int i = 0; i < kQ; ++i) {
+      int nl, kl;
+      coords(t, i, nl, kl);
+      float4 e;
+      if (lin) {
+        e = v[i];
+      } else if (B_KMAJ) {
+        const float s = shift[i];
+        e = make_float4(exp_shifted(v[i].x, s), exp_shifted(v[i].y, s), exp_shifted(v[i].z, s), exp_shifted(v[i].w, s));
+      } else {
+        e = make_float4(exp_shifted(v[i].x, shift[0]), exp_shifted(v[i].y, shift[1]), exp_shifted(v[i].z, shift[2]),
+                        exp_shifted(v[i].w, shift[3]));
+      }
+      float4 h, l;
+      split_rn(e.x, h.x, l.x);
+      split_rn(e.y, h.y, l.y);
+      split_rn(e.z, h.z, l.z);
+      split_rn(e.w, h.w, l.w);
+      const uint32_t off = B_KMAJ ? kmajor_off(nl, kl >> 2) : mnmajor_off(kl, nl >> 2);
+      sts_v4(hi + off, h);
+      sts_v4(lo + off, l);
+    }
+  }
+};
+
+// ---------------------------------------------------------------------------
+
+template <int BN, int AMODE, bool A_KMAJ, bool B_KMAJ, bool VEC, int TJ>
 __global__ void __launch_bounds__(kThreads, 1) lse_gemm_kernel(const Params p) {
-  using C = Cfg<BN, SPLIT_ACC>;
-  using L = Loader<BN, A_KMAJ, B_KMAJ, VEC>;
+  using C = Cfg<BN>;
+  using ARowT = ARow<AMODE, A_KMAJ, VEC, TJ>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  uint64_t* bars = (uint64_t*)(smem + C::kStages * C::kStageBytes);
-  uint64_t* full = bars;                         // [kStages]
-  uint64_t* empty = full + C::kStages;           // [kStages]
-  uint64_t* acc_full = empty + C::kStages;       // [kNumAcc]
-  uint64_t* acc_empty = acc_full + C::kNumAcc;   // [kNumAcc]
-  uint64_t* drain = acc_empty + C::kNumAcc;      // [1]
+  float* running = (float*)(smem + kStages * C::kStageBytes);  // [BN][128], column-major
+  uint64_t* bars = (uint64_t*)(smem + kStages * C::kStageBytes + C::kRunningBytes);
+  uint64_t* full = bars;                    // [kStages], one arrival per A and B warp
+  uint64_t* empty = full + kStages;         // [kStages], tcgen05.commit
+  uint64_t* chunk_full = empty + kStages;   // [2], tcgen05.commit
+  uint64_t* chunk_empty = chunk_full + 2;   // [2], drain warps
+  uint64_t* corr_empty = chunk_empty + 2;   // [1], drain warps
+  uint64_t* drain = corr_empty + 1;         // [1], teardown
   uint32_t* tmem_slot = (uint32_t*)(drain + 1);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
@@ -292,14 +416,15 @@ __global__ void __launch_bounds__(kThreads, 1) lse_gemm_kernel(const Params p) {
   const int lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < C::kStages; ++s) {
-      mbar_init(&full[s], kTransformWarps);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], kAWarps + kBWarps);
       mbar_init(&empty[s], 1);
     }
-    for (int a = 0; a < C::kNumAcc; ++a) {
-      mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], kEpiWarps);
+    for (int c = 0; c < 2; ++c) {
+      mbar_init(&chunk_full[c], 1);
+      mbar_init(&chunk_empty[c], kDrainWarps);
     }
+    mbar_init(corr_empty, kDrainWarps);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbarrier_init();
@@ -308,101 +433,140 @@ __global__ void __launch_bounds__(kThreads, 1) lse_gemm_kernel(const Params p) {
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t tmem = *tmem_slot;
   const uint32_t smem_base = smem_u32(smem);
 
-  if (warp < kTransformWarps) {
-    // ------------------------------------------------------------ transform
-    const int t = threadIdx.x;
+  if (warp < kAWarps) {
+    // ------------------------------------------------------------ A rows
+    const int r = warp * 32 + lane;  // warp w may access TMEM lanes 32w..32w+31
+    const uint32_t lane_bits = (uint32_t)(warp * 32) << 16;
+    ARowT a;
     uint32_t it = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
       int bb, mt, nt;
       decode_tile(p, tile, bb, mt, nt);
-      const int m0 = mt * kBM, n0 = nt * BN;
-      float sa[4];
-      float sb[L::kBS];
-      L::load_a_shift(p, bb, m0, t, sa);
-      L::load_b_shift(p, bb, n0, t, sb);
-      float4 ra[L::kAQ], rb[L::kBQ];
-      L::load_a(p, bb, m0, 0, t, ra);
-      L::load_b(p, bb, n0, 0, t, rb);
+      a.begin_tile(p, bb, mt * kBM + r, true);
+      float cur[32], nxt[32];
+      a.load(p, 0, cur);
       for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
-        float4 na[L::kAQ], nb[L::kBQ];
         const bool more = kb + 1 < p.num_kb;
-        if (more) {
-          L::load_a(p, bb, m0, (kb + 1) * kBK, t, na);
-          L::load_b(p, bb, n0, (kb + 1) * kBK, t, nb);
+        if (more) a.load(p, (kb + 1) * kBK, nxt);
+        const uint32_t s = it % kStages;
+        const uint32_t ph = (it / kStages) & 1;
+        if (!mbar_wait(&empty[s], ph ^ 1, kSiteGemmEmpty, abort_flag)) {
+          ok = false;
+          break;
         }
-        const uint32_t s = it % C::kStages;
-        const uint32_t ph = (it / C::kStages) & 1;
+        tc_fence_after();
+        const uint32_t col = tmem + lane_bits + C::kTmemA + 64 * s;
+        {
+          float hi[16], lo[16];
+          a.template transform_half<0>(cur, kb * kBK, hi, lo);
+          tmem_st16(col, hi);
+          tmem_st16(col + 32, lo);
+        }
+        {
+          float hi[16], lo[16];
+          a.template transform_half<1>(cur, kb * kBK, hi, lo);
+          tmem_st16(col + 16, hi);
+          tmem_st16(col + 48, lo);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&full[s]);
+        if (more) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) cur[j] = nxt[j];
+        }
+      }
+    }
+  } else if (warp < kAWarps + kBWarps) {
+    // ------------------------------------------------------------ B tiles
+    const int t = threadIdx.x - kAWarps * 32;
+    using BT = BTile<BN, B_KMAJ, VEC>;
+    BT bt;
+    uint32_t it = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+      int bb, mt, nt;
+      decode_tile(p, tile, bb, mt, nt);
+      const int n0 = nt * BN;
+      bt.begin_tile(p, bb, n0, t);
+      float4 cur[BT::kQ], nxt[BT::kQ];
+      bt.load(p, bb, n0, 0, t, cur);
+      for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+        const bool more = kb + 1 < p.num_kb;
+        if (more) bt.load(p, bb, n0, (kb + 1) * kBK, t, nxt);
+        const uint32_t s = it % kStages;
+        const uint32_t ph = (it / kStages) & 1;
         if (!mbar_wait(&empty[s], ph ^ 1, kSiteGemmEmpty, abort_flag)) {
           ok = false;
           break;
         }
         const uint32_t st = smem_base + s * C::kStageBytes;
-        L::store_a(p, st, st + C::kATile, t, ra, sa);
-        L::store_b(p, st + 2 * C::kATile, st + 2 * C::kATile + C::kBTile, t, rb, sb);
+        bt.store(p, st, st + C::kBTile, t, cur);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&full[s]);
         if (more) {
 #pragma unroll
-          for (int i = 0; i < L::kAQ; ++i) ra[i] = na[i];
-#pragma unroll
-          for (int i = 0; i < L::kBQ; ++i) rb[i] = nb[i];
+          for (int i = 0; i < BT::kQ; ++i) cur[i] = nxt[i];
         }
       }
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issue
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_tf32(kBM, BN, !A_KMAJ, !B_KMAJ);
-      // K-major tiles advance 32 bytes per 8-element k-step inside the
-      // swizzle row; MN-major tiles advance one 8-row group (1024 bytes).
-      constexpr uint32_t a_lbo = A_KMAJ ? 16 : 4096, a_sbo = 1024, a_step = A_KMAJ ? 32 : 1024;
-      constexpr uint32_t b_lbo = B_KMAJ ? 16 : 4096, b_sbo = 1024, b_step = B_KMAJ ? 32 : 1024;
-      uint32_t it = 0, tl = 0;
+      constexpr uint32_t idesc = idesc_tf32(kBM, BN, false, !B_KMAJ);
+      // K-major B advances 32 bytes per 8-element k-step inside the swizzle
+      // row; MN-major B advances two 4-row groups (1024 bytes).
+      constexpr uint32_t b_lbo = B_KMAJ ? 16 : 4096, b_sbo = B_KMAJ ? 1024 : 512, b_step = B_KMAJ ? 32 : 1024;
+      constexpr uint32_t b_lay = B_KMAJ ? kLayoutSW128 : kLayoutSW128Base32B;
+      uint32_t it = 0, gc = 0, tl = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++tl) {
-        const uint32_t acc = tl % C::kNumAcc;
-        const uint32_t acc_ph = (tl / C::kNumAcc) & 1;
-        if (!mbar_wait(&acc_empty[acc], acc_ph ^ 1, kSiteGemmAccEmpty, abort_flag)) {
+        if (!mbar_wait(corr_empty, (tl & 1) ^ 1, kSiteGemmAccEmpty, abort_flag)) {
           ok = false;
           break;
         }
-        tc_fence_after();
-        const uint32_t d_main = tmem_base + acc * C::kAccCols;
-        const uint32_t d_corr = SPLIT_ACC ? d_main + BN : d_main;
+        const uint32_t d_corr = tmem + C::kTmemCorr;
+        uint32_t d_main = 0;
         for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
-          const uint32_t s = it % C::kStages;
-          const uint32_t ph = (it / C::kStages) & 1;
+          const int kc = kb % kChunkKB;
+          if (kc == 0) {
+            const uint32_t cb = gc & 1;
+            if (!mbar_wait(&chunk_empty[cb], ((gc >> 1) & 1) ^ 1, kSiteGemmAccEmpty, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            d_main = tmem + C::kTmemMain + cb * BN;
+          }
+          const uint32_t s = it % kStages;
+          const uint32_t ph = (it / kStages) & 1;
           if (!mbar_wait(&full[s], ph, kSiteGemmFull, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t st = smem_base + s * C::kStageBytes;
-          const uint32_t a_hi = st, a_lo = st + C::kATile;
-          const uint32_t b_hi = st + 2 * C::kATile, b_lo = b_hi + C::kBTile;
+          const uint32_t a_hi = tmem + C::kTmemA + 64 * s, a_lo = a_hi + 32;
+          const uint32_t b_hi = smem_base + s * C::kStageBytes, b_lo = b_hi + C::kBTile;
 #pragma unroll
           for (int kk = 0; kk < kBK / 8; ++kk) {
-            const uint64_t dah = smem_desc_sw128(a_hi + kk * a_step, a_lbo, a_sbo);
-            const uint64_t dal = smem_desc_sw128(a_lo + kk * a_step, a_lbo, a_sbo);
-            const uint64_t dbh = smem_desc_sw128(b_hi + kk * b_step, b_lbo, b_sbo);
-            const uint64_t dbl = smem_desc_sw128(b_lo + kk * b_step, b_lbo, b_sbo);
-            const uint32_t first = (kb | kk) != 0;
-            umma_tf32(d_main, dah, dbh, idesc, first);
-            if (SPLIT_ACC) {
-              umma_tf32(d_corr, dah, dbl, idesc, first);
-            } else {
-              umma_tf32(d_corr, dah, dbl, idesc, 1);
-            }
-            umma_tf32(d_corr, dal, dbh, idesc, 1);
+            const uint64_t dbh = smem_desc(b_hi + kk * b_step, b_lbo, b_sbo, b_lay);
+            const uint64_t dbl = smem_desc(b_lo + kk * b_step, b_lbo, b_sbo, b_lay);
+            umma_tf32_ts(d_main, a_hi + kk * 8, dbh, idesc, (kc | kk) != 0);
+            umma_tf32_ts(d_corr, a_hi + kk * 8, dbl, idesc, (kb | kk) != 0);
+            umma_tf32_ts(d_corr, a_lo + kk * 8, dbh, idesc, 1);
           }
           umma_commit(&empty[s]);
+          if (kc == kChunkKB - 1 || kb == p.num_kb - 1) {
+            umma_commit(&chunk_full[gc & 1]);
+            ++gc;
+          }
         }
-        if (ok) umma_commit(&acc_full[acc]);
       }
       // All issued MMAs must finish before TMEM is released.
       umma_commit(drain);
@@ -410,46 +574,78 @@ __global__ void __launch_bounds__(kThreads, 1) lse_gemm_kernel(const Params p) {
     }
     __syncwarp();
   } else {
-    // ------------------------------------------------------------ epilogue
-    const int q = warp & 3;  // TMEM lane quadrant this warp may access
-    const int row = q * 32 + lane;
-    uint32_t tl = 0;
-    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++tl) {
+    // ------------------------------------------------------------ drain + epilogue
+    const int q = warp & 3;  // TMEM lane quadrant of this warp
+    const int r = q * 32 + lane;
+    const uint32_t lane_bits = (uint32_t)(q * 32) << 16;
+    ARowT a;  // recomputes this row's shifts at the end of each tile
+    uint32_t gc = 0;
+    bool ok = true;
+    const int chunks = (p.num_kb + kChunkKB - 1) / kChunkKB;
+    for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
       int bb, mt, nt;
       decode_tile(p, tile, bb, mt, nt);
-      const int m = mt * kBM + row;
+      const int m = mt * kBM + r;
       const int n0 = nt * BN;
-      const uint32_t acc = tl % C::kNumAcc;
-      const uint32_t acc_ph = (tl / C::kNumAcc) & 1;
-      if (!mbar_wait(&acc_full[acc], acc_ph, kSiteGemmAccFull, abort_flag)) break;
-      tc_fence_after();
-      const float sa = (p.shift_a && m < p.M) ? __ldg(p.shift_a + (int64_t)bb * p.M + m) : 0.0f;
+      for (int c = 0; c < chunks; ++c, ++gc) {
+        const uint32_t cb = gc & 1;
+        if (!mbar_wait(&chunk_full[cb], (gc >> 1) & 1, kSiteGemmAccFull, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll 1
+        for (int sl = 0; sl < BN / 32; ++sl) {
+          float v[32];
+          tmem_ld32(tmem + lane_bits + C::kTmemMain + cb * BN + sl * 32, v);
+          tmem_wait_ld();
+          float* run = running + sl * 32 * kBM + r;
+          if (c == 0) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) run[j * kBM] = v[j];
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) run[j * kBM] += v[j];
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&chunk_empty[cb]);
+      }
+      if (!ok) break;
+      // Epilogue: the last chunk commit covered every MMA of this tile.
+      float s1 = 0.0f, s2 = 0.0f;
+      if (AMODE != kALinear) {
+        a.begin_tile(p, bb, m, false);
+        s1 = AMODE == kATucker ? a.sl : a.shift;
+        s2 = AMODE == kATucker ? a.shift : 0.0f;
+      }
       const float* sbp = p.shift_b ? p.shift_b + (int64_t)bb * p.N : nullptr;
       float* crow = p.c + (int64_t)bb * p.c_sb + (int64_t)m * p.c_sm;
-      const uint32_t t_main = tmem_base + ((uint32_t)(q * 32) << 16) + acc * C::kAccCols;
 #pragma unroll 1
-      for (int ch = 0; ch < BN / 32; ++ch) {
-        float vm[32], vc[32];
-        tmem_ld32(t_main + ch * 32, vm);
-        if (SPLIT_ACC) tmem_ld32(t_main + BN + ch * 32, vc);
+      for (int sl = 0; sl < BN / 32; ++sl) {
+        float v[32];
+        tmem_ld32(tmem + lane_bits + C::kTmemCorr + sl * 32, v);
         tmem_wait_ld();
-        const int nb = n0 + ch * 32;
+        const int nb = n0 + sl * 32;
         if (m < p.M && nb < p.N) {
+          const float* run = running + sl * 32 * kBM + r;
           float out[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
-            float v = SPLIT_ACC ? vm[j] + vc[j] : vm[j];
-            float r = logf(v);
-            if (p.shift_a) r += sa;
-            if (sbp) {
-              const int n = nb + j;
-              r += (n < p.N) ? __ldg(sbp + n) : 0.0f;
-            }
-            out[j] = r;
+            const float main = run[j * kBM];
+            // an overflowed main term carries the result; its correction is NaN
+            const float acc = isinf(main) ? main : main + v[j];
+            float o = logf(acc);
+            if (AMODE != kALinear) o += s1;
+            if (AMODE == kATucker) o += s2;
+            if (sbp) o += (nb + j < p.N) ? __ldg(sbp + nb + j) : 0.0f;
+            out[j] = o;
           }
           if (p.c_vec && nb + 32 <= p.N) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 4) stg_v4(crow + nb + j, make_float4(out[j], out[j + 1], out[j + 2], out[j + 3]));
+            for (int j = 0; j < 32; j += 4)
+              stg_v4(crow + nb + j, make_float4(out[j], out[j + 1], out[j + 2], out[j + 3]));
           } else {
 #pragma unroll
             for (int j = 0; j < 32; ++j)
@@ -459,14 +655,14 @@ __global__ void __launch_bounds__(kThreads, 1) lse_gemm_kernel(const Params p) {
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[acc]);
+      if (lane == 0) mbar_arrive(corr_empty);
     }
   }
 
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == kMmaWarp) tmem_dealloc<C::kTmemCols>(tmem_base);
+  if (warp == kMmaWarp) tmem_dealloc<C::kTmemCols>(tmem);
 }
 
 }  // namespace gemm

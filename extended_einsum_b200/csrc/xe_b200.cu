@@ -71,10 +71,10 @@ cudaError_t prepare_kernel(K kernel, int smem_bytes, std::atomic<uint32_t>& done
   return e;
 }
 
-template <int BN, bool AK, bool BK, bool VEC, bool SPLIT>
+template <int BN, int AMODE, bool AK, bool BK, bool VEC, int TJ>
 xe_status launch_gemm_t(const Params& p, cudaStream_t stream) {
-  using C = xe::gemm::Cfg<BN, SPLIT>;
-  auto kernel = xe::gemm::lse_gemm_kernel<BN, AK, BK, VEC, SPLIT>;
+  using C = xe::gemm::Cfg<BN>;
+  auto kernel = xe::gemm::lse_gemm_kernel<BN, AMODE, AK, BK, VEC, TJ>;
   static std::atomic<uint32_t> attribute_set{0};
   cudaError_t e = prepare_kernel(kernel, C::kSmemBytes, attribute_set);
   if (e != cudaSuccess) return fail(XE_ERR_CUDA, "xe_logspace_gemm: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
@@ -83,14 +83,14 @@ xe_status launch_gemm_t(const Params& p, cudaStream_t stream) {
   return check_launch("xe_logspace_gemm");
 }
 
-template <int BN, bool SPLIT>
+template <int BN, int AMODE>
 xe_status launch_gemm_layout(const Params& p, bool ak, bool bk, bool vec, cudaStream_t s) {
   if (ak) {
-    if (bk) return vec ? launch_gemm_t<BN, true, true, true, SPLIT>(p, s) : launch_gemm_t<BN, true, true, false, SPLIT>(p, s);
-    return vec ? launch_gemm_t<BN, true, false, true, SPLIT>(p, s) : launch_gemm_t<BN, true, false, false, SPLIT>(p, s);
+    if (bk) return vec ? launch_gemm_t<BN, AMODE, true, true, true, 0>(p, s) : launch_gemm_t<BN, AMODE, true, true, false, 0>(p, s);
+    return vec ? launch_gemm_t<BN, AMODE, true, false, true, 0>(p, s) : launch_gemm_t<BN, AMODE, true, false, false, 0>(p, s);
   }
-  if (bk) return vec ? launch_gemm_t<BN, false, true, true, SPLIT>(p, s) : launch_gemm_t<BN, false, true, false, SPLIT>(p, s);
-  return vec ? launch_gemm_t<BN, false, false, true, SPLIT>(p, s) : launch_gemm_t<BN, false, false, false, SPLIT>(p, s);
+  if (bk) return vec ? launch_gemm_t<BN, AMODE, false, true, true, 0>(p, s) : launch_gemm_t<BN, AMODE, false, true, false, 0>(p, s);
+  return vec ? launch_gemm_t<BN, AMODE, false, false, true, 0>(p, s) : launch_gemm_t<BN, AMODE, false, false, false, 0>(p, s);
 }
 
 int env_int(const char* name, int dflt) {
@@ -100,26 +100,28 @@ int env_int(const char* name, int dflt) {
 
 int pick_bn(int64_t n) {
   const int forced = env_int("XE_GEMM_BN", 0);
-  if (forced == 32 || forced == 64 || forced == 128 || forced == 256) return forced;
+  if (forced == 32 || forced == 64 || forced == 128) return forced;
   if (n <= 32) return 32;
   if (n <= 64) return 64;
-  if (n <= 128) return 128;
-  return 256;
+  return 128;
 }
 
-xe_status launch_gemm(const Params& p, bool ak, bool bk, bool vec, cudaStream_t s) {
+void set_tiling(Params& q, int bn) {
+  q.tiles_m = (int)((q.M + xe::gemm::kBM - 1) / xe::gemm::kBM);
+  q.tiles_n = (int)((q.N + bn - 1) / bn);
+  q.num_tiles = q.tiles_m * q.tiles_n * q.batch;
+  q.num_kb = (q.K + xe::gemm::kBK - 1) / xe::gemm::kBK;
+}
+
+xe_status launch_gemm(const Params& p, bool a_linear, bool ak, bool bk, bool vec, cudaStream_t s) {
   const int bn = pick_bn(p.N);
-  const bool split = env_int("XE_GEMM_SPLIT_ACC", 1) != 0;
   Params q = p;
-  q.tiles_m = (int)((p.M + xe::gemm::kBM - 1) / xe::gemm::kBM);
-  q.tiles_n = (int)((p.N + bn - 1) / bn);
-  q.num_tiles = q.tiles_m * q.tiles_n * p.batch;
-  q.num_kb = (p.K + xe::gemm::kBK - 1) / xe::gemm::kBK;
+  set_tiling(q, bn);
+  using namespace xe::gemm;
   switch (bn) {
-    case 32: return split ? launch_gemm_layout<32, true>(q, ak, bk, vec, s) : launch_gemm_layout<32, false>(q, ak, bk, vec, s);
-    case 64: return split ? launch_gemm_layout<64, true>(q, ak, bk, vec, s) : launch_gemm_layout<64, false>(q, ak, bk, vec, s);
-    case 128: return split ? launch_gemm_layout<128, true>(q, ak, bk, vec, s) : launch_gemm_layout<128, false>(q, ak, bk, vec, s);
-    default: return split ? launch_gemm_layout<256, true>(q, ak, bk, vec, s) : launch_gemm_layout<256, false>(q, ak, bk, vec, s);
+    case 32: return a_linear ? launch_gemm_layout<32, kALinear>(q, ak, bk, vec, s) : launch_gemm_layout<32, kALog>(q, ak, bk, vec, s);
+    case 64: return a_linear ? launch_gemm_layout<64, kALinear>(q, ak, bk, vec, s) : launch_gemm_layout<64, kALog>(q, ak, bk, vec, s);
+    default: return a_linear ? launch_gemm_layout<128, kALinear>(q, ak, bk, vec, s) : launch_gemm_layout<128, kALog>(q, ak, bk, vec, s);
   }
 }
 
@@ -226,10 +228,10 @@ xe_status xe_logspace_shift(const float* x, const float* x2, int64_t sb, int64_t
 
 namespace {
 
-xe_status gemm_launch(const float* a, const float* a2, int64_t a_sb, int64_t a_sm, int64_t a_sk, const float* shift_a,
-                      const float* b, int64_t b_sb, int64_t b_sk, int64_t b_sn, const float* shift_b, float* c,
-                      int64_t c_sb, int64_t c_sm, int64_t c_sn, int64_t batch, int64_t m, int64_t n, int64_t k,
-                      cudaStream_t s) {
+xe_status gemm_launch(const float* a, const float* a2, int64_t a_sb, int64_t a_sm, int64_t a_sk, bool a_linear,
+                      const float* shift_a, const float* b, int64_t b_sb, int64_t b_sk, int64_t b_sn,
+                      const float* shift_b, float* c, int64_t c_sb, int64_t c_sm, int64_t c_sn, int64_t batch, int64_t m,
+                      int64_t n, int64_t k, bool shift_min, cudaStream_t s) {
   Params p{};
   p.a = a;
   p.a2 = a2;
@@ -251,6 +253,7 @@ xe_status gemm_launch(const float* a, const float* a2, int64_t a_sb, int64_t a_s
   p.N = (int)n;
   p.K = (int)k;
   p.c_vec = (c_sn == 1 && n % 4 == 0 && c_sm % 4 == 0 && c_sb % 4 == 0 && aligned16(c)) ? 1 : 0;
+  p.shift_min = shift_min ? 1 : 0;
 
   // Operand staging layout: K-major unless the M (resp. N) axis is the
   // unit-stride one.  16-byte loads need the unit-stride axis, every other
@@ -262,7 +265,7 @@ xe_status gemm_launch(const float* a, const float* a2, int64_t a_sb, int64_t a_s
                      (ak ? (a_sk == 1 && k % 4 == 0 && a_sm % 4 == 0) : (a_sm == 1 && m % 4 == 0 && a_sk % 4 == 0));
   const bool b_vec = aligned16(b) && b_sb % 4 == 0 &&
                      (bk ? (b_sk == 1 && k % 4 == 0 && b_sn % 4 == 0) : (b_sn == 1 && n % 4 == 0 && b_sk % 4 == 0));
-  return launch_gemm(p, ak, bk, a_vec && b_vec, s);
+  return launch_gemm(p, a_linear, ak, bk, a_vec && b_vec, s);
 }
 
 xe_status gemm_check(const char* who, const float* a, const float* b, const float* c, int64_t batch, int64_t m,
@@ -304,18 +307,21 @@ xe_status xe_logspace_gemm(const float* a, const float* a2, int64_t a_sb, int64_
   float* shift_a = nullptr;
   float* shift_b = nullptr;
   if (!a_linear) {
-    shift_a = ws;
+    // small K: the kernel computes the row shifts itself (shift_a stays null)
+    if (k > xe::gemm::kInlineShiftK) {
+      shift_a = ws;
+      st = shift_impl(a, a2, a_sb, a_sm, a_sk, batch, m, k, maxmode, shift_a, s);
+      if (st != XE_OK) return st;
+    }
     ws = reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + round_up((size_t)batch * m * sizeof(float)));
-    st = shift_impl(a, a2, a_sb, a_sm, a_sk, batch, m, k, maxmode, shift_a, s);
-    if (st != XE_OK) return st;
   }
   if (!b_linear) {
     shift_b = ws;
     st = shift_impl(b, nullptr, b_sb, b_sn, b_sk, batch, n, k, maxmode, shift_b, s);
     if (st != XE_OK) return st;
   }
-  return gemm_launch(a, a2, a_sb, a_sm, a_sk, shift_a, b, b_sb, b_sk, b_sn, shift_b, c, c_sb, c_sm, c_sn, batch, m, n,
-                     k, s);
+  return gemm_launch(a, a2, a_sb, a_sm, a_sk, a_linear != 0, shift_a, b, b_sb, b_sk, b_sn, shift_b, c, c_sb, c_sm,
+                     c_sn, batch, m, n, k, !maxmode, s);
 }
 
 xe_status xe_logspace_gemm_shifted(const float* a, const float* a2, int64_t a_sb, int64_t a_sm, int64_t a_sk,
@@ -327,8 +333,8 @@ xe_status xe_logspace_gemm_shifted(const float* a, const float* a2, int64_t a_sb
   if (a2 && !shift_a)
     return fail(XE_ERR_INVALID_ARGUMENT, "xe_logspace_gemm_shifted: a fused addend requires a log-domain A operand");
   if (batch == 0 || m == 0 || n == 0) return XE_OK;
-  return gemm_launch(a, a2, a_sb, a_sm, a_sk, shift_a, b, b_sb, b_sk, b_sn, shift_b, c, c_sb, c_sm, c_sn, batch, m, n,
-                     k, as_stream(stream));
+  return gemm_launch(a, a2, a_sb, a_sm, a_sk, shift_a == nullptr, shift_a, b, b_sb, b_sk, b_sn, shift_b, c, c_sb, c_sm,
+                     c_sn, batch, m, n, k, false, as_stream(stream));
 }
 
 xe_status xe_softmax(const float* x, float* y, int64_t outer, int64_t axis_len, int64_t inner, int32_t log_output,
@@ -491,7 +497,53 @@ xe_status xe_logspace_tucker(const float* l, const float* r, const float* w, flo
 
 }  // extern "C"
 
-static xe_status xe_tucker_impl(const float*, const float*, const float*, float*, int64_t, int64_t, int64_t, int64_t,
-                                int64_t, int32_t, cudaStream_t) {
-  return fail(XE_ERR_NOT_SUPPORTED, "xe_logspace_tucker: not built yet");
+template <int TJ>
+xe_status launch_tucker(const Params& p, cudaStream_t s) {
+  using namespace xe::gemm;
+  const int bn = pick_bn(p.N);
+  Params q = p;
+  set_tiling(q, bn);
+  switch (bn) {
+    case 32: return launch_gemm_t<32, kATucker, true, true, true, TJ>(q, s);
+    case 64: return launch_gemm_t<64, kATucker, true, true, true, TJ>(q, s);
+    default: return launch_gemm_t<128, kATucker, true, true, true, TJ>(q, s);
+  }
+}
+
+static xe_status xe_tucker_impl(const float* l, const float* r, const float* w, float* y, int64_t batch, int64_t folds,
+                                int64_t i_dim, int64_t j_dim, int64_t o_dim, int32_t shift_mode, cudaStream_t stream) {
+  if (!l || !r || !w || !y) return fail(XE_ERR_INVALID_ARGUMENT, "xe_logspace_tucker: null pointer");
+  if (batch < 0 || folds < 0 || i_dim <= 0 || j_dim <= 0 || o_dim < 0)
+    return fail(XE_ERR_INVALID_ARGUMENT, "xe_logspace_tucker: invalid extents");
+  if (shift_mode != XE_SHIFT_MAX && shift_mode != XE_SHIFT_MIN)
+    return fail(XE_ERR_INVALID_ARGUMENT, "xe_logspace_tucker: unknown shift mode %d", shift_mode);
+  if ((j_dim != 32 && j_dim != 64) || i_dim % 8 != 0)
+    return fail(XE_ERR_NOT_SUPPORTED, "xe_logspace_tucker: J must be 32 or 64 and I a multiple of 8 (got I=%lld, J=%lld)",
+                (long long)i_dim, (long long)j_dim);
+  if (batch > INT32_MAX || folds > INT32_MAX || i_dim * j_dim > INT32_MAX || o_dim > INT32_MAX)
+    return fail(XE_ERR_NOT_SUPPORTED, "xe_logspace_tucker: extents above 2^31-1 are not supported");
+  if (!aligned16(l) || !aligned16(r) || !aligned16(w) || !aligned16(y))
+    return fail(XE_ERR_INVALID_ARGUMENT, "xe_logspace_tucker: operands must be 16-byte aligned");
+  if (batch == 0 || folds == 0 || o_dim == 0) return XE_OK;
+  Params p{};
+  // the weights are the linear, K-major B operand of a batched contraction over folds
+  p.b = w;
+  p.b_sb = o_dim * i_dim * j_dim;
+  p.b_sk = 1;
+  p.b_sn = i_dim * j_dim;
+  p.c = y;
+  p.c_sb = o_dim;
+  p.c_sm = folds * o_dim;
+  p.c_sn = 1;
+  p.batch = (int)folds;
+  p.M = (int)batch;
+  p.N = (int)o_dim;
+  p.K = (int)(i_dim * j_dim);
+  p.c_vec = (o_dim % 4 == 0) ? 1 : 0;
+  p.tl = l;
+  p.tr = r;
+  p.t_folds = (int)folds;
+  p.t_i = (int)i_dim;
+  p.shift_min = shift_mode == XE_SHIFT_MIN;
+  return j_dim == 32 ? launch_tucker<32>(p, stream) : launch_tucker<64>(p, stream);
 }

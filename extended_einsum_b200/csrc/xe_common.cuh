@@ -160,18 +160,24 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // ---------------------------------------------------------------------------
-// UMMA descriptors (layouts are 128-byte swizzled; every tile base is
-// 1024-byte aligned).
+// UMMA descriptors (every tile base is 1024-byte aligned).
 //
+// K-major tiles use the 128-byte swizzle (layout type 2): 128-byte rows,
+// 16-byte chunk index XOR (row & 7), 8-row groups.  MN-major TF32 tiles must
+// use the 128-byte swizzle with 32-byte atoms (layout type 1): 128-byte
+// k-rows along MN, 32-byte chunk index XOR (k-row & 3), 4-row groups.
+enum : uint32_t { kLayoutSW128Base32B = 1, kLayoutSW128 = 2 };
+
 // Shared-memory matrix descriptor: start address, leading and stride byte
-// offsets (16-byte units), descriptor version 1, layout type 2 = 128B swizzle.
-__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+// offsets (16-byte units), descriptor version 1, layout type.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes,
+                                              uint32_t layout) {
   uint64_t d = 0;
   d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
   d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
   d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
   d |= (uint64_t)1u << 46;  // version
-  d |= (uint64_t)2u << 61;  // SWIZZLE_128B
+  d |= (uint64_t)(layout & 7u) << 61;
   return d;
 }
 

@@ -46,9 +46,15 @@ def test_golden_programs(golden, golden_programs, mode):
             if _outputs_log_domain(spec):
                 log_close(out, ref32)
             else:
-                # raw outputs: relative error = absolute error of the log value
-                np.testing.assert_allclose(out, ref32, rtol=2e-5, atol=0, equal_nan=True)
-                np.testing.assert_allclose(out, ref64, rtol=2e-5, atol=0, equal_nan=True)
+                # raw outputs: relative error = absolute error of the log value.  Where
+                # intermediate log-values are large (the 1e30-scaled chain reaches ~550,
+                # fp32 ulp 6.1e-5) the reference's own fp32 path is off by more than
+                # 2e-5; the bound is then twice the reference's fp32 error vs fp64.
+                with np.errstate(invalid="ignore", divide="ignore"):
+                    ref_err = np.nanmax(np.abs(ref32 - ref64) / np.abs(ref64)) if ref64.size else 0.0
+                rtol = max(2e-5, 2.0 * float(ref_err))
+                np.testing.assert_allclose(out, ref32, rtol=rtol, atol=0, equal_nan=True)
+                np.testing.assert_allclose(out, ref64, rtol=rtol, atol=0, equal_nan=True)
         except AssertionError as e:
             failures.append(f"{name}: {e}")
     assert not failures, "\n".join(failures)
