@@ -6,24 +6,30 @@
 // (backend_translation/translate.py:686-750) spreads over ~16 backend calls
 // for a binary contraction, fused into one persistent kernel.  Roles (warps):
 //
-//   A transform (0-3)  one thread per tile row: global fp32 -> exp(x - shift)
-//                      (or the linear value, or the Tucker outer product) ->
-//                      TF32 hi/lo split -> tcgen05.st into a TMEM stage
-//   B transform (4-7)  global fp32 -> exp / split -> 128B-swizzled smem stage
+//   A rows (0-3)       one thread per tile row: raw fp32 (from a TMA-filled
+//                      staging ring, or global loads) -> exp(x - shift) (or
+//                      the linear value, or the Tucker outer product) -> TF32
+//                      hi/lo split -> tcgen05.st into a TMEM stage
+//   B tiles (4-7)      global fp32 -> exp / split -> 128B-swizzled smem stage
 //   MMA (8, 1 thread)  per 8-wide k-step: main += A_hi*B_hi,
 //                      corr += A_hi*B_lo + A_lo*B_hi  (tcgen05.mma, A in TMEM)
 //   drain (9-12)       one thread per row: adds each finished main-accumulator
 //                      chunk into an fp32 running sum in smem (round to
 //                      nearest), then log(running + corr) + shifts -> global
+//   producer (13)      one thread: TMA loads of the raw A tiles (and of the
+//                      fused addend) into the staging ring; no multicast
 //
 // The tensor core accumulates in fp32 with truncation, a bias that grows
 // linearly with the number of accumulating instructions; the main
 // accumulator is therefore restarted every kChunkKB k-blocks (two chunk
 // buffers, so the MMA continues while the previous chunk is drained).  The
 // correction products are ~2^-10 of the main ones and accumulate over the
-// whole tile.  Stages and chunks are handed over with mbarriers; every wait is
-// bounded (xe_common.cuh).
+// whole tile.  Row shifts reach the drain warps through shared memory.
+// Stages, chunks and shift slots are handed over with mbarriers; every wait
+// is bounded (xe_common.cuh).
 #pragma once
+
+#include <cuda.h>
 
 #include "xe_common.cuh"
 
@@ -37,12 +43,17 @@ constexpr int kBWarps = 4;
 constexpr int kMmaWarp = kAWarps + kBWarps;  // 8
 constexpr int kDrainWarp0 = kMmaWarp + 1;    // 9..12
 constexpr int kDrainWarps = 4;
-constexpr int kThreads = (kMmaWarp + 1 + kDrainWarps) * 32;  // 416
+constexpr int kProducerWarp = kDrainWarp0 + kDrainWarps;  // 13
+constexpr int kThreads = (kProducerWarp + 1) * 32;        // 448
 constexpr int kStages = 2;
-constexpr int kChunkKB = 4;         // 128 k per main-accumulator chunk
-constexpr int kInlineShiftK = 128;  // A row shifts computed in-kernel up to this K
+constexpr int kChunkKB = 4;  // 128 k per main-accumulator chunk
+constexpr int kATileBytes = kBM * kBK * 4;  // one raw A tile (16 KB)
 
 enum AMode : int { kALog = 0, kALinear = 1, kATucker = 2 };
+// Where the A rows come from: a TMA-filled staging ring (K-major A with
+// 16-byte aligned strides), the same plus a second ring for the fused addend,
+// or per-thread global loads (any layout).
+enum ASource : int { kATma = 0, kATma2 = 1, kALdg = 2 };
 
 struct Params {
   const float* a;
@@ -57,6 +68,7 @@ struct Params {
   int batch, M, N, K;
   int tiles_m, tiles_n, num_tiles, num_kb;
   int c_vec;      // output rows may be written with 16-byte stores
+  int a_vec;      // LDG source: rows are k-contiguous and 16-byte aligned
   int shift_min;  // row extremes computed in-kernel use min instead of max
   // Tucker layer: l (rows, folds, I), r (rows, folds, J) contiguous; batch = fold
   const float* tl;
@@ -70,20 +82,30 @@ __host__ __device__ constexpr int pow2_at_least(int x) {
   return p;
 }
 
-template <int BN>
+template <int BN, int ASRC>
 struct Cfg {
   static_assert(BN == 32 || BN == 64 || BN == 128, "BN");
   static constexpr int kBTile = BN * kBK * 4;  // bytes, one of hi/lo
   static constexpr int kStageBytes = 2 * kBTile;
   static constexpr int kRunningBytes = BN * kBM * 4;
+  // raw A staging ring (TMA sources only)
+  static constexpr int kAStageBytes = ASRC == kATma2 ? 2 * kATileBytes : kATileBytes;
+  static constexpr int kAStages = ASRC == kALdg ? 0 : ((ASRC == kATma2 && BN == 128) ? 2 : 4);
+  static constexpr int kShiftBytes = 2 * 2 * kBM * 4;  // [slot][s1,s2][row]
   // TMEM columns: A stages (hi 32 + lo 32 each), two main chunks, correction
   static constexpr int kTmemA = 0;
   static constexpr int kTmemMain = 64 * kStages;
   static constexpr int kTmemCorr = kTmemMain + 2 * BN;
   static constexpr int kTmemCols = pow2_at_least(kTmemCorr + BN);
   static constexpr int kBarrierBytes = 256;
-  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kRunningBytes + kBarrierBytes;
+  static constexpr int kOffB = 0;
+  static constexpr int kOffA = kOffB + kStages * kStageBytes;
+  static constexpr int kOffRun = kOffA + kAStages * kAStageBytes;
+  static constexpr int kOffShift = kOffRun + kRunningBytes;
+  static constexpr int kOffBar = kOffShift + kShiftBytes;
+  static constexpr int kSmemBytes = 1024 + kOffBar + kBarrierBytes;
   static_assert(kTmemCorr + BN <= 512, "TMEM");
+  static_assert(kSmemBytes <= 232448, "shared memory");
 };
 
 // Byte offset of the 16-byte chunk holding elements (row, 4q..4q+3) of a
@@ -154,6 +176,24 @@ __device__ __forceinline__ void umma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, u
       : "memory");
 }
 
+// 3-D tiled TMA load into shared memory, completing on an mbarrier (no multicast).
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+      "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ float4 lds_v4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+  return v;
+}
+
 __device__ __forceinline__ float extreme(float a, float b, bool is_min) {
   float r;
   if (is_min)
@@ -173,22 +213,31 @@ __device__ __forceinline__ void decode_tile(const Params& p, int tile, int& bb, 
 // ---------------------------------------------------------------------------
 // A operand, one thread per tile row.
 
-template <int AMODE, bool A_KMAJ, bool VEC, int TJ>
+template <int AMODE, int TJ>
 struct ARow {
   static constexpr int kTJ = TJ > 0 ? TJ : 1;
-  const float* row = nullptr;   // element (m, 0) of this row (log / linear)
+  const float* row = nullptr;   // element (m, 0) of this row (global-load source)
   const float* row2 = nullptr;  // fused addend
   int64_t step = 1;             // element stride along k
   bool valid = false;
-  float shift = 0.0f;  // exp(x - shift); 0 for linear rows; sr for Tucker
+  float shift = 0.0f;  // exp(x - shift): the row shift (sr for Tucker)
   // Tucker
   const float* lrow = nullptr;
   float sl = 0.0f;
   float er[kTJ];
 
-  // Row extreme of the (possibly fused) operand over all k, for small K.
+  __device__ void set_row(const Params& p, int bb, int m) {
+    valid = m < p.M;
+    const int64_t base = (int64_t)bb * p.a_sb + (int64_t)(valid ? m : 0) * p.a_sm;
+    row = p.a + base;
+    row2 = p.a2 ? p.a2 + base : nullptr;
+    step = p.a_sk;
+  }
+
+  // Row extreme over all k by global loads (small K, global-load source).
   __device__ float scan_extreme(const Params& p, bool is_min) const {
     float e = is_min ? INFINITY : -INFINITY;
+#pragma unroll 8
     for (int k = 0; k < p.K; ++k) {
       float v = __ldg(row + k * step);
       if (row2) v += __ldg(row2 + k * step);
@@ -197,75 +246,63 @@ struct ARow {
     return e;
   }
 
-  __device__ void begin_tile(const Params& p, int bb, int m, bool want_er) {
+  // Tucker: row extremes of l and r; exp(r - sr) kept for the whole tile.
+  __device__ void tucker_row(const Params& p, int bb, int m, bool want_er) {
     valid = m < p.M;
-    const int mm = valid ? m : 0;
     const bool is_min = p.shift_min != 0;
-    if (AMODE == kATucker) {
-      const int64_t r = (int64_t)mm * p.t_folds + bb;
-      lrow = p.tl + r * p.t_i;
-      const float* rrow = p.tr + r * kTJ;
-      float e1 = is_min ? INFINITY : -INFINITY, e2 = e1;
-      for (int i = 0; i < p.t_i; ++i) e1 = extreme(e1, __ldg(lrow + i), is_min);
-#pragma unroll
-      for (int j = 0; j < kTJ; j += 4) {
-        const float4 v = ldg_v4(rrow + j);
-        e2 = extreme(extreme(e2, v.x, is_min), extreme(v.y, extreme(v.z, v.w, is_min), is_min), is_min);
-      }
-      sl = e1;
-      shift = e2;
-      if (want_er) {
-#pragma unroll
-        for (int j = 0; j < kTJ; j += 4) {
-          const float4 v = ldg_v4(rrow + j);
-          er[j] = valid ? exp_shifted(v.x, e2) : 0.0f;
-          er[j + 1] = valid ? exp_shifted(v.y, e2) : 0.0f;
-          er[j + 2] = valid ? exp_shifted(v.z, e2) : 0.0f;
-          er[j + 3] = valid ? exp_shifted(v.w, e2) : 0.0f;
-        }
-      }
-      return;
+    const int64_t r = (int64_t)(valid ? m : 0) * p.t_folds + bb;
+    lrow = p.tl + r * p.t_i;
+    const float* rrow = p.tr + r * kTJ;
+    float e1 = is_min ? INFINITY : -INFINITY, e2 = e1;
+#pragma unroll 4
+    for (int i = 0; i < p.t_i; i += 4) {
+      const float4 v = ldg_v4(lrow + i);
+      e1 = extreme(extreme(e1, v.x, is_min), extreme(v.y, extreme(v.z, v.w, is_min), is_min), is_min);
     }
-    const int64_t base = (int64_t)bb * p.a_sb + (int64_t)mm * p.a_sm;
-    row = p.a + base;
-    row2 = p.a2 ? p.a2 + base : nullptr;
-    step = p.a_sk;
-    if (AMODE == kALinear) {
-      shift = 0.0f;
-    } else if (p.shift_a) {
-      shift = valid ? __ldg(p.shift_a + (int64_t)bb * p.M + m) : 0.0f;
-    } else {
-      shift = valid ? scan_extreme(p, is_min) : 0.0f;
+    float4 rv[kTJ / 4 > 0 ? kTJ / 4 : 1];
+#pragma unroll
+    for (int j = 0; j < kTJ / 4; ++j) {
+      rv[j] = ldg_v4(rrow + 4 * j);
+      e2 = extreme(extreme(e2, rv[j].x, is_min), extreme(rv[j].y, extreme(rv[j].z, rv[j].w, is_min), is_min), is_min);
+    }
+    sl = e1;
+    shift = e2;
+    if (want_er) {
+#pragma unroll
+      for (int j = 0; j < kTJ / 4; ++j) {
+        er[4 * j] = valid ? exp_shifted(rv[j].x, e2) : 0.0f;
+        er[4 * j + 1] = valid ? exp_shifted(rv[j].y, e2) : 0.0f;
+        er[4 * j + 2] = valid ? exp_shifted(rv[j].z, e2) : 0.0f;
+        er[4 * j + 3] = valid ? exp_shifted(rv[j].w, e2) : 0.0f;
+      }
     }
   }
 
-  // Raw values of k0 .. k0+31 (with the fused addend) into v.
-  __device__ void load(const Params& p, int k0, float (&v)[32]) const {
+  // Raw values of k0 .. k0+31 (with the fused addend) by global loads.
+  __device__ void load_global(const Params& p, int k0, float (&v)[32]) const {
     if (AMODE == kATucker) {
       v[0] = valid ? __ldg(lrow + k0 / kTJ) : -INFINITY;  // one l value per k-block
       return;
     }
     const float fill = (AMODE == kALinear) ? 0.0f : -INFINITY;
-    if (VEC && A_KMAJ) {
-      if (valid && k0 + 32 <= p.K) {
-        const float* r = row + k0;
+    if (p.a_vec && valid && k0 + 32 <= p.K) {
+      const float* r = row + k0;
 #pragma unroll
-        for (int j = 0; j < 32; j += 4) {
-          float4 x = ldg_v4(r + j);
-          if (row2) {
-            const float4 y = ldg_v4(row2 + k0 + j);
-            x.x += y.x;
-            x.y += y.y;
-            x.z += y.z;
-            x.w += y.w;
-          }
-          v[j] = x.x;
-          v[j + 1] = x.y;
-          v[j + 2] = x.z;
-          v[j + 3] = x.w;
+      for (int j = 0; j < 32; j += 4) {
+        float4 x = ldg_v4(r + j);
+        if (row2) {
+          const float4 y = ldg_v4(row2 + k0 + j);
+          x.x += y.x;
+          x.y += y.y;
+          x.z += y.z;
+          x.w += y.w;
         }
-        return;
+        v[j] = x.x;
+        v[j + 1] = x.y;
+        v[j + 2] = x.z;
+        v[j + 3] = x.w;
       }
+      return;
     }
     const float* r = row + (int64_t)k0 * step;
 #pragma unroll
@@ -300,6 +337,35 @@ struct ARow {
     }
   }
 };
+
+// Raw values of row r of a TMA-staged A tile (128 rows x 32 fp32, 128-byte
+// swizzle: 16-byte chunk j of row r at chunk j ^ (r & 7)), plus the staged
+// addend, masked to the tile's valid rows and k.
+template <int ASRC>
+__device__ __forceinline__ void load_staged_row(uint32_t stage, int r, bool valid, int kvalid, float fill,
+                                                float (&v)[32]) {
+  const uint32_t row = stage + r * 128;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    float4 x = lds_v4(row + ((j ^ (r & 7)) << 4));
+    if (ASRC == kATma2) {
+      const float4 y = lds_v4(row + kATileBytes + ((j ^ (r & 7)) << 4));
+      x.x += y.x;
+      x.y += y.y;
+      x.z += y.z;
+      x.w += y.w;
+    }
+    v[4 * j] = x.x;
+    v[4 * j + 1] = x.y;
+    v[4 * j + 2] = x.z;
+    v[4 * j + 3] = x.w;
+  }
+  if (!valid || kvalid < 32) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (!valid || j >= kvalid) v[j] = fill;
+  }
+}
 
 // ---------------------------------------------------------------------------
 // B operand: 128 threads, 16-byte chunks.  MN-major: thread t covers n-quad
@@ -395,20 +461,28 @@ struct BTile {
 
 // ---------------------------------------------------------------------------
 
-template <int BN, int AMODE, bool A_KMAJ, bool B_KMAJ, bool VEC, int TJ>
-__global__ void __launch_bounds__(kThreads, 1) lse_gemm_kernel(const Params p) {
-  using C = Cfg<BN>;
-  using ARowT = ARow<AMODE, A_KMAJ, VEC, TJ>;
+template <int BN, int AMODE, int ASRC, bool B_KMAJ, bool BVEC, int TJ>
+__global__ void __launch_bounds__(kThreads, 1)
+    lse_gemm_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtensorMap tmap_a,
+                    const __grid_constant__ CUtensorMap tmap_a2) {
+  using C = Cfg<BN, ASRC>;
+  using ARowT = ARow<AMODE, TJ>;
+  static_assert(AMODE != kATucker || ASRC == kALdg, "the Tucker operand is generated from global loads");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  float* running = (float*)(smem + kStages * C::kStageBytes);  // [BN][128], column-major
-  uint64_t* bars = (uint64_t*)(smem + kStages * C::kStageBytes + C::kRunningBytes);
-  uint64_t* full = bars;                    // [kStages], one arrival per A and B warp
-  uint64_t* empty = full + kStages;         // [kStages], tcgen05.commit
-  uint64_t* chunk_full = empty + kStages;   // [2], tcgen05.commit
-  uint64_t* chunk_empty = chunk_full + 2;   // [2], drain warps
-  uint64_t* corr_empty = chunk_empty + 2;   // [1], drain warps
-  uint64_t* drain = corr_empty + 1;         // [1], teardown
+  float* running = (float*)(smem + C::kOffRun);    // [BN][128], column-major
+  float* shifts = (float*)(smem + C::kOffShift);   // [2 slots][s1, s2][128 rows]
+  uint64_t* bars = (uint64_t*)(smem + C::kOffBar);
+  uint64_t* full = bars;                        // [kStages], one arrival per A and B warp
+  uint64_t* empty = full + kStages;             // [kStages], tcgen05.commit
+  uint64_t* chunk_full = empty + kStages;       // [2], tcgen05.commit
+  uint64_t* chunk_empty = chunk_full + 2;       // [2], drain warps
+  uint64_t* corr_empty = chunk_empty + 2;       // [1], drain warps
+  uint64_t* shift_full = corr_empty + 1;        // [2], A warps
+  uint64_t* shift_empty = shift_full + 2;       // [2], drain warps
+  uint64_t* a_full = shift_empty + 2;           // [4], TMA transactions
+  uint64_t* a_empty = a_full + 4;               // [4], A warps
+  uint64_t* drain = a_empty + 4;                // [1], teardown
   uint32_t* tmem_slot = (uint32_t*)(drain + 1);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
@@ -423,6 +497,12 @@ __global__ void __launch_bounds__(kThreads, 1) lse_gemm_kernel(const Params p) {
     for (int c = 0; c < 2; ++c) {
       mbar_init(&chunk_full[c], 1);
       mbar_init(&chunk_empty[c], kDrainWarps);
+      mbar_init(&shift_full[c], kAWarps);
+      mbar_init(&shift_empty[c], kDrainWarps);
+    }
+    for (int s = 0; s < 4; ++s) {
+      mbar_init(&a_full[s], 1);
+      mbar_init(&a_empty[s], kAWarps);
     }
     mbar_init(corr_empty, kDrainWarps);
     mbar_init(drain, 1);
@@ -440,18 +520,78 @@ __global__ void __launch_bounds__(kThreads, 1) lse_gemm_kernel(const Params p) {
     // ------------------------------------------------------------ A rows
     const int r = warp * 32 + lane;  // warp w may access TMEM lanes 32w..32w+31
     const uint32_t lane_bits = (uint32_t)(warp * 32) << 16;
+    const bool is_min = p.shift_min != 0;
+    const float fill = (AMODE == kALinear) ? 0.0f : -INFINITY;
     ARowT a;
-    uint32_t it = 0;
+    uint32_t it = 0, ait = 0, tl = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+    for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++tl) {
       int bb, mt, nt;
       decode_tile(p, tile, bb, mt, nt);
-      a.begin_tile(p, bb, mt * kBM + r, true);
+      const int m = mt * kBM + r;
+      // -------- row shifts
+      float s1 = 0.0f, s2 = 0.0f;
+      if (AMODE == kATucker) {
+        a.tucker_row(p, bb, m, true);
+        s1 = a.sl;
+        s2 = a.shift;
+      } else {
+        a.set_row(p, bb, m);
+        if (AMODE == kALog) {
+          if (p.shift_a) {
+            a.shift = a.valid ? __ldg(p.shift_a + (int64_t)bb * p.M + m) : 0.0f;
+          } else if (ASRC != kALdg) {
+            // every k-block of this tile is staged (num_kb <= kAStages): scan them
+            float e = is_min ? INFINITY : -INFINITY;
+            for (int kb = 0; kb < p.num_kb; ++kb) {
+              const uint32_t sidx = (ait + kb) % C::kAStages;
+              if (!mbar_wait(&a_full[sidx], ((ait + kb) / C::kAStages) & 1, kSiteGemmFull, abort_flag)) {
+                ok = false;
+                break;
+              }
+              float v[32];
+              const int kvalid = p.K - kb * kBK;
+              load_staged_row<ASRC>(smem_base + C::kOffA + sidx * C::kAStageBytes, r, a.valid, kvalid, fill, v);
+              // the k tail is masked with -inf for exp(); it must not enter a min
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (j < kvalid) e = extreme(e, v[j], is_min);
+            }
+            if (!ok) break;
+            a.shift = a.valid ? e : 0.0f;
+          } else {
+            a.shift = a.valid ? a.scan_extreme(p, is_min) : 0.0f;
+          }
+          s1 = a.shift;
+        }
+      }
+      // -------- publish the row shifts for the epilogue
+      {
+        const uint32_t slot = tl & 1;
+        if (!mbar_wait(&shift_empty[slot], ((tl >> 1) & 1) ^ 1, kSiteGemmAccEmpty, abort_flag)) break;
+        shifts[(slot * 2 + 0) * kBM + r] = s1;
+        shifts[(slot * 2 + 1) * kBM + r] = s2;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&shift_full[slot]);
+      }
+      // -------- k loop
       float cur[32], nxt[32];
-      a.load(p, 0, cur);
+      if (ASRC == kALdg) a.load_global(p, 0, cur);
       for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
-        const bool more = kb + 1 < p.num_kb;
-        if (more) a.load(p, (kb + 1) * kBK, nxt);
+        if (ASRC != kALdg) {
+          const uint32_t sidx = ait % C::kAStages;
+          if (!mbar_wait(&a_full[sidx], (ait / C::kAStages) & 1, kSiteGemmFull, abort_flag)) {
+            ok = false;
+            break;
+          }
+          load_staged_row<ASRC>(smem_base + C::kOffA + sidx * C::kAStageBytes, r, a.valid, p.K - kb * kBK, fill,
+                                cur);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&a_empty[sidx]);
+          ++ait;
+        } else if (kb + 1 < p.num_kb) {
+          a.load_global(p, (kb + 1) * kBK, nxt);
+        }
         const uint32_t s = it % kStages;
         const uint32_t ph = (it / kStages) & 1;
         if (!mbar_wait(&empty[s], ph ^ 1, kSiteGemmEmpty, abort_flag)) {
@@ -476,7 +616,7 @@ __global__ void __launch_bounds__(kThreads, 1) lse_gemm_kernel(const Params p) {
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&full[s]);
-        if (more) {
+        if (ASRC == kALdg && kb + 1 < p.num_kb) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) cur[j] = nxt[j];
         }
@@ -485,7 +625,7 @@ __global__ void __launch_bounds__(kThreads, 1) lse_gemm_kernel(const Params p) {
   } else if (warp < kAWarps + kBWarps) {
     // ------------------------------------------------------------ B tiles
     const int t = threadIdx.x - kAWarps * 32;
-    using BT = BTile<BN, B_KMAJ, VEC>;
+    using BT = BTile<BN, B_KMAJ, BVEC>;
     BT bt;
     uint32_t it = 0;
     bool ok = true;
@@ -505,7 +645,7 @@ __global__ void __launch_bounds__(kThreads, 1) lse_gemm_kernel(const Params p) {
           ok = false;
           break;
         }
-        const uint32_t st = smem_base + s * C::kStageBytes;
+        const uint32_t st = smem_base + C::kOffB + s * C::kStageBytes;
         bt.store(p, st, st + C::kBTile, t, cur);
         fence_proxy_async_smem();
         __syncwarp();
@@ -552,7 +692,7 @@ __global__ void __launch_bounds__(kThreads, 1) lse_gemm_kernel(const Params p) {
           }
           tc_fence_after();
           const uint32_t a_hi = tmem + C::kTmemA + 64 * s, a_lo = a_hi + 32;
-          const uint32_t b_hi = smem_base + s * C::kStageBytes, b_lo = b_hi + C::kBTile;
+          const uint32_t b_hi = smem_base + C::kOffB + s * C::kStageBytes, b_lo = b_hi + C::kBTile;
 #pragma unroll
           for (int kk = 0; kk < kBK / 8; ++kk) {
             const uint64_t dbh = smem_desc(b_hi + kk * b_step, b_lbo, b_sbo, b_lay);
@@ -573,16 +713,15 @@ __global__ void __launch_bounds__(kThreads, 1) lse_gemm_kernel(const Params p) {
       mbar_wait(drain, 0, kSiteGemmDrain, abort_flag, /*honor_abort=*/false);
     }
     __syncwarp();
-  } else {
+  } else if (warp < kProducerWarp) {
     // ------------------------------------------------------------ drain + epilogue
     const int q = warp & 3;  // TMEM lane quadrant of this warp
     const int r = q * 32 + lane;
     const uint32_t lane_bits = (uint32_t)(q * 32) << 16;
-    ARowT a;  // recomputes this row's shifts at the end of each tile
-    uint32_t gc = 0;
+    uint32_t gc = 0, tl = 0;
     bool ok = true;
     const int chunks = (p.num_kb + kChunkKB - 1) / kChunkKB;
-    for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+    for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++tl) {
       int bb, mt, nt;
       decode_tile(p, tile, bb, mt, nt);
       const int m = mt * kBM + r;
@@ -614,12 +753,12 @@ __global__ void __launch_bounds__(kThreads, 1) lse_gemm_kernel(const Params p) {
       }
       if (!ok) break;
       // Epilogue: the last chunk commit covered every MMA of this tile.
-      float s1 = 0.0f, s2 = 0.0f;
-      if (AMODE != kALinear) {
-        a.begin_tile(p, bb, m, false);
-        s1 = AMODE == kATucker ? a.sl : a.shift;
-        s2 = AMODE == kATucker ? a.shift : 0.0f;
-      }
+      const uint32_t slot = tl & 1;
+      if (!mbar_wait(&shift_full[slot], (tl >> 1) & 1, kSiteGemmAccFull, abort_flag)) break;
+      const float s1 = shifts[(slot * 2 + 0) * kBM + r];
+      const float s2 = shifts[(slot * 2 + 1) * kBM + r];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&shift_empty[slot]);
       const float* sbp = p.shift_b ? p.shift_b + (int64_t)bb * p.N : nullptr;
       float* crow = p.c + (int64_t)bb * p.c_sb + (int64_t)m * p.c_sm;
 #pragma unroll 1
@@ -656,6 +795,25 @@ __global__ void __launch_bounds__(kThreads, 1) lse_gemm_kernel(const Params p) {
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(corr_empty);
+    }
+  } else if (ASRC != kALdg && lane == 0) {
+    // ------------------------------------------------------------ TMA producer
+    uint32_t ait = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+      int bb, mt, nt;
+      decode_tile(p, tile, bb, mt, nt);
+      for (int kb = 0; kb < p.num_kb; ++kb, ++ait) {
+        const uint32_t sidx = ait % C::kAStages;
+        if (!mbar_wait(&a_empty[sidx], ((ait / C::kAStages) & 1) ^ 1, kSiteGemmEmpty, abort_flag)) {
+          ok = false;
+          break;
+        }
+        const uint32_t dst = smem_base + C::kOffA + sidx * C::kAStageBytes;
+        mbar_expect_tx(&a_full[sidx], C::kAStageBytes);
+        tma_load_3d(dst, &tmap_a, kb * kBK, mt * kBM, bb, &a_full[sidx]);
+        if (ASRC == kATma2) tma_load_3d(dst + kATileBytes, &tmap_a2, kb * kBK, mt * kBM, bb, &a_full[sidx]);
+      }
     }
   }
 

@@ -1,5 +1,7 @@
 // C ABI of the sm_100a kernels (declared in include/xe_b200.h).  One
 // translation unit so that the device status word is shared by all kernels.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -71,26 +73,60 @@ cudaError_t prepare_kernel(K kernel, int smem_bytes, std::atomic<uint32_t>& done
   return e;
 }
 
-template <int BN, int AMODE, bool AK, bool BK, bool VEC, int TJ>
-xe_status launch_gemm_t(const Params& p, cudaStream_t stream) {
-  using C = xe::gemm::Cfg<BN>;
-  auto kernel = xe::gemm::lse_gemm_kernel<BN, AMODE, AK, BK, VEC, TJ>;
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// dependency on libcuda).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::atomic<int> state{0};
+  if (state.load() == 0) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess && ptr) {
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+      state.store(1);
+    } else {
+      state.store(2);
+    }
+  }
+  return fn;
+}
+
+// Tensor map of a (batch, rows, k) fp32 operand with k contiguous: boxes of
+// 32 k x 128 rows, 128-byte swizzle (the layout load_staged_row reads).
+bool encode_a_map(CUtensorMap* map, const float* base, int64_t batch, int64_t rows, int64_t k, int64_t s_row,
+                  int64_t s_batch) {
+  PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+  if (!encode) return false;
+  const int64_t sb = batch > 1 ? s_batch : rows * s_row;
+  if (s_row <= 0 || sb <= 0 || (s_row * 4) % 16 != 0 || (sb * 4) % 16 != 0 || !aligned16(base)) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)k, (cuuint64_t)rows, (cuuint64_t)batch};
+  cuuint64_t strides[2] = {(cuuint64_t)(s_row * 4), (cuuint64_t)(sb * 4)};
+  cuuint32_t box[3] = {32, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int BN, int AMODE, int ASRC, bool BK, bool BVEC, int TJ>
+xe_status launch_gemm_t(const Params& p, const CUtensorMap& ma, const CUtensorMap& ma2, cudaStream_t stream) {
+  using C = xe::gemm::Cfg<BN, ASRC>;
+  auto kernel = xe::gemm::lse_gemm_kernel<BN, AMODE, ASRC, BK, BVEC, TJ>;
   static std::atomic<uint32_t> attribute_set{0};
   cudaError_t e = prepare_kernel(kernel, C::kSmemBytes, attribute_set);
   if (e != cudaSuccess) return fail(XE_ERR_CUDA, "xe_logspace_gemm: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
   const int grid = (int)std::min<int64_t>(p.num_tiles, current_device_sms());
-  kernel<<<grid, xe::gemm::kThreads, C::kSmemBytes, stream>>>(p);
+  kernel<<<grid, xe::gemm::kThreads, C::kSmemBytes, stream>>>(p, ma, ma2);
   return check_launch("xe_logspace_gemm");
 }
 
-template <int BN, int AMODE>
-xe_status launch_gemm_layout(const Params& p, bool ak, bool bk, bool vec, cudaStream_t s) {
-  if (ak) {
-    if (bk) return vec ? launch_gemm_t<BN, AMODE, true, true, true, 0>(p, s) : launch_gemm_t<BN, AMODE, true, true, false, 0>(p, s);
-    return vec ? launch_gemm_t<BN, AMODE, true, false, true, 0>(p, s) : launch_gemm_t<BN, AMODE, true, false, false, 0>(p, s);
-  }
-  if (bk) return vec ? launch_gemm_t<BN, AMODE, false, true, true, 0>(p, s) : launch_gemm_t<BN, AMODE, false, true, false, 0>(p, s);
-  return vec ? launch_gemm_t<BN, AMODE, false, false, true, 0>(p, s) : launch_gemm_t<BN, AMODE, false, false, false, 0>(p, s);
+template <int BN, int AMODE, int ASRC>
+xe_status launch_gemm_b(const Params& p, const CUtensorMap& ma, const CUtensorMap& ma2, bool bk, bool bvec,
+                        cudaStream_t s) {
+  if (bk) return bvec ? launch_gemm_t<BN, AMODE, ASRC, true, true, 0>(p, ma, ma2, s) : launch_gemm_t<BN, AMODE, ASRC, true, false, 0>(p, ma, ma2, s);
+  return bvec ? launch_gemm_t<BN, AMODE, ASRC, false, true, 0>(p, ma, ma2, s) : launch_gemm_t<BN, AMODE, ASRC, false, false, 0>(p, ma, ma2, s);
 }
 
 int env_int(const char* name, int dflt) {
@@ -113,16 +149,58 @@ void set_tiling(Params& q, int bn) {
   q.num_kb = (q.K + xe::gemm::kBK - 1) / xe::gemm::kBK;
 }
 
-xe_status launch_gemm(const Params& p, bool a_linear, bool ak, bool bk, bool vec, cudaStream_t s) {
-  const int bn = pick_bn(p.N);
-  Params q = p;
-  set_tiling(q, bn);
+// How one contraction runs: the tile width, where the A rows come from, and
+// whether the A row shifts are computed in the kernel.
+struct GemmPlan {
+  int bn = 128;
+  int asrc = xe::gemm::kALdg;
+  bool inline_shift = false;
+  CUtensorMap ma{};
+  CUtensorMap ma2{};
+};
+
+int staged_k_capacity(int bn, int asrc) {
   using namespace xe::gemm;
-  switch (bn) {
-    case 32: return a_linear ? launch_gemm_layout<32, kALinear>(q, ak, bk, vec, s) : launch_gemm_layout<32, kALog>(q, ak, bk, vec, s);
-    case 64: return a_linear ? launch_gemm_layout<64, kALinear>(q, ak, bk, vec, s) : launch_gemm_layout<64, kALog>(q, ak, bk, vec, s);
-    default: return a_linear ? launch_gemm_layout<128, kALinear>(q, ak, bk, vec, s) : launch_gemm_layout<128, kALog>(q, ak, bk, vec, s);
+  int stages = 0;
+  if (asrc == kATma) stages = Cfg<128, kATma>::kAStages;
+  if (asrc == kATma2) stages = bn == 128 ? Cfg<128, kATma2>::kAStages : Cfg<64, kATma2>::kAStages;
+  return stages * kBK;
+}
+
+GemmPlan plan_gemm(const float* a, const float* a2, int64_t a_sb, int64_t a_sm, int64_t a_sk, bool a_linear,
+                   int64_t batch, int64_t m, int64_t n, int64_t k) {
+  using namespace xe::gemm;
+  GemmPlan g;
+  g.bn = pick_bn(n);
+  const bool tma_ok = env_int("XE_GEMM_NO_TMA", 0) == 0 && a_sk == 1 && (a_sm != 1 || m == 1) &&
+                      encode_a_map(&g.ma, a, batch, m, k, a_sm, a_sb) &&
+                      (a2 == nullptr || encode_a_map(&g.ma2, a2, batch, m, k, a_sm, a_sb));
+  if (tma_ok) g.asrc = a2 ? kATma2 : kATma;
+  const int inline_k = g.asrc == kALdg ? 128 : staged_k_capacity(g.bn, g.asrc);
+  g.inline_shift = !a_linear && k <= inline_k;
+  return g;
+}
+
+xe_status launch_gemm(const Params& p, const GemmPlan& g, bool a_linear, bool bk, bool bvec, cudaStream_t s) {
+  using namespace xe::gemm;
+  Params q = p;
+  set_tiling(q, g.bn);
+#define XE_LAUNCH_BN(BN)                                                                                        \
+  do {                                                                                                          \
+    if (a_linear) {                                                                                             \
+      if (g.asrc == kATma) return launch_gemm_b<BN, kALinear, kATma>(q, g.ma, g.ma2, bk, bvec, s);              \
+      return launch_gemm_b<BN, kALinear, kALdg>(q, g.ma, g.ma2, bk, bvec, s);                                   \
+    }                                                                                                           \
+    if (g.asrc == kATma) return launch_gemm_b<BN, kALog, kATma>(q, g.ma, g.ma2, bk, bvec, s);                   \
+    if (g.asrc == kATma2) return launch_gemm_b<BN, kALog, kATma2>(q, g.ma, g.ma2, bk, bvec, s);                 \
+    return launch_gemm_b<BN, kALog, kALdg>(q, g.ma, g.ma2, bk, bvec, s);                                        \
+  } while (0)
+  switch (g.bn) {
+    case 32: XE_LAUNCH_BN(32);
+    case 64: XE_LAUNCH_BN(64);
+    default: XE_LAUNCH_BN(128);
   }
+#undef XE_LAUNCH_BN
 }
 
 xe_status shift_impl(const float* x, const float* x2, int64_t sb, int64_t sr, int64_t sk, int64_t batch, int64_t rows,
@@ -231,7 +309,7 @@ namespace {
 xe_status gemm_launch(const float* a, const float* a2, int64_t a_sb, int64_t a_sm, int64_t a_sk, bool a_linear,
                       const float* shift_a, const float* b, int64_t b_sb, int64_t b_sk, int64_t b_sn,
                       const float* shift_b, float* c, int64_t c_sb, int64_t c_sm, int64_t c_sn, int64_t batch, int64_t m,
-                      int64_t n, int64_t k, bool shift_min, cudaStream_t s) {
+                      int64_t n, int64_t k, bool shift_min, const GemmPlan& g, cudaStream_t s) {
   Params p{};
   p.a = a;
   p.a2 = a2;
@@ -253,19 +331,16 @@ xe_status gemm_launch(const float* a, const float* a2, int64_t a_sb, int64_t a_s
   p.N = (int)n;
   p.K = (int)k;
   p.c_vec = (c_sn == 1 && n % 4 == 0 && c_sm % 4 == 0 && c_sb % 4 == 0 && aligned16(c)) ? 1 : 0;
+  p.a_vec = (a_sk == 1 && k % 4 == 0 && a_sm % 4 == 0 && a_sb % 4 == 0 && aligned16(a) &&
+             (a2 == nullptr || aligned16(a2))) ? 1 : 0;
   p.shift_min = shift_min ? 1 : 0;
-
-  // Operand staging layout: K-major unless the M (resp. N) axis is the
-  // unit-stride one.  16-byte loads need the unit-stride axis, every other
-  // stride and the base pointers to be multiples of four elements.
-  const bool ak = !(a_sm == 1 && a_sk != 1);
+  // B staging layout: K-major unless the N axis is the unit-stride one.
+  // 16-byte loads need the unit-stride axis, every other stride and the base
+  // pointer to be multiples of four elements.
   const bool bk = !(b_sn == 1) && b_sk == 1;
-  const bool a_al = aligned16(a) && (a2 == nullptr || aligned16(a2));
-  const bool a_vec = a_al && a_sb % 4 == 0 &&
-                     (ak ? (a_sk == 1 && k % 4 == 0 && a_sm % 4 == 0) : (a_sm == 1 && m % 4 == 0 && a_sk % 4 == 0));
   const bool b_vec = aligned16(b) && b_sb % 4 == 0 &&
                      (bk ? (b_sk == 1 && k % 4 == 0 && b_sn % 4 == 0) : (b_sn == 1 && n % 4 == 0 && b_sk % 4 == 0));
-  return launch_gemm(p, a_linear, ak, bk, a_vec && b_vec, s);
+  return launch_gemm(p, g, a_linear, bk, b_vec, s);
 }
 
 xe_status gemm_check(const char* who, const float* a, const float* b, const float* c, int64_t batch, int64_t m,
@@ -306,9 +381,10 @@ xe_status xe_logspace_gemm(const float* a, const float* a2, int64_t a_sb, int64_
   float* ws = static_cast<float*>(workspace);
   float* shift_a = nullptr;
   float* shift_b = nullptr;
+  const GemmPlan plan = plan_gemm(a, a2, a_sb, a_sm, a_sk, a_linear != 0, batch, m, n, k);
   if (!a_linear) {
     // small K: the kernel computes the row shifts itself (shift_a stays null)
-    if (k > xe::gemm::kInlineShiftK) {
+    if (!plan.inline_shift) {
       shift_a = ws;
       st = shift_impl(a, a2, a_sb, a_sm, a_sk, batch, m, k, maxmode, shift_a, s);
       if (st != XE_OK) return st;
@@ -321,7 +397,7 @@ xe_status xe_logspace_gemm(const float* a, const float* a2, int64_t a_sb, int64_
     if (st != XE_OK) return st;
   }
   return gemm_launch(a, a2, a_sb, a_sm, a_sk, a_linear != 0, shift_a, b, b_sb, b_sk, b_sn, shift_b, c, c_sb, c_sm,
-                     c_sn, batch, m, n, k, !maxmode, s);
+                     c_sn, batch, m, n, k, !maxmode, plan, s);
 }
 
 xe_status xe_logspace_gemm_shifted(const float* a, const float* a2, int64_t a_sb, int64_t a_sm, int64_t a_sk,
@@ -333,8 +409,10 @@ xe_status xe_logspace_gemm_shifted(const float* a, const float* a2, int64_t a_sb
   if (a2 && !shift_a)
     return fail(XE_ERR_INVALID_ARGUMENT, "xe_logspace_gemm_shifted: a fused addend requires a log-domain A operand");
   if (batch == 0 || m == 0 || n == 0) return XE_OK;
+  GemmPlan plan = plan_gemm(a, a2, a_sb, a_sm, a_sk, shift_a == nullptr, batch, m, n, k);
+  plan.inline_shift = false;
   return gemm_launch(a, a2, a_sb, a_sm, a_sk, shift_a == nullptr, shift_a, b, b_sb, b_sk, b_sn, shift_b, c, c_sb, c_sm,
-                     c_sn, batch, m, n, k, false, as_stream(stream));
+                     c_sn, batch, m, n, k, false, plan, as_stream(stream));
 }
 
 xe_status xe_softmax(const float* x, float* y, int64_t outer, int64_t axis_len, int64_t inner, int32_t log_output,
@@ -503,10 +581,11 @@ xe_status launch_tucker(const Params& p, cudaStream_t s) {
   const int bn = pick_bn(p.N);
   Params q = p;
   set_tiling(q, bn);
+  const CUtensorMap none{};
   switch (bn) {
-    case 32: return launch_gemm_t<32, kATucker, true, true, true, TJ>(q, s);
-    case 64: return launch_gemm_t<64, kATucker, true, true, true, TJ>(q, s);
-    default: return launch_gemm_t<128, kATucker, true, true, true, TJ>(q, s);
+    case 32: return launch_gemm_t<32, kATucker, kALdg, true, true, TJ>(q, none, none, s);
+    case 64: return launch_gemm_t<64, kATucker, kALdg, true, true, TJ>(q, none, none, s);
+    default: return launch_gemm_t<128, kATucker, kALdg, true, true, TJ>(q, none, none, s);
   }
 }
 

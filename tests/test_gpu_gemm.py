@@ -41,7 +41,11 @@ def _expected(a64, b64, a_lin, b_lin, mode):
 @pytest.mark.parametrize("layout", LAYOUTS, ids=[f"A{a}-B{b}" for a, b in LAYOUTS])
 @pytest.mark.parametrize("linear", [(False, False), (False, True), (True, False)], ids=["log-log", "log-lin", "lin-log"])
 @pytest.mark.parametrize("mode", ["max", "min"])
-def test_gemm_matches_oracle(shape, layout, linear, mode):
+@pytest.mark.parametrize("tma", ["1", "0"], ids=["tma", "ldg"])
+def test_gemm_matches_oracle(shape, layout, linear, mode, tma, monkeypatch):
+    # A rows come from a TMA-filled staging ring when A is k-contiguous; the
+    # global-load path is forced here for the other half of the sweep
+    monkeypatch.setenv("XE_GEMM_NO_TMA", "0" if tma == "1" else "1")
     batch, m, n, k = shape
     gen = torch.Generator().manual_seed(hash((shape, layout, linear, mode)) % 2**31)
     # A is (batch, M, K): layout 'k' -> k contiguous, 'mn' -> m contiguous
