@@ -90,7 +90,11 @@ struct Cfg {
   static constexpr int kRunningBytes = BN * kBM * 4;
   // raw A staging ring (TMA sources only)
   static constexpr int kAStageBytes = ASRC == kATma2 ? 2 * kATileBytes : kATileBytes;
-  static constexpr int kAStages = ASRC == kALdg ? 0 : ((ASRC == kATma2 && BN == 128) ? 2 : 4);
+  static constexpr int kAStages =
+      ASRC == kALdg ? 0 : (ASRC == kATma2 ? (BN == 128 ? 2 : 3) : (BN == 128 ? 3 : 4));
+  // output staging for the coalesced copy-out: [128 rows][32 cols] per buffer
+  static constexpr int kOutBufs = (ASRC == kATma2 && BN == 128) ? 1 : 2;
+  static constexpr int kOutBytes = kBM * 32 * 4;
   static constexpr int kShiftBytes = 2 * 2 * kBM * 4;  // [slot][s1,s2][row]
   // TMEM columns: A stages (hi 32 + lo 32 each), two main chunks, correction
   static constexpr int kTmemA = 0;
@@ -102,7 +106,10 @@ struct Cfg {
   static constexpr int kOffA = kOffB + kStages * kStageBytes;
   static constexpr int kOffRun = kOffA + kAStages * kAStageBytes;
   static constexpr int kOffShift = kOffRun + kRunningBytes;
-  static constexpr int kOffBar = kOffShift + kShiftBytes;
+  static constexpr int kOffColShift = kOffShift + kShiftBytes;  // [2 slots][BN floats]
+  static constexpr int kOffOut = kOffColShift + 2 * BN * 4;       // 1024-aligned below
+  static constexpr int kOffOutAligned = (kOffOut + 1023) / 1024 * 1024;
+  static constexpr int kOffBar = kOffOutAligned + kOutBufs * kOutBytes;
   static constexpr int kSmemBytes = 1024 + kOffBar + kBarrierBytes;
   static_assert(kTmemCorr + BN <= 512, "TMEM");
   static_assert(kSmemBytes <= 232448, "shared memory");
@@ -193,6 +200,14 @@ __device__ __forceinline__ float4 lds_v4(uint32_t addr) {
   asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
   return v;
 }
+
+// log(x) = log2(x) * ln 2 (lg2.approx: absolute error ~2^-22 in log2).
+__device__ __forceinline__ float fast_log(float x) {
+  float y;
+  asm("lg2.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y * 0.6931471805599453f;
+}
+
 
 __device__ __forceinline__ float extreme(float a, float b, bool is_min) {
   float r;
@@ -483,7 +498,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* a_full = shift_empty + 2;           // [4], TMA transactions
   uint64_t* a_empty = a_full + 4;               // [4], A warps
   uint64_t* drain = a_empty + 4;                // [1], teardown
-  uint32_t* tmem_slot = (uint32_t*)(drain + 1);
+  uint64_t* drain_sync = drain + 1;             // [1], barrier among the drain warps
+  uint32_t* tmem_slot = (uint32_t*)(drain_sync + 1);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -506,6 +522,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(corr_empty, kDrainWarps);
     mbar_init(drain, 1);
+    mbar_init(drain_sync, kDrainWarps);
     *abort_flag = 0;
     fence_mbarrier_init();
   }
@@ -545,7 +562,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             float e = is_min ? INFINITY : -INFINITY;
             for (int kb = 0; kb < p.num_kb; ++kb) {
               const uint32_t sidx = (ait + kb) % C::kAStages;
-              if (!mbar_wait(&a_full[sidx], ((ait + kb) / C::kAStages) & 1, kSiteGemmFull, abort_flag)) {
+              if (!mbar_wait(&a_full[sidx], ((ait + kb) / C::kAStages) & 1, kSiteAStaged, abort_flag)) {
                 ok = false;
                 break;
               }
@@ -568,7 +585,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // -------- publish the row shifts for the epilogue
       {
         const uint32_t slot = tl & 1;
-        if (!mbar_wait(&shift_empty[slot], ((tl >> 1) & 1) ^ 1, kSiteGemmAccEmpty, abort_flag)) break;
+        if (!mbar_wait(&shift_empty[slot], ((tl >> 1) & 1) ^ 1, kSiteAShiftSlot, abort_flag)) break;
         shifts[(slot * 2 + 0) * kBM + r] = s1;
         shifts[(slot * 2 + 1) * kBM + r] = s2;
         __syncwarp();
@@ -578,9 +595,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       float cur[32], nxt[32];
       if (ASRC == kALdg) a.load_global(p, 0, cur);
       for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+        XE_SEGMENT_BEGIN(seg_load);
         if (ASRC != kALdg) {
           const uint32_t sidx = ait % C::kAStages;
-          if (!mbar_wait(&a_full[sidx], (ait / C::kAStages) & 1, kSiteGemmFull, abort_flag)) {
+          if (!mbar_wait(&a_full[sidx], (ait / C::kAStages) & 1, kSiteAStaged, abort_flag)) {
             ok = false;
             break;
           }
@@ -592,13 +610,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else if (kb + 1 < p.num_kb) {
           a.load_global(p, (kb + 1) * kBK, nxt);
         }
+        XE_SEGMENT_END(seg_load, 1);
         const uint32_t s = it % kStages;
         const uint32_t ph = (it / kStages) & 1;
-        if (!mbar_wait(&empty[s], ph ^ 1, kSiteGemmEmpty, abort_flag)) {
+        if (!mbar_wait(&empty[s], ph ^ 1, kSiteAStage, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
+        XE_SEGMENT_BEGIN(seg_tr);
         const uint32_t col = tmem + lane_bits + C::kTmemA + 64 * s;
         {
           float hi[16], lo[16];
@@ -612,7 +632,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_st16(col + 16, hi);
           tmem_st16(col + 48, lo);
         }
+        XE_SEGMENT_END(seg_tr, 2);
+        XE_SEGMENT_BEGIN(seg_st);
         tmem_wait_st();
+        XE_SEGMENT_END(seg_st, 3);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&full[s]);
@@ -641,12 +664,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (more) bt.load(p, bb, n0, (kb + 1) * kBK, t, nxt);
         const uint32_t s = it % kStages;
         const uint32_t ph = (it / kStages) & 1;
-        if (!mbar_wait(&empty[s], ph ^ 1, kSiteGemmEmpty, abort_flag)) {
+        if (!mbar_wait(&empty[s], ph ^ 1, kSiteBStage, abort_flag)) {
           ok = false;
           break;
         }
         const uint32_t st = smem_base + C::kOffB + s * C::kStageBytes;
+        XE_SEGMENT_BEGIN(seg_b);
         bt.store(p, st, st + C::kBTile, t, cur);
+        XE_SEGMENT_END(seg_b, 4);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&full[s]);
@@ -667,7 +692,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t it = 0, gc = 0, tl = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++tl) {
-        if (!mbar_wait(corr_empty, (tl & 1) ^ 1, kSiteGemmAccEmpty, abort_flag)) {
+        if (!mbar_wait(corr_empty, (tl & 1) ^ 1, kSiteMmaCorr, abort_flag)) {
           ok = false;
           break;
         }
@@ -677,7 +702,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int kc = kb % kChunkKB;
           if (kc == 0) {
             const uint32_t cb = gc & 1;
-            if (!mbar_wait(&chunk_empty[cb], ((gc >> 1) & 1) ^ 1, kSiteGemmAccEmpty, abort_flag)) {
+            if (!mbar_wait(&chunk_empty[cb], ((gc >> 1) & 1) ^ 1, kSiteMmaChunk, abort_flag)) {
               ok = false;
               break;
             }
@@ -686,7 +711,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           const uint32_t s = it % kStages;
           const uint32_t ph = (it / kStages) & 1;
-          if (!mbar_wait(&full[s], ph, kSiteGemmFull, abort_flag)) {
+          if (!mbar_wait(&full[s], ph, kSiteMmaFull, abort_flag)) {
             ok = false;
             break;
           }
@@ -718,83 +743,112 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;  // TMEM lane quadrant of this warp
     const int r = q * 32 + lane;
     const uint32_t lane_bits = (uint32_t)(q * 32) << 16;
-    uint32_t gc = 0, tl = 0;
+    float* col_shift = (float*)(smem + C::kOffColShift);
+    uint32_t gc = 0, tl = 0, ob = 0, syncs = 0;
     bool ok = true;
+    // barrier among the four drain warps (bounded, like every wait here)
+    auto sync_drain = [&]() -> bool {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(drain_sync);
+      const bool done = mbar_wait(drain_sync, syncs & 1, kSiteDrainShift, abort_flag);
+      ++syncs;
+      if (!done) ok = false;
+      return done;
+    };
     const int chunks = (p.num_kb + kChunkKB - 1) / kChunkKB;
     for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++tl) {
       int bb, mt, nt;
       decode_tile(p, tile, bb, mt, nt);
-      const int m = mt * kBM + r;
+      const int m0 = mt * kBM;
       const int n0 = nt * BN;
+      // -------- chunks: running[col][row] (+)= main chunk; the last one adds corr
       for (int c = 0; c < chunks; ++c, ++gc) {
         const uint32_t cb = gc & 1;
-        if (!mbar_wait(&chunk_full[cb], (gc >> 1) & 1, kSiteGemmAccFull, abort_flag)) {
+        const bool last = c == chunks - 1;
+        if (!mbar_wait(&chunk_full[cb], (gc >> 1) & 1, kSiteDrainChunk, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
+        XE_SEGMENT_BEGIN(seg_dr);
 #pragma unroll 1
         for (int sl = 0; sl < BN / 32; ++sl) {
-          float v[32];
+          float v[32], w[32];
           tmem_ld32(tmem + lane_bits + C::kTmemMain + cb * BN + sl * 32, v);
+          if (last) tmem_ld32(tmem + lane_bits + C::kTmemCorr + sl * 32, w);
           tmem_wait_ld();
           float* run = running + sl * 32 * kBM + r;
-          if (c == 0) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) run[j * kBM] = v[j];
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) run[j * kBM] += v[j];
+          for (int j = 0; j < 32; ++j) {
+            float t = (c == 0) ? v[j] : run[j * kBM] + v[j];
+            // an overflowed main term carries the result; its correction is NaN
+            if (last) t = isinf(t) ? t : t + w[j];
+            run[j * kBM] = t;
           }
         }
+        XE_SEGMENT_END(seg_dr, 5);
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&chunk_empty[cb]);
+        if (lane == 0) {
+          mbar_arrive(&chunk_empty[cb]);
+          if (last) mbar_arrive(corr_empty);  // TMEM is free for the next tile
+        }
       }
       if (!ok) break;
-      // Epilogue: the last chunk commit covered every MMA of this tile.
+      // -------- epilogue from shared memory, overlapping the next tile's MMAs
+      XE_SEGMENT_BEGIN(seg_ep);
       const uint32_t slot = tl & 1;
-      if (!mbar_wait(&shift_full[slot], (tl >> 1) & 1, kSiteGemmAccFull, abort_flag)) break;
+      if (!mbar_wait(&shift_full[slot], (tl >> 1) & 1, kSiteDrainShift, abort_flag)) break;
       const float s1 = shifts[(slot * 2 + 0) * kBM + r];
       const float s2 = shifts[(slot * 2 + 1) * kBM + r];
       __syncwarp();
       if (lane == 0) mbar_arrive(&shift_empty[slot]);
-      const float* sbp = p.shift_b ? p.shift_b + (int64_t)bb * p.N : nullptr;
-      float* crow = p.c + (int64_t)bb * p.c_sb + (int64_t)m * p.c_sm;
+      float* cshift = col_shift + slot * BN;
+      if (r < BN) cshift[r] = (p.shift_b && n0 + r < p.N) ? __ldg(p.shift_b + (int64_t)bb * p.N + n0 + r) : 0.0f;
+      if (!sync_drain()) break;
+      float* cbase = p.c + (int64_t)bb * p.c_sb;
 #pragma unroll 1
       for (int sl = 0; sl < BN / 32; ++sl) {
-        float v[32];
-        tmem_ld32(tmem + lane_bits + C::kTmemCorr + sl * 32, v);
-        tmem_wait_ld();
-        const int nb = n0 + sl * 32;
-        if (m < p.M && nb < p.N) {
-          const float* run = running + sl * 32 * kBM + r;
-          float out[32];
+        const float* run = running + sl * 32 * kBM + r;  // this row's 32 sums of the slice
+        float out[32];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float main = run[j * kBM];
-            // an overflowed main term carries the result; its correction is NaN
-            const float acc = isinf(main) ? main : main + v[j];
-            float o = logf(acc);
-            if (AMODE != kALinear) o += s1;
-            if (AMODE == kATucker) o += s2;
-            if (sbp) o += (nb + j < p.N) ? __ldg(sbp + nb + j) : 0.0f;
-            out[j] = o;
-          }
-          if (p.c_vec && nb + 32 <= p.N) {
+        for (int j = 0; j < 32; ++j) {
+          float o = fast_log(run[j * kBM]);
+          if (AMODE != kALinear) o += s1;
+          if (AMODE == kATucker) o += s2;
+          if (p.shift_b) o += cshift[sl * 32 + j];
+          out[j] = o;
+        }
+        if (C::kOutBufs == 1 && !sync_drain()) break;  // the single buffer's previous copy-out is done
+        // staging buffer as [128 rows][32 cols], 16-byte chunks swizzled by (row & 7)
+        const uint32_t stage = smem_base + C::kOffOutAligned + (ob % C::kOutBufs) * C::kOutBytes;
+        ++ob;
+        const uint32_t srow = stage + r * 128;
 #pragma unroll
-            for (int j = 0; j < 32; j += 4)
-              stg_v4(crow + nb + j, make_float4(out[j], out[j + 1], out[j + 2], out[j + 3]));
+        for (int j = 0; j < 8; ++j)
+          sts_v4(srow + ((j ^ (r & 7)) << 4), make_float4(out[4 * j], out[4 * j + 1], out[4 * j + 2], out[4 * j + 3]));
+        if (!sync_drain()) break;
+        // coalesced copy-out: each warp writes 32 rows, 4 rows (512 B) per instruction
+        const int chunk = lane & 7;
+        const int n = n0 + sl * 32 + 4 * chunk;
+#pragma unroll
+        for (int it = 0; it < 8; ++it) {
+          const int row = q * 32 + 4 * it + (lane >> 3);
+          const int m = m0 + row;
+          if (m >= p.M || n >= p.N) continue;
+          const float4 val = lds_v4(stage + row * 128 + ((chunk ^ (row & 7)) << 4));
+          float* dst = cbase + (int64_t)m * p.c_sm;
+          if (p.c_vec && n + 4 <= p.N) {
+            stg_v4(dst + n, val);
           } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (nb + j < p.N) crow[(int64_t)(nb + j) * p.c_sn] = out[j];
+            dst[(int64_t)n * p.c_sn] = val.x;
+            if (n + 1 < p.N) dst[(int64_t)(n + 1) * p.c_sn] = val.y;
+            if (n + 2 < p.N) dst[(int64_t)(n + 2) * p.c_sn] = val.z;
+            if (n + 3 < p.N) dst[(int64_t)(n + 3) * p.c_sn] = val.w;
           }
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(corr_empty);
+      XE_SEGMENT_END(seg_ep, 6);
     }
   } else if (ASRC != kALdg && lane == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -805,7 +859,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       decode_tile(p, tile, bb, mt, nt);
       for (int kb = 0; kb < p.num_kb; ++kb, ++ait) {
         const uint32_t sidx = ait % C::kAStages;
-        if (!mbar_wait(&a_empty[sidx], ((ait / C::kAStages) & 1) ^ 1, kSiteGemmEmpty, abort_flag)) {
+        if (!mbar_wait(&a_empty[sidx], ((ait / C::kAStages) & 1) ^ 1, kSiteProducer, abort_flag)) {
           ok = false;
           break;
         }

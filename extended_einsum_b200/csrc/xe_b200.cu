@@ -162,7 +162,7 @@ struct GemmPlan {
 int staged_k_capacity(int bn, int asrc) {
   using namespace xe::gemm;
   int stages = 0;
-  if (asrc == kATma) stages = Cfg<128, kATma>::kAStages;
+  if (asrc == kATma) stages = bn == 128 ? Cfg<128, kATma>::kAStages : Cfg<64, kATma>::kAStages;
   if (asrc == kATma2) stages = bn == 128 ? Cfg<128, kATma2>::kAStages : Cfg<64, kATma2>::kAStages;
   return stages * kBK;
 }
@@ -282,6 +282,25 @@ int xe_device_status(int clear) {
   }
   return v;
 }
+
+#ifdef XE_PROFILE
+// Profiling builds only: copies (and optionally clears) the per-site wait-cycle counters.
+int xe_profile_wait_cycles(unsigned long long* out, int n, int clear) {
+  const int count = n < xe::kNumSites ? n : xe::kNumSites;
+  if (cudaDeviceSynchronize() != cudaSuccess) return -1;
+  if (cudaMemcpyFromSymbol(out, xe::g_wait_cycles, count * sizeof(unsigned long long)) != cudaSuccess) return -1;
+  if (n >= 2 * xe::kNumSites &&
+      cudaMemcpyFromSymbol(out + xe::kNumSites, xe::g_segment_cycles, xe::kNumSites * sizeof(unsigned long long)) !=
+          cudaSuccess)
+    return -1;
+  if (clear) {
+    unsigned long long zero[xe::kNumSites] = {};
+    cudaMemcpyToSymbol(xe::g_wait_cycles, zero, sizeof(zero));
+    cudaMemcpyToSymbol(xe::g_segment_cycles, zero, sizeof(zero));
+  }
+  return count;
+}
+#endif
 
 size_t xe_logspace_gemm_workspace_size(int64_t batch, int64_t m, int64_t n, int64_t k, int32_t a_linear,
                                        int32_t b_linear) {

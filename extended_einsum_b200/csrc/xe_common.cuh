@@ -25,10 +25,31 @@ enum WaitSite : int {
   kSiteGemmAccFull = 3,
   kSiteGemmAccEmpty = 4,
   kSiteGemmDrain = 5,
-  kSiteTuckerFull = 6,
-  kSiteTuckerEmpty = 7,
-  kSiteTuckerAcc = 8,
+  // finer sites, distinguished only by the wait-time counters below
+  kSiteAStaged = 6,
+  kSiteAShiftSlot = 7,
+  kSiteAStage = 8,
+  kSiteBStage = 9,
+  kSiteMmaCorr = 10,
+  kSiteMmaChunk = 11,
+  kSiteMmaFull = 12,
+  kSiteDrainChunk = 13,
+  kSiteDrainShift = 14,
+  kSiteProducer = 15,
+  kNumSites = 16,
 };
+
+#ifdef XE_PROFILE
+// Cycles spent in each wait site, summed over threads that waited, and in
+// timed code segments (profiling builds only: compiled with -DXE_PROFILE).
+__device__ unsigned long long g_wait_cycles[kNumSites];
+__device__ unsigned long long g_segment_cycles[kNumSites];
+#define XE_SEGMENT_BEGIN(name) const long long name##_t0 = clock64()
+#define XE_SEGMENT_END(name, idx) atomicAdd(&::xe::g_segment_cycles[idx], (unsigned long long)(clock64() - name##_t0))
+#else
+#define XE_SEGMENT_BEGIN(name)
+#define XE_SEGMENT_END(name, idx)
+#endif
 
 // About two seconds: far above any legitimate wait in these kernels.
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;
@@ -84,8 +105,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int si
   const uint32_t addr = smem_u32(bar);
   if (mbar_try_wait(addr, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
+#ifdef XE_PROFILE
+  const long long c0 = clock64();
+#endif
   for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait(addr, parity)) return true;
+    if (mbar_try_wait(addr, parity)) {
+#ifdef XE_PROFILE
+      atomicAdd(&g_wait_cycles[site & (kNumSites - 1)], (unsigned long long)(clock64() - c0));
+#endif
+      return true;
+    }
     if ((i & 255u) == 0) {
       if (honor_abort && *abort) return false;
       if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
