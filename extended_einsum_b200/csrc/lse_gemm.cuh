@@ -46,7 +46,7 @@ constexpr int kDrainWarps = 4;
 constexpr int kProducerWarp = kDrainWarp0 + kDrainWarps;  // 13
 constexpr int kThreads = (kProducerWarp + 1) * 32;        // 448
 constexpr int kStages = 2;
-constexpr int kChunkKB = 4;  // 128 k per main-accumulator chunk
+constexpr int kChunkKB = 8;  // 256 k per main-accumulator chunk
 constexpr int kATileBytes = kBM * kBK * 4;  // one raw A tile (16 KB)
 
 enum AMode : int { kALog = 0, kALinear = 1, kATucker = 2 };
@@ -54,6 +54,9 @@ enum AMode : int { kALog = 0, kALinear = 1, kATucker = 2 };
 // 16-byte aligned strides), the same plus a second ring for the fused addend,
 // or per-thread global loads (any layout).
 enum ASource : int { kATma = 0, kATma2 = 1, kALdg = 2 };
+// Where the raw B tiles come from: a TMA-filled staging ring (16-byte aligned
+// strides), or global loads with or without 16-byte vectors.
+enum BSource : int { kBTma = 0, kBLdgVec = 1, kBLdg = 2 };
 
 struct Params {
   const float* a;
@@ -82,37 +85,47 @@ __host__ __device__ constexpr int pow2_at_least(int x) {
   return p;
 }
 
-template <int BN, int ASRC>
+template <int BN, int ASRC, int BSRC>
 struct Cfg {
   static_assert(BN == 32 || BN == 64 || BN == 128, "BN");
-  static constexpr int kBTile = BN * kBK * 4;  // bytes, one of hi/lo
+  static constexpr int kSmemLimit = 232448;
+  static constexpr int kBTile = BN * kBK * 4;  // bytes, one of hi/lo (also one raw B tile)
   static constexpr int kStageBytes = 2 * kBTile;
   static constexpr int kRunningBytes = BN * kBM * 4;
-  // raw A staging ring (TMA sources only)
-  static constexpr int kAStageBytes = ASRC == kATma2 ? 2 * kATileBytes : kATileBytes;
-  static constexpr int kAStages =
-      ASRC == kALdg ? 0 : (ASRC == kATma2 ? (BN == 128 ? 2 : 3) : (BN == 128 ? 3 : 4));
-  // output staging for the coalesced copy-out: [128 rows][32 cols] per buffer
-  static constexpr int kOutBufs = (ASRC == kATma2 && BN == 128) ? 1 : 2;
-  static constexpr int kOutBytes = kBM * 32 * 4;
   static constexpr int kShiftBytes = 2 * 2 * kBM * 4;  // [slot][s1,s2][row]
+  static constexpr int kColShiftBytes = 2 * BN * 4;    // [slot][BN]
+  static constexpr int kOutBytes = kBM * 32 * 4;       // one [128 rows][32 cols] output staging buffer
+  static constexpr int kAStageBytes = ASRC == kATma2 ? 2 * kATileBytes : kATileBytes;
+  // everything except the two TMA rings and the output staging
+  static constexpr int kFixed = 1024 + kStages * kStageBytes + kRunningBytes + kShiftBytes + kColShiftBytes + 512;
+  static constexpr int kBRawBytes = BSRC == kBTma ? kBTile : 0;
+  static constexpr int kMinRings = (ASRC == kALdg ? 0 : 2 * kAStageBytes) + 2 * kBRawBytes;
+  static constexpr int kOutBufs = (kFixed + kMinRings + 2 * kOutBytes <= kSmemLimit) ? 2 : 1;
+  static constexpr int kRingBudget = kSmemLimit - kFixed - kOutBufs * kOutBytes - 1024;
+  // up to four stages per ring, A first
+  static constexpr int kAStages =
+      ASRC == kALdg ? 0
+                    : ((kRingBudget - 2 * kBRawBytes) / kAStageBytes >= 4 ? 4 : (kRingBudget - 2 * kBRawBytes) / kAStageBytes);
+  static constexpr int kBRawStages =
+      BSRC != kBTma ? 0 : ((kRingBudget - kAStages * kAStageBytes) / kBRawBytes >= 4 ? 4 : (kRingBudget - kAStages * kAStageBytes) / kBRawBytes);
   // TMEM columns: A stages (hi 32 + lo 32 each), two main chunks, correction
   static constexpr int kTmemA = 0;
   static constexpr int kTmemMain = 64 * kStages;
   static constexpr int kTmemCorr = kTmemMain + 2 * BN;
   static constexpr int kTmemCols = pow2_at_least(kTmemCorr + BN);
-  static constexpr int kBarrierBytes = 256;
   static constexpr int kOffB = 0;
   static constexpr int kOffA = kOffB + kStages * kStageBytes;
-  static constexpr int kOffRun = kOffA + kAStages * kAStageBytes;
+  static constexpr int kOffBRaw = kOffA + kAStages * kAStageBytes;
+  static constexpr int kOffRun = kOffBRaw + kBRawStages * kBRawBytes;
   static constexpr int kOffShift = kOffRun + kRunningBytes;
-  static constexpr int kOffColShift = kOffShift + kShiftBytes;  // [2 slots][BN floats]
-  static constexpr int kOffOut = kOffColShift + 2 * BN * 4;       // 1024-aligned below
-  static constexpr int kOffOutAligned = (kOffOut + 1023) / 1024 * 1024;
+  static constexpr int kOffColShift = kOffShift + kShiftBytes;
+  static constexpr int kOffOutAligned = (kOffColShift + kColShiftBytes + 1023) / 1024 * 1024;
   static constexpr int kOffBar = kOffOutAligned + kOutBufs * kOutBytes;
-  static constexpr int kSmemBytes = 1024 + kOffBar + kBarrierBytes;
+  static constexpr int kSmemBytes = 1024 + kOffBar + 512;
   static_assert(kTmemCorr + BN <= 512, "TMEM");
-  static_assert(kSmemBytes <= 232448, "shared memory");
+  // whether this combination fits (both rings at least double-buffered)
+  static constexpr bool kFits = (ASRC == kALdg || kAStages >= 2) && (BSRC != kBTma || kBRawStages >= 2) &&
+                                kSmemBytes <= kSmemLimit;
 };
 
 // Byte offset of the 16-byte chunk holding elements (row, 4q..4q+3) of a
@@ -386,8 +399,9 @@ __device__ __forceinline__ void load_staged_row(uint32_t stage, int r, bool vali
 // B operand: 128 threads, 16-byte chunks.  MN-major: thread t covers n-quad
 // t % (BN/4) of k-rows t / (BN/4) + (512/BN)*i; K-major: k-quad t % 8 of
 // n-rows t / 8 + 16*i.
-template <int BN, bool B_KMAJ, bool VEC>
+template <int BN, bool B_KMAJ, int BSRC>
 struct BTile {
+  static constexpr bool VEC = BSRC != kBLdg;
   static constexpr int kQ = BN / 16;  // float4 per thread
   static constexpr int kQPR = BN / 4;
   static constexpr int kRPP = 128 / kQPR;
@@ -446,6 +460,38 @@ struct BTile {
     }
   }
 
+  // Raw values from a TMA-staged tile (unswizzled: MN-major [32 k][BN n],
+  // K-major [BN n][32 k]), masked to the operand's extents.
+  __device__ void load_staged(const Params& p, uint32_t stage, int n0, int k0, int t, float4 (&v)[kQ]) const {
+    const float fill = p.shift_b == nullptr ? 0.0f : -INFINITY;
+#pragma unroll
+    for (int i = 0; i < kQ; ++i) {
+      int nl, kl;
+      coords(t, i, nl, kl);
+      const uint32_t off = B_KMAJ ? (uint32_t)(nl * 32 + kl) * 4 : (uint32_t)(kl * BN + nl) * 4;
+      float4 x = lds_v4(stage + off);
+      const int n = n0 + nl, k = k0 + kl;
+      if (B_KMAJ) {
+        if (n >= p.N) x = make_float4(fill, fill, fill, fill);
+        if (k + 4 > p.K) {
+          if (k >= p.K) x.x = fill;
+          if (k + 1 >= p.K) x.y = fill;
+          if (k + 2 >= p.K) x.z = fill;
+          if (k + 3 >= p.K) x.w = fill;
+        }
+      } else {
+        if (k >= p.K) x = make_float4(fill, fill, fill, fill);
+        if (n + 4 > p.N) {
+          if (n >= p.N) x.x = fill;
+          if (n + 1 >= p.N) x.y = fill;
+          if (n + 2 >= p.N) x.z = fill;
+          if (n + 3 >= p.N) x.w = fill;
+        }
+      }
+      v[i] = x;
+    }
+  }
+
   __device__ void store(const Params& p, uint32_t hi, uint32_t lo, int t, const float4 (&v)[kQ]) const {
     const bool lin = p.shift_b == nullptr;
 #pragma unroll
@@ -476,12 +522,13 @@ struct BTile {
 
 // ---------------------------------------------------------------------------
 
-template <int BN, int AMODE, int ASRC, bool B_KMAJ, bool BVEC, int TJ>
+template <int BN, int AMODE, int ASRC, bool B_KMAJ, int BSRC, int TJ>
 __global__ void __launch_bounds__(kThreads, 1)
     lse_gemm_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtensorMap tmap_a,
-                    const __grid_constant__ CUtensorMap tmap_a2) {
-  using C = Cfg<BN, ASRC>;
+                    const __grid_constant__ CUtensorMap tmap_a2, const __grid_constant__ CUtensorMap tmap_b) {
+  using C = Cfg<BN, ASRC, BSRC>;
   using ARowT = ARow<AMODE, TJ>;
+  static_assert(C::kFits, "shared memory configuration");
   static_assert(AMODE != kATucker || ASRC == kALdg, "the Tucker operand is generated from global loads");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -497,7 +544,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* shift_empty = shift_full + 2;       // [2], drain warps
   uint64_t* a_full = shift_empty + 2;           // [4], TMA transactions
   uint64_t* a_empty = a_full + 4;               // [4], A warps
-  uint64_t* drain = a_empty + 4;                // [1], teardown
+  uint64_t* b_full = a_empty + 4;               // [4], TMA transactions
+  uint64_t* b_empty = b_full + 4;               // [4], B warps
+  uint64_t* drain = b_empty + 4;                // [1], teardown
   uint64_t* drain_sync = drain + 1;             // [1], barrier among the drain warps
   uint32_t* tmem_slot = (uint32_t*)(drain_sync + 1);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
@@ -519,6 +568,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < 4; ++s) {
       mbar_init(&a_full[s], 1);
       mbar_init(&a_empty[s], kAWarps);
+      mbar_init(&b_full[s], 1);
+      mbar_init(&b_empty[s], kBWarps);
     }
     mbar_init(corr_empty, kDrainWarps);
     mbar_init(drain, 1);
@@ -648,9 +699,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp < kAWarps + kBWarps) {
     // ------------------------------------------------------------ B tiles
     const int t = threadIdx.x - kAWarps * 32;
-    using BT = BTile<BN, B_KMAJ, BVEC>;
+    using BT = BTile<BN, B_KMAJ, BSRC>;
     BT bt;
-    uint32_t it = 0;
+    uint32_t it = 0, bit = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
       int bb, mt, nt;
@@ -658,10 +709,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int n0 = nt * BN;
       bt.begin_tile(p, bb, n0, t);
       float4 cur[BT::kQ], nxt[BT::kQ];
-      bt.load(p, bb, n0, 0, t, cur);
+      if (BSRC != kBTma) bt.load(p, bb, n0, 0, t, cur);
       for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
         const bool more = kb + 1 < p.num_kb;
-        if (more) bt.load(p, bb, n0, (kb + 1) * kBK, t, nxt);
+        if (BSRC == kBTma) {
+          const uint32_t sidx = bit % C::kBRawStages;
+          if (!mbar_wait(&b_full[sidx], (bit / C::kBRawStages) & 1, kSiteBStage, abort_flag)) {
+            ok = false;
+            break;
+          }
+          bt.load_staged(p, smem_base + C::kOffBRaw + sidx * C::kBRawBytes, n0, kb * kBK, t, cur);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&b_empty[sidx]);
+          ++bit;
+        } else if (more) {
+          bt.load(p, bb, n0, (kb + 1) * kBK, t, nxt);
+        }
         const uint32_t s = it % kStages;
         const uint32_t ph = (it / kStages) & 1;
         if (!mbar_wait(&empty[s], ph ^ 1, kSiteBStage, abort_flag)) {
@@ -675,7 +738,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&full[s]);
-        if (more) {
+        if (BSRC != kBTma && more) {
 #pragma unroll
           for (int i = 0; i < BT::kQ; ++i) cur[i] = nxt[i];
         }
@@ -761,8 +824,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       decode_tile(p, tile, bb, mt, nt);
       const int m0 = mt * kBM;
       const int n0 = nt * BN;
-      // -------- chunks: running[col][row] (+)= main chunk; the last one adds corr
-      for (int c = 0; c < chunks; ++c, ++gc) {
+      // -------- chunks: running[col][row] (+)= main chunk; the last one adds corr.
+      // A tile with a single chunk skips the running sum (epilogue below).
+      for (int c = 0; c < chunks && chunks > 1; ++c, ++gc) {
         const uint32_t cb = gc & 1;
         const bool last = c == chunks - 1;
         if (!mbar_wait(&chunk_full[cb], (gc >> 1) & 1, kSiteDrainChunk, abort_flag)) {
@@ -795,6 +859,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (!ok) break;
+      const bool direct = chunks == 1;
+      uint32_t dcb = 0;
+      if (direct) {
+        dcb = gc & 1;
+        if (!mbar_wait(&chunk_full[dcb], (gc >> 1) & 1, kSiteDrainChunk, abort_flag)) break;
+        tc_fence_after();
+        ++gc;
+      }
       // -------- epilogue from shared memory, overlapping the next tile's MMAs
       XE_SEGMENT_BEGIN(seg_ep);
       const uint32_t slot = tl & 1;
@@ -811,9 +883,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int sl = 0; sl < BN / 32; ++sl) {
         const float* run = running + sl * 32 * kBM + r;  // this row's 32 sums of the slice
         float out[32];
+        if (direct) {
+          // single chunk: the sums come straight from TMEM (main + corr)
+          float v[32], w[32];
+          tmem_ld32(tmem + lane_bits + C::kTmemMain + dcb * BN + sl * 32, v);
+          tmem_ld32(tmem + lane_bits + C::kTmemCorr + sl * 32, w);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) out[j] = isinf(v[j]) ? v[j] : v[j] + w[j];
+          if (sl == BN / 32 - 1) {  // every TMEM column of this tile has been read
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+              mbar_arrive(&chunk_empty[dcb]);
+              mbar_arrive(corr_empty);
+            }
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) out[j] = run[j * kBM];
+        }
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
-          float o = fast_log(run[j * kBM]);
+          float o = fast_log(out[j]);
           if (AMODE != kALinear) o += s1;
           if (AMODE == kATucker) o += s2;
           if (p.shift_b) o += cshift[sl * 32 + j];
@@ -850,23 +942,40 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       XE_SEGMENT_END(seg_ep, 6);
     }
-  } else if (ASRC != kALdg && lane == 0) {
+  } else if ((ASRC != kALdg || BSRC == kBTma) && lane == 0) {
     // ------------------------------------------------------------ TMA producer
-    uint32_t ait = 0;
+    uint32_t ait = 0, bit = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
       int bb, mt, nt;
       decode_tile(p, tile, bb, mt, nt);
-      for (int kb = 0; kb < p.num_kb; ++kb, ++ait) {
-        const uint32_t sidx = ait % C::kAStages;
-        if (!mbar_wait(&a_empty[sidx], ((ait / C::kAStages) & 1) ^ 1, kSiteProducer, abort_flag)) {
-          ok = false;
-          break;
+      for (int kb = 0; kb < p.num_kb; ++kb) {
+        if (ASRC != kALdg) {
+          const uint32_t sidx = ait % C::kAStages;
+          if (!mbar_wait(&a_empty[sidx], ((ait / C::kAStages) & 1) ^ 1, kSiteProducer, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t dst = smem_base + C::kOffA + sidx * C::kAStageBytes;
+          mbar_expect_tx(&a_full[sidx], C::kAStageBytes);
+          tma_load_3d(dst, &tmap_a, kb * kBK, mt * kBM, bb, &a_full[sidx]);
+          if (ASRC == kATma2) tma_load_3d(dst + kATileBytes, &tmap_a2, kb * kBK, mt * kBM, bb, &a_full[sidx]);
+          ++ait;
         }
-        const uint32_t dst = smem_base + C::kOffA + sidx * C::kAStageBytes;
-        mbar_expect_tx(&a_full[sidx], C::kAStageBytes);
-        tma_load_3d(dst, &tmap_a, kb * kBK, mt * kBM, bb, &a_full[sidx]);
-        if (ASRC == kATma2) tma_load_3d(dst + kATileBytes, &tmap_a2, kb * kBK, mt * kBM, bb, &a_full[sidx]);
+        if (BSRC == kBTma) {
+          const uint32_t sidx = bit % C::kBRawStages;
+          if (!mbar_wait(&b_empty[sidx], ((bit / C::kBRawStages) & 1) ^ 1, kSiteProducer, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t dst = smem_base + C::kOffBRaw + sidx * C::kBRawBytes;
+          mbar_expect_tx(&b_full[sidx], C::kBRawBytes);
+          if (B_KMAJ)
+            tma_load_3d(dst, &tmap_b, kb * kBK, nt * BN, bb, &b_full[sidx]);
+          else
+            tma_load_3d(dst, &tmap_b, nt * BN, kb * kBK, bb, &b_full[sidx]);
+          ++bit;
+        }
       }
     }
   }

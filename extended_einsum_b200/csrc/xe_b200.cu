@@ -110,23 +110,68 @@ bool encode_a_map(CUtensorMap* map, const float* base, int64_t batch, int64_t ro
   return r == CUDA_SUCCESS;
 }
 
-template <int BN, int AMODE, int ASRC, bool BK, bool BVEC, int TJ>
-xe_status launch_gemm_t(const Params& p, const CUtensorMap& ma, const CUtensorMap& ma2, cudaStream_t stream) {
-  using C = xe::gemm::Cfg<BN, ASRC>;
-  auto kernel = xe::gemm::lse_gemm_kernel<BN, AMODE, ASRC, BK, BVEC, TJ>;
-  static std::atomic<uint32_t> attribute_set{0};
-  cudaError_t e = prepare_kernel(kernel, C::kSmemBytes, attribute_set);
-  if (e != cudaSuccess) return fail(XE_ERR_CUDA, "xe_logspace_gemm: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-  const int grid = (int)std::min<int64_t>(p.num_tiles, current_device_sms());
-  kernel<<<grid, xe::gemm::kThreads, C::kSmemBytes, stream>>>(p, ma, ma2);
-  return check_launch("xe_logspace_gemm");
+// Tensor map of the raw B operand (batch, k, n): MN-major (n contiguous) boxes
+// of BN n x 32 k, K-major (k contiguous) boxes of 32 k x BN n; unswizzled.
+bool encode_b_map(CUtensorMap* map, const float* base, int64_t batch, int64_t k, int64_t n, int64_t s_k, int64_t s_n,
+                  int64_t s_batch, bool kmajor, int bn) {
+  PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+  if (!encode || !aligned16(base)) return false;
+  const int64_t s_outer = kmajor ? s_n : s_k;  // stride of the non-contiguous axis
+  const int64_t rows = kmajor ? n : k;
+  const int64_t sb = batch > 1 ? s_batch : rows * s_outer;
+  if (s_outer <= 0 || sb <= 0 || (s_outer * 4) % 16 != 0 || (sb * 4) % 16 != 0) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)(kmajor ? k : n), (cuuint64_t)rows, (cuuint64_t)batch};
+  cuuint64_t strides[2] = {(cuuint64_t)(s_outer * 4), (cuuint64_t)(sb * 4)};
+  cuuint32_t box[3] = {(cuuint32_t)(kmajor ? 32 : bn), (cuuint32_t)(kmajor ? bn : 32), 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int BN, int AMODE, int ASRC, bool BK, int BSRC, int TJ>
+xe_status launch_gemm_t(const Params& p, const CUtensorMap& ma, const CUtensorMap& ma2, const CUtensorMap& mb,
+                        cudaStream_t stream) {
+  using C = xe::gemm::Cfg<BN, ASRC, BSRC>;
+  if constexpr (!C::kFits) {
+    return fail(XE_ERR_NOT_SUPPORTED, "xe_logspace_gemm: staging configuration does not fit in shared memory");
+  } else {
+    auto kernel = xe::gemm::lse_gemm_kernel<BN, AMODE, ASRC, BK, BSRC, TJ>;
+    static std::atomic<uint32_t> attribute_set{0};
+    cudaError_t e = prepare_kernel(kernel, C::kSmemBytes, attribute_set);
+    if (e != cudaSuccess) return fail(XE_ERR_CUDA, "xe_logspace_gemm: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    const int grid = (int)std::min<int64_t>(p.num_tiles, current_device_sms());
+    kernel<<<grid, xe::gemm::kThreads, C::kSmemBytes, stream>>>(p, ma, ma2, mb);
+    return check_launch("xe_logspace_gemm");
+  }
+}
+
+template <int BN, int ASRC>
+bool b_ring_fits() {
+  using namespace xe::gemm;
+  return Cfg<BN, ASRC, kBTma>::kFits;
+}
+
+bool b_ring_fits(int bn, int asrc) {
+  using namespace xe::gemm;
+  if (bn == 128) return asrc == kATma ? b_ring_fits<128, kATma>() : asrc == kATma2 ? b_ring_fits<128, kATma2>() : b_ring_fits<128, kALdg>();
+  if (bn == 64) return asrc == kATma ? b_ring_fits<64, kATma>() : asrc == kATma2 ? b_ring_fits<64, kATma2>() : b_ring_fits<64, kALdg>();
+  return asrc == kATma ? b_ring_fits<32, kATma>() : asrc == kATma2 ? b_ring_fits<32, kATma2>() : b_ring_fits<32, kALdg>();
 }
 
 template <int BN, int AMODE, int ASRC>
-xe_status launch_gemm_b(const Params& p, const CUtensorMap& ma, const CUtensorMap& ma2, bool bk, bool bvec,
-                        cudaStream_t s) {
-  if (bk) return bvec ? launch_gemm_t<BN, AMODE, ASRC, true, true, 0>(p, ma, ma2, s) : launch_gemm_t<BN, AMODE, ASRC, true, false, 0>(p, ma, ma2, s);
-  return bvec ? launch_gemm_t<BN, AMODE, ASRC, false, true, 0>(p, ma, ma2, s) : launch_gemm_t<BN, AMODE, ASRC, false, false, 0>(p, ma, ma2, s);
+xe_status launch_gemm_b(const Params& p, const CUtensorMap& ma, const CUtensorMap& ma2, const CUtensorMap& mb, bool bk,
+                        int bsrc, cudaStream_t s) {
+  using namespace xe::gemm;
+  if (bk) {
+    if (bsrc == kBTma) return launch_gemm_t<BN, AMODE, ASRC, true, kBTma, 0>(p, ma, ma2, mb, s);
+    if (bsrc == kBLdgVec) return launch_gemm_t<BN, AMODE, ASRC, true, kBLdgVec, 0>(p, ma, ma2, mb, s);
+    return launch_gemm_t<BN, AMODE, ASRC, true, kBLdg, 0>(p, ma, ma2, mb, s);
+  }
+  if (bsrc == kBTma) return launch_gemm_t<BN, AMODE, ASRC, false, kBTma, 0>(p, ma, ma2, mb, s);
+  if (bsrc == kBLdgVec) return launch_gemm_t<BN, AMODE, ASRC, false, kBLdgVec, 0>(p, ma, ma2, mb, s);
+  return launch_gemm_t<BN, AMODE, ASRC, false, kBLdg, 0>(p, ma, ma2, mb, s);
 }
 
 int env_int(const char* name, int dflt) {
@@ -154,46 +199,64 @@ void set_tiling(Params& q, int bn) {
 struct GemmPlan {
   int bn = 128;
   int asrc = xe::gemm::kALdg;
+  int bsrc = xe::gemm::kBLdg;
   bool inline_shift = false;
   CUtensorMap ma{};
   CUtensorMap ma2{};
+  CUtensorMap mb{};
 };
 
-int staged_k_capacity(int bn, int asrc) {
+template <int BN, int ASRC>
+int a_stages(int bsrc) {
+  using namespace xe::gemm;
+  return (bsrc == kBTma && Cfg<BN, ASRC, kBTma>::kFits) ? Cfg<BN, ASRC, kBTma>::kAStages : Cfg<BN, ASRC, kBLdg>::kAStages;
+}
+
+int staged_k_capacity(int bn, int asrc, int bsrc) {
   using namespace xe::gemm;
   int stages = 0;
-  if (asrc == kATma) stages = bn == 128 ? Cfg<128, kATma>::kAStages : Cfg<64, kATma>::kAStages;
-  if (asrc == kATma2) stages = bn == 128 ? Cfg<128, kATma2>::kAStages : Cfg<64, kATma2>::kAStages;
+  if (asrc == kATma) stages = bn == 128 ? a_stages<128, kATma>(bsrc) : bn == 64 ? a_stages<64, kATma>(bsrc) : a_stages<32, kATma>(bsrc);
+  if (asrc == kATma2) stages = bn == 128 ? a_stages<128, kATma2>(bsrc) : bn == 64 ? a_stages<64, kATma2>(bsrc) : a_stages<32, kATma2>(bsrc);
   return stages * kBK;
 }
 
 GemmPlan plan_gemm(const float* a, const float* a2, int64_t a_sb, int64_t a_sm, int64_t a_sk, bool a_linear,
-                   int64_t batch, int64_t m, int64_t n, int64_t k) {
+                   const float* b, int64_t b_sb, int64_t b_sk, int64_t b_sn, int64_t batch, int64_t m, int64_t n,
+                   int64_t k) {
   using namespace xe::gemm;
   GemmPlan g;
   g.bn = pick_bn(n);
-  const bool tma_ok = env_int("XE_GEMM_NO_TMA", 0) == 0 && a_sk == 1 && (a_sm != 1 || m == 1) &&
-                      encode_a_map(&g.ma, a, batch, m, k, a_sm, a_sb) &&
-                      (a2 == nullptr || encode_a_map(&g.ma2, a2, batch, m, k, a_sm, a_sb));
-  if (tma_ok) g.asrc = a2 ? kATma2 : kATma;
-  const int inline_k = g.asrc == kALdg ? 128 : staged_k_capacity(g.bn, g.asrc);
+  const bool no_tma = env_int("XE_GEMM_NO_TMA", 0) != 0;
+  const bool a_tma = !no_tma && a_sk == 1 && (a_sm != 1 || m == 1) && encode_a_map(&g.ma, a, batch, m, k, a_sm, a_sb) &&
+                     (a2 == nullptr || encode_a_map(&g.ma2, a2, batch, m, k, a_sm, a_sb));
+  if (a_tma) g.asrc = a2 ? kATma2 : kATma;
+  // B staging layout: K-major unless the N axis is the unit-stride one
+  const bool bk = !(b_sn == 1) && b_sk == 1;
+  const bool b_vec = aligned16(b) && b_sb % 4 == 0 &&
+                     (bk ? (b_sk == 1 && k % 4 == 0 && b_sn % 4 == 0) : (b_sn == 1 && n % 4 == 0 && b_sk % 4 == 0));
+  if (!no_tma && b_ring_fits(g.bn, g.asrc) && (bk ? b_sk == 1 : b_sn == 1) &&
+      encode_b_map(&g.mb, b, batch, k, n, b_sk, b_sn, b_sb, bk, g.bn))
+    g.bsrc = kBTma;
+  else
+    g.bsrc = b_vec ? kBLdgVec : kBLdg;
+  const int inline_k = g.asrc == kALdg ? 128 : staged_k_capacity(g.bn, g.asrc, g.bsrc);
   g.inline_shift = !a_linear && k <= inline_k;
   return g;
 }
 
-xe_status launch_gemm(const Params& p, const GemmPlan& g, bool a_linear, bool bk, bool bvec, cudaStream_t s) {
+xe_status launch_gemm(const Params& p, const GemmPlan& g, bool a_linear, bool bk, cudaStream_t s) {
   using namespace xe::gemm;
   Params q = p;
   set_tiling(q, g.bn);
-#define XE_LAUNCH_BN(BN)                                                                                        \
-  do {                                                                                                          \
-    if (a_linear) {                                                                                             \
-      if (g.asrc == kATma) return launch_gemm_b<BN, kALinear, kATma>(q, g.ma, g.ma2, bk, bvec, s);              \
-      return launch_gemm_b<BN, kALinear, kALdg>(q, g.ma, g.ma2, bk, bvec, s);                                   \
-    }                                                                                                           \
-    if (g.asrc == kATma) return launch_gemm_b<BN, kALog, kATma>(q, g.ma, g.ma2, bk, bvec, s);                   \
-    if (g.asrc == kATma2) return launch_gemm_b<BN, kALog, kATma2>(q, g.ma, g.ma2, bk, bvec, s);                 \
-    return launch_gemm_b<BN, kALog, kALdg>(q, g.ma, g.ma2, bk, bvec, s);                                        \
+#define XE_LAUNCH_BN(BN)                                                                                           \
+  do {                                                                                                             \
+    if (a_linear) {                                                                                                \
+      if (g.asrc == kATma) return launch_gemm_b<BN, kALinear, kATma>(q, g.ma, g.ma2, g.mb, bk, g.bsrc, s);         \
+      return launch_gemm_b<BN, kALinear, kALdg>(q, g.ma, g.ma2, g.mb, bk, g.bsrc, s);                              \
+    }                                                                                                              \
+    if (g.asrc == kATma) return launch_gemm_b<BN, kALog, kATma>(q, g.ma, g.ma2, g.mb, bk, g.bsrc, s);              \
+    if (g.asrc == kATma2) return launch_gemm_b<BN, kALog, kATma2>(q, g.ma, g.ma2, g.mb, bk, g.bsrc, s);            \
+    return launch_gemm_b<BN, kALog, kALdg>(q, g.ma, g.ma2, g.mb, bk, g.bsrc, s);                                   \
   } while (0)
   switch (g.bn) {
     case 32: XE_LAUNCH_BN(32);
@@ -353,13 +416,8 @@ xe_status gemm_launch(const float* a, const float* a2, int64_t a_sb, int64_t a_s
   p.a_vec = (a_sk == 1 && k % 4 == 0 && a_sm % 4 == 0 && a_sb % 4 == 0 && aligned16(a) &&
              (a2 == nullptr || aligned16(a2))) ? 1 : 0;
   p.shift_min = shift_min ? 1 : 0;
-  // B staging layout: K-major unless the N axis is the unit-stride one.
-  // 16-byte loads need the unit-stride axis, every other stride and the base
-  // pointer to be multiples of four elements.
   const bool bk = !(b_sn == 1) && b_sk == 1;
-  const bool b_vec = aligned16(b) && b_sb % 4 == 0 &&
-                     (bk ? (b_sk == 1 && k % 4 == 0 && b_sn % 4 == 0) : (b_sn == 1 && n % 4 == 0 && b_sk % 4 == 0));
-  return launch_gemm(p, g, a_linear, bk, b_vec, s);
+  return launch_gemm(p, g, a_linear, bk, s);
 }
 
 xe_status gemm_check(const char* who, const float* a, const float* b, const float* c, int64_t batch, int64_t m,
@@ -400,7 +458,7 @@ xe_status xe_logspace_gemm(const float* a, const float* a2, int64_t a_sb, int64_
   float* ws = static_cast<float*>(workspace);
   float* shift_a = nullptr;
   float* shift_b = nullptr;
-  const GemmPlan plan = plan_gemm(a, a2, a_sb, a_sm, a_sk, a_linear != 0, batch, m, n, k);
+  const GemmPlan plan = plan_gemm(a, a2, a_sb, a_sm, a_sk, a_linear != 0, b, b_sb, b_sk, b_sn, batch, m, n, k);
   if (!a_linear) {
     // small K: the kernel computes the row shifts itself (shift_a stays null)
     if (!plan.inline_shift) {
@@ -428,7 +486,7 @@ xe_status xe_logspace_gemm_shifted(const float* a, const float* a2, int64_t a_sb
   if (a2 && !shift_a)
     return fail(XE_ERR_INVALID_ARGUMENT, "xe_logspace_gemm_shifted: a fused addend requires a log-domain A operand");
   if (batch == 0 || m == 0 || n == 0) return XE_OK;
-  GemmPlan plan = plan_gemm(a, a2, a_sb, a_sm, a_sk, shift_a == nullptr, batch, m, n, k);
+  GemmPlan plan = plan_gemm(a, a2, a_sb, a_sm, a_sk, shift_a == nullptr, b, b_sb, b_sk, b_sn, batch, m, n, k);
   plan.inline_shift = false;
   return gemm_launch(a, a2, a_sb, a_sm, a_sk, shift_a == nullptr, shift_a, b, b_sb, b_sk, b_sn, shift_b, c, c_sb, c_sm,
                      c_sn, batch, m, n, k, false, plan, as_stream(stream));
@@ -601,11 +659,18 @@ xe_status launch_tucker(const Params& p, cudaStream_t s) {
   Params q = p;
   set_tiling(q, bn);
   const CUtensorMap none{};
+  CUtensorMap mb{};
+  const bool b_tma = env_int("XE_GEMM_NO_TMA", 0) == 0 &&
+                     encode_b_map(&mb, p.b, p.batch, p.K, p.N, p.b_sk, p.b_sn, p.b_sb, true, bn);
+#define XE_TUCKER_BN(BN)                                                                   \
+  return b_tma ? launch_gemm_t<BN, kATucker, kALdg, true, kBTma, TJ>(q, none, none, mb, s) \
+               : launch_gemm_t<BN, kATucker, kALdg, true, kBLdgVec, TJ>(q, none, none, mb, s)
   switch (bn) {
-    case 32: return launch_gemm_t<32, kATucker, kALdg, true, true, TJ>(q, none, none, s);
-    case 64: return launch_gemm_t<64, kATucker, kALdg, true, true, TJ>(q, none, none, s);
-    default: return launch_gemm_t<128, kATucker, kALdg, true, true, TJ>(q, none, none, s);
+    case 32: XE_TUCKER_BN(32);
+    case 64: XE_TUCKER_BN(64);
+    default: XE_TUCKER_BN(128);
   }
+#undef XE_TUCKER_BN
 }
 
 static xe_status xe_tucker_impl(const float* l, const float* r, const float* w, float* y, int64_t batch, int64_t folds,
