@@ -44,6 +44,16 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
             _c_i32, _c_ptr, _c_size, _c_ptr,  # shift_mode, workspace, bytes, stream
         ],
     ),
+    "xe_logspace_gemm_noalloc": (
+        _c_i32,
+        [
+            _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64, _c_i32,  # a, a2, strides, a_linear
+            _c_ptr, _c_i64, _c_i64, _c_i64, _c_i32,  # b, strides, b_linear
+            _c_ptr, _c_i64, _c_i64, _c_i64,  # c, strides
+            _c_i64, _c_i64, _c_i64, _c_i64,  # batch, m, n, k
+            _c_i32, _c_ptr,  # shift_mode, stream
+        ],
+    ),
     "xe_logspace_gemm_shifted": (
         _c_i32,
         [

@@ -10,6 +10,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <string>
 
 #include "../../include/xe_b200.h"
@@ -475,6 +476,59 @@ xe_status xe_logspace_gemm(const float* a, const float* a2, int64_t a_sb, int64_
   }
   return gemm_launch(a, a2, a_sb, a_sm, a_sk, a_linear != 0, shift_a, b, b_sb, b_sk, b_sn, shift_b, c, c_sb, c_sm,
                      c_sn, batch, m, n, k, !maxmode, plan, s);
+}
+
+// ------------------------------------------------------------------------
+// Allocation-free variant: the shift vectors live in this static array.
+static __device__ __align__(256) float g_noalloc_scratch[XE_NOALLOC_SCRATCH_BYTES / sizeof(float)];
+
+}  // extern "C"
+
+namespace {
+
+std::mutex g_noalloc_mutex;
+void* g_noalloc_scratch_ptr[64] = {};
+
+// Device address of g_noalloc_scratch on the current device, resolved once per
+// device.  In host code the array's name is only a stand-in for the symbol.
+xe_status noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(XE_ERR_CUDA, "xe_logspace_gemm_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return fail(XE_ERR_NOT_SUPPORTED, "xe_logspace_gemm_noalloc: device index %d above 63", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_scratch_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess || ptr == nullptr)
+      return fail(XE_ERR_CUDA, "xe_logspace_gemm_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    g_noalloc_scratch_ptr[dev] = ptr;
+  }
+  *out = g_noalloc_scratch_ptr[dev];
+  return XE_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+xe_status xe_logspace_gemm_noalloc(const float* a, const float* a2, int64_t a_sb, int64_t a_sm, int64_t a_sk,
+                                   int32_t a_linear, const float* b, int64_t b_sb, int64_t b_sk, int64_t b_sn,
+                                   int32_t b_linear, float* c, int64_t c_sb, int64_t c_sm, int64_t c_sn, int64_t batch,
+                                   int64_t m, int64_t n, int64_t k, int32_t shift_mode, void* stream) {
+  if (batch < 0 || m < 0 || n < 0 || k < 0)
+    return fail(XE_ERR_INVALID_ARGUMENT, "xe_logspace_gemm_noalloc: negative extent");
+  const size_t need = xe_logspace_gemm_workspace_size(batch, m, n, k, a_linear, b_linear);
+  if (need > XE_NOALLOC_SCRATCH_BYTES)
+    return fail(XE_ERR_INVALID_ARGUMENT,
+                "xe_logspace_gemm_noalloc: the shift vectors need %zu bytes, above the %u-byte static scratch "
+                "(batch*(m+n) too large); use xe_logspace_gemm with a workspace",
+                need, (unsigned)XE_NOALLOC_SCRATCH_BYTES);
+  void* scratch = nullptr;
+  xe_status st = noalloc_scratch(&scratch);
+  if (st != XE_OK) return st;
+  return xe_logspace_gemm(a, a2, a_sb, a_sm, a_sk, a_linear, b, b_sb, b_sk, b_sn, b_linear, c, c_sb, c_sm, c_sn, batch,
+                          m, n, k, shift_mode, scratch, XE_NOALLOC_SCRATCH_BYTES, stream);
 }
 
 xe_status xe_logspace_gemm_shifted(const float* a, const float* a2, int64_t a_sb, int64_t a_sm, int64_t a_sk,

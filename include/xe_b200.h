@@ -86,6 +86,33 @@ xe_status xe_logspace_gemm(const float* a, const float* a2, int64_t a_sb, int64_
                            int64_t batch, int64_t m, int64_t n, int64_t k, int32_t shift_mode,
                            void* workspace, size_t workspace_bytes, void* stream);
 
+/* xe_logspace_gemm without a caller-provided workspace, for callers that
+ * cannot allocate device memory: code running where cudaMalloc is not
+ * permitted or not wanted (inside a stream-ordered region that must not
+ * synchronise, a host without its own allocator, an embedding runtime that
+ * owns all device memory), which still pass their own A, B and C.
+ * No counterpart in the reference (which has no allocation-free variant).
+ *
+ * The shift vectors live in a static device array of this library,
+ * XE_NOALLOC_SCRATCH_BYTES (4 MiB) per GPU, held by every GPU that loads the
+ * library until the process exits.  A call needs
+ * xe_logspace_gemm_workspace_size(batch, m, n, k, a_linear, b_linear) bytes of
+ * it (about 4*batch*(m+n) when both operands are log-domain); larger problems
+ * return XE_ERR_INVALID_ARGUMENT.
+ * The first call on a device resolves that array's device address (with the
+ * device current), so make the first call before any stream capture.  Calls
+ * share the array: calls that overlap on the GPU (other streams, other host
+ * threads) race on it.  Nothing in it needs clearing; every call overwrites
+ * what it reads.  Allocates nothing (no cudaMalloc, cudaFree or allocating
+ * library call). */
+#define XE_NOALLOC_SCRATCH_BYTES (4u << 20)
+xe_status xe_logspace_gemm_noalloc(const float* a, const float* a2, int64_t a_sb, int64_t a_sm, int64_t a_sk,
+                                   int32_t a_linear,
+                                   const float* b, int64_t b_sb, int64_t b_sk, int64_t b_sn, int32_t b_linear,
+                                   float* c, int64_t c_sb, int64_t c_sm, int64_t c_sn,
+                                   int64_t batch, int64_t m, int64_t n, int64_t k, int32_t shift_mode,
+                                   void* stream);
+
 /* The contraction kernel of xe_logspace_gemm alone, with caller-provided
  * shift vectors: `shift_a` (batch*m floats) for a log-domain A, NULL for a
  * linear A; `shift_b` (batch*n floats) likewise.  xe_logspace_gemm is
