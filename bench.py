@@ -9,7 +9,8 @@ N(0, 8^2) from seed 1, logspace_max mode — "log-space einsum TFLOP/s" over
 algorithmic FLOPs (2*b*i*j*k per step).  A step is one pass of the hot path
 over the whole batch: the shift pre-pass and the fused contraction kernel.
 The line also carries the folded-circuit throughput (samples/s) of the 32x32
-quad-tree circuit, batch 8192 per GPU, as `secondary`.
+quad-tree circuit, batch 8192 per GPU (--circuit-batch), as `secondary`, and
+the same contraction materialized in the scaled_sum mode as `scaled_sum`.
 
 Multi-GPU (torchrun, one process per GPU, NCCL): the batch is sharded by
 construction — every rank processes its own batch of the same size (weak
@@ -178,6 +179,16 @@ class LogspaceBmm:
         result = xb.log(xb.einsum("bik,bkj->bij", xb.exp(xb.array(a)), xb.exp(xb.array(b)))).materialize("logspace_max")
         self.out_host.copy_(result.backend_array, non_blocking=True)
 
+    def scaled_step(self) -> None:
+        """The same expression lowered in the scaled_sum mode, inputs resident on the device."""
+        import extended_einsum_b200 as xb
+
+        if not hasattr(self, "_scaled_program"):
+            expr = xb.log(xb.einsum("bik,bkj->bij", xb.exp(xb.array(self.a)), xb.exp(xb.array(self.b))))
+            program, _ = xb.extract_program(expr, "scaled_sum")
+            self._scaled_program = xb.lower(program)
+        xb.run_program(self._scaled_program, [self.a, self.b])
+
     @property
     def e2e_bytes(self) -> tuple[int, int]:
         return self.a_host.numel() * 4 + self.b_host.numel() * 4, self.out_host.numel() * 4
@@ -294,8 +305,12 @@ def run_ours(args, rank: int, world: int, device: torch.device, dist_on: bool) -
     e2e_value = world * work.flops_per_step / (e2e_ms * 1e-3) / 1e12
     h2d, d2h = work.e2e_bytes
 
+    # the same contraction in the scaled_sum mode (device-resident inputs, lowered program)
+    scaled_ms = time_region(lambda record: work.scaled_step(), max(3, args.steps // 2), 3, dist_on) / max(3, args.steps // 2)
+    scaled_value = world * work.flops_per_step / (scaled_ms * 1e-3) / 1e12
+
     # secondary: the folded circuit, batch-sharded
-    circ = Circuit(device, rank)
+    circ = Circuit(device, rank, args.circuit_batch)
 
     def circuit_step(record: bool) -> None:
         ll = circ.step()
@@ -325,21 +340,21 @@ def run_ours(args, rank: int, world: int, device: torch.device, dist_on: bool) -
         "clocks": sampler.report(),
         "secondary": {
             "metric": "circuit samples/s", "value": round(c_value, 1), "unit": "samples/s",
-            "workload": "folded 32x32 quad-tree CP circuit, K=64, 256 states, batch 8192 per GPU, uint8 pixels seed 3",
+            "workload": f"folded 32x32 quad-tree CP circuit, K=64, 256 states, batch {args.circuit_batch} per GPU, uint8 pixels seed 3",
             "ms_per_step": round(c_ms, 4),
             "hbm_frac": round(bytes_sample * c_value / world / 1e9 / peaks["hbm_gbs"], 4),
             "hbm_gbs_algorithmic": round(bytes_sample * c_value / world / 1e9, 1),
             "tflops_algorithmic": round(flops_sample * c_value / world / 1e12, 2),
-            "e2e_samples_per_s": round(world * circ_batch(world) / (c_e2e_ms * 1e-3), 1),
+            "e2e_samples_per_s": round(world * args.circuit_batch / (c_e2e_ms * 1e-3), 1),
+        },
+        "scaled_sum": {
+            "metric": "log-space einsum TFLOP/s, scaled_sum mode", "value": round(scaled_value, 3), "unit": "TFLOP/s",
+            "ms_per_step": round(scaled_ms, 4), "workload": "the headline contraction materialized in scaled_sum",
         },
     }
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = LogspaceBmm.cpu_sample()
     return line
-
-
-def circ_batch(world: int) -> int:
-    return 8192
 
 
 def run_reference(args, rank: int) -> dict | None:
@@ -378,6 +393,7 @@ def main() -> None:
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--circuit-batch", type=int, default=8192, help="circuit samples per GPU (default 8192)")
     args = parser.parse_args()
     if args.warmup < 3:
         parser.error("--warmup must be at least 3")

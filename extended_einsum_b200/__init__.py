@@ -10,7 +10,8 @@ Public surface:
   ``run_program`` / ``B200Compiler`` to execute it;
 * ``enable()`` routes the reference package's own
   ``TensorExpression.materialize`` (interface/tensor_expression.py:104-117)
-  through ``lower`` for log-space modes when every input is a CUDA tensor;
+  through ``lower`` for the log-space and scaled modes when every input is
+  a CUDA tensor;
 * ``ops`` — the torch-tensor entry points of libxe_b200.so;
 * ``circuit`` — the folded quad-tree circuit driver.
 """
@@ -65,13 +66,14 @@ __all__ = [
 ]
 
 _ORIGINAL_MATERIALIZE = None
+STABLE_MODES = ("logspace_max", "logspace_min", "scaled_sum", "scaled_max", "scaled_min")
 
 
 def enable() -> None:
     """Routes the reference's TensorExpression.materialize through the B200 lowering.
 
-    Applies to log-space stability modes when every input of the expression
-    is a CUDA float32 tensor; every other call goes to the reference's own
+    Applies to the log-space and scaled stability modes when every input of
+    the expression is a CUDA float32 tensor; every other call goes to the reference's own
     implementation unchanged.  Requires the reference package (extended_einsum).
     """
     global _ORIGINAL_MATERIALIZE
@@ -83,7 +85,7 @@ def enable() -> None:
     original = reference.TensorExpression.materialize
 
     def materialize_on_b200(self, stability_mode="unstable"):
-        if stability_mode in ("logspace_max", "logspace_min"):
+        if stability_mode in STABLE_MODES:
             program, arguments = reference.extract_program(self, stability_mode)
             tensors = [a.backend_array for a in arguments]
             if all(isinstance(t, torch.Tensor) and t.is_cuda and t.dtype == torch.float32 for t in tensors):
@@ -108,3 +110,4 @@ def disable() -> None:
 
     reference.TensorExpression.materialize = _ORIGINAL_MATERIALIZE
     _ORIGINAL_MATERIALIZE = None
+STABLE_MODES = ("logspace_max", "logspace_min", "scaled_sum", "scaled_max", "scaled_min")

@@ -22,6 +22,22 @@ XE_ERR_DEVICE_TIMEOUT = 4
 XE_SHIFT_MAX = 0
 XE_SHIFT_MIN = 1
 
+XE_FIBER_SUM = 0
+XE_FIBER_MAX = 1
+XE_FIBER_MIN = 2
+XE_FIBER_EXP = 3
+XE_FIBER_LSE = 4
+
+XE_OP_ADD = 0
+XE_OP_SUB = 1
+XE_OP_MUL = 2
+XE_OP_DIV = 3
+XE_OP_MAX = 4
+XE_OP_MIN = 5
+XE_OP_MUL_EXP = 6
+XE_OP_LOG_ADD = 7
+XE_OP_RESCALE = 8
+
 _c_i32 = ctypes.c_int32
 _c_i64 = ctypes.c_int64
 _c_size = ctypes.c_size_t
@@ -85,6 +101,21 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "xe_logspace_tucker": (
         _c_i32,
         [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i32, _c_ptr],
+    ),
+    "xe_scaled_gemm": (
+        _c_i32,
+        [
+            _c_ptr, _c_i64, _c_i64, _c_i64,  # a, strides
+            _c_ptr, _c_i64, _c_i64, _c_i64,  # b, strides
+            _c_ptr, _c_i64, _c_i64, _c_i64,  # c, strides
+            _c_i64, _c_i64, _c_i64, _c_i64, _c_ptr,  # batch, m, n, k, stream
+        ],
+    ),
+    "xe_fiber_normalize": (_c_i32, [_c_ptr, _c_i64p, _c_i64p, _c_i32, _c_i32, _c_ptr, _c_ptr, _c_ptr]),
+    "xe_reduce": (_c_i32, [_c_ptr, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i32, _c_ptr, _c_ptr]),
+    "xe_elementwise": (
+        _c_i32,
+        [_c_i32, _c_ptr, _c_i64p, _c_ptr, _c_i64p, _c_ptr, _c_i64p, _c_ptr, _c_i64p, _c_i32, _c_ptr],
     ),
 }
 

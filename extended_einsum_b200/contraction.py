@@ -156,3 +156,95 @@ def _match_tucker(input_strings, output_string, linear):
 
 def _tucker(input_strings, output_string, order, left, right, weights, shift, sizes, out_shape) -> torch.Tensor:
     return ops.logspace_tucker(left, right, weights, shift=shift)
+
+
+# ---------------------------------------------------------------------------
+# linear einsum (the scaled modes' einsum of normalized operands,
+# translate.py:372, and einsums of parameter-derived values, :306-309)
+
+
+def linear_einsum(format_string: str, *operands: torch.Tensor) -> torch.Tensor:
+    """torch.einsum semantics for fp32 CUDA operands on the B200 kernels.
+
+    * one operand: a permutation, or xe_reduce (sum) over the dropped labels;
+    * contraction-free: a broadcast product (xe_elementwise mul);
+    * two operands: labels summed within one operand are summed first, then
+      xe_scaled_gemm over the batch / M / N / K grouping;
+    * 'bfi,bfj,foij->bfo': the Tucker kernel on the logs of the operands.
+    """
+    input_strings, output_string = parse_format_string(format_string)
+    if len(input_strings) != len(operands):
+        raise ValueError(f"The einsum format string has {len(input_strings)} inputs, but the instruction has {len(operands)} arguments.")
+    _check_labels(input_strings, output_string)
+    sizes = _sizes(input_strings, operands)
+    missing = set(output_string) - set("".join(input_strings))
+    if missing:
+        raise ValueError(f"einsum: output labels {''.join(sorted(missing))!r} appear in no operand")
+    if len(operands) == 1:
+        return _linear_reduce(input_strings[0], output_string, operands[0], sizes)
+    if _contraction_free(input_strings, output_string):
+        return _linear_broadcast_product(input_strings, output_string, operands, sizes)
+    if len(operands) == 2:
+        return _linear_binary(input_strings, output_string, operands, sizes)
+    if len(operands) == 3:
+        tucker = _match_tucker(input_strings, output_string, (False, False, True))
+        if tucker is not None:
+            left, right, weights = (operands[i] for i in tucker)
+            logits = ops.logspace_tucker(ops.log(left), ops.log(right), weights, shift="max")
+            return ops.exp(logits)
+    raise NotImplementedError(f"einsum {format_string!r} with {len(operands)} operands has no fused kernel on this path")
+
+
+def _contraction_free(input_strings: list[str], output_string: str) -> bool:
+    out = set(output_string)
+    return all(set(s) <= out for s in input_strings)
+
+
+def _linear_reduce(labels: str, output_string: str, x: torch.Tensor, sizes: dict[str, int]) -> torch.Tensor:
+    reduced = [axis for axis, label in enumerate(labels) if label not in output_string]
+    kept = "".join(label for label in labels if label in output_string)
+    if reduced:
+        x = ops.reduce(x, reduced, "sum")
+    if kept != output_string:
+        x = x.permute([kept.index(label) for label in output_string])
+    return x
+
+
+def _aligned(labels: str, output_string: str, operand: torch.Tensor, sizes: dict[str, int]) -> torch.Tensor:
+    order = [labels.index(label) for label in output_string if label in labels]
+    view = operand.permute(order) if order else operand
+    return view.reshape([sizes[label] if label in labels else 1 for label in output_string])
+
+
+def _linear_broadcast_product(input_strings, output_string, operands, sizes) -> torch.Tensor:
+    result = _aligned(input_strings[0], output_string, operands[0], sizes)
+    for labels, operand in zip(input_strings[1:], operands[1:], strict=True):
+        result = ops.elementwise("mul", result, _aligned(labels, output_string, operand, sizes))
+    shape = [sizes[label] for label in output_string]
+    if list(result.shape) != shape:  # a single operand broadcast to the output
+        result = ops.elementwise("mul", result, torch.ones((), device=result.device, dtype=result.dtype).expand(shape))
+    return result
+
+
+def _linear_binary(input_strings, output_string, operands, sizes) -> torch.Tensor:
+    la, lb = input_strings
+    a, b = operands
+    # a label present in one operand only and absent from the output is summed there first
+    private_a = "".join(label for label in la if label not in lb and label not in output_string)
+    private_b = "".join(label for label in lb if label not in la and label not in output_string)
+    if private_a:
+        a = ops.reduce(a, [la.index(label) for label in private_a], "sum")
+        la = "".join(label for label in la if label not in private_a)
+    if private_b:
+        b = ops.reduce(b, [lb.index(label) for label in private_b], "sum")
+        lb = "".join(label for label in lb if label not in private_b)
+    batch = "".join(label for label in output_string if label in la and label in lb)
+    m_labels = "".join(label for label in output_string if label in la and label not in lb)
+    n_labels = "".join(label for label in output_string if label in lb and label not in la)
+    k_labels = "".join(label for label in la if label in lb and label not in output_string)
+    a3 = _group(a, la, [batch, m_labels, k_labels], sizes)
+    b3 = _group(b, lb, [batch, k_labels, n_labels], sizes)
+    c = ops.scaled_gemm(a3, b3)
+    grouped = batch + m_labels + n_labels
+    c = c.reshape([sizes[label] for label in grouped])
+    return c.permute([grouped.index(label) for label in output_string])

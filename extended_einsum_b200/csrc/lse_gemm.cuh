@@ -73,6 +73,7 @@ struct Params {
   int c_vec;      // output rows may be written with 16-byte stores
   int a_vec;      // LDG source: rows are k-contiguous and 16-byte aligned
   int shift_min;  // row extremes computed in-kernel use min instead of max
+  int raw_out;    // write the plain sums (linear operands, scaled modes) instead of log + shifts
   // Tucker layer: l (rows, folds, I), r (rows, folds, J) contiguous; batch = fold
   const float* tl;
   const float* tr;
@@ -905,6 +906,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
+          if (p.raw_out) continue;
           float o = fast_log(out[j]);
           if (AMODE != kALinear) o += s1;
           if (AMODE == kATucker) o += s2;

@@ -471,4 +471,159 @@ __global__ void __launch_bounds__(256) unary_map4(const float4* __restrict__ x, 
   }
 }
 
+// ---------------------------------------------------------------------------
+// Scaled stability modes (sum / max / min fibre normalisation).  A value is
+// a pair (normalized, log_scale) with raw = normalized * exp(log_scale) and
+// one scale per last-axis fibre; these kernels are its glue.
+
+// Elementwise ops over up to three broadcast operands (strides may be 0).
+enum ElementwiseOp : int {
+  kOpAdd = 0,       // a + b
+  kOpSub = 1,       // a - b
+  kOpMul = 2,       // a * b
+  kOpDiv = 3,       // a / b
+  kOpMax = 4,       // maximum(a, b), NaN-propagating
+  kOpMin = 5,       // minimum(a, b), NaN-propagating
+  kOpMulExp = 6,    // a * exp(b)            (a scaled pair back to raw)
+  kOpLogAdd = 7,    // log(a) + b            (log of a scaled pair)
+  kOpRescale = 8,   // a * exp(b - c)        (a pair brought to the common scale c)
+  kNumElementwiseOps = 9
+};
+
+struct NdShape3 {
+  int64_t shape[6];
+  int64_t as[6];
+  int64_t bs[6];
+  int64_t cs[6];
+  int ndim;
+};
+
+template <int OP>
+__device__ __forceinline__ float elementwise_apply(float a, float b, float c) {
+  if (OP == kOpAdd) return a + b;
+  if (OP == kOpSub) return a - b;
+  if (OP == kOpMul) return a * b;
+  if (OP == kOpDiv) return a / b;
+  if (OP == kOpMax) return (isnan(a) || a > b) ? a : b;
+  if (OP == kOpMin) return (isnan(a) || a < b) ? a : b;
+  if (OP == kOpMulExp) return a * expf(b);
+  if (OP == kOpLogAdd) return logf(a) + b;
+  return a * expf(b - c);
+}
+
+template <int OP>
+__global__ void __launch_bounds__(256) elementwise_nd(const float* __restrict__ a, const float* __restrict__ b,
+                                                      const float* __restrict__ c, float* __restrict__ y, NdShape3 s,
+                                                      int64_t total) {
+  for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < total; g += (int64_t)gridDim.x * blockDim.x) {
+    int64_t rem = g, oa = 0, ob = 0, oc = 0;
+    for (int d = s.ndim - 1; d >= 0; --d) {
+      const int64_t idx = rem % s.shape[d];
+      rem /= s.shape[d];
+      oa += idx * s.as[d];
+      ob += idx * s.bs[d];
+      oc += idx * s.cs[d];
+    }
+    y[g] = elementwise_apply<OP>(a[oa], b ? b[ob] : 0.0f, c ? c[oc] : 0.0f);
+  }
+}
+
+// All three operands dense and 16-byte aligned (same shape, no broadcast).
+template <int OP>
+__global__ void __launch_bounds__(256) elementwise_contig4(const float4* __restrict__ a, const float4* __restrict__ b,
+                                                           const float4* __restrict__ c, float4* __restrict__ y,
+                                                           int64_t n4) {
+  for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < n4; g += (int64_t)gridDim.x * blockDim.x) {
+    const float4 u = a[g];
+    const float4 v = b ? b[g] : make_float4(0.f, 0.f, 0.f, 0.f);
+    const float4 w = c ? c[g] : make_float4(0.f, 0.f, 0.f, 0.f);
+    y[g] = make_float4(elementwise_apply<OP>(u.x, v.x, w.x), elementwise_apply<OP>(u.y, v.y, w.y),
+                       elementwise_apply<OP>(u.z, v.z, w.z), elementwise_apply<OP>(u.w, v.w, w.w));
+  }
+}
+
+// Leading (non-fibre) axes of a strided tensor: row index -> element offset.
+struct RowIndexer {
+  int64_t shape[6];
+  int64_t stride[6];
+  int ndim;
+  __device__ __forceinline__ int64_t offset(int64_t row) const {
+    int64_t off = 0;
+    for (int d = ndim - 1; d >= 0; --d) {
+      const int64_t idx = row % shape[d];
+      row /= shape[d];
+      off += idx * stride[d];
+    }
+    return off;
+  }
+};
+
+// Fibre statistics and the normalised fibre, one warp per fibre.
+enum FiberKind : int {
+  kFiberSum = 0,  // total = sum;  normalized = x / total; log_scale = log(total)
+  kFiberMax = 1,  // total = max;  same
+  kFiberMin = 2,  // total = min;  same
+  kFiberExp = 3,  // exp of a raw fibre: log_scale = max x; normalized = exp(x - log_scale)
+  kFiberLse = 4,  // exp of a log-domain fibre, sum-normalised: log_scale = logsumexp x; normalized = exp(x - log_scale)
+};
+
+template <int KIND>
+__global__ void __launch_bounds__(256) fiber_rows(const float* __restrict__ x, RowIndexer ri, int64_t rows, int64_t n,
+                                                  int64_t sn, float* __restrict__ normalized,
+                                                  float* __restrict__ log_scale) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < rows; row += warps) {
+    const float* px = x + ri.offset(row);
+    float acc = KIND == kFiberSum ? 0.0f : (KIND == kFiberMin ? INFINITY : -INFINITY);
+    for (int64_t j = lane; j < n; j += 32) {
+      const float v = px[j * sn];
+      if (KIND == kFiberSum) acc += v;
+      else acc = nan_extreme<KIND != kFiberMin>(acc, v);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float other = __shfl_xor_sync(0xffffffffu, acc, o);
+      acc = KIND == kFiberSum ? acc + other : nan_extreme<KIND != kFiberMin>(acc, other);
+    }
+    float total = acc;
+    if (KIND == kFiberLse) {
+      float s = 0.0f;
+      for (int64_t j = lane; j < n; j += 32) s += expf(px[j * sn] - acc);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+      total = isinf(acc) ? acc : acc + logf(s);
+    }
+    float* py = normalized + row * n;
+    for (int64_t j = lane; j < n; j += 32) {
+      const float v = px[j * sn];
+      py[j] = (KIND == kFiberExp || KIND == kFiberLse) ? expf(v - total) : v / total;
+    }
+    if (lane == 0) log_scale[row] = (KIND == kFiberExp || KIND == kFiberLse) ? total : logf(total);
+  }
+}
+
+// Plain reduction over k of a (batch, rows, k) strided view: sum, max or min.
+template <int KIND>
+__global__ void __launch_bounds__(256) reduce_rows(const float* __restrict__ x, int64_t sb, int64_t sr, int64_t sk,
+                                                   int64_t batch, int64_t rows, int64_t k, float* __restrict__ y) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t g = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); g < batch * rows; g += warps) {
+    const float* px = x + (g / rows) * sb + (g % rows) * sr;
+    float acc = KIND == kFiberSum ? 0.0f : (KIND == kFiberMin ? INFINITY : -INFINITY);
+    for (int64_t j = lane; j < k; j += 32) {
+      const float v = px[j * sk];
+      if (KIND == kFiberSum) acc += v;
+      else acc = nan_extreme<KIND != kFiberMin>(acc, v);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float other = __shfl_xor_sync(0xffffffffu, acc, o);
+      acc = KIND == kFiberSum ? acc + other : nan_extreme<KIND != kFiberMin>(acc, other);
+    }
+    if (lane == 0) y[g] = acc;
+  }
+}
+
 }  // namespace xe

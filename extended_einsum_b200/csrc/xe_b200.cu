@@ -392,7 +392,8 @@ namespace {
 xe_status gemm_launch(const float* a, const float* a2, int64_t a_sb, int64_t a_sm, int64_t a_sk, bool a_linear,
                       const float* shift_a, const float* b, int64_t b_sb, int64_t b_sk, int64_t b_sn,
                       const float* shift_b, float* c, int64_t c_sb, int64_t c_sm, int64_t c_sn, int64_t batch, int64_t m,
-                      int64_t n, int64_t k, bool shift_min, const GemmPlan& g, cudaStream_t s) {
+                      int64_t n, int64_t k, bool shift_min, const GemmPlan& g, cudaStream_t s,
+                      bool raw_out = false) {
   Params p{};
   p.a = a;
   p.a2 = a2;
@@ -417,6 +418,7 @@ xe_status gemm_launch(const float* a, const float* a2, int64_t a_sb, int64_t a_s
   p.a_vec = (a_sk == 1 && k % 4 == 0 && a_sm % 4 == 0 && a_sb % 4 == 0 && aligned16(a) &&
              (a2 == nullptr || aligned16(a2))) ? 1 : 0;
   p.shift_min = shift_min ? 1 : 0;
+  p.raw_out = raw_out ? 1 : 0;
   const bool bk = !(b_sn == 1) && b_sk == 1;
   return launch_gemm(p, g, a_linear, bk, s);
 }
@@ -764,3 +766,151 @@ static xe_status xe_tucker_impl(const float* l, const float* r, const float* w, 
   p.shift_min = shift_mode == XE_SHIFT_MIN;
   return j_dim == 32 ? launch_tucker<32>(p, stream) : launch_tucker<64>(p, stream);
 }
+
+// ------------------------------------------------------------------------
+// Scaled stability modes.
+
+namespace {
+
+template <int OP>
+void launch_elementwise(const float* a, const float* b, const float* c, float* y, const xe::NdShape3& sh, int64_t total,
+                        bool contig, cudaStream_t s) {
+  const int cap = current_device_sms() * 8;
+  if (contig && total % 4 == 0 && aligned16(a) && (!b || aligned16(b)) && (!c || aligned16(c)) && aligned16(y)) {
+    const int64_t n4 = total / 4;
+    xe::elementwise_contig4<OP><<<(unsigned)grid_for(n4, 256, cap), 256, 0, s>>>(
+        reinterpret_cast<const float4*>(a), reinterpret_cast<const float4*>(b), reinterpret_cast<const float4*>(c),
+        reinterpret_cast<float4*>(y), n4);
+  } else {
+    xe::elementwise_nd<OP><<<(unsigned)grid_for(total, 256, cap), 256, 0, s>>>(a, b, c, y, sh, total);
+  }
+}
+
+template <int KIND>
+void launch_fiber(const float* x, const xe::RowIndexer& ri, int64_t rows, int64_t n, int64_t sn, float* normalized,
+                  float* log_scale, cudaStream_t s) {
+  const int64_t blocks = grid_for(rows, 8, (int64_t)current_device_sms() * 16);
+  xe::fiber_rows<KIND><<<(unsigned)blocks, 256, 0, s>>>(x, ri, rows, n, sn, normalized, log_scale);
+}
+
+template <int KIND>
+void launch_reduce(const float* x, int64_t sb, int64_t sr, int64_t sk, int64_t batch, int64_t rows, int64_t k, float* y,
+                   cudaStream_t s) {
+  const int64_t blocks = grid_for(batch * rows, 8, (int64_t)current_device_sms() * 16);
+  xe::reduce_rows<KIND><<<(unsigned)blocks, 256, 0, s>>>(x, sb, sr, sk, batch, rows, k, y);
+}
+
+}  // namespace
+
+extern "C" {
+
+xe_status xe_scaled_gemm(const float* a, int64_t a_sb, int64_t a_sm, int64_t a_sk, const float* b, int64_t b_sb,
+                         int64_t b_sk, int64_t b_sn, float* c, int64_t c_sb, int64_t c_sm, int64_t c_sn, int64_t batch,
+                         int64_t m, int64_t n, int64_t k, void* stream) {
+  xe_status st = gemm_check("xe_scaled_gemm", a, b, c, batch, m, n, k);
+  if (st != XE_OK) return st;
+  if (batch == 0 || m == 0 || n == 0) return XE_OK;
+  const GemmPlan plan = plan_gemm(a, nullptr, a_sb, a_sm, a_sk, true, b, b_sb, b_sk, b_sn, batch, m, n, k);
+  return gemm_launch(a, nullptr, a_sb, a_sm, a_sk, true, nullptr, b, b_sb, b_sk, b_sn, nullptr, c, c_sb, c_sm, c_sn,
+                     batch, m, n, k, false, plan, as_stream(stream), true);
+}
+
+xe_status xe_fiber_normalize(const float* x, const int64_t* shape, const int64_t* strides, int32_t ndim, int32_t kind,
+                             float* normalized, float* log_scale, void* stream) {
+  if (!x || !normalized || !log_scale || (ndim > 0 && (!shape || !strides)))
+    return fail(XE_ERR_INVALID_ARGUMENT, "xe_fiber_normalize: null pointer");
+  if (ndim < 0 || ndim > 7) return fail(XE_ERR_NOT_SUPPORTED, "xe_fiber_normalize: rank %d above 7 is not supported", ndim);
+  if (kind < XE_FIBER_SUM || kind > XE_FIBER_LSE) return fail(XE_ERR_INVALID_ARGUMENT, "xe_fiber_normalize: unknown kind %d", kind);
+  xe::RowIndexer ri{};
+  int64_t rows = 1, n = 1, sn = 0;
+  if (ndim > 0) {
+    n = shape[ndim - 1];
+    sn = strides[ndim - 1];
+    ri.ndim = ndim - 1;
+    for (int d = 0; d < ndim - 1; ++d) {
+      if (shape[d] < 0) return fail(XE_ERR_INVALID_ARGUMENT, "xe_fiber_normalize: negative extent");
+      ri.shape[d] = shape[d];
+      ri.stride[d] = strides[d];
+      rows *= shape[d];
+    }
+    if (n < 0) return fail(XE_ERR_INVALID_ARGUMENT, "xe_fiber_normalize: negative extent");
+  }
+  if (ri.ndim == 0) {
+    ri.ndim = 1;
+    ri.shape[0] = 1;
+    ri.stride[0] = 0;
+  }
+  if (n == 0 && kind != XE_FIBER_SUM && kind != XE_FIBER_LSE && rows > 0)
+    return fail(XE_ERR_INVALID_ARGUMENT, "xe_fiber_normalize: max/min of an empty fibre");
+  if (rows == 0) return XE_OK;
+  cudaStream_t s = as_stream(stream);
+  switch (kind) {
+    case XE_FIBER_SUM: launch_fiber<xe::kFiberSum>(x, ri, rows, n, sn, normalized, log_scale, s); break;
+    case XE_FIBER_MAX: launch_fiber<xe::kFiberMax>(x, ri, rows, n, sn, normalized, log_scale, s); break;
+    case XE_FIBER_MIN: launch_fiber<xe::kFiberMin>(x, ri, rows, n, sn, normalized, log_scale, s); break;
+    case XE_FIBER_EXP: launch_fiber<xe::kFiberExp>(x, ri, rows, n, sn, normalized, log_scale, s); break;
+    default: launch_fiber<xe::kFiberLse>(x, ri, rows, n, sn, normalized, log_scale, s); break;
+  }
+  return check_launch("xe_fiber_normalize");
+}
+
+xe_status xe_reduce(const float* x, int64_t sb, int64_t sr, int64_t sk, int64_t batch, int64_t rows, int64_t k,
+                    int32_t kind, float* y, void* stream) {
+  if (!x || !y) return fail(XE_ERR_INVALID_ARGUMENT, "xe_reduce: null pointer");
+  if (batch < 0 || rows < 0 || k < 0) return fail(XE_ERR_INVALID_ARGUMENT, "xe_reduce: negative extent");
+  if (kind != XE_FIBER_SUM && kind != XE_FIBER_MAX && kind != XE_FIBER_MIN)
+    return fail(XE_ERR_INVALID_ARGUMENT, "xe_reduce: unknown kind %d", kind);
+  if (k == 0 && kind != XE_FIBER_SUM && batch * rows > 0)
+    return fail(XE_ERR_INVALID_ARGUMENT, "xe_reduce: max/min over an empty axis");
+  if (batch == 0 || rows == 0) return XE_OK;
+  cudaStream_t s = as_stream(stream);
+  if (kind == XE_FIBER_SUM) launch_reduce<xe::kFiberSum>(x, sb, sr, sk, batch, rows, k, y, s);
+  else if (kind == XE_FIBER_MAX) launch_reduce<xe::kFiberMax>(x, sb, sr, sk, batch, rows, k, y, s);
+  else launch_reduce<xe::kFiberMin>(x, sb, sr, sk, batch, rows, k, y, s);
+  return check_launch("xe_reduce");
+}
+
+xe_status xe_elementwise(int32_t op, const float* a, const int64_t* a_strides, const float* b, const int64_t* b_strides,
+                         const float* c, const int64_t* c_strides, float* y, const int64_t* shape, int32_t ndim,
+                         void* stream) {
+  if (op < XE_OP_ADD || op > XE_OP_RESCALE) return fail(XE_ERR_INVALID_ARGUMENT, "xe_elementwise: unknown op %d", op);
+  const bool needs_c = op == XE_OP_RESCALE;
+  if (!a || !b || !y || (needs_c && !c) || (ndim > 0 && (!shape || !a_strides || !b_strides || (needs_c && !c_strides))))
+    return fail(XE_ERR_INVALID_ARGUMENT, "xe_elementwise: null pointer");
+  if (ndim < 0 || ndim > 6) return fail(XE_ERR_NOT_SUPPORTED, "xe_elementwise: rank %d above 6 is not supported", ndim);
+  if (!needs_c) c = nullptr;
+  xe::NdShape3 sh{};
+  sh.ndim = ndim;
+  int64_t total = 1, expect = 1;
+  bool contig = true;
+  for (int d = ndim - 1; d >= 0; --d) {
+    if (shape[d] < 0) return fail(XE_ERR_INVALID_ARGUMENT, "xe_elementwise: negative extent");
+    sh.shape[d] = shape[d];
+    sh.as[d] = a_strides[d];
+    sh.bs[d] = b_strides[d];
+    sh.cs[d] = c ? c_strides[d] : 0;
+    if (shape[d] != 1 && (sh.as[d] != expect || sh.bs[d] != expect || (c && sh.cs[d] != expect))) contig = false;
+    expect *= shape[d];
+    total *= shape[d];
+  }
+  if (ndim == 0) {
+    sh.ndim = 1;
+    sh.shape[0] = 1;
+  }
+  if (total == 0) return XE_OK;
+  cudaStream_t s = as_stream(stream);
+  switch (op) {
+    case XE_OP_ADD: launch_elementwise<xe::kOpAdd>(a, b, c, y, sh, total, contig, s); break;
+    case XE_OP_SUB: launch_elementwise<xe::kOpSub>(a, b, c, y, sh, total, contig, s); break;
+    case XE_OP_MUL: launch_elementwise<xe::kOpMul>(a, b, c, y, sh, total, contig, s); break;
+    case XE_OP_DIV: launch_elementwise<xe::kOpDiv>(a, b, c, y, sh, total, contig, s); break;
+    case XE_OP_MAX: launch_elementwise<xe::kOpMax>(a, b, c, y, sh, total, contig, s); break;
+    case XE_OP_MIN: launch_elementwise<xe::kOpMin>(a, b, c, y, sh, total, contig, s); break;
+    case XE_OP_MUL_EXP: launch_elementwise<xe::kOpMulExp>(a, b, c, y, sh, total, contig, s); break;
+    case XE_OP_LOG_ADD: launch_elementwise<xe::kOpLogAdd>(a, b, c, y, sh, total, contig, s); break;
+    default: launch_elementwise<xe::kOpRescale>(a, b, c, y, sh, total, contig, s); break;
+  }
+  return check_launch("xe_elementwise");
+}
+
+}  // extern "C"

@@ -85,11 +85,21 @@ def parameter_derived_ssa_ids(program: Any) -> frozenset[int]:
 
 
 def lower(program: Any) -> BackendProgram:
-    """Lowers a RichProgram in a log-space stability mode onto the B200 kernels."""
+    """Lowers a RichProgram in a log-space or scaled stability mode onto the B200 kernels.
+
+    Mode dispatch as in translate_to_backend_program (translate.py:32-41):
+    logspace_max / logspace_min -> the log-space lowering below,
+    scaled_sum / scaled_max / scaled_min -> scaled.py; anything else is
+    NotImplementedError (the unstable mode has nothing to stabilise).
+    """
+    from .scaled import SCALED_NORMS, _ScaledLowering
+
     mode = program.stability_mode
-    if mode not in LOGSPACE_SHIFTS:
-        raise NotImplementedError(f"The B200 lowering is not implemented for stability mode {mode}.")
-    return _LogspaceLowering(program, LOGSPACE_SHIFTS[mode]).run()
+    if mode in LOGSPACE_SHIFTS:
+        return _LogspaceLowering(program, LOGSPACE_SHIFTS[mode]).run()
+    if mode in SCALED_NORMS:
+        return _ScaledLowering(program, SCALED_NORMS[mode], _Builder(program.n_inputs), parameter_derived_ssa_ids(program)).run()
+    raise NotImplementedError(f"The B200 lowering is not implemented for stability mode {mode}.")
 
 
 class _LogspaceLowering:

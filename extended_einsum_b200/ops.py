@@ -318,6 +318,122 @@ def logspace_tucker(
     return y
 
 
+# ---------------------------------------------------------------------------
+# scaled stability modes: a value is (normalized, log_scale) with
+# raw = normalized * exp(log_scale), one scale per last-axis fibre
+
+FIBER_KINDS = {"sum": _lib.XE_FIBER_SUM, "max": _lib.XE_FIBER_MAX, "min": _lib.XE_FIBER_MIN,
+               "exp": _lib.XE_FIBER_EXP, "lse": _lib.XE_FIBER_LSE}
+ELEMENTWISE_OPS = {
+    "add": _lib.XE_OP_ADD, "sub": _lib.XE_OP_SUB, "mul": _lib.XE_OP_MUL, "div": _lib.XE_OP_DIV,
+    "max": _lib.XE_OP_MAX, "min": _lib.XE_OP_MIN, "mul_exp": _lib.XE_OP_MUL_EXP, "log_add": _lib.XE_OP_LOG_ADD,
+    "rescale": _lib.XE_OP_RESCALE,
+}
+
+
+def scaled_gemm(a: torch.Tensor, b: torch.Tensor, *, out: torch.Tensor | None = None) -> torch.Tensor:
+    """C[t,m,n] = sum_k A[t,m,k] B[t,k,n] for linear fp32 operands (xe_scaled_gemm), any strides."""
+    tensors = [a, b] + ([out] if out is not None else [])
+    device = _check_tensors("scaled_gemm", *tensors)
+    if a.dim() != 3 or b.dim() != 3:
+        raise ValueError("scaled_gemm: operands must be 3-D (batch, M, K) and (batch, K, N)")
+    batch, m, k = a.shape
+    if b.shape[0] != batch or b.shape[1] != k:
+        raise ValueError(f"scaled_gemm: incompatible shapes {tuple(a.shape)} and {tuple(b.shape)}")
+    n = b.shape[2]
+    if out is None:
+        out = torch.empty((batch, m, n), device=device, dtype=torch.float32)
+    elif out.shape != (batch, m, n):
+        raise ValueError(f"scaled_gemm: out has shape {tuple(out.shape)}, expected {(batch, m, n)}")
+    if k == 0:  # an empty contraction is zero (torch.einsum semantics)
+        return out.zero_()
+    status = _lib.load().xe_scaled_gemm(
+        a.data_ptr(), a.stride(0), a.stride(1), a.stride(2),
+        b.data_ptr(), b.stride(0), b.stride(1), b.stride(2),
+        out.data_ptr(), out.stride(0), out.stride(1), out.stride(2),
+        batch, m, n, k, _stream(device),
+    )
+    _lib.check(status, "xe_scaled_gemm")
+    return out
+
+
+def fiber_normalize(x: torch.Tensor, kind: str) -> tuple[torch.Tensor, torch.Tensor]:
+    """(normalized, log_scale) of x over its last axis (xe_fiber_normalize).
+
+    kind 'sum' / 'max' / 'min' normalise a raw x by that fibre statistic
+    (translate.py:174-199); 'exp' gives the pair of exp(x) for a raw x
+    (translate.py:436-444); 'lse' gives the sum-normalised pair of exp(x) for
+    a log-domain x.  log_scale has x's shape with the last axis 1 (a rank-0 x
+    gives rank-0 results).
+    """
+    device = _check_tensors("fiber_normalize", x)
+    try:
+        code = FIBER_KINDS[kind]
+    except KeyError:
+        raise ValueError(f"fiber_normalize: unknown kind {kind!r}") from None
+    if x.dim() > 7:
+        raise NotImplementedError(f"fiber_normalize: rank {x.dim()} above 7 is not supported")
+    normalized = torch.empty(x.shape, device=device, dtype=torch.float32)
+    scale_shape = (*x.shape[:-1], 1) if x.dim() else ()
+    log_scale = torch.empty(scale_shape, device=device, dtype=torch.float32)
+    status = _lib.load().xe_fiber_normalize(
+        x.data_ptr(), _lib.int64_array(x.shape), _lib.int64_array(x.stride()), x.dim(), code,
+        normalized.data_ptr(), log_scale.data_ptr(), _stream(device),
+    )
+    _lib.check(status, "xe_fiber_normalize")
+    return normalized, log_scale
+
+
+def reduce(x: torch.Tensor, axes: Sequence[int] | None, kind: str, *, keepdims: bool = False) -> torch.Tensor:
+    """sum / amax / amin of x over ``axes`` (None = all), xe_reduce."""
+    device = _check_tensors("reduce", x)
+    if kind not in ("sum", "max", "min"):
+        raise ValueError(f"reduce: unknown kind {kind!r}")
+    nd = x.dim()
+    axes = tuple(range(nd)) if axes is None else tuple(sorted({a + nd if a < 0 else a for a in axes}))
+    if any(not 0 <= a < nd for a in axes):
+        raise ValueError(f"reduce: axes out of range for a {nd}-D tensor")
+    keep = [d for d in range(nd) if d not in axes]
+    kept_shape = [x.shape[d] for d in keep]
+    rows = math.prod(kept_shape)
+    k = math.prod(x.shape[d] for d in axes)
+    view = x.permute(keep + list(axes)).reshape(1, rows, k)
+    y = torch.empty(rows, device=device, dtype=torch.float32)
+    status = _lib.load().xe_reduce(
+        view.data_ptr(), view.stride(0), view.stride(1), view.stride(2), 1, rows, k, FIBER_KINDS[kind], y.data_ptr(),
+        _stream(device),
+    )
+    _lib.check(status, "xe_reduce")
+    if keepdims:
+        return y.reshape([1 if d in axes else x.shape[d] for d in range(nd)])
+    return y.reshape(kept_shape)
+
+
+def elementwise(op: str, a: torch.Tensor, b: torch.Tensor, c: torch.Tensor | None = None) -> torch.Tensor:
+    """Broadcast elementwise glue of the scaled modes (xe_elementwise): add, sub, mul, div, max, min,
+    mul_exp (a*exp(b)), log_add (log(a)+b), rescale (a*exp(b-c))."""
+    operands = [a, b] + ([c] if c is not None else [])
+    device = _check_tensors("elementwise", *operands)
+    try:
+        code = ELEMENTWISE_OPS[op]
+    except KeyError:
+        raise ValueError(f"elementwise: unknown op {op!r}") from None
+    if (op == "rescale") != (c is not None):
+        raise ValueError("elementwise: the third operand belongs to 'rescale' only")
+    shape = torch.broadcast_shapes(*(t.shape for t in operands))
+    if len(shape) > 6:
+        raise NotImplementedError(f"elementwise: rank {len(shape)} above 6 is not supported")
+    y = torch.empty(shape, device=device, dtype=torch.float32)
+    c_strides = _lib.int64_array(_broadcast_strides(c, shape)) if c is not None else None
+    status = _lib.load().xe_elementwise(
+        code, a.data_ptr(), _lib.int64_array(_broadcast_strides(a, shape)),
+        b.data_ptr(), _lib.int64_array(_broadcast_strides(b, shape)),
+        _ptr(c), c_strides, y.data_ptr(), _lib.int64_array(shape), len(shape), _stream(device),
+    )
+    _lib.check(status, "xe_elementwise")
+    return y
+
+
 def device_status(clear: bool = True) -> int:
     """The device-side status word (non-zero after a bounded wait ran out)."""
     return int(_lib.load().xe_device_status(int(clear)))

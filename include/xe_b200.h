@@ -201,6 +201,66 @@ xe_status xe_logspace_tucker(const float* l, const float* r, const float* w, flo
                              int64_t folds, int64_t i_dim, int64_t j_dim, int64_t o_dim, int32_t shift_mode,
                              void* stream);
 
+/* ------------------------------------------------------------------------ */
+/* Scaled stability modes (scaled_sum / scaled_max / scaled_min,
+ * translate.py:115-585).  A value is a pair (normalized, log_scale) with
+ * raw = normalized * exp(log_scale) and one log scale per last-axis fibre
+ * (translate.py:119-126, 174-199). */
+
+/* The einsum of normalized (linear) operands (translate.py:372): the batched
+ * fp32 product C[b,m,n] = sum_k A[b,m,k] B[b,k,n] on the tensor cores (three
+ * TF32 products per multiply-add, fp32 accumulation), raw output.  Strides as
+ * in xe_logspace_gemm.  k must be >= 1. */
+xe_status xe_scaled_gemm(const float* a, int64_t a_sb, int64_t a_sm, int64_t a_sk, const float* b, int64_t b_sb,
+                         int64_t b_sk, int64_t b_sn, float* c, int64_t c_sb, int64_t c_sm, int64_t c_sn, int64_t batch,
+                         int64_t m, int64_t n, int64_t k, void* stream);
+
+/* Fibre normalisation of a strided tensor of rank <= 7 over its last axis
+ * (translate.py:174-199, 373-382 and the exp rule :436-444):
+ *   XE_FIBER_SUM / MAX / MIN: t = sum / max / min of the fibre,
+ *                             normalized = x / t, log_scale = log(t)
+ *   XE_FIBER_EXP: x is raw, the result is the pair of exp(x):
+ *                             log_scale = max x, normalized = exp(x - log_scale)
+ *   XE_FIBER_LSE: x is log-domain, the result is the sum-normalised pair of exp(x):
+ *                             log_scale = logsumexp x, normalized = exp(x - log_scale)
+ * normalized is written contiguous in x's shape, log_scale contiguous with one
+ * value per fibre.  A rank-0 x is one fibre of length 1.  max / min reductions
+ * propagate NaN (torch.amax / torch.amin).  MAX, MIN and EXP need a non-empty
+ * fibre. */
+typedef enum { XE_FIBER_SUM = 0, XE_FIBER_MAX = 1, XE_FIBER_MIN = 2, XE_FIBER_EXP = 3, XE_FIBER_LSE = 4 } xe_fiber_kind;
+xe_status xe_fiber_normalize(const float* x, const int64_t* shape, const int64_t* strides, int32_t ndim, int32_t kind,
+                             float* normalized, float* log_scale, void* stream);
+
+/* Plain reduction y[b*rows + r] = sum / max / min over k of x[b*sb + r*sr + k*sk]
+ * (the sum / amax / amin backend calls of the scaled translation, e.g.
+ * translate.py:336, 396-400).  kind is XE_FIBER_SUM, XE_FIBER_MAX or
+ * XE_FIBER_MIN; max and min need k >= 1. */
+xe_status xe_reduce(const float* x, int64_t sb, int64_t sr, int64_t sk, int64_t batch, int64_t rows, int64_t k,
+                    int32_t kind, float* y, void* stream);
+
+/* Broadcast elementwise glue of the scaled translation, rank <= 6,
+ * y contiguous in `shape`, operand strides in elements (0 = broadcast):
+ *   XE_OP_ADD a+b, XE_OP_SUB a-b, XE_OP_MUL a*b, XE_OP_DIV a/b,
+ *   XE_OP_MAX / XE_OP_MIN NaN-propagating maximum / minimum (torch.maximum),
+ *   XE_OP_MUL_EXP  a*exp(b)    (raw value of a pair, translate.py:168-170)
+ *   XE_OP_LOG_ADD  log(a)+b    (log of a pair, translate.py:445-449)
+ *   XE_OP_RESCALE  a*exp(b-c)  (a pair at the common scale c, translate.py:253-257, 336-339)
+ * c is used by XE_OP_RESCALE only and may be NULL otherwise. */
+typedef enum {
+  XE_OP_ADD = 0,
+  XE_OP_SUB = 1,
+  XE_OP_MUL = 2,
+  XE_OP_DIV = 3,
+  XE_OP_MAX = 4,
+  XE_OP_MIN = 5,
+  XE_OP_MUL_EXP = 6,
+  XE_OP_LOG_ADD = 7,
+  XE_OP_RESCALE = 8
+} xe_elementwise_op;
+xe_status xe_elementwise(int32_t op, const float* a, const int64_t* a_strides, const float* b, const int64_t* b_strides,
+                         const float* c, const int64_t* c_strides, float* y, const int64_t* shape, int32_t ndim,
+                         void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -34,7 +34,7 @@ def _run(spec, name, golden, mode):
     return out.cpu().numpy()
 
 
-@pytest.mark.parametrize("mode", ["logspace_max", "logspace_min"])
+@pytest.mark.parametrize("mode", ["logspace_max", "logspace_min", "scaled_sum", "scaled_max", "scaled_min"])
 def test_golden_programs(golden, golden_programs, mode):
     failures = []
     for name, spec in golden_programs.items():
@@ -60,8 +60,9 @@ def test_golden_programs(golden, golden_programs, mode):
     assert not failures, "\n".join(failures)
 
 
-def test_public_api_materialize(golden):
+@pytest.mark.parametrize("mode", ["logspace_max", "scaled_sum"])
+def test_public_api_materialize(golden, mode):
     a = torch.from_numpy(golden["matmul_logu/in0"]).cuda()
     b = torch.from_numpy(golden["matmul_logu/in1"]).cuda()
-    result = xb.log(xb.einsum("ik,kj->ij", xb.exp(xb.array(a)), xb.exp(xb.array(b)))).materialize("logspace_max")
-    log_close(result.backend_array.cpu().numpy(), golden["matmul_logu/logspace_max/f32"])
+    result = xb.log(xb.einsum("ik,kj->ij", xb.exp(xb.array(a)), xb.exp(xb.array(b)))).materialize(mode)
+    log_close(result.backend_array.cpu().numpy(), golden[f"matmul_logu/{mode}/f32"])

@@ -129,3 +129,29 @@ def test_front_end_matches_reference_extract_program():
     assert [(i.operator.name, i.argument_ssa_ids) for i in ours.instructions] == [(i.operator.name, i.argument_ssa_ids) for i in theirs.instructions]
     # the lowering accepts the reference's own program object
     assert len(xb.lower(theirs).backend_calls) == len(xb.lower(ours).backend_calls) == 2
+
+
+@pytest.mark.parametrize("mode", ["scaled_sum", "scaled_max", "scaled_min"])
+def test_scaled_modes_lower_every_golden_program(golden_programs, mode):
+    """The scaled lowering (translate.py:115-585) accepts every golden program; nothing runs."""
+    for name, spec in golden_programs.items():
+        lowered = xb.lower(build_program(spec, mode))
+        assert lowered.n_inputs == spec["n_inputs"]
+        assert len(lowered.backend_calls) == len(lowered.call_arguments)
+
+
+def test_scaled_matmul_uses_one_tensor_core_contraction():
+    from extended_einsum_b200.contraction import linear_einsum
+
+    a = xb.array(torch.zeros(4, 3))
+    b = xb.array(torch.zeros(3, 5))
+    program, _ = xb.extract_program(xb.log(xb.einsum("ik,kj->ij", xb.exp(a), xb.exp(b))), "scaled_sum")
+    fns = _fns(xb.lower(program))
+    einsums = [f for f in fns if getattr(f, "func", None) is linear_einsum]
+    assert len(einsums) == 1 and einsums[0].args == ("ik,kj->ij",)
+
+
+def test_unknown_stability_mode_is_not_implemented():
+    program = fe.dense_program([fe.RichInstruction(fe.OperatorExp(), (0,))], 1, "unstable")
+    with pytest.raises(NotImplementedError):
+        xb.lower(program)

@@ -92,3 +92,30 @@ def test_reference_known_answers_hold_in_golden(golden):
     m = log_values.max(axis=0, keepdims=True)
     expected = m.T + np.log(np.einsum("ib,io->bo", np.exp(log_values - m), weights))
     np.testing.assert_allclose(golden["axis_reorder_minus1000/logspace_max/f64"], expected, rtol=1e-9)
+
+
+@pytest.mark.parametrize("norm", ["sum", "max", "min"])
+def test_scaled_oracle_pattern_functions(golden, norm):
+    """oracle/scaled.py == the reference's fp64 scaled-mode outputs (translate.py:293-394, 436-449)."""
+    from oracle import scaled as oracle_scaled
+
+    mode = f"scaled_{norm}"
+    f64 = lambda key: golden[key].astype(np.float64)  # noqa: E731
+    np.testing.assert_allclose(
+        oracle_scaled.scaled_matmul(f64("matmul_logu/in0"), f64("matmul_logu/in1"), norm), golden[f"matmul_logu/{mode}/f64"], rtol=1e-12
+    )
+    np.testing.assert_allclose(
+        oracle_scaled.scaled_matmul(f64("batched_n64/in0"), f64("batched_n64/in1"), norm), golden[f"batched_n64/{mode}/f64"], rtol=1e-12
+    )
+    w = oracle.softmax(f64("cp_layer/in1"), 2)
+    np.testing.assert_allclose(oracle_scaled.scaled_cp_layer(f64("cp_layer/in0"), w, norm), golden[f"cp_layer/{mode}/f64"], rtol=1e-12)
+    w = oracle.softmax(f64("tucker/in2"), (2, 3))
+    np.testing.assert_allclose(
+        oracle_scaled.scaled_tucker(f64("tucker/in0"), f64("tucker/in1"), w, norm), golden[f"tucker/{mode}/f64"], rtol=1e-12
+    )
+
+
+def test_golden_records_every_stable_mode(golden_programs):
+    """The reference accepts every golden program in all five stable modes."""
+    for name, spec in golden_programs.items():
+        assert set(spec["modes"]) == {"logspace_max", "logspace_min", "scaled_sum", "scaled_max", "scaled_min"}, name
