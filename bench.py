@@ -283,8 +283,19 @@ def time_region(fn, steps: int, warmup: int, dist_on: bool) -> float:
     return ms
 
 
+def large_matmul_step(a: torch.Tensor, b: torch.Tensor):
+    """One 8192^3 log-space contraction 'ik,kj->ij' (shifts + kernel)."""
+    from extended_einsum_b200 import ops
+
+    def step(record: bool) -> None:
+        ops.logspace_gemm(a, b)
+
+    return step
+
+
 def run_ours(args, rank: int, world: int, device: torch.device, dist_on: bool) -> dict | None:
     from extended_einsum_b200 import _lib
+    from extended_einsum_b200 import distributed as xd
 
     _lib.load()
     peaks = measured_peaks()
@@ -309,14 +320,22 @@ def run_ours(args, rank: int, world: int, device: torch.device, dist_on: bool) -
     scaled_ms = time_region(lambda record: work.scaled_step(), max(3, args.steps // 2), 3, dist_on) / max(3, args.steps // 2)
     scaled_value = world * work.flops_per_step / (scaled_ms * 1e-3) / 1e12
 
+    # the 8192^3 contraction (per GPU, weak), log(U(0,1)) values
+    gen = torch.Generator(device=device).manual_seed(4 + 1000 * rank)
+    big_a = torch.log(torch.rand(1, 8192, 8192, device=device, generator=gen))
+    big_b = torch.log(torch.rand(1, 8192, 8192, device=device, generator=gen))
+    big_ms = time_region(large_matmul_step(big_a, big_b), 5, 3, dist_on) / 5
+    big_value = world * 2.0 * 8192**3 / (big_ms * 1e-3) / 1e12
+    del big_a, big_b
+
     # secondary: the folded circuit, batch-sharded
     circ = Circuit(device, rank, args.circuit_batch)
 
     def circuit_step(record: bool) -> None:
         ll = circ.step()
         if dist_on:
-            gathered = torch.empty(world * circ.batch, 1, device=device)
-            torch.distributed.all_gather_into_tensor(gathered, ll)
+            # batch-sharded: the per-sample log-likelihoods of all ranks, in rank order
+            xd.gather_rows(ll, world * circ.batch)
 
     c_steps = max(3, args.steps // 2)
     c_ms = time_region(circuit_step, c_steps, max(3, args.warmup), dist_on) / c_steps
@@ -346,6 +365,11 @@ def run_ours(args, rank: int, world: int, device: torch.device, dist_on: bool) -
             "hbm_gbs_algorithmic": round(bytes_sample * c_value / world / 1e9, 1),
             "tflops_algorithmic": round(flops_sample * c_value / world / 1e12, 2),
             "e2e_samples_per_s": round(world * args.circuit_batch / (c_e2e_ms * 1e-3), 1),
+        },
+        "large_8192": {
+            "metric": "log-space einsum TFLOP/s, 'ik,kj->ij' 8192^3 per GPU", "value": round(big_value, 2), "unit": "TFLOP/s",
+            "ms_per_step": round(big_ms, 3), "frac_of_split_tf32_peak": round(big_value / world / (peaks["bf16_tflops"] / 6.0), 4),
+            "workload": "A, B = log(U(0,1)) 8192x8192 fp32, logspace_max, shift passes + contraction kernel",
         },
         "scaled_sum": {
             "metric": "log-space einsum TFLOP/s, scaled_sum mode", "value": round(scaled_value, 3), "unit": "TFLOP/s",

@@ -10,9 +10,10 @@ circuit), and a root sum 'ab,cb->ac'.
 
 Per forward pass the launches are:
   1  log-softmax of the categorical logits over the states      (xe_softmax, log output)
-  1  categorical gather of the per-pixel log-probabilities        (xe_categorical_gather)
   L  softmax of each level's sum-layer logits                     (xe_softmax)
-  L  CP sum layers, the Hadamard product fused into the A operand (xe_logspace_gemm, a2)
+  1  first CP sum layer with the categorical gather fused into
+     its A rows                                                   (xe_logspace_gemm_gather)
+  L-1 CP sum layers, the Hadamard product fused into the A operand (xe_logspace_gemm, a2)
   1  root softmax + 1 root sum layer                              (xe_softmax, xe_logspace_gemm)
 and the whole sequence can be captured in one CUDA graph.
 
@@ -107,20 +108,21 @@ class QuadTreeCircuit:
         return 2 * k * k * sum(self.fold_counts) + 2 * k
 
     def hbm_bytes_per_sample(self) -> int:
-        """Algorithmic HBM bytes per sample with the Hadamard fused into the next sum layer.
+        """HBM bytes per sample that the layer kernels must move.
 
-        Level 0 reads its (V, K) input and writes (V, K); level l >= 1 reads
-        the previous output (2F_l, K) and writes (F_l, K); the root reads
-        (2, K) and writes one value.  The gathered input is written once.
+        Level 0 reads the sample's V uint8 pixels (its categorical
+        log-probability rows come from a table that stays in L2) and writes
+        (V, K); level l >= 1 reads the previous output (2F_l, K), the two
+        Hadamard halves, and writes (F_l, K); the root reads (2, K) and
+        writes one value.  fp32 values.
         """
         k = self.units
         counts = self.fold_counts
-        elements = counts[0] * k  # gather output
-        elements += counts[0] * k + counts[0] * k  # level 0
+        elements = counts[0] * k  # level 0 output
         for f in counts[1:]:
             elements += 2 * f * k + f * k
         elements += 2 * k + 1
-        return 4 * elements
+        return 4 * elements + self.variables
 
 
 class CircuitForward:
@@ -138,13 +140,13 @@ class CircuitForward:
     def __call__(self, pixels: torch.Tensor) -> torch.Tensor:
         """Log-likelihoods (B, 1) of uint8 pixels (B, variables)."""
         table = ops.softmax(self.categorical, 1, log_output=True)
-        x = ops.categorical_gather(table, pixels, self.var_of_fold)
         y = None
         for level, logits in enumerate(self.levels):
             w = ops.softmax(logits, 2)  # (F, O, K) linear weights
             b_op = w.permute(0, 2, 1)  # (F, K, O), k contiguous
             if level == 0:
-                y = ops.logspace_gemm(x, b_op, b_linear=True, shift=self.shift)
+                # the categorical gather is fused into the first sum layer's A rows
+                y = ops.logspace_gemm_gather(table, pixels, self.var_of_fold, b_op, b_linear=True, shift=self.shift)
             else:
                 half = y.shape[0] // 2
                 y = ops.logspace_gemm(y[:half], b_op, a2=y[half:], b_linear=True, shift=self.shift)

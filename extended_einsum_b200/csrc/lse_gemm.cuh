@@ -74,6 +74,12 @@ struct Params {
   int a_vec;      // LDG source: rows are k-contiguous and 16-byte aligned
   int shift_min;  // row extremes computed in-kernel use min instead of max
   int raw_out;    // write the plain sums (linear operands, scaled modes) instead of log + shifts
+  // A rows gathered from a (folds, states, K) table by uint8 pixels (categorical input units
+  // feeding a sum layer): row (bb, m) = a + bb * a_sb + pixels[m * g_stride + var[bb]] * a_sm
+  const uint8_t* g_pixels;
+  const int32_t* g_var;  // nullptr: variable bb
+  int64_t g_stride;
+  int g_states;
   // Tucker layer: l (rows, folds, I), r (rows, folds, J) contiguous; batch = fold
   const float* tl;
   const float* tr;
@@ -94,7 +100,7 @@ struct Cfg {
   static constexpr int kStageBytes = 2 * kBTile;
   static constexpr int kRunningBytes = BN * kBM * 4;
   static constexpr int kShiftBytes = 2 * 2 * kBM * 4;  // [slot][s1,s2][row]
-  static constexpr int kColShiftBytes = 2 * BN * 4;    // [slot][BN]
+  static constexpr int kColShiftBytes = 4 * BN * 4;    // [drain warp][BN]
   static constexpr int kOutBytes = kBM * 32 * 4;       // one [128 rows][32 cols] output staging buffer
   static constexpr int kAStageBytes = ASRC == kATma2 ? 2 * kATileBytes : kATileBytes;
   // everything except the two TMA rings and the output staging
@@ -113,7 +119,10 @@ struct Cfg {
   static constexpr int kTmemA = 0;
   static constexpr int kTmemMain = 64 * kStages;
   static constexpr int kTmemCorr = kTmemMain + 2 * BN;
-  static constexpr int kTmemCols = pow2_at_least(kTmemCorr + BN);
+  // two correction accumulators (the next tile's MMAs need not wait for this
+  // tile's epilogue) where TMEM has room: BN <= 64
+  static constexpr int kCorrBufs = kTmemCorr + 2 * BN <= 512 ? 2 : 1;
+  static constexpr int kTmemCols = pow2_at_least(kTmemCorr + kCorrBufs * BN);
   static constexpr int kOffB = 0;
   static constexpr int kOffA = kOffB + kStages * kStageBytes;
   static constexpr int kOffBRaw = kOffA + kAStages * kAStageBytes;
@@ -123,7 +132,7 @@ struct Cfg {
   static constexpr int kOffOutAligned = (kOffColShift + kColShiftBytes + 1023) / 1024 * 1024;
   static constexpr int kOffBar = kOffOutAligned + kOutBufs * kOutBytes;
   static constexpr int kSmemBytes = 1024 + kOffBar + 512;
-  static_assert(kTmemCorr + BN <= 512, "TMEM");
+  static_assert(kTmemCorr + kCorrBufs * BN <= 512, "TMEM");
   // whether this combination fits (both rings at least double-buffered)
   static constexpr bool kFits = (ASRC == kALdg || kAStages >= 2) && (BSRC != kBTma || kBRawStages >= 2) &&
                                 kSmemBytes <= kSmemLimit;
@@ -257,7 +266,20 @@ struct ARow {
 
   __device__ void set_row(const Params& p, int bb, int m) {
     valid = m < p.M;
-    const int64_t base = (int64_t)bb * p.a_sb + (int64_t)(valid ? m : 0) * p.a_sm;
+    int64_t base = (int64_t)bb * p.a_sb + (int64_t)(valid ? m : 0) * p.a_sm;
+    if (p.g_pixels) {
+      int64_t v = p.g_var ? (int64_t)__ldg(p.g_var + bb) : (int64_t)bb;
+      if (v < 0 || v >= p.g_stride) {
+        record_bad_index(kSiteGemmGatherState);
+        v = 0;
+      }
+      int64_t state = valid ? (int64_t)__ldg(p.g_pixels + (int64_t)m * p.g_stride + v) : 0;
+      if (state >= p.g_states) {
+        record_bad_index(kSiteGemmGatherState);
+        state = p.g_states - 1;
+      }
+      base = (int64_t)bb * p.a_sb + state * p.a_sm;
+    }
     row = p.a + base;
     row2 = p.a2 ? p.a2 + base : nullptr;
     step = p.a_sk;
@@ -266,6 +288,21 @@ struct ARow {
   // Row extreme over all k by global loads (small K, global-load source).
   __device__ float scan_extreme(const Params& p, bool is_min) const {
     float e = is_min ? INFINITY : -INFINITY;
+    if (p.a_vec) {
+#pragma unroll 4
+      for (int k = 0; k < p.K; k += 4) {
+        float4 v = ldg_v4(row + k);
+        if (row2) {
+          const float4 w = ldg_v4(row2 + k);
+          v.x += w.x;
+          v.y += w.y;
+          v.z += w.z;
+          v.w += w.w;
+        }
+        e = extreme(extreme(e, v.x, is_min), extreme(v.y, extreme(v.z, v.w, is_min), is_min), is_min);
+      }
+      return e;
+    }
 #pragma unroll 8
     for (int k = 0; k < p.K; ++k) {
       float v = __ldg(row + k * step);
@@ -540,16 +577,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* empty = full + kStages;             // [kStages], tcgen05.commit
   uint64_t* chunk_full = empty + kStages;       // [2], tcgen05.commit
   uint64_t* chunk_empty = chunk_full + 2;       // [2], drain warps
-  uint64_t* corr_empty = chunk_empty + 2;       // [1], drain warps
-  uint64_t* shift_full = corr_empty + 1;        // [2], A warps
+  uint64_t* corr_empty = chunk_empty + 2;       // [kCorrBufs], drain warps
+  uint64_t* shift_full = corr_empty + 2;        // [2], A warps
   uint64_t* shift_empty = shift_full + 2;       // [2], drain warps
   uint64_t* a_full = shift_empty + 2;           // [4], TMA transactions
   uint64_t* a_empty = a_full + 4;               // [4], A warps
   uint64_t* b_full = a_empty + 4;               // [4], TMA transactions
   uint64_t* b_empty = b_full + 4;               // [4], B warps
   uint64_t* drain = b_empty + 4;                // [1], teardown
-  uint64_t* drain_sync = drain + 1;             // [1], barrier among the drain warps
-  uint32_t* tmem_slot = (uint32_t*)(drain_sync + 1);
+  uint32_t* tmem_slot = (uint32_t*)(drain + 1);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -572,9 +608,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&b_full[s], 1);
       mbar_init(&b_empty[s], kBWarps);
     }
-    mbar_init(corr_empty, kDrainWarps);
+    for (int c = 0; c < C::kCorrBufs; ++c) mbar_init(&corr_empty[c], kDrainWarps);
     mbar_init(drain, 1);
-    mbar_init(drain_sync, kDrainWarps);
     *abort_flag = 0;
     fence_mbarrier_init();
   }
@@ -600,6 +635,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int m = mt * kBM + r;
       // -------- row shifts
       float s1 = 0.0f, s2 = 0.0f;
+      float cur[32], nxt[32];
+      bool preloaded = false;  // global-load source: both k-blocks of the tile already in cur / nxt
       if (AMODE == kATucker) {
         a.tucker_row(p, bb, m, true);
         s1 = a.sl;
@@ -610,24 +647,61 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (p.shift_a) {
             a.shift = a.valid ? __ldg(p.shift_a + (int64_t)bb * p.M + m) : 0.0f;
           } else if (ASRC != kALdg) {
-            // every k-block of this tile is staged (num_kb <= kAStages): scan them
+            // every k-block of this tile is staged (num_kb <= kAStages): scan them.  A row of
+            // at most two k-blocks stays in registers (cur, nxt) and its stages are released here.
             float e = is_min ? INFINITY : -INFINITY;
+            const bool keep = p.num_kb <= 2;
             for (int kb = 0; kb < p.num_kb; ++kb) {
               const uint32_t sidx = (ait + kb) % C::kAStages;
               if (!mbar_wait(&a_full[sidx], ((ait + kb) / C::kAStages) & 1, kSiteAStaged, abort_flag)) {
                 ok = false;
                 break;
               }
-              float v[32];
               const int kvalid = p.K - kb * kBK;
-              load_staged_row<ASRC>(smem_base + C::kOffA + sidx * C::kAStageBytes, r, a.valid, kvalid, fill, v);
+              const uint32_t stage = smem_base + C::kOffA + sidx * C::kAStageBytes;
               // the k tail is masked with -inf for exp(); it must not enter a min
+              if (keep && kb == 0) {
+                load_staged_row<ASRC>(stage, r, a.valid, kvalid, fill, cur);
 #pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (j < kvalid) e = extreme(e, v[j], is_min);
+                for (int j = 0; j < 32; ++j)
+                  if (j < kvalid) e = extreme(e, cur[j], is_min);
+              } else if (keep) {
+                load_staged_row<ASRC>(stage, r, a.valid, kvalid, fill, nxt);
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  if (j < kvalid) e = extreme(e, nxt[j], is_min);
+              } else {
+                float v[32];
+                load_staged_row<ASRC>(stage, r, a.valid, kvalid, fill, v);
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  if (j < kvalid) e = extreme(e, v[j], is_min);
+              }
             }
             if (!ok) break;
+            if (keep) {
+              __syncwarp();
+              if (lane == 0)
+                for (int kb = 0; kb < p.num_kb; ++kb) mbar_arrive(&a_empty[(ait + kb) % C::kAStages]);
+              ait += p.num_kb;
+              preloaded = true;
+            }
             a.shift = a.valid ? e : 0.0f;
+          } else if (p.num_kb <= 2) {
+            // global-load source, one or two k-blocks: load the row once, scan it in registers
+            a.load_global(p, 0, cur);
+            if (p.num_kb == 2) a.load_global(p, kBK, nxt);
+            float e = is_min ? INFINITY : -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j < p.K) e = extreme(e, cur[j], is_min);
+            if (p.num_kb == 2) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (kBK + j < p.K) e = extreme(e, nxt[j], is_min);
+            }
+            a.shift = a.valid ? e : 0.0f;
+            preloaded = true;
           } else {
             a.shift = a.valid ? a.scan_extreme(p, is_min) : 0.0f;
           }
@@ -644,11 +718,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive(&shift_full[slot]);
       }
       // -------- k loop
-      float cur[32], nxt[32];
-      if (ASRC == kALdg) a.load_global(p, 0, cur);
+      if (ASRC == kALdg && !preloaded) a.load_global(p, 0, cur);
       for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
         XE_SEGMENT_BEGIN(seg_load);
-        if (ASRC != kALdg) {
+        if (ASRC != kALdg && !preloaded) {
           const uint32_t sidx = ait % C::kAStages;
           if (!mbar_wait(&a_full[sidx], (ait / C::kAStages) & 1, kSiteAStaged, abort_flag)) {
             ok = false;
@@ -659,7 +732,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(&a_empty[sidx]);
           ++ait;
-        } else if (kb + 1 < p.num_kb) {
+        } else if (ASRC == kALdg && kb + 1 < p.num_kb && !preloaded) {
           a.load_global(p, (kb + 1) * kBK, nxt);
         }
         XE_SEGMENT_END(seg_load, 1);
@@ -691,7 +764,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&full[s]);
-        if (ASRC == kALdg && kb + 1 < p.num_kb) {
+        if ((ASRC == kALdg || preloaded) && kb + 1 < p.num_kb) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) cur[j] = nxt[j];
         }
@@ -756,11 +829,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t it = 0, gc = 0, tl = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++tl) {
-        if (!mbar_wait(corr_empty, (tl & 1) ^ 1, kSiteMmaCorr, abort_flag)) {
+        const uint32_t cbuf = tl % C::kCorrBufs;
+        if (!mbar_wait(&corr_empty[cbuf], ((tl / C::kCorrBufs) & 1) ^ 1, kSiteMmaCorr, abort_flag)) {
           ok = false;
           break;
         }
-        const uint32_t d_corr = tmem + C::kTmemCorr;
+        const uint32_t d_corr = tmem + C::kTmemCorr + cbuf * BN;
         uint32_t d_main = 0;
         for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
           const int kc = kb % kChunkKB;
@@ -807,18 +881,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;  // TMEM lane quadrant of this warp
     const int r = q * 32 + lane;
     const uint32_t lane_bits = (uint32_t)(q * 32) << 16;
-    float* col_shift = (float*)(smem + C::kOffColShift);
-    uint32_t gc = 0, tl = 0, ob = 0, syncs = 0;
+    // Each drain warp owns TMEM lanes (rows) 32q..32q+31 from the accumulator
+    // to the copy-out, so the drain warps never wait for one another.
+    uint32_t gc = 0, tl = 0, ob = 0;
     bool ok = true;
-    // barrier among the four drain warps (bounded, like every wait here)
-    auto sync_drain = [&]() -> bool {
-      __syncwarp();
-      if (lane == 0) mbar_arrive(drain_sync);
-      const bool done = mbar_wait(drain_sync, syncs & 1, kSiteDrainShift, abort_flag);
-      ++syncs;
-      if (!done) ok = false;
-      return done;
-    };
     const int chunks = (p.num_kb + kChunkKB - 1) / kChunkKB;
     for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++tl) {
       int bb, mt, nt;
@@ -840,7 +906,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int sl = 0; sl < BN / 32; ++sl) {
           float v[32], w[32];
           tmem_ld32(tmem + lane_bits + C::kTmemMain + cb * BN + sl * 32, v);
-          if (last) tmem_ld32(tmem + lane_bits + C::kTmemCorr + sl * 32, w);
+          if (last) tmem_ld32(tmem + lane_bits + C::kTmemCorr + (tl % C::kCorrBufs) * BN + sl * 32, w);
           tmem_wait_ld();
           float* run = running + sl * 32 * kBM + r;
 #pragma unroll
@@ -856,7 +922,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(&chunk_empty[cb]);
-          if (last) mbar_arrive(corr_empty);  // TMEM is free for the next tile
+          if (last) mbar_arrive(&corr_empty[tl % C::kCorrBufs]);  // this correction buffer is free
         }
       }
       if (!ok) break;
@@ -876,19 +942,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float s2 = shifts[(slot * 2 + 1) * kBM + r];
       __syncwarp();
       if (lane == 0) mbar_arrive(&shift_empty[slot]);
-      float* cshift = col_shift + slot * BN;
-      if (r < BN) cshift[r] = (p.shift_b && n0 + r < p.N) ? __ldg(p.shift_b + (int64_t)bb * p.N + n0 + r) : 0.0f;
-      if (!sync_drain()) break;
+      // column shifts of a log-domain B, copied into this warp's own slice of shared memory
+      float* cshift = p.shift_b ? (float*)(smem + C::kOffColShift) + q * BN : nullptr;
+      if (cshift) {
+#pragma unroll
+        for (int c = lane; c < BN; c += 32) cshift[c] = (n0 + c < p.N) ? __ldg(p.shift_b + (int64_t)bb * p.N + n0 + c) : 0.0f;
+        __syncwarp();
+      }
+      XE_SEGMENT_END(seg_ep, 7);
       float* cbase = p.c + (int64_t)bb * p.c_sb;
 #pragma unroll 1
       for (int sl = 0; sl < BN / 32; ++sl) {
         const float* run = running + sl * 32 * kBM + r;  // this row's 32 sums of the slice
         float out[32];
+        XE_SEGMENT_BEGIN(seg_e1);
         if (direct) {
           // single chunk: the sums come straight from TMEM (main + corr)
           float v[32], w[32];
           tmem_ld32(tmem + lane_bits + C::kTmemMain + dcb * BN + sl * 32, v);
-          tmem_ld32(tmem + lane_bits + C::kTmemCorr + sl * 32, w);
+          tmem_ld32(tmem + lane_bits + C::kTmemCorr + (tl % C::kCorrBufs) * BN + sl * 32, w);
           tmem_wait_ld();
 #pragma unroll
           for (int j = 0; j < 32; ++j) out[j] = isinf(v[j]) ? v[j] : v[j] + w[j];
@@ -897,23 +969,26 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) {
               mbar_arrive(&chunk_empty[dcb]);
-              mbar_arrive(corr_empty);
+              mbar_arrive(&corr_empty[tl % C::kCorrBufs]);
             }
           }
         } else {
 #pragma unroll
           for (int j = 0; j < 32; ++j) out[j] = run[j * kBM];
         }
+        XE_SEGMENT_END(seg_e1, 8);
+        XE_SEGMENT_BEGIN(seg_e2);
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           if (p.raw_out) continue;
           float o = fast_log(out[j]);
           if (AMODE != kALinear) o += s1;
           if (AMODE == kATucker) o += s2;
-          if (p.shift_b) o += cshift[sl * 32 + j];
+          if (cshift) o += cshift[sl * 32 + j];
           out[j] = o;
         }
-        if (C::kOutBufs == 1 && !sync_drain()) break;  // the single buffer's previous copy-out is done
+        // every warp stages and copies out its own 32 rows: warp-level ordering suffices
+        if (C::kOutBufs == 1) __syncwarp();  // the single buffer's previous copy-out is done
         // staging buffer as [128 rows][32 cols], 16-byte chunks swizzled by (row & 7)
         const uint32_t stage = smem_base + C::kOffOutAligned + (ob % C::kOutBufs) * C::kOutBytes;
         ++ob;
@@ -921,7 +996,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int j = 0; j < 8; ++j)
           sts_v4(srow + ((j ^ (r & 7)) << 4), make_float4(out[4 * j], out[4 * j + 1], out[4 * j + 2], out[4 * j + 3]));
-        if (!sync_drain()) break;
+        XE_SEGMENT_END(seg_e2, 9);
+        XE_SEGMENT_BEGIN(seg_e3);
+        __syncwarp();
+        XE_SEGMENT_END(seg_e3, 10);
+        XE_SEGMENT_BEGIN(seg_e4);
         // coalesced copy-out: each warp writes 32 rows, 4 rows (512 B) per instruction
         const int chunk = lane & 7;
         const int n = n0 + sl * 32 + 4 * chunk;
@@ -941,8 +1020,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (n + 3 < p.N) dst[(int64_t)(n + 3) * p.c_sn] = val.w;
           }
         }
+        XE_SEGMENT_END(seg_e4, 11);
       }
-      XE_SEGMENT_END(seg_ep, 6);
     }
   } else if ((ASRC != kALdg || BSRC == kBTma) && lane == 0) {
     // ------------------------------------------------------------ TMA producer

@@ -308,8 +308,16 @@ __global__ void __launch_bounds__(256) categorical_gather4(const float* __restri
     const int64_t q = g % uq;
     const int64_t row = g / uq;  // f*batch + b
     const int64_t f = row / batch, b = row - f * batch;
-    const int64_t v = var_of_fold ? (int64_t)__ldg(var_of_fold + f) : f;
-    const int64_t s = (int64_t)__ldg(pixels + b * ps + v);
+    int64_t v = var_of_fold ? (int64_t)__ldg(var_of_fold + f) : f;
+    if (v < 0 || v >= ps) {
+      record_bad_index(kSiteGatherState);
+      v = 0;
+    }
+    int64_t s = (int64_t)__ldg(pixels + b * ps + v);
+    if (s >= states) {
+      record_bad_index(kSiteGatherState);
+      s = states - 1;
+    }
     const float4 t = ldg_nc_v4(table + (f * states + s) * units + 4 * q);
     stg_v4(y + row * units + 4 * q, t);
   }
@@ -325,8 +333,16 @@ __global__ void __launch_bounds__(256) categorical_gather1(const float* __restri
     const int64_t u = g % units;
     const int64_t row = g / units;
     const int64_t f = row / batch, b = row - f * batch;
-    const int64_t v = var_of_fold ? (int64_t)__ldg(var_of_fold + f) : f;
-    const int64_t s = (int64_t)__ldg(pixels + b * ps + v);
+    int64_t v = var_of_fold ? (int64_t)__ldg(var_of_fold + f) : f;
+    if (v < 0 || v >= ps) {
+      record_bad_index(kSiteGatherState);
+      v = 0;
+    }
+    int64_t s = (int64_t)__ldg(pixels + b * ps + v);
+    if (s >= states) {
+      record_bad_index(kSiteGatherState);
+      s = states - 1;
+    }
     y[g] = __ldg(table + (f * states + s) * units + u);
   }
 }
@@ -525,6 +541,32 @@ __global__ void __launch_bounds__(256) elementwise_nd(const float* __restrict__ 
       oc += idx * s.cs[d];
     }
     y[g] = elementwise_apply<OP>(a[oa], b ? b[ob] : 0.0f, c ? c[oc] : 0.0f);
+  }
+}
+
+// One warp per row of the last axis: the index arithmetic of the leading axes
+// is done once per row, the row itself is streamed (coalesced where the last
+// axis is contiguous, a broadcast scale read once per row where its stride is 0).
+template <int OP>
+__global__ void __launch_bounds__(256) elementwise_rows(const float* __restrict__ a, const float* __restrict__ b,
+                                                        const float* __restrict__ c, float* __restrict__ y, NdShape3 s,
+                                                        int64_t rows, int64_t n) {
+  const int lane = threadIdx.x & 31;
+  const int last = s.ndim - 1;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < rows; row += warps) {
+    int64_t rem = row, oa = 0, ob = 0, oc = 0;
+    for (int d = last - 1; d >= 0; --d) {
+      const int64_t idx = rem % s.shape[d];
+      rem /= s.shape[d];
+      oa += idx * s.as[d];
+      ob += idx * s.bs[d];
+      oc += idx * s.cs[d];
+    }
+    float* py = y + row * n;
+    for (int64_t j = lane; j < n; j += 32)
+      py[j] = elementwise_apply<OP>(a[oa + j * s.as[last]], b ? b[ob + j * s.bs[last]] : 0.0f,
+                                    c ? c[oc + j * s.cs[last]] : 0.0f);
   }
 }
 

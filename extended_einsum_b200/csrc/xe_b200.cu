@@ -223,12 +223,12 @@ int staged_k_capacity(int bn, int asrc, int bsrc) {
 
 GemmPlan plan_gemm(const float* a, const float* a2, int64_t a_sb, int64_t a_sm, int64_t a_sk, bool a_linear,
                    const float* b, int64_t b_sb, int64_t b_sk, int64_t b_sn, int64_t batch, int64_t m, int64_t n,
-                   int64_t k) {
+                   int64_t k, bool a_rows_gathered = false) {
   using namespace xe::gemm;
   GemmPlan g;
   g.bn = pick_bn(n);
   const bool no_tma = env_int("XE_GEMM_NO_TMA", 0) != 0;
-  const bool a_tma = !no_tma && a_sk == 1 && (a_sm != 1 || m == 1) && encode_a_map(&g.ma, a, batch, m, k, a_sm, a_sb) &&
+  const bool a_tma = !no_tma && !a_rows_gathered && a_sk == 1 && (a_sm != 1 || m == 1) && encode_a_map(&g.ma, a, batch, m, k, a_sm, a_sb) &&
                      (a2 == nullptr || encode_a_map(&g.ma2, a2, batch, m, k, a_sm, a_sb));
   if (a_tma) g.asrc = a2 ? kATma2 : kATma;
   // B staging layout: K-major unless the N axis is the unit-stride one
@@ -389,11 +389,19 @@ xe_status xe_logspace_shift(const float* x, const float* x2, int64_t sb, int64_t
 
 namespace {
 
+// A rows gathered by uint8 pixel values (categorical input units, see Params::g_pixels).
+struct GatherA {
+  const uint8_t* pixels;
+  const int32_t* var;
+  int64_t stride;
+  int states;
+};
+
 xe_status gemm_launch(const float* a, const float* a2, int64_t a_sb, int64_t a_sm, int64_t a_sk, bool a_linear,
                       const float* shift_a, const float* b, int64_t b_sb, int64_t b_sk, int64_t b_sn,
                       const float* shift_b, float* c, int64_t c_sb, int64_t c_sm, int64_t c_sn, int64_t batch, int64_t m,
                       int64_t n, int64_t k, bool shift_min, const GemmPlan& g, cudaStream_t s,
-                      bool raw_out = false) {
+                      bool raw_out = false, const GatherA* gather = nullptr) {
   Params p{};
   p.a = a;
   p.a2 = a2;
@@ -419,6 +427,13 @@ xe_status gemm_launch(const float* a, const float* a2, int64_t a_sb, int64_t a_s
              (a2 == nullptr || aligned16(a2))) ? 1 : 0;
   p.shift_min = shift_min ? 1 : 0;
   p.raw_out = raw_out ? 1 : 0;
+  if (gather) {
+    p.g_pixels = gather->pixels;
+    p.g_var = gather->var;
+    p.g_stride = gather->stride;
+    p.g_states = gather->states;
+    p.a_vec = (k % 4 == 0 && a_sm % 4 == 0 && a_sb % 4 == 0 && aligned16(a)) ? 1 : 0;
+  }
   const bool bk = !(b_sn == 1) && b_sk == 1;
   return launch_gemm(p, g, a_linear, bk, s);
 }
@@ -531,6 +546,44 @@ xe_status xe_logspace_gemm_noalloc(const float* a, const float* a2, int64_t a_sb
   if (st != XE_OK) return st;
   return xe_logspace_gemm(a, a2, a_sb, a_sm, a_sk, a_linear, b, b_sb, b_sk, b_sn, b_linear, c, c_sb, c_sm, c_sn, batch,
                           m, n, k, shift_mode, scratch, XE_NOALLOC_SCRATCH_BYTES, stream);
+}
+
+xe_status xe_logspace_gemm_gather(const float* table, int64_t t_sf, int64_t t_ss, int64_t states, const uint8_t* pixels,
+                                  int64_t pixel_stride, const int32_t* var_of_fold, const float* b, int64_t b_sb,
+                                  int64_t b_sk, int64_t b_sn, int32_t b_linear, float* c, int64_t c_sb, int64_t c_sm,
+                                  int64_t c_sn, int64_t folds, int64_t batch, int64_t n, int64_t k, int32_t shift_mode,
+                                  void* workspace, size_t workspace_bytes, void* stream) {
+  xe_status st = gemm_check("xe_logspace_gemm_gather", table, b, c, folds, batch, n, k);
+  if (st != XE_OK) return st;
+  if (!pixels) return fail(XE_ERR_INVALID_ARGUMENT, "xe_logspace_gemm_gather: null pixels");
+  if (states <= 0 || states > 256)
+    return fail(XE_ERR_INVALID_ARGUMENT, "xe_logspace_gemm_gather: uint8 pixels address 1 to 256 states (got %lld)",
+                (long long)states);
+  if (pixel_stride <= 0) return fail(XE_ERR_INVALID_ARGUMENT, "xe_logspace_gemm_gather: pixel_stride must be positive");
+  if (shift_mode != XE_SHIFT_MAX && shift_mode != XE_SHIFT_MIN)
+    return fail(XE_ERR_INVALID_ARGUMENT, "xe_logspace_gemm_gather: unknown shift mode %d", shift_mode);
+  if (k > 128)
+    return fail(XE_ERR_NOT_SUPPORTED, "xe_logspace_gemm_gather: at most 128 units per input row (got %lld)", (long long)k);
+  if (folds == 0 || batch == 0 || n == 0) return XE_OK;
+  const size_t need = xe_logspace_gemm_workspace_size(folds, batch, n, k, 1, b_linear);
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need))
+    return fail(XE_ERR_INVALID_ARGUMENT, "xe_logspace_gemm_gather: workspace of %zu bytes required, %zu given", need,
+                workspace_bytes);
+  if ((reinterpret_cast<uintptr_t>(workspace) & (kAlign - 1)) != 0)
+    return fail(XE_ERR_INVALID_ARGUMENT, "xe_logspace_gemm_gather: workspace must be 256-byte aligned");
+  cudaStream_t s = as_stream(stream);
+  float* shift_b = nullptr;
+  if (!b_linear) {
+    shift_b = static_cast<float*>(workspace);
+    st = shift_impl(b, nullptr, b_sb, b_sn, b_sk, folds, n, k, shift_mode == XE_SHIFT_MAX, shift_b, s);
+    if (st != XE_OK) return st;
+  }
+  // the A rows are gathered per thread (global loads), their shifts computed in the kernel
+  GemmPlan plan = plan_gemm(table, nullptr, t_sf, t_ss, 1, false, b, b_sb, b_sk, b_sn, folds, batch, n, k, true);
+  plan.inline_shift = true;
+  const GatherA gather{pixels, var_of_fold, pixel_stride, (int)states};
+  return gemm_launch(table, nullptr, t_sf, t_ss, 1, false, nullptr, b, b_sb, b_sk, b_sn, shift_b, c, c_sb, c_sm, c_sn,
+                     folds, batch, n, k, shift_mode == XE_SHIFT_MIN, plan, s, false, &gather);
 }
 
 xe_status xe_logspace_gemm_shifted(const float* a, const float* a2, int64_t a_sb, int64_t a_sm, int64_t a_sk,
@@ -781,6 +834,11 @@ void launch_elementwise(const float* a, const float* b, const float* c, float* y
     xe::elementwise_contig4<OP><<<(unsigned)grid_for(n4, 256, cap), 256, 0, s>>>(
         reinterpret_cast<const float4*>(a), reinterpret_cast<const float4*>(b), reinterpret_cast<const float4*>(c),
         reinterpret_cast<float4*>(y), n4);
+  } else if (sh.ndim >= 1 && sh.shape[sh.ndim - 1] >= 32) {
+    const int64_t n = sh.shape[sh.ndim - 1];
+    const int64_t rows = total / n;
+    xe::elementwise_rows<OP><<<(unsigned)grid_for(rows, 8, (int64_t)current_device_sms() * 16), 256, 0, s>>>(
+        a, b, c, y, sh, rows, n);
   } else {
     xe::elementwise_nd<OP><<<(unsigned)grid_for(total, 256, cap), 256, 0, s>>>(a, b, c, y, sh, total);
   }

@@ -58,6 +58,14 @@ __device__ __forceinline__ void record_timeout(int site) {
   atomicCAS(&g_device_status, 0, (XE_ERR_DEVICE_TIMEOUT << 16) | site);
 }
 
+// Data-dependent index checks (a uint8 pixel value at or above the number of
+// states): the access is clamped into bounds and the first offence recorded.
+enum IndexSite : int { kSiteGatherState = 32, kSiteGemmGatherState = 33 };
+
+__device__ __forceinline__ void record_bad_index(int site) {
+  atomicCAS(&g_device_status, 0, (XE_ERR_INVALID_ARGUMENT << 16) | site);
+}
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

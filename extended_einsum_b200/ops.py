@@ -296,6 +296,55 @@ def categorical_gather(
     return y
 
 
+def logspace_gemm_gather(
+    log_table: torch.Tensor,
+    pixels: torch.Tensor,
+    var_of_fold: torch.Tensor | None,
+    b: torch.Tensor,
+    *,
+    b_linear: bool = False,
+    shift: str = "max",
+) -> torch.Tensor:
+    """C[f,b,n] = log(sum_k exp(T[f, pixels[b, var[f]], k] - s) B'[f,k,n]) + shifts (xe_logspace_gemm_gather).
+
+    The categorical input gather fused into the first sum layer: ``log_table``
+    is (folds, states, K) with K contiguous, ``pixels`` (batch, variables)
+    uint8, ``b`` (folds, K, N).  Returns (folds, batch, N).
+    """
+    device = _check_tensors("logspace_gemm_gather", log_table, b)
+    if pixels.device != device or pixels.dtype != torch.uint8 or pixels.dim() != 2:
+        raise ValueError("logspace_gemm_gather: pixels must be a (batch, variables) uint8 tensor on the table's device")
+    if pixels.stride(1) != 1:
+        pixels = pixels.contiguous()
+    if log_table.dim() != 3 or b.dim() != 3:
+        raise ValueError("logspace_gemm_gather: expected a (folds, states, K) table and a (folds, K, N) operand")
+    if log_table.stride(2) != 1:
+        log_table = log_table.contiguous()
+    folds, states, k = log_table.shape
+    if b.shape[0] != folds or b.shape[1] != k:
+        raise ValueError(f"logspace_gemm_gather: incompatible shapes {tuple(log_table.shape)} and {tuple(b.shape)}")
+    if var_of_fold is not None:
+        if var_of_fold.dtype != torch.int32 or var_of_fold.device != device or var_of_fold.numel() != folds:
+            raise ValueError("logspace_gemm_gather: var_of_fold must be int32 with one entry per fold")
+        var_of_fold = var_of_fold.contiguous()
+    elif pixels.shape[1] < folds:
+        raise ValueError("logspace_gemm_gather: fewer pixel variables than folds")
+    batch = pixels.shape[0]
+    n = b.shape[2]
+    out = torch.empty((folds, batch, n), device=device, dtype=torch.float32)
+    lib = _lib.load()
+    ws_bytes = lib.xe_logspace_gemm_workspace_size(folds, batch, n, k, 1, int(b_linear))
+    ws = torch.empty(ws_bytes, device=device, dtype=torch.uint8) if ws_bytes else None
+    status = lib.xe_logspace_gemm_gather(
+        log_table.data_ptr(), log_table.stride(0), log_table.stride(1), states, pixels.data_ptr(), pixels.stride(0),
+        _ptr(var_of_fold), b.data_ptr(), b.stride(0), b.stride(1), b.stride(2), int(b_linear),
+        out.data_ptr(), out.stride(0), out.stride(1), out.stride(2), folds, batch, n, k, _shift(shift),
+        _ptr(ws), ws_bytes, _stream(device),
+    )
+    _lib.check(status, "xe_logspace_gemm_gather")
+    return out
+
+
 def logspace_tucker(
     left: torch.Tensor, right: torch.Tensor, weights: torch.Tensor, *, shift: str = "max"
 ) -> torch.Tensor:

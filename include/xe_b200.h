@@ -189,6 +189,26 @@ xe_status xe_categorical_gather(const float* table, const uint8_t* pixels, int64
                                 const int32_t* var_of_fold, float* y, int64_t folds, int64_t states,
                                 int64_t units, int64_t batch, void* stream);
 
+/* The first sum layer of a circuit over categorical input units, with the
+ * gather fused into the contraction (replaces xe_categorical_gather followed
+ * by xe_logspace_gemm on its output; demo/cirkit.py:525-527 feeding the
+ * folded CP layer 'dac,dbc->dab', preprocess.py:1310-1337, lowered by
+ * translate.py:686-750):
+ *   C[f,b,n] = log( sum_k exp(T[f, x_b, k] - s) B'[f,k,n] ) + s (+ B's shift)
+ *   with x_b = pixels[b*pixel_stride + var_of_fold[f]] and s = max (or min)
+ *   over k of T[f, x_b, :].
+ * T is the (folds, states, k) log table, k contiguous, fold stride t_sf and
+ * state stride t_ss in elements.  B and C as in xe_logspace_gemm (batch =
+ * folds, M = batch of samples).  var_of_fold may be NULL for the identity;
+ * its entries must lie in [0, pixel_stride).  k <= 128.  A pixel value at or
+ * above `states` (or a variable out of range) is clamped and recorded:
+ * xe_device_status() then reports XE_ERR_INVALID_ARGUMENT << 16. */
+xe_status xe_logspace_gemm_gather(const float* table, int64_t t_sf, int64_t t_ss, int64_t states, const uint8_t* pixels,
+                                  int64_t pixel_stride, const int32_t* var_of_fold, const float* b, int64_t b_sb,
+                                  int64_t b_sk, int64_t b_sn, int32_t b_linear, float* c, int64_t c_sb, int64_t c_sm,
+                                  int64_t c_sn, int64_t folds, int64_t batch, int64_t n, int64_t k, int32_t shift_mode,
+                                  void* workspace, size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Log-space Tucker layer 'bfi,bfj,foij->bfo' (the ternary einsum that
  * OptimizeContractionPaths fuses for Tucker circuits, preprocess.py:1095-1106,

@@ -65,3 +65,36 @@ def test_full_circuit_configuration_sample():
 
 def test_no_device_wait_timed_out():
     assert ops.device_status() == 0
+
+
+@pytest.mark.parametrize("folds,states,units,batch,n,b_linear", [(16, 256, 64, 1000, 64, True), (6, 7, 32, 130, 40, False), (3, 256, 128, 257, 1, True)])
+def test_gemm_gather_equals_gather_then_gemm(folds, states, units, batch, n, b_linear):
+    """The fused first sum layer == xe_categorical_gather followed by xe_logspace_gemm."""
+    g = torch.Generator().manual_seed(folds * states + units)
+    variables = folds + 3
+    table = torch.log_softmax(torch.randn(folds, states, units, generator=g), dim=1).cuda()
+    pixels = torch.randint(states, (batch, variables), generator=g, dtype=torch.uint8).cuda()
+    var = torch.randperm(variables, generator=g)[:folds].to(torch.int32).cuda()
+    b = (torch.rand(folds, units, n, generator=g) if b_linear else torch.randn(folds, units, n, generator=g)).cuda()
+    fused = ops.logspace_gemm_gather(table, pixels, var, b, b_linear=b_linear)
+    x = ops.categorical_gather(table, pixels, var)
+    unfused = ops.logspace_gemm(x, b, b_linear=b_linear)
+    log_close(fused.cpu().numpy(), unfused.cpu().numpy(), atol=2e-6, rtol=2e-7)
+    assert ops.device_status() == 0
+
+
+def test_out_of_range_pixels_are_clamped_and_reported():
+    g = torch.Generator().manual_seed(5)
+    table = torch.log_softmax(torch.randn(4, 10, 32, generator=g), dim=1).cuda()
+    pixels = torch.randint(10, (64, 4), generator=g, dtype=torch.uint8)
+    pixels[5, 2] = 250  # no such state
+    pixels = pixels.cuda()
+    b = torch.rand(4, 32, 32, generator=g).cuda()
+    assert ops.device_status() == 0
+    ops.logspace_gemm_gather(table, pixels, None, b, b_linear=True)
+    status = ops.device_status(clear=True)
+    assert status >> 16 == 1 and status & 0xFFFF == 33  # XE_ERR_INVALID_ARGUMENT, the fused-gather site
+    ops.categorical_gather(table, pixels, None)
+    status = ops.device_status(clear=True)
+    assert status >> 16 == 1 and status & 0xFFFF == 32
+    assert ops.device_status() == 0

@@ -105,7 +105,7 @@ def test_circuit_cost_model():
     c = QuadTreeCircuit(32, 32, 64, 256)
     assert c.fold_counts == [1024 >> l for l in range(10)]
     assert c.flops_per_sample() == 2 * 64 * 64 * 2046 + 2 * 64
-    assert c.hbm_bytes_per_sample() == 4 * 64 * (1024 * 3 + 3 * (512 + 256 + 128 + 64 + 32 + 16 + 8 + 4 + 2)) + 4 * (2 * 64 + 1)
+    assert c.hbm_bytes_per_sample() == 4 * 64 * (1024 + 3 * (512 + 256 + 128 + 64 + 32 + 16 + 8 + 4 + 2)) + 4 * (2 * 64 + 1) + 1024
 
 
 REFERENCE_SRC = Path("/root/reference/src")
