@@ -426,6 +426,17 @@ def main() -> None:
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
+        if world > 1:
+            # torchrun pins every rank to one OpenMP thread; rank 0 times the CPU path in a
+            # fresh process with the host's threads, the other ranks have nothing to do
+            if rank == 0:
+                env = {k: v for k, v in os.environ.items()
+                       if k not in ("OMP_NUM_THREADS", "MKL_NUM_THREADS", "WORLD_SIZE", "RANK", "LOCAL_RANK",
+                                    "LOCAL_WORLD_SIZE", "GROUP_RANK", "ROLE_RANK", "TORCHELASTIC_RUN_ID")}
+                import subprocess
+
+                subprocess.run([sys.executable, str(Path(__file__).resolve()), *sys.argv[1:]], env=env, check=True)
+            return
         line = run_reference(args, rank)
         if line is not None:
             print(json.dumps(line), flush=True)
