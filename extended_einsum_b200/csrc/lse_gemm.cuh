@@ -100,14 +100,19 @@ struct Cfg {
   static constexpr int kStageBytes = 2 * kBTile;
   static constexpr int kRunningBytes = BN * kBM * 4;
   static constexpr int kShiftBytes = 2 * 2 * kBM * 4;  // [slot][s1,s2][row]
-  static constexpr int kColShiftBytes = 4 * BN * 4;    // [drain warp][BN]
+  // Tiles of at most 64 columns have little tensor work per tile and are
+  // bound by the epilogue: two drain warp groups take alternate tiles
+  // (warps 14..17 join 9..12; each group owns one staging buffer).
+  static constexpr int kDrainGroups = BN <= 64 ? 2 : 1;
+  static constexpr int kThreads = (kProducerWarp + 1 + 4 * (kDrainGroups - 1)) * 32;
+  static constexpr int kColShiftBytes = 4 * kDrainGroups * BN * 4;  // [drain warp][BN]
   static constexpr int kOutBytes = kBM * 32 * 4;       // one [128 rows][32 cols] output staging buffer
   static constexpr int kAStageBytes = ASRC == kATma2 ? 2 * kATileBytes : kATileBytes;
   // everything except the two TMA rings and the output staging
   static constexpr int kFixed = 1024 + kStages * kStageBytes + kRunningBytes + kShiftBytes + kColShiftBytes + 512;
   static constexpr int kBRawBytes = BSRC == kBTma ? kBTile : 0;
   static constexpr int kMinRings = (ASRC == kALdg ? 0 : 2 * kAStageBytes) + 2 * kBRawBytes;
-  static constexpr int kOutBufs = (kFixed + kMinRings + 2 * kOutBytes <= kSmemLimit) ? 2 : 1;
+  static constexpr int kOutBufs = (kDrainGroups == 2 || kFixed + kMinRings + 2 * kOutBytes <= kSmemLimit) ? 2 : 1;
   static constexpr int kRingBudget = kSmemLimit - kFixed - kOutBufs * kOutBytes - 1024;
   // up to four stages per ring, A first
   static constexpr int kAStages =
@@ -182,6 +187,20 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
       "f"(v[19]), "f"(v[20]), "f"(v[21]), "f"(v[22]), "f"(v[23]), "f"(v[24]), "f"(v[25]), "f"(v[26]), "f"(v[27]),
       "f"(v[28]), "f"(v[29]), "f"(v[30]), "f"(v[31])
       : "memory");
+}
+
+// 16 consecutive fp32 columns of the calling warp's 32 TMEM lanes.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) {
@@ -561,7 +580,7 @@ struct BTile {
 // ---------------------------------------------------------------------------
 
 template <int BN, int AMODE, int ASRC, bool B_KMAJ, int BSRC, int TJ>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
     lse_gemm_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtensorMap tmap_a,
                     const __grid_constant__ CUtensorMap tmap_a2, const __grid_constant__ CUtensorMap tmap_b) {
   using C = Cfg<BN, ASRC, BSRC>;
@@ -650,7 +669,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // every k-block of this tile is staged (num_kb <= kAStages): scan them.  A row of
             // at most two k-blocks stays in registers (cur, nxt) and its stages are released here.
             float e = is_min ? INFINITY : -INFINITY;
-            const bool keep = p.num_kb <= 2;
+            const bool keep = C::kDrainGroups == 1 && p.num_kb <= 2;
             for (int kb = 0; kb < p.num_kb; ++kb) {
               const uint32_t sidx = (ait + kb) % C::kAStages;
               if (!mbar_wait(&a_full[sidx], ((ait + kb) / C::kAStages) & 1, kSiteAStaged, abort_flag)) {
@@ -687,7 +706,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               preloaded = true;
             }
             a.shift = a.valid ? e : 0.0f;
-          } else if (p.num_kb <= 2) {
+          } else if (C::kDrainGroups == 1 && p.num_kb <= 2) {
             // global-load source, one or two k-blocks: load the row once, scan it in registers
             a.load_global(p, 0, cur);
             if (p.num_kb == 2) a.load_global(p, kBK, nxt);
@@ -876,17 +895,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(drain, 0, kSiteGemmDrain, abort_flag, /*honor_abort=*/false);
     }
     __syncwarp();
-  } else if (warp < kProducerWarp) {
+  } else if (warp < kProducerWarp || warp > kProducerWarp) {
     // ------------------------------------------------------------ drain + epilogue
     const int q = warp & 3;  // TMEM lane quadrant of this warp
     const int r = q * 32 + lane;
     const uint32_t lane_bits = (uint32_t)(q * 32) << 16;
     // Each drain warp owns TMEM lanes (rows) 32q..32q+31 from the accumulator
     // to the copy-out, so the drain warps never wait for one another.
+    const int group = warp > kProducerWarp ? 1 : 0;
     uint32_t gc = 0, tl = 0, ob = 0;
     bool ok = true;
     const int chunks = (p.num_kb + kChunkKB - 1) / kChunkKB;
+    // Two groups split the tiles when every tile is a single chunk: the tile's chunk
+    // buffer, correction buffer, shift slot and staging buffer all alternate with it.
+    // Otherwise group 0 takes every tile.
+    const bool split = C::kDrainGroups == 2 && chunks == 1;
+    if (group == 1 && !split) ok = false;
     for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++tl) {
+      if (split && (int)(tl & 1) != group) continue;
+      if (split) {
+        gc = tl;
+        ob = group;
+      }
       int bb, mt, nt;
       decode_tile(p, tile, bb, mt, nt);
       const int m0 = mt * kBM;
@@ -943,7 +973,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&shift_empty[slot]);
       // column shifts of a log-domain B, copied into this warp's own slice of shared memory
-      float* cshift = p.shift_b ? (float*)(smem + C::kOffColShift) + q * BN : nullptr;
+      float* cshift = p.shift_b ? (float*)(smem + C::kOffColShift) + (group * 4 + q) * BN : nullptr;
       if (cshift) {
 #pragma unroll
         for (int c = lane; c < BN; c += 32) cshift[c] = (n0 + c < p.N) ? __ldg(p.shift_b + (int64_t)bb * p.N + n0 + c) : 0.0f;
@@ -957,13 +987,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         float out[32];
         XE_SEGMENT_BEGIN(seg_e1);
         if (direct) {
-          // single chunk: the sums come straight from TMEM (main + corr)
-          float v[32], w[32];
-          tmem_ld32(tmem + lane_bits + C::kTmemMain + dcb * BN + sl * 32, v);
-          tmem_ld32(tmem + lane_bits + C::kTmemCorr + (tl % C::kCorrBufs) * BN + sl * 32, w);
-          tmem_wait_ld();
+          // single chunk: the sums come straight from TMEM (main + corr), 16 columns at a time
 #pragma unroll
-          for (int j = 0; j < 32; ++j) out[j] = isinf(v[j]) ? v[j] : v[j] + w[j];
+          for (int h = 0; h < 2; ++h) {
+            float v[16], w[16];
+            tmem_ld16(tmem + lane_bits + C::kTmemMain + dcb * BN + sl * 32 + 16 * h, v);
+            tmem_ld16(tmem + lane_bits + C::kTmemCorr + (tl % C::kCorrBufs) * BN + sl * 32 + 16 * h, w);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) out[16 * h + j] = isinf(v[j]) ? v[j] : v[j] + w[j];
+          }
           if (sl == BN / 32 - 1) {  // every TMEM column of this tile has been read
             tc_fence_before();
             __syncwarp();
@@ -988,10 +1021,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           out[j] = o;
         }
         // every warp stages and copies out its own 32 rows: warp-level ordering suffices
-        if (C::kOutBufs == 1) __syncwarp();  // the single buffer's previous copy-out is done
+        if (C::kOutBufs == 1 || split) __syncwarp();  // this buffer's previous copy-out is done
         // staging buffer as [128 rows][32 cols], 16-byte chunks swizzled by (row & 7)
         const uint32_t stage = smem_base + C::kOffOutAligned + (ob % C::kOutBufs) * C::kOutBytes;
-        ++ob;
+        if (!split) ++ob;
         const uint32_t srow = stage + r * 128;
 #pragma unroll
         for (int j = 0; j < 8; ++j)

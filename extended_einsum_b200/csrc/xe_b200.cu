@@ -143,7 +143,7 @@ xe_status launch_gemm_t(const Params& p, const CUtensorMap& ma, const CUtensorMa
     cudaError_t e = prepare_kernel(kernel, C::kSmemBytes, attribute_set);
     if (e != cudaSuccess) return fail(XE_ERR_CUDA, "xe_logspace_gemm: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     const int grid = (int)std::min<int64_t>(p.num_tiles, current_device_sms());
-    kernel<<<grid, xe::gemm::kThreads, C::kSmemBytes, stream>>>(p, ma, ma2, mb);
+    kernel<<<grid, C::kThreads, C::kSmemBytes, stream>>>(p, ma, ma2, mb);
     return check_launch("xe_logspace_gemm");
   }
 }
