@@ -53,7 +53,9 @@ enum AMode : int { kALog = 0, kALinear = 1, kATucker = 2 };
 // Where the A rows come from: a TMA-filled staging ring (K-major A with
 // 16-byte aligned strides), the same plus a second ring for the fused addend,
 // or per-thread global loads (any layout).
-enum ASource : int { kATma = 0, kATma2 = 1, kALdg = 2 };
+// kAGather: the A rows are gathered rows of a table (Params::g_pixels), staged in
+// the same swizzled ring by the producer warp with 16-byte cp.async copies.
+enum ASource : int { kATma = 0, kATma2 = 1, kALdg = 2, kAGather = 3 };
 // Where the raw B tiles come from: a TMA-filled staging ring (16-byte aligned
 // strides), or global loads with or without 16-byte vectors.
 enum BSource : int { kBTma = 0, kBLdgVec = 1, kBLdg = 2 };
@@ -231,6 +233,17 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
       "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
       "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
       : "memory");
+}
+
+// 16-byte asynchronous global -> shared copy (L2 only).
+__device__ __forceinline__ void cp_async16(uint32_t dst, const float* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+
+// One arrival on `bar` once this thread's earlier cp.async copies have landed
+// (the barrier's expected count includes it).
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
@@ -622,7 +635,7 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
       mbar_init(&shift_empty[c], kDrainWarps);
     }
     for (int s = 0; s < 4; ++s) {
-      mbar_init(&a_full[s], 1);
+      mbar_init(&a_full[s], ASRC == kAGather ? 32 : 1);
       mbar_init(&a_empty[s], kAWarps);
       mbar_init(&b_full[s], 1);
       mbar_init(&b_empty[s], kBWarps);
@@ -1054,6 +1067,72 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
           }
         }
         XE_SEGMENT_END(seg_e4, 11);
+      }
+    }
+  } else if (ASRC == kAGather) {
+    // ------------------------------------------------------------ gather producer (whole warp)
+    // Lane l stages rows 4l..4l+3 of each k-block: table row pixels[m, var[bb]] of fold bb,
+    // 16-byte cp.async copies into the 128-byte-swizzled layout the A warps read; each lane's
+    // copies complete on a_full with one arrival (a_full counts 32 per phase).  B tiles
+    // come through TMA from lane 0.
+    uint32_t ait = 0, bit = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+      int bb, mt, nt;
+      decode_tile(p, tile, bb, mt, nt);
+      int64_t v = p.g_var ? (int64_t)__ldg(p.g_var + bb) : (int64_t)bb;
+      if (v < 0 || v >= p.g_stride) {
+        record_bad_index(kSiteGemmGatherState);
+        v = 0;
+      }
+      const float* src[4];
+      bool valid[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int m = mt * kBM + lane * 4 + i;
+        valid[i] = m < p.M;
+        int64_t state = valid[i] ? (int64_t)__ldg(p.g_pixels + (int64_t)m * p.g_stride + v) : 0;
+        if (state >= p.g_states) {
+          record_bad_index(kSiteGemmGatherState);
+          state = p.g_states - 1;
+        }
+        src[i] = p.a + (int64_t)bb * p.a_sb + state * p.a_sm;
+      }
+      for (int kb = 0; kb < p.num_kb; ++kb) {
+        const uint32_t sidx = ait % C::kAStages;
+        bool free_slot = true;
+        if (lane == 0) free_slot = mbar_wait(&a_empty[sidx], ((ait / C::kAStages) & 1) ^ 1, kSiteProducer, abort_flag);
+        if (__shfl_sync(0xffffffffu, free_slot ? 1 : 0, 0) == 0) {  // the warp leaves together
+          ok = false;
+          break;
+        }
+        const uint32_t dst = smem_base + C::kOffA + sidx * C::kAStageBytes;
+        const int kvalid = p.K - kb * kBK;  // a multiple of 4 (checked on the host)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int r = lane * 4 + i;
+          if (!valid[i]) continue;  // the A warps mask rows past M
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            if (4 * c < kvalid) cp_async16(dst + r * 128 + ((c ^ (r & 7)) << 4), src[i] + kb * kBK + 4 * c);
+        }
+        cp_async_arrive_noinc(&a_full[sidx]);
+        ++ait;
+        if (BSRC == kBTma && lane == 0) {
+          const uint32_t bidx = bit % C::kBRawStages;
+          if (!mbar_wait(&b_empty[bidx], ((bit / C::kBRawStages) & 1) ^ 1, kSiteProducer, abort_flag)) {
+            ok = false;
+          } else {
+            const uint32_t bdst = smem_base + C::kOffBRaw + bidx * C::kBRawBytes;
+            mbar_expect_tx(&b_full[bidx], C::kBRawBytes);
+            if (B_KMAJ)
+              tma_load_3d(bdst, &tmap_b, kb * kBK, nt * BN, bb, &b_full[bidx]);
+            else
+              tma_load_3d(bdst, &tmap_b, nt * BN, kb * kBK, bb, &b_full[bidx]);
+            ++bit;
+          }
+        }
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
       }
     }
   } else if ((ASRC != kALdg || BSRC == kBTma) && lane == 0) {

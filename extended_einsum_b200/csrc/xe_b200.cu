@@ -245,10 +245,24 @@ GemmPlan plan_gemm(const float* a, const float* a2, int64_t a_sb, int64_t a_sm, 
   return g;
 }
 
+// The gathered-row source: K-major B staged by TMA or 16-byte loads only.
+template <int BN>
+xe_status launch_gemm_gather(const Params& q, const GemmPlan& g, cudaStream_t s) {
+  using namespace xe::gemm;
+  if (g.bsrc == kBTma) return launch_gemm_t<BN, kALog, kAGather, true, kBTma, 0>(q, g.ma, g.ma2, g.mb, s);
+  return launch_gemm_t<BN, kALog, kAGather, true, kBLdgVec, 0>(q, g.ma, g.ma2, g.mb, s);
+}
+
 xe_status launch_gemm(const Params& p, const GemmPlan& g, bool a_linear, bool bk, cudaStream_t s) {
   using namespace xe::gemm;
   Params q = p;
   set_tiling(q, g.bn);
+  if (g.asrc == kAGather) {
+    if (a_linear || !bk || g.bsrc == kBLdg)
+      return fail(XE_ERR_NOT_SUPPORTED, "xe_logspace_gemm_gather: staged gather needs a log table and K-major B");
+    return g.bn == 32 ? launch_gemm_gather<32>(q, g, s) : g.bn == 64 ? launch_gemm_gather<64>(q, g, s)
+                                                                      : launch_gemm_gather<128>(q, g, s);
+  }
 #define XE_LAUNCH_BN(BN)                                                                                           \
   do {                                                                                                             \
     if (a_linear) {                                                                                                \
@@ -581,6 +595,20 @@ xe_status xe_logspace_gemm_gather(const float* table, int64_t t_sf, int64_t t_ss
   // the A rows are gathered per thread (global loads), their shifts computed in the kernel
   GemmPlan plan = plan_gemm(table, nullptr, t_sf, t_ss, 1, false, b, b_sb, b_sk, b_sn, folds, batch, n, k, true);
   plan.inline_shift = true;
+  // rows staged by 16-byte copies when the table allows them and B is K-major
+  const bool bk = !(b_sn == 1) && b_sk == 1;
+  if (env_int("XE_GEMM_NO_TMA", 0) == 0 && k % 4 == 0 && t_ss % 4 == 0 && t_sf % 4 == 0 && aligned16(table) && bk) {
+    using namespace xe::gemm;
+    int bsrc = plan.bsrc;
+    if (bsrc == kBTma && !b_ring_fits(plan.bn, kATma)) bsrc = kBLdgVec;
+    const bool b_vec = aligned16(b) && b_sb % 4 == 0 && k % 4 == 0 && b_sn % 4 == 0;
+    if (bsrc != kBTma && b_vec) bsrc = kBLdgVec;
+    // the in-kernel row shift needs every k-block of a tile staged at once
+    if ((bsrc == kBTma || bsrc == kBLdgVec) && k <= staged_k_capacity(plan.bn, kATma, bsrc)) {
+      plan.asrc = kAGather;
+      plan.bsrc = bsrc == kBTma ? kBTma : kBLdgVec;
+    }
+  }
   const GatherA gather{pixels, var_of_fold, pixel_stride, (int)states};
   return gemm_launch(table, nullptr, t_sf, t_ss, 1, false, nullptr, b, b_sb, b_sk, b_sn, shift_b, c, c_sb, c_sm, c_sn,
                      folds, batch, n, k, shift_mode == XE_SHIFT_MIN, plan, s, false, &gather);

@@ -67,7 +67,10 @@ def test_no_device_wait_timed_out():
     assert ops.device_status() == 0
 
 
-@pytest.mark.parametrize("folds,states,units,batch,n,b_linear", [(16, 256, 64, 1000, 64, True), (6, 7, 32, 130, 40, False), (3, 256, 128, 257, 1, True)])
+@pytest.mark.parametrize(
+    "folds,states,units,batch,n,b_linear",
+    [(16, 256, 64, 1000, 64, True), (6, 7, 32, 130, 40, False), (3, 256, 128, 257, 1, True), (4, 256, 128, 300, 128, True), (5, 256, 60, 129, 64, True)],
+)
 def test_gemm_gather_equals_gather_then_gemm(folds, states, units, batch, n, b_linear):
     """The fused first sum layer == xe_categorical_gather followed by xe_logspace_gemm."""
     g = torch.Generator().manual_seed(folds * states + units)
