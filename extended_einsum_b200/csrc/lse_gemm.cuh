@@ -1024,14 +1024,19 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
         }
         XE_SEGMENT_END(seg_e1, 8);
         XE_SEGMENT_BEGIN(seg_e2);
+        if (!p.raw_out) {
+          // log + shifts in the reference's order; uniform branches per slice, not per element
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          if (p.raw_out) continue;
-          float o = fast_log(out[j]);
-          if (AMODE != kALinear) o += s1;
-          if (AMODE == kATucker) o += s2;
-          if (cshift) o += cshift[sl * 32 + j];
-          out[j] = o;
+          for (int j = 0; j < 32; ++j) {
+            float o = fast_log(out[j]);
+            if (AMODE != kALinear) o += s1;
+            if (AMODE == kATucker) o += s2;
+            out[j] = o;
+          }
+          if (cshift) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) out[j] += cshift[sl * 32 + j];
+          }
         }
         // every warp stages and copies out its own 32 rows: warp-level ordering suffices
         if (C::kOutBufs == 1 || split) __syncwarp();  // this buffer's previous copy-out is done
@@ -1050,7 +1055,17 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
         // coalesced copy-out: each warp writes 32 rows, 4 rows (512 B) per instruction
         const int chunk = lane & 7;
         const int n = n0 + sl * 32 + 4 * chunk;
+        if (p.c_vec && m0 + kBM <= p.M && n0 + sl * 32 + 32 <= p.N) {
+          // interior slice: every row and column in bounds, 16-byte stores
 #pragma unroll
+          for (int it = 0; it < 8; ++it) {
+            const int row = q * 32 + 4 * it + (lane >> 3);
+            stg_v4(cbase + (int64_t)(m0 + row) * p.c_sm + n, lds_v4(stage + row * 128 + ((chunk ^ (row & 7)) << 4)));
+          }
+          XE_SEGMENT_END(seg_e4, 11);
+          continue;
+        }
+#pragma unroll 1
         for (int it = 0; it < 8; ++it) {
           const int row = q * 32 + 4 * it + (lane >> 3);
           const int m = m0 + row;
