@@ -533,6 +533,15 @@ struct BTile {
   // Raw values from a TMA-staged tile (unswizzled: MN-major [32 k][BN n],
   // K-major [BN n][32 k]), masked to the operand's extents.
   __device__ void load_staged(const Params& p, uint32_t stage, int n0, int k0, int t, float4 (&v)[kQ]) const {
+    if (n0 + BN <= p.N && k0 + kBK <= p.K) {  // interior tile: nothing to mask
+#pragma unroll
+      for (int i = 0; i < kQ; ++i) {
+        int nl, kl;
+        coords(t, i, nl, kl);
+        v[i] = lds_v4(stage + (B_KMAJ ? (uint32_t)(nl * 32 + kl) * 4 : (uint32_t)(kl * BN + nl) * 4));
+      }
+      return;
+    }
     const float fill = p.shift_b == nullptr ? 0.0f : -INFINITY;
 #pragma unroll
     for (int i = 0; i < kQ; ++i) {
@@ -563,15 +572,28 @@ struct BTile {
   }
 
   __device__ void store(const Params& p, uint32_t hi, uint32_t lo, int t, const float4 (&v)[kQ]) const {
-    const bool lin = p.shift_b == nullptr;
+    if (p.shift_b == nullptr) {  // linear B: the split alone
+#pragma unroll
+      for (int i = 0; i < kQ; ++i) {
+        int nl, kl;
+        coords(t, i, nl, kl);
+        float4 h, l;
+        split_rn(v[i].x, h.x, l.x);
+        split_rn(v[i].y, h.y, l.y);
+        split_rn(v[i].z, h.z, l.z);
+        split_rn(v[i].w, h.w, l.w);
+        const uint32_t off = B_KMAJ ? kmajor_off(nl, kl >> 2) : mnmajor_off(kl, nl >> 2);
+        sts_v4(hi + off, h);
+        sts_v4(lo + off, l);
+      }
+      return;
+    }
 #pragma unroll
     for (int i = 0; i < kQ; ++i) {
       int nl, kl;
       coords(t, i, nl, kl);
       float4 e;
-      if (lin) {
-        e = v[i];
-      } else if (B_KMAJ) {
+      if (B_KMAJ) {
         const float s = shift[i];
         e = make_float4(exp_shifted(v[i].x, s), exp_shifted(v[i].y, s), exp_shifted(v[i].z, s), exp_shifted(v[i].w, s));
       } else {
@@ -705,9 +727,14 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
               } else {
                 float v[32];
                 load_staged_row<ASRC>(stage, r, a.valid, kvalid, fill, v);
+                if (kvalid >= 32) {
 #pragma unroll
-                for (int j = 0; j < 32; ++j)
-                  if (j < kvalid) e = extreme(e, v[j], is_min);
+                  for (int j = 0; j < 32; ++j) e = extreme(e, v[j], is_min);
+                } else {
+#pragma unroll
+                  for (int j = 0; j < 32; ++j)
+                    if (j < kvalid) e = extreme(e, v[j], is_min);
+                }
               }
             }
             if (!ok) break;
