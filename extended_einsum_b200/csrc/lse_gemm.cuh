@@ -181,6 +181,7 @@ __device__ __forceinline__ float4 ldg_v4(const float* p) {
 }
 
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+  __syncwarp();  // .sync.aligned: the whole warp, converged
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
       "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
@@ -193,6 +194,7 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
 
 // 16 consecutive fp32 columns of the calling warp's 32 TMEM lanes.
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+  __syncwarp();  // .sync.aligned: the whole warp, converged
   uint32_t r[16];
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
@@ -206,6 +208,7 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
 }
 
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) {
+  __syncwarp();  // .sync.aligned: the whole warp, converged
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
           taddr),
@@ -214,7 +217,10 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) 
       : "memory");
 }
 
-__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() {
+  __syncwarp();
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
 
 // D[tmem] (+)= A[tmem] * B[smem], kind::tf32, one CTA.
 __device__ __forceinline__ void umma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
@@ -780,6 +786,10 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
       if (ASRC == kALdg && !preloaded) a.load_global(p, 0, cur);
       for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
         XE_SEGMENT_BEGIN(seg_load);
+        // The staged slot is released only once its values have been used (transformed below):
+        // a shared-memory load may still be in flight when the next instruction issues, and the
+        // producer's TMA would overwrite the slot.
+        int release = -1;
         if (ASRC != kALdg && !preloaded) {
           const uint32_t sidx = ait % C::kAStages;
           if (!mbar_wait(&a_full[sidx], (ait / C::kAStages) & 1, kSiteAStaged, abort_flag)) {
@@ -788,8 +798,7 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
           }
           load_staged_row<ASRC>(smem_base + C::kOffA + sidx * C::kAStageBytes, r, a.valid, p.K - kb * kBK, fill,
                                 cur);
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&a_empty[sidx]);
+          release = (int)sidx;
           ++ait;
         } else if (ASRC == kALdg && kb + 1 < p.num_kb && !preloaded) {
           a.load_global(p, (kb + 1) * kBK, nxt);
@@ -797,7 +806,7 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
         XE_SEGMENT_END(seg_load, 1);
         const uint32_t s = it % kStages;
         const uint32_t ph = (it / kStages) & 1;
-        if (!mbar_wait(&empty[s], ph ^ 1, kSiteAStage, abort_flag)) {
+        if (!mbar_wait_warp(&empty[s], ph ^ 1, kSiteAStage, abort_flag)) {
           ok = false;
           break;
         }
@@ -822,7 +831,10 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
         XE_SEGMENT_END(seg_st, 3);
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&full[s]);
+        if (lane == 0) {
+          mbar_arrive(&full[s]);
+          if (release >= 0) mbar_arrive(&a_empty[release]);
+        }
         if ((ASRC == kALdg || preloaded) && kb + 1 < p.num_kb) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) cur[j] = nxt[j];
@@ -845,6 +857,7 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
       if (BSRC != kBTma) bt.load(p, bb, n0, 0, t, cur);
       for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
         const bool more = kb + 1 < p.num_kb;
+        int release = -1;
         if (BSRC == kBTma) {
           const uint32_t sidx = bit % C::kBRawStages;
           if (!mbar_wait(&b_full[sidx], (bit / C::kBRawStages) & 1, kSiteBStage, abort_flag)) {
@@ -852,8 +865,7 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
             break;
           }
           bt.load_staged(p, smem_base + C::kOffBRaw + sidx * C::kBRawBytes, n0, kb * kBK, t, cur);
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&b_empty[sidx]);
+          release = (int)sidx;  // released after the values are used (see the A rows)
           ++bit;
         } else if (more) {
           bt.load(p, bb, n0, (kb + 1) * kBK, t, nxt);
@@ -870,7 +882,10 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
         XE_SEGMENT_END(seg_b, 4);
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&full[s]);
+        if (lane == 0) {
+          mbar_arrive(&full[s]);
+          if (release >= 0) mbar_arrive(&b_empty[release]);
+        }
         if (BSRC != kBTma && more) {
 #pragma unroll
           for (int i = 0; i < BT::kQ; ++i) cur[i] = nxt[i];
@@ -966,7 +981,7 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
       for (int c = 0; c < chunks && chunks > 1; ++c, ++gc) {
         const uint32_t cb = gc & 1;
         const bool last = c == chunks - 1;
-        if (!mbar_wait(&chunk_full[cb], (gc >> 1) & 1, kSiteDrainChunk, abort_flag)) {
+        if (!mbar_wait_warp(&chunk_full[cb], (gc >> 1) & 1, kSiteDrainChunk, abort_flag)) {
           ok = false;
           break;
         }
@@ -1000,7 +1015,7 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
       uint32_t dcb = 0;
       if (direct) {
         dcb = gc & 1;
-        if (!mbar_wait(&chunk_full[dcb], (gc >> 1) & 1, kSiteDrainChunk, abort_flag)) break;
+        if (!mbar_wait_warp(&chunk_full[dcb], (gc >> 1) & 1, kSiteDrainChunk, abort_flag)) break;
         tc_fence_after();
         ++gc;
       }
@@ -1024,57 +1039,55 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
 #pragma unroll 1
       for (int sl = 0; sl < BN / 32; ++sl) {
         const float* run = running + sl * 32 * kBM + r;  // this row's 32 sums of the slice
-        float out[32];
-        XE_SEGMENT_BEGIN(seg_e1);
-        if (direct) {
-          // single chunk: the sums come straight from TMEM (main + corr), 16 columns at a time
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            float v[16], w[16];
-            tmem_ld16(tmem + lane_bits + C::kTmemMain + dcb * BN + sl * 32 + 16 * h, v);
-            tmem_ld16(tmem + lane_bits + C::kTmemCorr + (tl % C::kCorrBufs) * BN + sl * 32 + 16 * h, w);
-            tmem_wait_ld();
-#pragma unroll
-            for (int j = 0; j < 16; ++j) out[16 * h + j] = isinf(v[j]) ? v[j] : v[j] + w[j];
-          }
-          if (sl == BN / 32 - 1) {  // every TMEM column of this tile has been read
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) {
-              mbar_arrive(&chunk_empty[dcb]);
-              mbar_arrive(&corr_empty[tl % C::kCorrBufs]);
-            }
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) out[j] = run[j * kBM];
-        }
-        XE_SEGMENT_END(seg_e1, 8);
-        XE_SEGMENT_BEGIN(seg_e2);
-        if (!p.raw_out) {
-          // log + shifts in the reference's order; uniform branches per slice, not per element
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            float o = fast_log(out[j]);
-            if (AMODE != kALinear) o += s1;
-            if (AMODE == kATucker) o += s2;
-            out[j] = o;
-          }
-          if (cshift) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) out[j] += cshift[sl * 32 + j];
-          }
-        }
         // every warp stages and copies out its own 32 rows: warp-level ordering suffices
         if (C::kOutBufs == 1 || split) __syncwarp();  // this buffer's previous copy-out is done
         // staging buffer as [128 rows][32 cols], 16-byte chunks swizzled by (row & 7)
         const uint32_t stage = smem_base + C::kOffOutAligned + (ob % C::kOutBufs) * C::kOutBytes;
         if (!split) ++ob;
         const uint32_t srow = stage + r * 128;
+        XE_SEGMENT_BEGIN(seg_e1);
+        // 16 columns at a time: sums (TMEM main + correction, or the running sum), log and
+        // shifts in the reference's order, staging
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-          sts_v4(srow + ((j ^ (r & 7)) << 4), make_float4(out[4 * j], out[4 * j + 1], out[4 * j + 2], out[4 * j + 3]));
-        XE_SEGMENT_END(seg_e2, 9);
+        for (int h = 0; h < 2; ++h) {
+          float out[16];
+          if (direct) {
+            float v[16], w[16];
+            tmem_ld16(tmem + lane_bits + C::kTmemMain + dcb * BN + sl * 32 + 16 * h, v);
+            tmem_ld16(tmem + lane_bits + C::kTmemCorr + (tl % C::kCorrBufs) * BN + sl * 32 + 16 * h, w);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) out[j] = isinf(v[j]) ? v[j] : v[j] + w[j];
+            if (sl == BN / 32 - 1 && h == 1) {  // every TMEM column of this tile has been read
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) {
+                mbar_arrive(&chunk_empty[dcb]);
+                mbar_arrive(&corr_empty[tl % C::kCorrBufs]);
+              }
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) out[j] = run[(16 * h + j) * kBM];
+          }
+          if (!p.raw_out) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              float o = fast_log(out[j]);
+              if (AMODE != kALinear) o += s1;
+              if (AMODE == kATucker) o += s2;
+              out[j] = o;
+            }
+            if (cshift) {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) out[j] += cshift[sl * 32 + 16 * h + j];
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            sts_v4(srow + (((4 * h + j) ^ (r & 7)) << 4), make_float4(out[4 * j], out[4 * j + 1], out[4 * j + 2], out[4 * j + 3]));
+        }
+        XE_SEGMENT_END(seg_e1, 8);
         XE_SEGMENT_BEGIN(seg_e3);
         __syncwarp();
         XE_SEGMENT_END(seg_e3, 10);

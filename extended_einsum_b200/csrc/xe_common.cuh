@@ -134,6 +134,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int si
   }
 }
 
+// A wait by every lane of a warp whose next steps are warp-collective
+// (tcgen05.ld / tcgen05.st are .sync.aligned): the lanes leave the spin loop at
+// different times, so the warp is reconverged here, and a timeout seen by any
+// lane is seen by all of them.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int site, volatile int* abort) {
+  const bool ok = mbar_wait(bar, parity, site, abort);
+  return __all_sync(0xffffffffu, ok);
+}
+
 // Orders this thread's generic-proxy shared-memory writes before later
 // async-proxy (tensor core) reads.
 __device__ __forceinline__ void fence_proxy_async_smem() {
@@ -179,6 +188,7 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
 
 // 32 consecutive fp32 columns of the calling warp's 32 TMEM lanes.
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  __syncwarp();  // .sync.aligned: the whole warp, converged
   uint32_t r[32];
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
@@ -194,7 +204,10 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_ld() {
+  __syncwarp();
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
 
 // ---------------------------------------------------------------------------
 // UMMA descriptors (every tile base is 1024-byte aligned).
