@@ -976,11 +976,10 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
       decode_tile(p, tile, bb, mt, nt);
       const int m0 = mt * kBM;
       const int n0 = nt * BN;
-      // -------- chunks: running[col][row] (+)= main chunk; the last one adds corr.
-      // A tile with a single chunk skips the running sum (epilogue below).
-      for (int c = 0; c < chunks && chunks > 1; ++c, ++gc) {
+      // -------- chunks: running[col][row] (+)= main chunk, for all but the last chunk;
+      // the epilogue reads the last chunk and the correction straight from TMEM.
+      for (int c = 0; c < chunks - 1; ++c, ++gc) {
         const uint32_t cb = gc & 1;
-        const bool last = c == chunks - 1;
         if (!mbar_wait_warp(&chunk_full[cb], (gc >> 1) & 1, kSiteDrainChunk, abort_flag)) {
           ok = false;
           break;
@@ -989,36 +988,24 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
         XE_SEGMENT_BEGIN(seg_dr);
 #pragma unroll 1
         for (int sl = 0; sl < BN / 32; ++sl) {
-          float v[32], w[32];
+          float v[32];
           tmem_ld32(tmem + lane_bits + C::kTmemMain + cb * BN + sl * 32, v);
-          if (last) tmem_ld32(tmem + lane_bits + C::kTmemCorr + (tl % C::kCorrBufs) * BN + sl * 32, w);
           tmem_wait_ld();
           float* run = running + sl * 32 * kBM + r;
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            float t = (c == 0) ? v[j] : run[j * kBM] + v[j];
-            // an overflowed main term carries the result; its correction is NaN
-            if (last) t = isinf(t) ? t : t + w[j];
-            run[j * kBM] = t;
-          }
+          for (int j = 0; j < 32; ++j) run[j * kBM] = (c == 0) ? v[j] : run[j * kBM] + v[j];
         }
         XE_SEGMENT_END(seg_dr, 5);
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&chunk_empty[cb]);
-          if (last) mbar_arrive(&corr_empty[tl % C::kCorrBufs]);  // this correction buffer is free
-        }
+        if (lane == 0) mbar_arrive(&chunk_empty[cb]);
       }
       if (!ok) break;
       const bool direct = chunks == 1;
-      uint32_t dcb = 0;
-      if (direct) {
-        dcb = gc & 1;
-        if (!mbar_wait_warp(&chunk_full[dcb], (gc >> 1) & 1, kSiteDrainChunk, abort_flag)) break;
-        tc_fence_after();
-        ++gc;
-      }
+      const uint32_t dcb = gc & 1;  // the last (or only) chunk
+      if (!mbar_wait_warp(&chunk_full[dcb], (gc >> 1) & 1, kSiteDrainChunk, abort_flag)) break;
+      tc_fence_after();
+      ++gc;
       // -------- epilogue from shared memory, overlapping the next tile's MMAs
       XE_SEGMENT_BEGIN(seg_ep);
       const uint32_t slot = tl & 1;
@@ -1051,13 +1038,18 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           float out[16];
-          if (direct) {
+          {
+            // the last chunk (plus the running sum of the earlier ones) and the correction
             float v[16], w[16];
             tmem_ld16(tmem + lane_bits + C::kTmemMain + dcb * BN + sl * 32 + 16 * h, v);
             tmem_ld16(tmem + lane_bits + C::kTmemCorr + (tl % C::kCorrBufs) * BN + sl * 32 + 16 * h, w);
             tmem_wait_ld();
 #pragma unroll
-            for (int j = 0; j < 16; ++j) out[j] = isinf(v[j]) ? v[j] : v[j] + w[j];
+            for (int j = 0; j < 16; ++j) {
+              const float t = direct ? v[j] : run[(16 * h + j) * kBM] + v[j];
+              // an overflowed main term carries the result; its correction is NaN
+              out[j] = isinf(t) ? t : t + w[j];
+            }
             if (sl == BN / 32 - 1 && h == 1) {  // every TMEM column of this tile has been read
               tc_fence_before();
               __syncwarp();
@@ -1066,9 +1058,6 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
                 mbar_arrive(&corr_empty[tl % C::kCorrBufs]);
               }
             }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) out[j] = run[(16 * h + j) * kBM];
           }
           if (!p.raw_out) {
 #pragma unroll
