@@ -313,7 +313,8 @@ def run_ours(args, rank: int, world: int, device: torch.device, dist_on: bool) -
     ms_per_step = ms / args.steps
     value = world * work.flops_per_step / (ms_per_step * 1e-3) / 1e12
     # end to end through the public API with host buffers
-    e2e_ms = time_region(lambda record: work.e2e_step(), max(3, args.steps // 4), 2, dist_on) / max(3, args.steps // 4)
+    e2e_steps = max(5, args.steps // 4)
+    e2e_ms = time_region(lambda record: work.e2e_step(), e2e_steps, 3, dist_on) / e2e_steps
     e2e_value = world * work.flops_per_step / (e2e_ms * 1e-3) / 1e12
     h2d, d2h = work.e2e_bytes
 

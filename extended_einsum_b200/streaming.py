@@ -24,6 +24,17 @@ from .frontend import extract_program, input_tensor
 from .lowering import lower, run_program
 
 
+_COPY_STREAMS: dict[int, tuple[torch.cuda.Stream, torch.cuda.Stream]] = {}
+
+
+def _copy_streams(device: torch.device) -> tuple[torch.cuda.Stream, torch.cuda.Stream]:
+    """The host-to-device and device-to-host copy streams of a device, created once."""
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    if index not in _COPY_STREAMS:
+        _COPY_STREAMS[index] = (torch.cuda.Stream(index), torch.cuda.Stream(index))
+    return _COPY_STREAMS[index]
+
+
 def materialize_streamed(
     build: Callable[..., Any],
     host_operands: Sequence[torch.Tensor],
@@ -52,8 +63,7 @@ def materialize_streamed(
     bounds = [(batch * i // chunks, batch * (i + 1) // chunks) for i in range(chunks)]
 
     compute = torch.cuda.current_stream(device)
-    copy_in = torch.cuda.Stream(device)
-    copy_out = torch.cuda.Stream(device)
+    copy_in, copy_out = _copy_streams(device)
     lowered: dict[tuple, tuple[Any, list[int]]] = {}
     # two device buffers per operand: chunk i + 1 is copied in while chunk i computes
     buffers = [[torch.empty((bounds[0][1] - bounds[0][0] + 1, *t.shape[1:]), dtype=t.dtype, device=device)
