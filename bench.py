@@ -389,7 +389,8 @@ def run_reference(args, rank: int) -> dict | None:
         return None
     from oracle import torch_port
 
-    torch.set_num_threads(os.cpu_count() or 1)
+    # every host thread this process may run on (the affinity set, not the machine's count)
+    torch.set_num_threads(len(os.sched_getaffinity(0)) or 1)
     gen = torch.Generator().manual_seed(1)
     sample_batches = 4
     a = 8.0 * torch.randn(sample_batches, 512, 512, generator=gen)
