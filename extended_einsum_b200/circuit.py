@@ -139,12 +139,19 @@ class CircuitForward:
 
     def __call__(self, pixels: torch.Tensor) -> torch.Tensor:
         """Log-likelihoods (B, 1) of uint8 pixels (B, variables)."""
+        if ops._needs_grad(self.categorical):
+            raise NotImplementedError("CircuitForward: no backward for the categorical input table on this path")
         table = ops.softmax(self.categorical, 1, log_output=True)
+        # the fused first layer has no backward: with gradients the gather runs on its own
+        differentiable = ops._needs_grad(*self.levels, self.root)
         y = None
         for level, logits in enumerate(self.levels):
             w = ops.softmax(logits, 2)  # (F, O, K) linear weights
             b_op = w.permute(0, 2, 1)  # (F, K, O), k contiguous
-            if level == 0:
+            if level == 0 and differentiable:
+                x = ops.categorical_gather(table, pixels, self.var_of_fold)
+                y = ops.logspace_gemm(x, b_op, b_linear=True, shift=self.shift)
+            elif level == 0:
                 # the categorical gather is fused into the first sum layer's A rows
                 y = ops.logspace_gemm_gather(table, pixels, self.var_of_fold, b_op, b_linear=True, shift=self.shift)
             else:

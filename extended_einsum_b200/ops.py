@@ -51,6 +51,15 @@ def _ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
 
+def _needs_grad(*tensors: torch.Tensor | None) -> bool:
+    return torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in tensors)
+
+
+def _no_backward(what: str, *tensors: torch.Tensor | None) -> None:
+    if _needs_grad(*tensors):
+        raise NotImplementedError(f"{what}: no backward pass on this path")
+
+
 # ---------------------------------------------------------------------------
 # log-space contraction
 
@@ -71,7 +80,12 @@ def logspace_gemm(
     operand X enters as exp(X - shift) with shift = max (or min) over k and the
     shift is added back, a linear operand enters as is.  ``a2`` (same shape
     and strides as ``a``) is added to ``a`` in the log domain first.
+    Differentiable (autograd.LogspaceGemm) when an operand requires grad.
     """
+    if out is None and _needs_grad(a, b, a2):
+        from .autograd import LogspaceGemm
+
+        return LogspaceGemm.apply(a, b, a2, a_linear, b_linear, shift)
     tensors = [a, b] + ([a2] if a2 is not None else []) + ([out] if out is not None else [])
     device = _check_tensors("logspace_gemm", *tensors)
     if a.dim() != 3 or b.dim() != 3:
@@ -109,6 +123,7 @@ def logspace_gemm_shifted(
     out: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """The contraction kernel alone with given shifts (None = linear operand), xe_logspace_gemm_shifted."""
+    _no_backward("logspace_gemm_shifted", a, b)
     extra = [t for t in (a2, out, shift_a, shift_b) if t is not None]
     device = _check_tensors("logspace_gemm_shifted", a, b, *extra)
     batch, m, k = a.shape
@@ -147,6 +162,10 @@ def logspace_shift(x: torch.Tensor, *, shift: str = "max", x2: torch.Tensor | No
 
 def logspace_reduce(x: torch.Tensor, *, shift: str = "max") -> torch.Tensor:
     """y[t,r] = log(sum_k exp(x[t,r,k] - s)) + s over a (batch, rows, k) view."""
+    if _needs_grad(x):
+        from .autograd import LogspaceReduce
+
+        return LogspaceReduce.apply(x, shift)
     device = _check_tensors("logspace_reduce", x)
     if x.dim() != 3:
         raise ValueError("logspace_reduce: expected a (batch, rows, k) tensor")
@@ -171,6 +190,10 @@ def softmax(x: torch.Tensor, axis: int | Sequence[int], *, log_output: bool = Fa
     backends/torch.py:107-110 does for a trailing block); other axis sets are
     moved to the end first.
     """
+    if _needs_grad(x):
+        from .autograd import Softmax
+
+        return Softmax.apply(x, axis, log_output)
     device = _check_tensors("softmax", x)
     if x.dim() == 0:
         raise ValueError("softmax requires an input tensor with at least one axis")
@@ -213,6 +236,10 @@ def _broadcast_strides(t: torch.Tensor, shape: torch.Size) -> list[int]:
 
 def log_add(a: torch.Tensor, b: torch.Tensor, *, negate_b: bool = False) -> torch.Tensor:
     """y = a + b (or a - b) with numpy broadcasting: a log-space product (quotient)."""
+    if _needs_grad(a, b):
+        from .autograd import LogAdd
+
+        return LogAdd.apply(a, b, negate_b)
     device = _check_tensors("log_add", a, b)
     shape = torch.broadcast_shapes(a.shape, b.shape)
     if len(shape) > 6:
@@ -229,6 +256,7 @@ def log_add(a: torch.Tensor, b: torch.Tensor, *, negate_b: bool = False) -> torc
 
 def log_add_exp(a: torch.Tensor, b: torch.Tensor, *, subtract: bool = False, shift: str = "max") -> torch.Tensor:
     """y = log(exp(a - m) +/- exp(b - m)) + m with the scalar m = extreme of a and b."""
+    _no_backward("log_add_exp", a, b)
     device = _check_tensors("log_add_exp", a, b)
     a = a.contiguous()
     b = b.contiguous()
@@ -257,11 +285,19 @@ def _unary(x: torch.Tensor, op: int, what: str) -> torch.Tensor:
 
 def exp(x: torch.Tensor) -> torch.Tensor:
     """Log space -> raw (translate.py:631-636)."""
+    if _needs_grad(x):
+        from .autograd import Exp
+
+        return Exp.apply(x)
     return _unary(x, 0, "exp")
 
 
 def log(x: torch.Tensor) -> torch.Tensor:
     """Raw -> log space (translate.py:639-644)."""
+    if _needs_grad(x):
+        from .autograd import Log
+
+        return Log.apply(x)
     return _unary(x, 1, "log")
 
 
@@ -273,6 +309,7 @@ def categorical_gather(
     log_table: torch.Tensor, pixels: torch.Tensor, var_of_fold: torch.Tensor | None = None
 ) -> torch.Tensor:
     """y[f,b,:] = log_table[f, pixels[b, var_of_fold[f]], :] for uint8 pixels (batch, variables)."""
+    _no_backward("categorical_gather", log_table)
     device = _check_tensors("categorical_gather", log_table)
     if pixels.device != device or pixels.dtype != torch.uint8 or pixels.dim() != 2:
         raise ValueError("categorical_gather: pixels must be a (batch, variables) uint8 tensor on the table's device")
@@ -311,6 +348,7 @@ def logspace_gemm_gather(
     is (folds, states, K) with K contiguous, ``pixels`` (batch, variables)
     uint8, ``b`` (folds, K, N).  Returns (folds, batch, N).
     """
+    _no_backward("logspace_gemm_gather", log_table, b)
     device = _check_tensors("logspace_gemm_gather", log_table, b)
     if pixels.device != device or pixels.dtype != torch.uint8 or pixels.dim() != 2:
         raise ValueError("logspace_gemm_gather: pixels must be a (batch, variables) uint8 tensor on the table's device")
@@ -349,6 +387,7 @@ def logspace_tucker(
     left: torch.Tensor, right: torch.Tensor, weights: torch.Tensor, *, shift: str = "max"
 ) -> torch.Tensor:
     """y[b,f,o] = log(sum_ij exp(l-sl) exp(r-sr) w[f,o,i,j]) + sl + sr (xe_logspace_tucker)."""
+    _no_backward("logspace_tucker", left, right, weights)
     device = _check_tensors("logspace_tucker", left, right, weights)
     if left.dim() != 3 or right.dim() != 3 or weights.dim() != 4:
         raise ValueError("logspace_tucker: expected (B,F,I), (B,F,J) and (F,O,I,J) tensors")
@@ -382,6 +421,7 @@ ELEMENTWISE_OPS = {
 
 def scaled_gemm(a: torch.Tensor, b: torch.Tensor, *, out: torch.Tensor | None = None) -> torch.Tensor:
     """C[t,m,n] = sum_k A[t,m,k] B[t,k,n] for linear fp32 operands (xe_scaled_gemm), any strides."""
+    _no_backward("scaled_gemm", a, b)
     tensors = [a, b] + ([out] if out is not None else [])
     device = _check_tensors("scaled_gemm", *tensors)
     if a.dim() != 3 or b.dim() != 3:
@@ -415,6 +455,7 @@ def fiber_normalize(x: torch.Tensor, kind: str) -> tuple[torch.Tensor, torch.Ten
     a log-domain x.  log_scale has x's shape with the last axis 1 (a rank-0 x
     gives rank-0 results).
     """
+    _no_backward("fiber_normalize", x)
     device = _check_tensors("fiber_normalize", x)
     try:
         code = FIBER_KINDS[kind]
@@ -435,6 +476,7 @@ def fiber_normalize(x: torch.Tensor, kind: str) -> tuple[torch.Tensor, torch.Ten
 
 def reduce(x: torch.Tensor, axes: Sequence[int] | None, kind: str, *, keepdims: bool = False) -> torch.Tensor:
     """sum / amax / amin of x over ``axes`` (None = all), xe_reduce."""
+    _no_backward("reduce", x)
     device = _check_tensors("reduce", x)
     if kind not in ("sum", "max", "min"):
         raise ValueError(f"reduce: unknown kind {kind!r}")
@@ -461,6 +503,7 @@ def reduce(x: torch.Tensor, axes: Sequence[int] | None, kind: str, *, keepdims: 
 def elementwise(op: str, a: torch.Tensor, b: torch.Tensor, c: torch.Tensor | None = None) -> torch.Tensor:
     """Broadcast elementwise glue of the scaled modes (xe_elementwise): add, sub, mul, div, max, min,
     mul_exp (a*exp(b)), log_add (log(a)+b), rescale (a*exp(b-c))."""
+    _no_backward("elementwise", a, b, c)
     operands = [a, b] + ([c] if c is not None else [])
     device = _check_tensors("elementwise", *operands)
     try:

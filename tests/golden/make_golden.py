@@ -10,7 +10,9 @@ tree) on seeded inputs and records inputs and outputs:
 
 in every stable mode the reference accepts for the program (logspace_max,
 logspace_min, scaled_sum, scaled_max, scaled_min; a mode the reference
-rejects is noted under "rejected").
+rejects is noted under "rejected"), and for a few programs the fp64
+gradients of sum(out * w) for a fixed seeded w (the reference's torch executor
+through autograd, shifts detached as it detaches them).
 
 Cases: small instances of every hot-path pattern (log-space matmul, batched
 matmul with N(0, 8^2) values, folded CP sum layer, Tucker layer, softmax, a
@@ -33,6 +35,8 @@ import torch
 
 OUT_DIR = Path(__file__).resolve().parent
 ALL_MODES = ("logspace_max", "logspace_min", "scaled_sum", "scaled_max", "scaled_min")
+# programs whose gradients (of sum(out * w), fixed w) are recorded, logspace_max, fp64
+GRAD_PROGRAMS = ("matmul_logu", "batched_n64", "cp_layer", "softmax_rows")
 
 
 def main(reference_root: str) -> None:
@@ -86,6 +90,14 @@ def main(reference_root: str) -> None:
         out64 = run_program(translate_to_backend_program(program, NumpyBackendFunctions()), np_inputs)
         return np.asarray(out32), np.asarray(out64)
 
+    def reference_grads(program, inputs: list[np.ndarray], seed: int):
+        """Gradients of sum(out * w) through the reference's torch executor, in fp64."""
+        tins = [torch.from_numpy(x.astype(np.float32).astype(np.float64)).requires_grad_(True) for x in inputs]
+        out = run_program(translate_to_backend_program(program, TorchBackendFunctions()), tins)
+        w = np.random.default_rng(seed).standard_normal(tuple(out.shape)).astype(np.float32)
+        (out * torch.from_numpy(w.astype(np.float64))).sum().backward()
+        return w, [t.grad.numpy() if t.grad is not None else None for t in tins]
+
     def record(name: str, program, inputs: list[np.ndarray], modes=ALL_MODES) -> None:
         programs[name] = serialize(program)
         for i, x in enumerate(inputs):
@@ -102,6 +114,12 @@ def main(reference_root: str) -> None:
             arrays[f"{name}/{mode}/f32"] = out32
             arrays[f"{name}/{mode}/f64"] = out64
             recorded.append(mode)
+            if mode == "logspace_max" and name in GRAD_PROGRAMS:
+                w, grads = reference_grads(with_mode(program, mode), inputs, seed=len(name))
+                arrays[f"{name}/{mode}/grad_weights"] = w
+                for i, grad in enumerate(grads):
+                    if grad is not None:
+                        arrays[f"{name}/{mode}/grad{i}"] = grad
         programs[name]["modes"] = recorded
 
     # -- hot-path patterns through the public expression API ------------------

@@ -119,3 +119,17 @@ def test_golden_records_every_stable_mode(golden_programs):
     """The reference accepts every golden program in all five stable modes."""
     for name, spec in golden_programs.items():
         assert set(spec["modes"]) == {"logspace_max", "logspace_min", "scaled_sum", "scaled_max", "scaled_min"}, name
+
+
+def test_reference_gradients_are_the_exact_function_gradients(golden):
+    """The recorded reference gradients (shifts detached, translate.py:727-740) equal the
+    autograd gradients of the exact log-sum-exp function, so the GPU backward can be
+    checked against either."""
+    import torch
+
+    a = torch.from_numpy(golden["matmul_logu/in0"].astype(np.float64)).requires_grad_(True)
+    b = torch.from_numpy(golden["matmul_logu/in1"].astype(np.float64)).requires_grad_(True)
+    w = torch.from_numpy(golden["matmul_logu/logspace_max/grad_weights"].astype(np.float64))
+    (torch.logsumexp(a[:, :, None] + b[None, :, :], dim=1) * w).sum().backward()
+    np.testing.assert_allclose(a.grad.numpy(), golden["matmul_logu/logspace_max/grad0"], rtol=1e-10, atol=1e-14)
+    np.testing.assert_allclose(b.grad.numpy(), golden["matmul_logu/logspace_max/grad1"], rtol=1e-10, atol=1e-14)
