@@ -157,6 +157,26 @@ def main(reference_root: str) -> None:
     prog, _ = xe.extract_program(expr, "logspace_max")
     record("cp_layer", prog, [x.numpy(), w_logits.numpy()])
 
+    # mixing layer of the quad-graph circuits (the demo's 'bhu,uh->bu' over stacked children,
+    # demo/cirkit.py:163-169) and a two-level Tucker circuit fragment
+    torch.manual_seed(6)
+    children = [torch.randn(48, 20) - 3.0 for _ in range(3)]
+    mix_logits = torch.randn(20, 3)
+    stacked = xe.stack([xe.exp(xe.array(ch)) for ch in children], axis=1)
+    expr = xe.log(xe.einsum("bhu,uh->bu", stacked, xe.softmax(Parameter(xe.array(mix_logits)), axis=1)))
+    prog, args = xe.extract_program(expr, "logspace_max")
+    record("mixing_layer", prog, [a.backend_array.numpy() for a in args])
+
+    torch.manual_seed(7)
+    leaves = [torch.randn(12, 4, 32) - 3.0 for _ in range(3)]
+    w1 = torch.randn(4, 32, 32, 32)
+    w2 = torch.randn(4, 32, 32, 32)
+    e = [xe.exp(xe.array(t)) for t in leaves]
+    lvl1 = xe.einsum("bfi,bfj,foij->bfo", e[0], e[1], xe.softmax(Parameter(xe.array(w1)), axis=(2, 3)))
+    expr = xe.log(xe.einsum("bfi,bfj,foij->bfo", lvl1, e[2], xe.softmax(Parameter(xe.array(w2)), axis=(2, 3))))
+    prog, args = xe.extract_program(expr, "logspace_max")
+    record("tucker_two_levels", prog, [a.backend_array.numpy() for a in args])
+
     torch.manual_seed(4)
     for name, shape, axis in (("softmax_rows", (6, 37), 1), ("softmax_block", (3, 5, 7), (1, 2)), ("softmax_mid", (4, 9, 5), 1), ("softmax_wide", (3, 1500), 1)):
         x = 2.0 * torch.randn(*shape)
