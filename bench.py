@@ -343,7 +343,8 @@ def run_ours(args, rank: int, world: int, device: torch.device, dist_on: bool) -
     c_ms = time_region(circuit_step, c_steps, max(3, args.warmup), dist_on) / c_steps
     c_e2e_ms = time_region(lambda record: circ.e2e_step(), max(3, c_steps // 2), 2, dist_on) / max(3, c_steps // 2)
     flops_sample = circ.circuit.flops_per_sample()
-    bytes_sample = circ.circuit.hbm_bytes_per_sample()
+    state_table = circ.circuit.uses_state_table(circ.batch)
+    bytes_sample = circ.circuit.hbm_bytes_per_sample(state_table)
     c_value = world * circ.batch / (c_ms * 1e-3)
     del circ
     torch.cuda.empty_cache()
@@ -362,6 +363,8 @@ def run_ours(args, rank: int, world: int, device: torch.device, dist_on: bool) -
         "secondary": {
             "metric": "circuit samples/s", "value": round(c_value, 1), "unit": "samples/s",
             "workload": f"folded 32x32 quad-tree CP circuit, K=64, 256 states, batch {args.circuit_batch} per GPU, uint8 pixels seed 3",
+            "first_layer": "state table (F0 x 256 rows) + gathered Hadamard pairs" if state_table else "per sample, gather fused",
+            "hbm_bytes_per_sample": bytes_sample,
             "ms_per_step": round(c_ms, 4),
             "hbm_frac": round(bytes_sample * c_value / world / 1e9 / peaks["hbm_gbs"], 4),
             "hbm_gbs_algorithmic": round(bytes_sample * c_value / world / 1e9, 1),

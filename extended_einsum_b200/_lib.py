@@ -112,6 +112,17 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
             _c_i32, _c_ptr, _c_size, _c_ptr,  # shift_mode, workspace, bytes, stream
         ],
     ),
+    "xe_logspace_gemm_gather_pair": (
+        _c_i32,
+        [
+            _c_ptr, _c_i64, _c_i64, _c_i64, _c_ptr, _c_i64, _c_ptr,  # table, strides, states, pixels, stride, var
+            _c_i64,  # fold_offset
+            _c_ptr, _c_i64, _c_i64, _c_i64, _c_i32,  # b, strides, b_linear
+            _c_ptr, _c_i64, _c_i64, _c_i64,  # c, strides
+            _c_i64, _c_i64, _c_i64, _c_i64,  # folds, batch, n, k
+            _c_i32, _c_ptr, _c_size, _c_ptr,  # shift_mode, workspace, bytes, stream
+        ],
+    ),
     "xe_scaled_gemm": (
         _c_i32,
         [

@@ -11,11 +11,21 @@ circuit), and a root sum 'ab,cb->ac'.
 Per forward pass the launches are:
   1  log-softmax of the categorical logits over the states      (xe_softmax, log output)
   L  softmax of each level's sum-layer logits                     (xe_softmax)
-  1  first CP sum layer with the categorical gather fused into
-     its A rows                                                   (xe_logspace_gemm_gather)
-  L-1 CP sum layers, the Hadamard product fused into the A operand (xe_logspace_gemm, a2)
+  1  first CP sum layer over every state of each variable: the
+     state table T[f, s, :] (F0 x states rows instead of F0 x B)  (xe_logspace_gemm)
+  1  second CP sum layer, its A rows the Hadamard product of two
+     gathered state-table rows                                    (xe_logspace_gemm_gather_pair)
+  L-2 CP sum layers, the Hadamard product fused into the A operand (xe_logspace_gemm, a2)
   1  root softmax + 1 root sum layer                              (xe_softmax, xe_logspace_gemm)
 and the whole sequence can be captured in one CUDA graph.
+
+A row of the first layer depends on the sample only through the pixel value of
+its variable, so its output for sample b is row pixels[b, var[f]] of the state
+table, computed by the same kernel on the same row: the values are those of the
+per-sample layer.  For batches smaller than half the states, and when the
+level parameters need gradients, the first layer runs per sample instead
+(the categorical gather fused into it, xe_logspace_gemm_gather, or the
+differentiable gather + contraction).
 
 Layout in HBM (fp32, contiguous): level output (F, B, K) with the batch
 inner to the fold, so that the two Hadamard halves of level l+1 are the two
@@ -107,22 +117,29 @@ class QuadTreeCircuit:
         k = self.units
         return 2 * k * k * sum(self.fold_counts) + 2 * k
 
-    def hbm_bytes_per_sample(self) -> int:
+    def hbm_bytes_per_sample(self, state_table: bool = False) -> int:
         """HBM bytes per sample that the layer kernels must move.
 
-        Level 0 reads the sample's V uint8 pixels (its categorical
+        Per sample: level 0 reads the sample's V uint8 pixels (its categorical
         log-probability rows come from a table that stays in L2) and writes
         (V, K); level l >= 1 reads the previous output (2F_l, K), the two
         Hadamard halves, and writes (F_l, K); the root reads (2, K) and
-        writes one value.  fp32 values.
+        writes one value.  fp32 values.  With the state table, level 0 is not
+        written per sample and level 1 reads its rows from the table (L2):
+        the sample's bytes are its pixels and levels 1 and up, less level 1's
+        reads.
         """
         k = self.units
         counts = self.fold_counts
-        elements = counts[0] * k  # level 0 output
-        for f in counts[1:]:
-            elements += 2 * f * k + f * k
+        elements = 0 if state_table else counts[0] * k  # level 0 output
+        for level, f in enumerate(counts[1:], start=1):
+            elements += (0 if state_table and level == 1 else 2 * f * k) + f * k
         elements += 2 * k + 1
         return 4 * elements + self.variables
+
+    def uses_state_table(self, batch: int) -> bool:
+        """Whether the first layer runs over the states (cheaper once the batch reaches half of them)."""
+        return 2 * batch >= self.states and len(self.fold_counts) >= 2
 
 
 class CircuitForward:
@@ -142,8 +159,9 @@ class CircuitForward:
         if ops._needs_grad(self.categorical):
             raise NotImplementedError("CircuitForward: no backward for the categorical input table on this path")
         table = ops.softmax(self.categorical, 1, log_output=True)
-        # the fused first layer has no backward: with gradients the gather runs on its own
+        # the fused first layers have no backward: with gradients the gather runs on its own
         differentiable = ops._needs_grad(*self.levels, self.root)
+        state_table = not differentiable and self.circuit.uses_state_table(pixels.shape[0])
         y = None
         for level, logits in enumerate(self.levels):
             w = ops.softmax(logits, 2)  # (F, O, K) linear weights
@@ -151,9 +169,15 @@ class CircuitForward:
             if level == 0 and differentiable:
                 x = ops.categorical_gather(table, pixels, self.var_of_fold)
                 y = ops.logspace_gemm(x, b_op, b_linear=True, shift=self.shift)
+            elif level == 0 and state_table:
+                # the first sum layer for every state of each variable: (F0, states, K)
+                y = ops.logspace_gemm(table, b_op, b_linear=True, shift=self.shift)
             elif level == 0:
                 # the categorical gather is fused into the first sum layer's A rows
                 y = ops.logspace_gemm_gather(table, pixels, self.var_of_fold, b_op, b_linear=True, shift=self.shift)
+            elif level == 1 and state_table:
+                # both Hadamard halves gathered from the state table
+                y = ops.logspace_gemm_gather_pair(y, pixels, self.var_of_fold, b_op, b_linear=True, shift=self.shift)
             else:
                 half = y.shape[0] // 2
                 y = ops.logspace_gemm(y[:half], b_op, a2=y[half:], b_linear=True, shift=self.shift)

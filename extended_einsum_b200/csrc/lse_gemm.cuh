@@ -55,7 +55,12 @@ enum AMode : int { kALog = 0, kALinear = 1, kATucker = 2 };
 // or per-thread global loads (any layout).
 // kAGather: the A rows are gathered rows of a table (Params::g_pixels), staged in
 // the same swizzled ring by the producer warp with 16-byte cp.async copies.
-enum ASource : int { kATma = 0, kATma2 = 1, kALdg = 2, kAGather = 3 };
+// kAGather2: two gathered rows per A row (folds bb and bb + Params::g_pair of the
+// table), staged like the kATma2 pair and added by the A warps.
+enum ASource : int { kATma = 0, kATma2 = 1, kALdg = 2, kAGather = 3, kAGather2 = 4 };
+
+__host__ __device__ constexpr bool a_pair(int asrc) { return asrc == kATma2 || asrc == kAGather2; }
+__host__ __device__ constexpr bool a_gathered(int asrc) { return asrc == kAGather || asrc == kAGather2; }
 // Where the raw B tiles come from: a TMA-filled staging ring (16-byte aligned
 // strides), or global loads with or without 16-byte vectors.
 enum BSource : int { kBTma = 0, kBLdgVec = 1, kBLdg = 2 };
@@ -82,6 +87,9 @@ struct Params {
   const int32_t* g_var;  // nullptr: variable bb
   int64_t g_stride;
   int g_states;
+  // > 0: the row gathered from fold bb + g_pair (its variable var[bb + g_pair]) is added
+  // (the Hadamard product of two input units feeding the sum layer)
+  int64_t g_pair;
   // Tucker layer: l (rows, folds, I), r (rows, folds, J) contiguous; batch = fold
   const float* tl;
   const float* tr;
@@ -109,7 +117,7 @@ struct Cfg {
   static constexpr int kThreads = (kProducerWarp + 1 + 4 * (kDrainGroups - 1)) * 32;
   static constexpr int kColShiftBytes = 4 * kDrainGroups * BN * 4;  // [drain warp][BN]
   static constexpr int kOutBytes = kBM * 32 * 4;       // one [128 rows][32 cols] output staging buffer
-  static constexpr int kAStageBytes = ASRC == kATma2 ? 2 * kATileBytes : kATileBytes;
+  static constexpr int kAStageBytes = a_pair(ASRC) ? 2 * kATileBytes : kATileBytes;
   // everything except the two TMA rings and the output staging
   static constexpr int kFixed = 1024 + kStages * kStageBytes + kRunningBytes + kShiftBytes + kColShiftBytes + 512;
   static constexpr int kBRawBytes = BSRC == kBTma ? kBTile : 0;
@@ -302,24 +310,31 @@ struct ARow {
   float sl = 0.0f;
   float er[kTJ];
 
+  // Element offset of the table row that pixel (m, var[fold]) selects in fold `fold`.
+  __device__ static int64_t gathered_row(const Params& p, int64_t fold, int m, bool valid) {
+    int64_t v = p.g_var ? (int64_t)__ldg(p.g_var + fold) : fold;
+    if (v < 0 || v >= p.g_stride) {
+      record_bad_index(kSiteGemmGatherState);
+      v = 0;
+    }
+    int64_t state = valid ? (int64_t)__ldg(p.g_pixels + (int64_t)m * p.g_stride + v) : 0;
+    if (state >= p.g_states) {
+      record_bad_index(kSiteGemmGatherState);
+      state = p.g_states - 1;
+    }
+    return fold * p.a_sb + state * p.a_sm;
+  }
+
   __device__ void set_row(const Params& p, int bb, int m) {
     valid = m < p.M;
-    int64_t base = (int64_t)bb * p.a_sb + (int64_t)(valid ? m : 0) * p.a_sm;
+    const int64_t base = (int64_t)bb * p.a_sb + (int64_t)(valid ? m : 0) * p.a_sm;
     if (p.g_pixels) {
-      int64_t v = p.g_var ? (int64_t)__ldg(p.g_var + bb) : (int64_t)bb;
-      if (v < 0 || v >= p.g_stride) {
-        record_bad_index(kSiteGemmGatherState);
-        v = 0;
-      }
-      int64_t state = valid ? (int64_t)__ldg(p.g_pixels + (int64_t)m * p.g_stride + v) : 0;
-      if (state >= p.g_states) {
-        record_bad_index(kSiteGemmGatherState);
-        state = p.g_states - 1;
-      }
-      base = (int64_t)bb * p.a_sb + state * p.a_sm;
+      row = p.a + gathered_row(p, bb, m, valid);
+      row2 = p.g_pair > 0 ? p.a + gathered_row(p, bb + p.g_pair, m, valid) : nullptr;
+    } else {
+      row = p.a + base;
+      row2 = p.a2 ? p.a2 + base : nullptr;
     }
-    row = p.a + base;
-    row2 = p.a2 ? p.a2 + base : nullptr;
     step = p.a_sk;
   }
 
@@ -452,7 +467,7 @@ __device__ __forceinline__ void load_staged_row(uint32_t stage, int r, bool vali
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     float4 x = lds_v4(row + ((j ^ (r & 7)) << 4));
-    if (ASRC == kATma2) {
+    if (a_pair(ASRC)) {
       const float4 y = lds_v4(row + kATileBytes + ((j ^ (r & 7)) << 4));
       x.x += y.x;
       x.y += y.y;
@@ -663,7 +678,7 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
       mbar_init(&shift_empty[c], kDrainWarps);
     }
     for (int s = 0; s < 4; ++s) {
-      mbar_init(&a_full[s], ASRC == kAGather ? 32 : 1);
+      mbar_init(&a_full[s], a_gathered(ASRC) ? 32 : 1);
       mbar_init(&a_empty[s], kAWarps);
       mbar_init(&b_full[s], 1);
       mbar_init(&b_empty[s], kBWarps);
@@ -1113,34 +1128,28 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
         XE_SEGMENT_END(seg_e4, 11);
       }
     }
-  } else if (ASRC == kAGather) {
+  } else if (a_gathered(ASRC)) {
     // ------------------------------------------------------------ gather producer (whole warp)
-    // Lane l stages rows 4l..4l+3 of each k-block: table row pixels[m, var[bb]] of fold bb,
-    // 16-byte cp.async copies into the 128-byte-swizzled layout the A warps read; each lane's
-    // copies complete on a_full with one arrival (a_full counts 32 per phase).  B tiles
-    // come through TMA from lane 0.
+    // Lane l stages rows 4l..4l+3 of each k-block: table row pixels[m, var[bb]] of fold bb
+    // (kAGather2: and row pixels[m, var[bb + g_pair]] of fold bb + g_pair into the second
+    // tile of the stage), 16-byte cp.async copies into the 128-byte-swizzled layout the A
+    // warps read; each lane's copies complete on a_full with one arrival (a_full counts 32
+    // per phase).  B tiles come through TMA from lane 0.
+    constexpr int kRows = ASRC == kAGather2 ? 2 : 1;
     uint32_t ait = 0, bit = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
       int bb, mt, nt;
       decode_tile(p, tile, bb, mt, nt);
-      int64_t v = p.g_var ? (int64_t)__ldg(p.g_var + bb) : (int64_t)bb;
-      if (v < 0 || v >= p.g_stride) {
-        record_bad_index(kSiteGemmGatherState);
-        v = 0;
-      }
-      const float* src[4];
+      const float* src[kRows][4];
       bool valid[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int m = mt * kBM + lane * 4 + i;
         valid[i] = m < p.M;
-        int64_t state = valid[i] ? (int64_t)__ldg(p.g_pixels + (int64_t)m * p.g_stride + v) : 0;
-        if (state >= p.g_states) {
-          record_bad_index(kSiteGemmGatherState);
-          state = p.g_states - 1;
-        }
-        src[i] = p.a + (int64_t)bb * p.a_sb + state * p.a_sm;
+#pragma unroll
+        for (int h = 0; h < kRows; ++h)
+          src[h][i] = p.a + ARow<kALog, 0>::gathered_row(p, (int64_t)bb + h * p.g_pair, m, valid[i]);
       }
       for (int kb = 0; kb < p.num_kb; ++kb) {
         const uint32_t sidx = ait % C::kAStages;
@@ -1157,8 +1166,11 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
           const int r = lane * 4 + i;
           if (!valid[i]) continue;  // the A warps mask rows past M
 #pragma unroll
-          for (int c = 0; c < 8; ++c)
-            if (4 * c < kvalid) cp_async16(dst + r * 128 + ((c ^ (r & 7)) << 4), src[i] + kb * kBK + 4 * c);
+          for (int h = 0; h < kRows; ++h)
+#pragma unroll
+            for (int c = 0; c < 8; ++c)
+              if (4 * c < kvalid)
+                cp_async16(dst + h * kATileBytes + r * 128 + ((c ^ (r & 7)) << 4), src[h][i] + kb * kBK + 4 * c);
         }
         cp_async_arrive_noinc(&a_full[sidx]);
         ++ait;

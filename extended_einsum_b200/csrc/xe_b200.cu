@@ -245,23 +245,28 @@ GemmPlan plan_gemm(const float* a, const float* a2, int64_t a_sb, int64_t a_sm, 
   return g;
 }
 
-// The gathered-row source: K-major B staged by TMA or 16-byte loads only.
-template <int BN>
+// The gathered-row sources: K-major B staged by TMA or 16-byte loads only.
+template <int BN, int ASRC>
 xe_status launch_gemm_gather(const Params& q, const GemmPlan& g, cudaStream_t s) {
   using namespace xe::gemm;
-  if (g.bsrc == kBTma) return launch_gemm_t<BN, kALog, kAGather, true, kBTma, 0>(q, g.ma, g.ma2, g.mb, s);
-  return launch_gemm_t<BN, kALog, kAGather, true, kBLdgVec, 0>(q, g.ma, g.ma2, g.mb, s);
+  if (g.bsrc == kBTma) return launch_gemm_t<BN, kALog, ASRC, true, kBTma, 0>(q, g.ma, g.ma2, g.mb, s);
+  return launch_gemm_t<BN, kALog, ASRC, true, kBLdgVec, 0>(q, g.ma, g.ma2, g.mb, s);
+}
+
+template <int ASRC>
+xe_status launch_gemm_gather(const Params& q, const GemmPlan& g, cudaStream_t s) {
+  return g.bn == 32 ? launch_gemm_gather<32, ASRC>(q, g, s)
+                    : g.bn == 64 ? launch_gemm_gather<64, ASRC>(q, g, s) : launch_gemm_gather<128, ASRC>(q, g, s);
 }
 
 xe_status launch_gemm(const Params& p, const GemmPlan& g, bool a_linear, bool bk, cudaStream_t s) {
   using namespace xe::gemm;
   Params q = p;
   set_tiling(q, g.bn);
-  if (g.asrc == kAGather) {
+  if (a_gathered(g.asrc)) {
     if (a_linear || !bk || g.bsrc == kBLdg)
       return fail(XE_ERR_NOT_SUPPORTED, "xe_logspace_gemm_gather: staged gather needs a log table and K-major B");
-    return g.bn == 32 ? launch_gemm_gather<32>(q, g, s) : g.bn == 64 ? launch_gemm_gather<64>(q, g, s)
-                                                                      : launch_gemm_gather<128>(q, g, s);
+    return g.asrc == kAGather ? launch_gemm_gather<kAGather>(q, g, s) : launch_gemm_gather<kAGather2>(q, g, s);
   }
 #define XE_LAUNCH_BN(BN)                                                                                           \
   do {                                                                                                             \
@@ -409,6 +414,7 @@ struct GatherA {
   const int32_t* var;
   int64_t stride;
   int states;
+  int64_t pair;  // > 0: the row of fold + pair is added (Params::g_pair)
 };
 
 xe_status gemm_launch(const float* a, const float* a2, int64_t a_sb, int64_t a_sm, int64_t a_sk, bool a_linear,
@@ -446,6 +452,7 @@ xe_status gemm_launch(const float* a, const float* a2, int64_t a_sb, int64_t a_s
     p.g_var = gather->var;
     p.g_stride = gather->stride;
     p.g_states = gather->states;
+    p.g_pair = gather->pair;
     p.a_vec = (k % 4 == 0 && a_sm % 4 == 0 && a_sb % 4 == 0 && aligned16(a)) ? 1 : 0;
   }
   const bool bk = !(b_sn == 1) && b_sk == 1;
@@ -562,29 +569,33 @@ xe_status xe_logspace_gemm_noalloc(const float* a, const float* a2, int64_t a_sb
                           m, n, k, shift_mode, scratch, XE_NOALLOC_SCRATCH_BYTES, stream);
 }
 
-xe_status xe_logspace_gemm_gather(const float* table, int64_t t_sf, int64_t t_ss, int64_t states, const uint8_t* pixels,
-                                  int64_t pixel_stride, const int32_t* var_of_fold, const float* b, int64_t b_sb,
-                                  int64_t b_sk, int64_t b_sn, int32_t b_linear, float* c, int64_t c_sb, int64_t c_sm,
-                                  int64_t c_sn, int64_t folds, int64_t batch, int64_t n, int64_t k, int32_t shift_mode,
-                                  void* workspace, size_t workspace_bytes, void* stream) {
-  xe_status st = gemm_check("xe_logspace_gemm_gather", table, b, c, folds, batch, n, k);
+}  // extern "C"
+
+namespace {
+
+// The sum layer over gathered table rows; pair > 0 adds the row of fold f + pair.
+xe_status gather_gemm(const char* who, const float* table, int64_t t_sf, int64_t t_ss, int64_t states,
+                      const uint8_t* pixels, int64_t pixel_stride, const int32_t* var_of_fold, int64_t pair,
+                      const float* b, int64_t b_sb, int64_t b_sk, int64_t b_sn, int32_t b_linear, float* c,
+                      int64_t c_sb, int64_t c_sm, int64_t c_sn, int64_t folds, int64_t batch, int64_t n, int64_t k,
+                      int32_t shift_mode, void* workspace, size_t workspace_bytes, void* stream) {
+  xe_status st = gemm_check(who, table, b, c, folds, batch, n, k);
   if (st != XE_OK) return st;
-  if (!pixels) return fail(XE_ERR_INVALID_ARGUMENT, "xe_logspace_gemm_gather: null pixels");
+  if (!pixels) return fail(XE_ERR_INVALID_ARGUMENT, "%s: null pixels", who);
   if (states <= 0 || states > 256)
-    return fail(XE_ERR_INVALID_ARGUMENT, "xe_logspace_gemm_gather: uint8 pixels address 1 to 256 states (got %lld)",
-                (long long)states);
-  if (pixel_stride <= 0) return fail(XE_ERR_INVALID_ARGUMENT, "xe_logspace_gemm_gather: pixel_stride must be positive");
+    return fail(XE_ERR_INVALID_ARGUMENT, "%s: uint8 pixels address 1 to 256 states (got %lld)", who, (long long)states);
+  if (pixel_stride <= 0) return fail(XE_ERR_INVALID_ARGUMENT, "%s: pixel_stride must be positive", who);
+  if (pair < 0) return fail(XE_ERR_INVALID_ARGUMENT, "%s: negative fold offset %lld", who, (long long)pair);
   if (shift_mode != XE_SHIFT_MAX && shift_mode != XE_SHIFT_MIN)
-    return fail(XE_ERR_INVALID_ARGUMENT, "xe_logspace_gemm_gather: unknown shift mode %d", shift_mode);
+    return fail(XE_ERR_INVALID_ARGUMENT, "%s: unknown shift mode %d", who, shift_mode);
   if (k > 128)
-    return fail(XE_ERR_NOT_SUPPORTED, "xe_logspace_gemm_gather: at most 128 units per input row (got %lld)", (long long)k);
+    return fail(XE_ERR_NOT_SUPPORTED, "%s: at most 128 units per input row (got %lld)", who, (long long)k);
   if (folds == 0 || batch == 0 || n == 0) return XE_OK;
   const size_t need = xe_logspace_gemm_workspace_size(folds, batch, n, k, 1, b_linear);
   if (need > 0 && (workspace == nullptr || workspace_bytes < need))
-    return fail(XE_ERR_INVALID_ARGUMENT, "xe_logspace_gemm_gather: workspace of %zu bytes required, %zu given", need,
-                workspace_bytes);
+    return fail(XE_ERR_INVALID_ARGUMENT, "%s: workspace of %zu bytes required, %zu given", who, need, workspace_bytes);
   if ((reinterpret_cast<uintptr_t>(workspace) & (kAlign - 1)) != 0)
-    return fail(XE_ERR_INVALID_ARGUMENT, "xe_logspace_gemm_gather: workspace must be 256-byte aligned");
+    return fail(XE_ERR_INVALID_ARGUMENT, "%s: workspace must be 256-byte aligned", who);
   cudaStream_t s = as_stream(stream);
   float* shift_b = nullptr;
   if (!b_linear) {
@@ -599,19 +610,49 @@ xe_status xe_logspace_gemm_gather(const float* table, int64_t t_sf, int64_t t_ss
   const bool bk = !(b_sn == 1) && b_sk == 1;
   if (env_int("XE_GEMM_NO_TMA", 0) == 0 && k % 4 == 0 && t_ss % 4 == 0 && t_sf % 4 == 0 && aligned16(table) && bk) {
     using namespace xe::gemm;
+    // the staging footprint of a (pair) gather is that of the (pair) TMA source
+    const int like = pair > 0 ? kATma2 : kATma;
     int bsrc = plan.bsrc;
-    if (bsrc == kBTma && !b_ring_fits(plan.bn, kATma)) bsrc = kBLdgVec;
+    if (bsrc == kBTma && !b_ring_fits(plan.bn, like)) bsrc = kBLdgVec;
     const bool b_vec = aligned16(b) && b_sb % 4 == 0 && k % 4 == 0 && b_sn % 4 == 0;
     if (bsrc != kBTma && b_vec) bsrc = kBLdgVec;
     // the in-kernel row shift needs every k-block of a tile staged at once
-    if ((bsrc == kBTma || bsrc == kBLdgVec) && k <= staged_k_capacity(plan.bn, kATma, bsrc)) {
-      plan.asrc = kAGather;
+    if ((bsrc == kBTma || bsrc == kBLdgVec) && k <= staged_k_capacity(plan.bn, like, bsrc)) {
+      plan.asrc = pair > 0 ? kAGather2 : kAGather;
       plan.bsrc = bsrc == kBTma ? kBTma : kBLdgVec;
     }
   }
-  const GatherA gather{pixels, var_of_fold, pixel_stride, (int)states};
+  const GatherA gather{pixels, var_of_fold, pixel_stride, (int)states, pair};
   return gemm_launch(table, nullptr, t_sf, t_ss, 1, false, nullptr, b, b_sb, b_sk, b_sn, shift_b, c, c_sb, c_sm, c_sn,
                      folds, batch, n, k, shift_mode == XE_SHIFT_MIN, plan, s, false, &gather);
+}
+
+}  // namespace
+
+extern "C" {
+
+xe_status xe_logspace_gemm_gather(const float* table, int64_t t_sf, int64_t t_ss, int64_t states, const uint8_t* pixels,
+                                  int64_t pixel_stride, const int32_t* var_of_fold, const float* b, int64_t b_sb,
+                                  int64_t b_sk, int64_t b_sn, int32_t b_linear, float* c, int64_t c_sb, int64_t c_sm,
+                                  int64_t c_sn, int64_t folds, int64_t batch, int64_t n, int64_t k, int32_t shift_mode,
+                                  void* workspace, size_t workspace_bytes, void* stream) {
+  return gather_gemm("xe_logspace_gemm_gather", table, t_sf, t_ss, states, pixels, pixel_stride, var_of_fold, 0, b,
+                     b_sb, b_sk, b_sn, b_linear, c, c_sb, c_sm, c_sn, folds, batch, n, k, shift_mode, workspace,
+                     workspace_bytes, stream);
+}
+
+xe_status xe_logspace_gemm_gather_pair(const float* table, int64_t t_sf, int64_t t_ss, int64_t states,
+                                       const uint8_t* pixels, int64_t pixel_stride, const int32_t* var_of_fold,
+                                       int64_t fold_offset, const float* b, int64_t b_sb, int64_t b_sk, int64_t b_sn,
+                                       int32_t b_linear, float* c, int64_t c_sb, int64_t c_sm, int64_t c_sn,
+                                       int64_t folds, int64_t batch, int64_t n, int64_t k, int32_t shift_mode,
+                                       void* workspace, size_t workspace_bytes, void* stream) {
+  if (fold_offset <= 0)
+    return fail(XE_ERR_INVALID_ARGUMENT, "xe_logspace_gemm_gather_pair: fold_offset must be positive (got %lld)",
+                (long long)fold_offset);
+  return gather_gemm("xe_logspace_gemm_gather_pair", table, t_sf, t_ss, states, pixels, pixel_stride, var_of_fold,
+                     fold_offset, b, b_sb, b_sk, b_sn, b_linear, c, c_sb, c_sm, c_sn, folds, batch, n, k, shift_mode,
+                     workspace, workspace_bytes, stream);
 }
 
 xe_status xe_logspace_gemm_shifted(const float* a, const float* a2, int64_t a_sb, int64_t a_sm, int64_t a_sk,

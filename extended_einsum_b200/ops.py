@@ -348,38 +348,69 @@ def logspace_gemm_gather(
     is (folds, states, K) with K contiguous, ``pixels`` (batch, variables)
     uint8, ``b`` (folds, K, N).  Returns (folds, batch, N).
     """
-    _no_backward("logspace_gemm_gather", log_table, b)
-    device = _check_tensors("logspace_gemm_gather", log_table, b)
+    return _gather_gemm("logspace_gemm_gather", log_table, pixels, var_of_fold, b, 0, b_linear, shift)
+
+
+def logspace_gemm_gather_pair(
+    state_table: torch.Tensor,
+    pixels: torch.Tensor,
+    var_of_fold: torch.Tensor | None,
+    b: torch.Tensor,
+    *,
+    b_linear: bool = False,
+    shift: str = "max",
+) -> torch.Tensor:
+    """The sum layer over the Hadamard product of two gathered halves (xe_logspace_gemm_gather_pair).
+
+    ``state_table`` is (2F, states, K): row (f, s) is the log-domain output
+    of the previous layer for pixel value s of fold f's variable.  With
+    A[f,b,:] = T[f, pixels[b, var[f]], :] + T[f+F, pixels[b, var[f+F]], :],
+    returns C[f,b,n] = log(sum_k exp(A[f,b,k] - s) B'[f,k,n]) + shifts, (F, batch, N)
+    for ``b`` (F, K, N).
+    """
+    if state_table.dim() != 3 or state_table.shape[0] % 2:
+        raise ValueError("logspace_gemm_gather_pair: expected a (2F, states, K) state table")
+    return _gather_gemm("logspace_gemm_gather_pair", state_table, pixels, var_of_fold, b,
+                        state_table.shape[0] // 2, b_linear, shift)
+
+
+def _gather_gemm(name, log_table, pixels, var_of_fold, b, fold_offset, b_linear, shift):
+    _no_backward(name, log_table, b)
+    device = _check_tensors(name, log_table, b)
     if pixels.device != device or pixels.dtype != torch.uint8 or pixels.dim() != 2:
-        raise ValueError("logspace_gemm_gather: pixels must be a (batch, variables) uint8 tensor on the table's device")
+        raise ValueError(f"{name}: pixels must be a (batch, variables) uint8 tensor on the table's device")
     if pixels.stride(1) != 1:
         pixels = pixels.contiguous()
     if log_table.dim() != 3 or b.dim() != 3:
-        raise ValueError("logspace_gemm_gather: expected a (folds, states, K) table and a (folds, K, N) operand")
+        raise ValueError(f"{name}: expected a (folds, states, K) table and a (folds, K, N) operand")
     if log_table.stride(2) != 1:
         log_table = log_table.contiguous()
-    folds, states, k = log_table.shape
+    table_folds, states, k = log_table.shape
+    folds = table_folds - fold_offset
     if b.shape[0] != folds or b.shape[1] != k:
-        raise ValueError(f"logspace_gemm_gather: incompatible shapes {tuple(log_table.shape)} and {tuple(b.shape)}")
+        raise ValueError(f"{name}: incompatible shapes {tuple(log_table.shape)} and {tuple(b.shape)}")
     if var_of_fold is not None:
-        if var_of_fold.dtype != torch.int32 or var_of_fold.device != device or var_of_fold.numel() != folds:
-            raise ValueError("logspace_gemm_gather: var_of_fold must be int32 with one entry per fold")
+        if var_of_fold.dtype != torch.int32 or var_of_fold.device != device or var_of_fold.numel() != table_folds:
+            raise ValueError(f"{name}: var_of_fold must be int32 with one entry per table fold")
         var_of_fold = var_of_fold.contiguous()
-    elif pixels.shape[1] < folds:
-        raise ValueError("logspace_gemm_gather: fewer pixel variables than folds")
+    elif pixels.shape[1] < table_folds:
+        raise ValueError(f"{name}: fewer pixel variables than table folds")
     batch = pixels.shape[0]
     n = b.shape[2]
     out = torch.empty((folds, batch, n), device=device, dtype=torch.float32)
     lib = _lib.load()
     ws_bytes = lib.xe_logspace_gemm_workspace_size(folds, batch, n, k, 1, int(b_linear))
     ws = torch.empty(ws_bytes, device=device, dtype=torch.uint8) if ws_bytes else None
-    status = lib.xe_logspace_gemm_gather(
-        log_table.data_ptr(), log_table.stride(0), log_table.stride(1), states, pixels.data_ptr(), pixels.stride(0),
-        _ptr(var_of_fold), b.data_ptr(), b.stride(0), b.stride(1), b.stride(2), int(b_linear),
-        out.data_ptr(), out.stride(0), out.stride(1), out.stride(2), folds, batch, n, k, _shift(shift),
-        _ptr(ws), ws_bytes, _stream(device),
-    )
-    _lib.check(status, "xe_logspace_gemm_gather")
+    head = (log_table.data_ptr(), log_table.stride(0), log_table.stride(1), states, pixels.data_ptr(),
+            pixels.stride(0), _ptr(var_of_fold))
+    tail = (b.data_ptr(), b.stride(0), b.stride(1), b.stride(2), int(b_linear),
+            out.data_ptr(), out.stride(0), out.stride(1), out.stride(2), folds, batch, n, k, _shift(shift),
+            _ptr(ws), ws_bytes, _stream(device))
+    if fold_offset:
+        status = lib.xe_logspace_gemm_gather_pair(*head, fold_offset, *tail)
+    else:
+        status = lib.xe_logspace_gemm_gather(*head, *tail)
+    _lib.check(status, "xe_" + name)
     return out
 
 

@@ -209,6 +209,27 @@ xe_status xe_logspace_gemm_gather(const float* table, int64_t t_sf, int64_t t_ss
                                   int64_t c_sn, int64_t folds, int64_t batch, int64_t n, int64_t k, int32_t shift_mode,
                                   void* workspace, size_t workspace_bytes, void* stream);
 
+/* The second sum layer of a circuit over categorical input units, with the
+ * first layer read from a state table and the Hadamard product of its two
+ * halves fused (replaces the first layer's per-sample output and the folded
+ * Hadamard product 'cab,cab->cab', translate.py:706-718, that the next CP
+ * layer 'dac,dbc->dab', preprocess.py:1310-1337, consumes):
+ *   A[f,b,:] = T[f, x_b, :] + T[f + fold_offset, x'_b, :]
+ *   with x_b = pixels[b*pixel_stride + var_of_fold[f]] and
+ *   x'_b = pixels[b*pixel_stride + var_of_fold[f + fold_offset]];
+ *   C[f,b,n] = log( sum_k exp(A[f,b,k] - s) B'[f,k,n] ) + s (+ B's shift).
+ * T is then the first layer's output for every state, (folds0, states, k),
+ * which one xe_logspace_gemm of the categorical table computes: a row of the
+ * first layer depends on the sample only through its pixel value.  Every
+ * argument as in xe_logspace_gemm_gather; fold_offset > 0, and the table and
+ * var_of_fold hold at least folds + fold_offset folds. */
+xe_status xe_logspace_gemm_gather_pair(const float* table, int64_t t_sf, int64_t t_ss, int64_t states,
+                                       const uint8_t* pixels, int64_t pixel_stride, const int32_t* var_of_fold,
+                                       int64_t fold_offset, const float* b, int64_t b_sb, int64_t b_sk, int64_t b_sn,
+                                       int32_t b_linear, float* c, int64_t c_sb, int64_t c_sm, int64_t c_sn,
+                                       int64_t folds, int64_t batch, int64_t n, int64_t k, int32_t shift_mode,
+                                       void* workspace, size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Log-space Tucker layer 'bfi,bfj,foij->bfo' (the ternary einsum that
  * OptimizeContractionPaths fuses for Tucker circuits, preprocess.py:1095-1106,

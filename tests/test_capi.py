@@ -63,6 +63,11 @@ def test_invalid_arguments_are_rejected_without_launch():
     assert lib.xe_unary(1, 1, 4, 9, None) == _lib.XE_ERR_INVALID_ARGUMENT
     assert lib.xe_categorical_gather(1, 1, 1, None, 1, 1, 300, 4, 1, None) == _lib.XE_ERR_INVALID_ARGUMENT
     assert lib.xe_logspace_reduce(1, 0, 1, 1, 1, 1, 0, 0, 1, None) == _lib.XE_ERR_INVALID_ARGUMENT
+    pair = (1, 64, 64, 4, 1, 8, None)  # table, strides, states, pixels, stride, var
+    tail = (1, 256, 1, 64, 1, 1, 256, 64, 1, 2, 4, 4, 64, 0, None, 0, None)
+    assert lib.xe_logspace_gemm_gather_pair(*pair, 0, *tail) == _lib.XE_ERR_INVALID_ARGUMENT
+    assert "fold_offset" in _lib.last_error()
+    assert lib.xe_logspace_gemm_gather_pair(*pair[:3], 300, *pair[4:], 2, *tail) == _lib.XE_ERR_INVALID_ARGUMENT
 
 
 def test_status_maps_to_reference_exceptions():

@@ -86,6 +86,50 @@ def test_gemm_gather_equals_gather_then_gemm(folds, states, units, batch, n, b_l
     assert ops.device_status() == 0
 
 
+@pytest.mark.parametrize(
+    "folds,states,units,batch,n,b_linear",
+    [(16, 256, 64, 1000, 64, True), (6, 7, 32, 130, 40, False), (3, 256, 128, 257, 1, True), (5, 256, 60, 129, 64, True),
+     (4, 9, 30, 70, 64, True)],
+)
+def test_gemm_gather_pair_equals_gathers_then_gemm(folds, states, units, batch, n, b_linear):
+    """The second sum layer over gathered state-table pairs == two gathers, then the layer with the addend.
+
+    units=30 takes the per-thread gather (rows not 16-byte aligned), the others the staged pair."""
+    g = torch.Generator().manual_seed(7 * folds + states + units)
+    variables = 2 * folds + 3
+    table = (torch.randn(2 * folds, states, units, generator=g) - 4.0).cuda()
+    pixels = torch.randint(states, (batch, variables), generator=g, dtype=torch.uint8).cuda()
+    var = torch.randperm(variables, generator=g)[: 2 * folds].to(torch.int32).cuda()
+    b = (torch.rand(folds, units, n, generator=g) if b_linear else torch.randn(folds, units, n, generator=g)).cuda()
+    fused = ops.logspace_gemm_gather_pair(table, pixels, var, b, b_linear=b_linear)
+    x = ops.categorical_gather(table, pixels, var)
+    unfused = ops.logspace_gemm(x[:folds], b, a2=x[folds:], b_linear=b_linear)
+    log_close(fused.cpu().numpy(), unfused.cpu().numpy(), atol=2e-6, rtol=2e-7)
+    assert ops.device_status() == 0
+
+
+def test_circuit_state_table_equals_per_sample_first_layer(monkeypatch):
+    """The state-table first layer gives the per-sample first layer's log-likelihoods."""
+    circuit = QuadTreeCircuit(8, 8, 64, 256)
+    gen = torch.Generator().manual_seed(11)
+    params = circuit.init_parameters(gen)
+    pixels = torch.randint(256, (300, circuit.variables), generator=gen, dtype=torch.uint8).cuda()
+    dev = {k: (v.cuda() if isinstance(v, torch.Tensor) else [t.cuda() for t in v]) for k, v in params.items()}
+    forward = CircuitForward(circuit, dev)
+    assert circuit.uses_state_table(300)
+    with_table = forward(pixels).cpu().numpy()
+    monkeypatch.setattr(QuadTreeCircuit, "uses_state_table", lambda self, batch: False)
+    per_sample = forward(pixels).cpu().numpy()
+    log_close(with_table, per_sample, atol=2e-6, rtol=2e-7)
+    assert ops.device_status() == 0
+
+
+def test_gather_pair_rejects_odd_table():
+    table = torch.zeros(3, 4, 32).cuda()
+    with pytest.raises(ValueError):
+        ops.logspace_gemm_gather_pair(table, torch.zeros(2, 3, dtype=torch.uint8).cuda(), None, torch.rand(1, 32, 8).cuda())
+
+
 def test_out_of_range_pixels_are_clamped_and_reported():
     g = torch.Generator().manual_seed(5)
     table = torch.log_softmax(torch.randn(4, 10, 32, generator=g), dim=1).cuda()
