@@ -54,7 +54,7 @@ enum AMode : int { kALog = 0, kALinear = 1, kATucker = 2 };
 // 16-byte aligned strides), the same plus a second ring for the fused addend,
 // or per-thread global loads (any layout).
 // kAGather: the A rows are gathered rows of a table (Params::g_pixels), staged in
-// the same swizzled ring by the producer warp with 16-byte cp.async copies.
+// the same swizzled ring by TMA tile::gather4 loads (four table rows each).
 // kAGather2: two gathered rows per A row (folds bb and bb + Params::g_pair of the
 // table), staged like the kATma2 pair and added by the A warps.
 enum ASource : int { kATma = 0, kATma2 = 1, kALdg = 2, kAGather = 3, kAGather2 = 4 };
@@ -108,7 +108,9 @@ struct Cfg {
   static constexpr int kSmemLimit = 232448;
   static constexpr int kBTile = BN * kBK * 4;  // bytes, one of hi/lo (also one raw B tile)
   static constexpr int kStageBytes = 2 * kBTile;
-  static constexpr int kRunningBytes = BN * kBM * 4;
+  // the running sum of the accumulation chunks before the last; gathered sources have
+  // K <= 128 (one chunk) and need none
+  static constexpr int kRunningBytes = a_gathered(ASRC) ? 0 : BN * kBM * 4;
   static constexpr int kShiftBytes = 2 * 2 * kBM * 4;  // [slot][s1,s2][row]
   // Tiles of at most 64 columns have little tensor work per tile and are
   // bound by the epilogue: two drain warp groups take alternate tiles
@@ -249,15 +251,15 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
-// 16-byte asynchronous global -> shared copy (L2 only).
-__device__ __forceinline__ void cp_async16(uint32_t dst, const float* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
-}
-
-// One arrival on `bar` once this thread's earlier cp.async copies have landed
-// (the barrier's expected count includes it).
-__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
-  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+// Four rows (r0..r3, each one box of the 2-D tensor map: columns x .. x+31) gathered into
+// four consecutive 128-byte rows of shared memory at dst, swizzled as the map says.
+__device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap* map, int x, int r0, int r1, int r2, int r3,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(dst),
+      "l"(map), "r"(x), "r"(r0), "r"(r1), "r"(r2), "r"(r3), "r"(smem_u32(bar))
+      : "memory");
 }
 
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
@@ -678,7 +680,7 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
       mbar_init(&shift_empty[c], kDrainWarps);
     }
     for (int s = 0; s < 4; ++s) {
-      mbar_init(&a_full[s], a_gathered(ASRC) ? 32 : 1);
+      mbar_init(&a_full[s], 1);
       mbar_init(&a_empty[s], kAWarps);
       mbar_init(&b_full[s], 1);
       mbar_init(&b_empty[s], kBWarps);
@@ -726,6 +728,7 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
             // at most two k-blocks stays in registers (cur, nxt) and its stages are released here.
             float e = is_min ? INFINITY : -INFINITY;
             const bool keep = C::kDrainGroups == 1 && p.num_kb <= 2;
+            XE_SEGMENT_BEGIN(seg_scan);
             for (int kb = 0; kb < p.num_kb; ++kb) {
               const uint32_t sidx = (ait + kb) % C::kAStages;
               if (!mbar_wait(&a_full[sidx], ((ait + kb) / C::kAStages) & 1, kSiteAStaged, abort_flag)) {
@@ -758,6 +761,7 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
                 }
               }
             }
+            XE_SEGMENT_END(seg_scan, 6);
             if (!ok) break;
             if (keep) {
               __syncwarp();
@@ -1130,49 +1134,73 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
     }
   } else if (a_gathered(ASRC)) {
     // ------------------------------------------------------------ gather producer (whole warp)
-    // Lane l stages rows 4l..4l+3 of each k-block: table row pixels[m, var[bb]] of fold bb
-    // (kAGather2: and row pixels[m, var[bb + g_pair]] of fold bb + g_pair into the second
-    // tile of the stage), 16-byte cp.async copies into the 128-byte-swizzled layout the A
-    // warps read; each lane's copies complete on a_full with one arrival (a_full counts 32
-    // per phase).  B tiles come through TMA from lane 0.
+    // Row r of a tile is table row pixels[m, var[bb]] of fold bb (kAGather2: plus row
+    // pixels[m, var[bb + g_pair]] of fold bb + g_pair, staged in the second tile of the
+    // stage).  tmap_a views the table as (folds * states) rows of K, 128-byte swizzled boxes
+    // of one row x 32 k.  Lane l issues the tile::gather4 loads of rows 4l..4l+3 (512 bytes
+    // at stage + 512 l: the swizzled layout the A warps read); lane 0 arms a_full with the
+    // stage's bytes first.  The pixel values of the next tile are loaded while this tile's
+    // rows are in flight.  B tiles come through TMA from lane 0.
     constexpr int kRows = ASRC == kAGather2 ? 2 : 1;
+    // pixel values of rows 4*lane .. 4*lane+3 of a tile (-1: row past M)
+    auto load_states = [&](int tile, int (&st)[kRows][4]) {
+      int bb, mt, nt;
+      decode_tile(p, tile, bb, mt, nt);
+#pragma unroll
+      for (int h = 0; h < kRows; ++h) {
+        const int64_t fold = (int64_t)bb + h * p.g_pair;
+        int64_t v = p.g_var ? (int64_t)__ldg(p.g_var + fold) : fold;
+        if (v < 0 || v >= p.g_stride) {
+          record_bad_index(kSiteGemmGatherState);
+          v = 0;
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int m = mt * kBM + lane * 4 + i;
+          st[h][i] = m < p.M ? (int)__ldg(p.g_pixels + (int64_t)m * p.g_stride + v) : -1;
+        }
+      }
+    };
     uint32_t ait = 0, bit = 0;
     bool ok = true;
+    int st[kRows][4];
+    if ((int)blockIdx.x < p.num_tiles) load_states(blockIdx.x, st);
     for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
       int bb, mt, nt;
       decode_tile(p, tile, bb, mt, nt);
-      const float* src[kRows][4];
-      bool valid[4];
+      // table rows (fold * states + state; the host checks they fit in 32 bits); a row past M
+      // loads its fold's first row, which the A warps mask
+      int row[kRows][4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int m = mt * kBM + lane * 4 + i;
-        valid[i] = m < p.M;
+      for (int h = 0; h < kRows; ++h)
 #pragma unroll
-        for (int h = 0; h < kRows; ++h)
-          src[h][i] = p.a + ARow<kALog, 0>::gathered_row(p, (int64_t)bb + h * p.g_pair, m, valid[i]);
-      }
+        for (int i = 0; i < 4; ++i) {
+          int state = st[h][i] < 0 ? 0 : st[h][i];
+          if (state >= p.g_states) {
+            record_bad_index(kSiteGemmGatherState);
+            state = p.g_states - 1;
+          }
+          row[h][i] = (bb + h * (int)p.g_pair) * p.g_states + state;
+        }
+      const bool have_next = tile + (int)gridDim.x < p.num_tiles;
+      if (have_next) load_states(tile + gridDim.x, st);
+      XE_SEGMENT_BEGIN(seg_prod);
       for (int kb = 0; kb < p.num_kb; ++kb) {
         const uint32_t sidx = ait % C::kAStages;
-        bool free_slot = true;
-        if (lane == 0) free_slot = mbar_wait(&a_empty[sidx], ((ait / C::kAStages) & 1) ^ 1, kSiteProducer, abort_flag);
-        if (__shfl_sync(0xffffffffu, free_slot ? 1 : 0, 0) == 0) {  // the warp leaves together
+        bool armed = true;
+        if (lane == 0) {
+          armed = mbar_wait(&a_empty[sidx], ((ait / C::kAStages) & 1) ^ 1, kSiteProducer, abort_flag);
+          if (armed) mbar_expect_tx(&a_full[sidx], C::kAStageBytes);
+        }
+        if (__shfl_sync(0xffffffffu, armed ? 1 : 0, 0) == 0) {  // the warp leaves together
           ok = false;
           break;
         }
-        const uint32_t dst = smem_base + C::kOffA + sidx * C::kAStageBytes;
-        const int kvalid = p.K - kb * kBK;  // a multiple of 4 (checked on the host)
+        const uint32_t dst = smem_base + C::kOffA + sidx * C::kAStageBytes + lane * 512;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int r = lane * 4 + i;
-          if (!valid[i]) continue;  // the A warps mask rows past M
-#pragma unroll
-          for (int h = 0; h < kRows; ++h)
-#pragma unroll
-            for (int c = 0; c < 8; ++c)
-              if (4 * c < kvalid)
-                cp_async16(dst + h * kATileBytes + r * 128 + ((c ^ (r & 7)) << 4), src[h][i] + kb * kBK + 4 * c);
-        }
-        cp_async_arrive_noinc(&a_full[sidx]);
+        for (int h = 0; h < kRows; ++h)
+          tma_gather4(dst + h * kATileBytes, &tmap_a, kb * kBK, row[h][0], row[h][1], row[h][2], row[h][3],
+                      &a_full[sidx]);
         ++ait;
         if (BSRC == kBTma && lane == 0) {
           const uint32_t bidx = bit % C::kBRawStages;
@@ -1190,6 +1218,7 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
         }
         ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
       }
+      XE_SEGMENT_END(seg_prod, 12);
     }
   } else if ((ASRC != kALdg || BSRC == kBTma) && lane == 0) {
     // ------------------------------------------------------------ TMA producer

@@ -111,6 +111,21 @@ bool encode_a_map(CUtensorMap* map, const float* base, int64_t batch, int64_t ro
   return r == CUDA_SUCCESS;
 }
 
+// Tensor map of a gather table viewed as `rows` rows of k fp32 (row stride s_row elements):
+// boxes of one row x 32 k, 128-byte swizzle, for tile::gather4 loads of four rows each.
+bool encode_gather_map(CUtensorMap* map, const float* base, int64_t rows, int64_t k, int64_t s_row) {
+  PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+  if (!encode || !aligned16(base) || s_row <= 0 || (s_row * 4) % 16 != 0) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(s_row * 4)};
+  cuuint32_t box[2] = {32, 1};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 // Tensor map of the raw B operand (batch, k, n): MN-major (n contiguous) boxes
 // of BN n x 32 k, K-major (k contiguous) boxes of 32 k x BN n; unswizzled.
 bool encode_b_map(CUtensorMap* map, const float* base, int64_t batch, int64_t k, int64_t n, int64_t s_k, int64_t s_n,
@@ -154,11 +169,20 @@ bool b_ring_fits() {
   return Cfg<BN, ASRC, kBTma>::kFits;
 }
 
-bool b_ring_fits(int bn, int asrc) {
+template <int BN>
+bool b_ring_fits_bn(int asrc) {
   using namespace xe::gemm;
-  if (bn == 128) return asrc == kATma ? b_ring_fits<128, kATma>() : asrc == kATma2 ? b_ring_fits<128, kATma2>() : b_ring_fits<128, kALdg>();
-  if (bn == 64) return asrc == kATma ? b_ring_fits<64, kATma>() : asrc == kATma2 ? b_ring_fits<64, kATma2>() : b_ring_fits<64, kALdg>();
-  return asrc == kATma ? b_ring_fits<32, kATma>() : asrc == kATma2 ? b_ring_fits<32, kATma2>() : b_ring_fits<32, kALdg>();
+  switch (asrc) {
+    case kATma: return b_ring_fits<BN, kATma>();
+    case kATma2: return b_ring_fits<BN, kATma2>();
+    case kAGather: return b_ring_fits<BN, kAGather>();
+    case kAGather2: return b_ring_fits<BN, kAGather2>();
+    default: return b_ring_fits<BN, kALdg>();
+  }
+}
+
+bool b_ring_fits(int bn, int asrc) {
+  return bn == 128 ? b_ring_fits_bn<128>(asrc) : bn == 64 ? b_ring_fits_bn<64>(asrc) : b_ring_fits_bn<32>(asrc);
 }
 
 template <int BN, int AMODE, int ASRC>
@@ -213,11 +237,21 @@ int a_stages(int bsrc) {
   return (bsrc == kBTma && Cfg<BN, ASRC, kBTma>::kFits) ? Cfg<BN, ASRC, kBTma>::kAStages : Cfg<BN, ASRC, kBLdg>::kAStages;
 }
 
+template <int BN>
+int a_stages_bn(int asrc, int bsrc) {
+  using namespace xe::gemm;
+  switch (asrc) {
+    case kATma: return a_stages<BN, kATma>(bsrc);
+    case kATma2: return a_stages<BN, kATma2>(bsrc);
+    case kAGather: return a_stages<BN, kAGather>(bsrc);
+    case kAGather2: return a_stages<BN, kAGather2>(bsrc);
+    default: return 0;
+  }
+}
+
 int staged_k_capacity(int bn, int asrc, int bsrc) {
   using namespace xe::gemm;
-  int stages = 0;
-  if (asrc == kATma) stages = bn == 128 ? a_stages<128, kATma>(bsrc) : bn == 64 ? a_stages<64, kATma>(bsrc) : a_stages<32, kATma>(bsrc);
-  if (asrc == kATma2) stages = bn == 128 ? a_stages<128, kATma2>(bsrc) : bn == 64 ? a_stages<64, kATma2>(bsrc) : a_stages<32, kATma2>(bsrc);
+  const int stages = bn == 128 ? a_stages_bn<128>(asrc, bsrc) : bn == 64 ? a_stages_bn<64>(asrc, bsrc) : a_stages_bn<32>(asrc, bsrc);
   return stages * kBK;
 }
 
@@ -606,19 +640,20 @@ xe_status gather_gemm(const char* who, const float* table, int64_t t_sf, int64_t
   // the A rows are gathered per thread (global loads), their shifts computed in the kernel
   GemmPlan plan = plan_gemm(table, nullptr, t_sf, t_ss, 1, false, b, b_sb, b_sk, b_sn, folds, batch, n, k, true);
   plan.inline_shift = true;
-  // rows staged by 16-byte copies when the table allows them and B is K-major
   const bool bk = !(b_sn == 1) && b_sk == 1;
-  if (env_int("XE_GEMM_NO_TMA", 0) == 0 && k % 4 == 0 && t_ss % 4 == 0 && t_sf % 4 == 0 && aligned16(table) && bk) {
+  // rows staged by TMA gather loads when the table is (folds * states) rows of 16-byte aligned stride
+  const int64_t table_rows = (folds + pair) * states;
+  if (env_int("XE_GEMM_NO_TMA", 0) == 0 && t_sf == states * t_ss && bk && table_rows <= INT32_MAX &&
+      encode_gather_map(&plan.ma, table, table_rows, k, t_ss)) {
     using namespace xe::gemm;
-    // the staging footprint of a (pair) gather is that of the (pair) TMA source
-    const int like = pair > 0 ? kATma2 : kATma;
+    const int asrc = pair > 0 ? kAGather2 : kAGather;
     int bsrc = plan.bsrc;
-    if (bsrc == kBTma && !b_ring_fits(plan.bn, like)) bsrc = kBLdgVec;
+    if (bsrc == kBTma && !b_ring_fits(plan.bn, asrc)) bsrc = kBLdgVec;
     const bool b_vec = aligned16(b) && b_sb % 4 == 0 && k % 4 == 0 && b_sn % 4 == 0;
     if (bsrc != kBTma && b_vec) bsrc = kBLdgVec;
     // the in-kernel row shift needs every k-block of a tile staged at once
-    if ((bsrc == kBTma || bsrc == kBLdgVec) && k <= staged_k_capacity(plan.bn, like, bsrc)) {
-      plan.asrc = pair > 0 ? kAGather2 : kAGather;
+    if ((bsrc == kBTma || bsrc == kBLdgVec) && k <= staged_k_capacity(plan.bn, asrc, bsrc)) {
+      plan.asrc = asrc;
       plan.bsrc = bsrc == kBTma ? kBTma : kBLdgVec;
     }
   }

@@ -111,11 +111,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int site, volatile int* abort,
                                           bool honor_abort = true) {
   const uint32_t addr = smem_u32(bar);
-  if (mbar_try_wait(addr, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
 #ifdef XE_PROFILE
+  // the first try_wait may itself suspend the thread for a while: count it too
   const long long c0 = clock64();
+  if (mbar_try_wait(addr, parity)) {
+    atomicAdd(&g_wait_cycles[site & (kNumSites - 1)], (unsigned long long)(clock64() - c0));
+    return true;
+  }
+#else
+  if (mbar_try_wait(addr, parity)) return true;
 #endif
+  const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(addr, parity)) {
 #ifdef XE_PROFILE
