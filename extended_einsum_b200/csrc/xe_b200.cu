@@ -15,6 +15,7 @@
 
 #include "../../include/xe_b200.h"
 #include "lse_gemm.cuh"
+#include "cp_layer.cuh"
 #include "pointwise.cuh"
 #include "tucker.cuh"
 
@@ -293,10 +294,62 @@ xe_status launch_gemm_gather(const Params& q, const GemmPlan& g, cudaStream_t s)
                     : g.bn == 64 ? launch_gemm_gather<64, ASRC>(q, g, s) : launch_gemm_gather<128, ASRC>(q, g, s);
 }
 
+// Tensor map of an output (batch, m, n) with n contiguous: 32 x 32 blocks, 128-byte swizzle (TMA stores).
+bool encode_c_map(CUtensorMap* map, float* base, int64_t batch, int64_t m, int64_t n, int64_t s_row, int64_t s_batch) {
+  PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+  if (!encode) return false;
+  const int64_t sb = batch > 1 ? s_batch : m * s_row;
+  if (s_row <= 0 || sb <= 0 || (s_row * 4) % 16 != 0 || (sb * 4) % 16 != 0 || !aligned16(base)) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)n, (cuuint64_t)m, (cuuint64_t)batch};
+  cuuint64_t strides[2] = {(cuuint64_t)(s_row * 4), (cuuint64_t)(sb * 4)};
+  cuuint32_t box[3] = {32, 32, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// The circuit's CP sum layer (K = N = 64, log A with its shifts computed in the kernel,
+// linear K-major B staged by TMA, contiguous output, at least 4 tiles per fold) runs on
+// its own kernel (cp_layer.cuh), which gives the same results as lse_gemm_kernel.
+// XE_GEMM_NO_CP_LAYER=1 selects the general kernel.
+xe_status try_cp_layer(const Params& q, const GemmPlan& g, bool a_linear, bool bk, cudaStream_t s, bool& launched) {
+  using namespace xe::gemm;
+  launched = false;
+  if (a_linear || !bk || q.K != xe::cp::kK || q.N != xe::cp::kN || q.shift_b != nullptr || q.shift_a != nullptr ||
+      q.raw_out || q.g_pixels != nullptr || (g.asrc != kATma && g.asrc != kATma2) || g.bsrc != kBTma || g.bn != 64 ||
+      q.c_sn != 1 || q.tiles_m < 4 /* the weight split is per fold */ || env_int("XE_GEMM_NO_CP_LAYER", 0) != 0)
+    return XE_OK;
+  CUtensorMap mc{};
+  if (!encode_c_map(&mc, q.c, q.batch, q.M, q.N, q.c_sm, q.c_sb)) return XE_OK;
+  xe::cp::Params cp{};
+  cp.folds = q.batch;
+  cp.M = q.M;
+  cp.tiles_m = q.tiles_m;
+  cp.num_tiles = q.batch * q.tiles_m;
+  cp.shift_min = q.shift_min;
+  const bool pair = g.asrc == kATma2;
+  const int smem = pair ? xe::cp::Cfg<true>::kSmemBytes : xe::cp::Cfg<false>::kSmemBytes;
+  auto kernel = pair ? xe::cp::cp_layer_kernel<true> : xe::cp::cp_layer_kernel<false>;
+  static std::atomic<uint32_t> attribute_set[2];
+  cudaError_t e = prepare_kernel(kernel, smem, attribute_set[pair ? 1 : 0]);
+  if (e != cudaSuccess) return fail(XE_ERR_CUDA, "xe_logspace_gemm: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  const int grid = (int)std::min<int64_t>(cp.num_tiles, current_device_sms());
+  kernel<<<grid, xe::cp::kThreads, smem, s>>>(cp, g.ma, g.ma2, g.mb, mc);
+  launched = true;
+  return check_launch("xe_logspace_gemm");
+}
+
 xe_status launch_gemm(const Params& p, const GemmPlan& g, bool a_linear, bool bk, cudaStream_t s) {
   using namespace xe::gemm;
   Params q = p;
   set_tiling(q, g.bn);
+  if (q.batch > 0 && q.M > 0) {
+    bool launched = false;
+    const xe_status st = try_cp_layer(q, g, a_linear, bk, s, launched);
+    if (launched || st != XE_OK) return st;
+  }
   if (a_gathered(g.asrc)) {
     if (a_linear || !bk || g.bsrc == kBLdg)
       return fail(XE_ERR_NOT_SUPPORTED, "xe_logspace_gemm_gather: staged gather needs a log table and K-major B");
