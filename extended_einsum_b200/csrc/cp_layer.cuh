@@ -20,6 +20,13 @@
 //    as soon as the row extreme is known;
 //  * outputs leave through TMA stores of 32 x 32 blocks.
 //
+// Sources of X: kDense (A), kDense2 (A + A2, both TMA-staged per tile), and
+// kSlab2, the second sum layer over a state table T (folds0, states, 64):
+// X[f,m,:] = T[f, x_m, :] + T[f + pair, x'_m, :] with x_m = pixels[m, var[f]]
+// and x'_m = pixels[m, var[f + pair]] (xe_logspace_gemm_gather_pair).  For
+// kSlab2 the two folds' table slabs (states x 64 each) are loaded into shared
+// memory once per fold and every row is read from them by its pixel value.
+//
 // Warps 0-3 and 4-7: the warp groups (thread = tile row); warp 8: TMEM
 // allocation and MMA issue; warp 9: TMA loads and the weight split.
 #pragma once
@@ -44,12 +51,17 @@ constexpr int kOutBytes = 32 * 32 * 4;  // per warp: 32 rows x 32 columns
 // main accumulator [128, 192); correction accumulator [192, 256)
 constexpr uint32_t kTmemMain = 128, kTmemCorr = 192, kTmemPerGroup = 256;
 
-template <bool PAIR>
+enum Source : int { kDense = 0, kDense2 = 1, kSlab2 = 2 };
+constexpr int kSlabKBlock = 256 * 128;  // one k-block of a slab: up to 256 states x 32 k
+
+template <int SRC>
 struct Cfg {
-  static constexpr int kStageBytes = (PAIR ? 2 : 1) * kATile;
-  static constexpr int kStages = PAIR ? 1 : 2;  // per warp group
-  static constexpr int kOffA = 0;
-  static constexpr int kOffBRaw = kOffA + 2 * kStages * kStageBytes;
+  static constexpr bool kPair = SRC != kDense;
+  static constexpr int kStageBytes = (kPair ? 2 : 1) * kATile;
+  static constexpr int kStages = SRC == kDense ? 2 : 1;  // per warp group
+  static constexpr int kOffA = 0;  // A stages, or the two slabs [2][2 k-blocks]
+  static constexpr int kABytes = SRC == kSlab2 ? 4 * kSlabKBlock : 2 * kStages * kStageBytes;
+  static constexpr int kOffBRaw = kOffA + kABytes;
   static constexpr int kOffBHi = kOffBRaw + kBBytes;
   static constexpr int kOffBLo = kOffBHi + kBBytes;
   static constexpr int kOffOut = kOffBLo + kBBytes;
@@ -61,6 +73,11 @@ struct Cfg {
 struct Params {
   int folds, M, tiles_m, num_tiles;
   int shift_min;
+  // kSlab2
+  const uint8_t* pixels;
+  const int32_t* var;  // nullptr: variable = fold
+  int64_t pixel_stride;
+  int states, pair;
 };
 
 __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t src, int x, int y, int z) {
@@ -78,12 +95,13 @@ __device__ __forceinline__ void tile_range(const Params& p, int& first, int& las
   last = (int)(((int64_t)p.num_tiles * (blockIdx.x + 1)) / gridDim.x);
 }
 
-template <bool PAIR>
+template <int SRC>
 __global__ void __launch_bounds__(kThreads, 1)
     cp_layer_kernel(const Params p, const __grid_constant__ CUtensorMap tmap_a,
                     const __grid_constant__ CUtensorMap tmap_a2, const __grid_constant__ CUtensorMap tmap_w,
                     const __grid_constant__ CUtensorMap tmap_c) {
-  using C = Cfg<PAIR>;
+  using C = Cfg<SRC>;
+  constexpr bool PAIR = C::kPair;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   const uint32_t smem_base = smem_u32(smem);
@@ -96,7 +114,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* b_free = b_ready + 1;
   uint64_t* raw_full = b_free + 1;
   uint64_t* drain = raw_full + 1;
-  uint32_t* tmem_slot = (uint32_t*)(drain + 1);
+  uint64_t* slab_full = drain + 1;
+  uint64_t* slab_empty = slab_full + 1;
+  uint32_t* tmem_slot = (uint32_t*)(slab_empty + 1);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -114,6 +134,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(b_free, 1);
     mbar_init(raw_full, 1);
     mbar_init(drain, 1);
+    mbar_init(slab_full, 1);
+    mbar_init(slab_empty, 256);
     *abort_flag = 0;
     fence_mbarrier_init();
   }
@@ -138,36 +160,94 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t out_buf = smem_base + C::kOffOut + warp * kOutBytes;
     const float fill = -INFINITY;
     bool ok = true;
+    // kSlab2: pixel values of this thread's row in the group's next tile (loaded a tile ahead).
+    // Every group acquires the slabs of every fold of the CTA in order (a wait on slab_full
+    // phase g), whether or not it has a tile there, and releases fold g (an arrival on
+    // slab_empty) only after acquiring it: neither barrier then runs more than one phase
+    // ahead of a waiter, and each release lands in its own fold's phase.
+    int px1 = 0, px2 = 0, released = 0, acquired = 0;
+    const int fold0 = first < last ? fold_of(first) : 0;
+    auto load_pixels = [&](int tile, int& s1, int& s2) {
+      const int f = fold_of(tile);
+      const int m = (tile - f * p.tiles_m) * kBM + r;
+      int64_t v1 = p.var ? (int64_t)__ldg(p.var + f) : f;
+      int64_t v2 = p.var ? (int64_t)__ldg(p.var + f + p.pair) : (int64_t)f + p.pair;
+      if (v1 < 0 || v1 >= p.pixel_stride || v2 < 0 || v2 >= p.pixel_stride) {
+        record_bad_index(kSiteGemmGatherState);
+        v1 = v2 = 0;
+      }
+      s1 = m < p.M ? (int)__ldg(p.pixels + (int64_t)m * p.pixel_stride + v1) : 0;
+      s2 = m < p.M ? (int)__ldg(p.pixels + (int64_t)m * p.pixel_stride + v2) : 0;
+    };
+    if (SRC == kSlab2 && first + group < last) load_pixels(first + group, px1, px2);
     for (int i = first + group, j = 0; i < last && ok; i += 2, ++j) {
       const int bb = fold_of(i);
       const int mt = i - bb * p.tiles_m;
       const bool valid = mt * kBM + r < p.M;
       // -------- the row, in registers, and its extreme
-      const int sidx = j % C::kStages;
-      const uint32_t u = j / C::kStages;
-      if (!mbar_wait(&a_full[group * C::kStages + sidx], u & 1, kSiteAStaged, abort_flag)) {
-        ok = false;
-        break;
-      }
-      const uint32_t stage = smem_base + C::kOffA + (group * C::kStages + sidx) * C::kStageBytes;
       float x[64];
+      const int sidx = j % C::kStages;
+      if (SRC == kSlab2) {
+        const int g = bb - fold0;
+        while (ok && acquired <= g) {
+          while (released < acquired) {  // folds before `acquired` are done with
+            mbar_arrive(slab_empty);
+            ++released;
+          }
+          ok = mbar_wait(slab_full, acquired & 1, kSiteAStaged, abort_flag);
+          ++acquired;
+        }
+        if (!ok) break;
+        int s1 = px1, s2 = px2;
+        if (i + 2 < last) load_pixels(i + 2, px1, px2);
+        if (s1 >= p.states || s2 >= p.states) {
+          record_bad_index(kSiteGemmGatherState);
+          s1 = min(s1, p.states - 1);
+          s2 = min(s2, p.states - 1);
+        }
 #pragma unroll
-      for (int kb = 0; kb < 2; ++kb) {
-        const uint32_t row = stage + kb * kAKBlock + r * 128;
+        for (int kb = 0; kb < 2; ++kb) {
+          const uint32_t row1 = smem_base + C::kOffA + kb * kSlabKBlock + s1 * 128;
+          const uint32_t row2 = smem_base + C::kOffA + (2 + kb) * kSlabKBlock + s2 * 128;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          float4 v = lds_v4(row + ((c ^ (r & 7)) << 4));
-          if (PAIR) {
-            const float4 w = lds_v4(row + kATile + ((c ^ (r & 7)) << 4));
+          for (int c = 0; c < 8; ++c) {
+            float4 v = lds_v4(row1 + ((c ^ (s1 & 7)) << 4));
+            const float4 w = lds_v4(row2 + ((c ^ (s2 & 7)) << 4));
             v.x += w.x;
             v.y += w.y;
             v.z += w.z;
             v.w += w.w;
+            x[32 * kb + 4 * c] = valid ? v.x : fill;
+            x[32 * kb + 4 * c + 1] = valid ? v.y : fill;
+            x[32 * kb + 4 * c + 2] = valid ? v.z : fill;
+            x[32 * kb + 4 * c + 3] = valid ? v.w : fill;
           }
-          x[32 * kb + 4 * c] = valid ? v.x : fill;
-          x[32 * kb + 4 * c + 1] = valid ? v.y : fill;
-          x[32 * kb + 4 * c + 2] = valid ? v.z : fill;
-          x[32 * kb + 4 * c + 3] = valid ? v.w : fill;
+        }
+      } else {
+        const uint32_t u = j / C::kStages;
+        if (!mbar_wait(&a_full[group * C::kStages + sidx], u & 1, kSiteAStaged, abort_flag)) {
+          ok = false;
+          break;
+        }
+        const uint32_t stage = smem_base + C::kOffA + (group * C::kStages + sidx) * C::kStageBytes;
+#pragma unroll
+        for (int kb = 0; kb < 2; ++kb) {
+          const uint32_t row = stage + kb * kAKBlock + r * 128;
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            float4 v = lds_v4(row + ((c ^ (r & 7)) << 4));
+            if (PAIR) {
+              const float4 w = lds_v4(row + kATile + ((c ^ (r & 7)) << 4));
+              v.x += w.x;
+              v.y += w.y;
+              v.z += w.z;
+              v.w += w.w;
+            }
+            x[32 * kb + 4 * c] = valid ? v.x : fill;
+            x[32 * kb + 4 * c + 1] = valid ? v.y : fill;
+            x[32 * kb + 4 * c + 2] = valid ? v.z : fill;
+            x[32 * kb + 4 * c + 3] = valid ? v.w : fill;
+          }
         }
       }
       float e = is_min ? INFINITY : -INFINITY;
@@ -175,7 +255,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int k = 0; k < 64; ++k) e = extreme(e, x[k], is_min);
       const float shift = valid ? e : 0.0f;
       // every value of the row has been used: the slot may be refilled
-      mbar_arrive(&a_empty[group * C::kStages + sidx]);
+      if (SRC != kSlab2) mbar_arrive(&a_empty[group * C::kStages + sidx]);
       // -------- exp / split into this group's A columns (free: the previous tile's
       // epilogue waited for its MMAs)
 #pragma unroll
@@ -233,6 +313,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       // overwrite it once its A columns are written (a_ready orders both)
       tc_fence_before();
     }
+    // kSlab2: release the remaining folds' slabs (this group may have no tile in the last ones)
+    if (SRC == kSlab2 && first < last && ok) {
+      const int folds_here = fold_of(last - 1) - fold0 + 1;
+      while (ok && acquired < folds_here) {
+        while (released < acquired) {
+          mbar_arrive(slab_empty);
+          ++released;
+        }
+        ok = mbar_wait(slab_full, acquired & 1, kSiteAStaged, abort_flag);
+        ++acquired;
+      }
+      while (released < acquired) {
+        mbar_arrive(slab_empty);
+        ++released;
+      }
+    }
     if (lane == 0) bulk_wait_all();
     __syncwarp();
   } else if (warp == kMmaWarp) {
@@ -287,10 +383,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = first, n = 0; i < last && ok; ++i, ++n) {
       const int bb = fold_of(i);
       if (i == first || bb != fold_of(i - 1)) {
-        // the previous fold's products are done with hi / lo; the raw weights have landed
+        // kSlab2: both warp groups are done with the previous fold's slabs; load this fold's
         bool ready = true;
+        if (SRC == kSlab2 && lane == 0) {
+          if (fold_count > 0) ready = mbar_wait(slab_empty, (fold_count - 1) & 1, kSiteProducer, abort_flag);
+          if (ready) {
+            mbar_expect_tx(slab_full, 4 * p.states * 128);
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+#pragma unroll
+              for (int kb = 0; kb < 2; ++kb)
+                tma_load_3d(smem_base + C::kOffA + (2 * h + kb) * kSlabKBlock, &tmap_a, 32 * kb, 0, bb + h * p.pair,
+                            slab_full);
+          }
+        }
+        // the previous fold's products are done with hi / lo; the raw weights have landed
         if (lane == 0) {
-          if (fold_count > 0) ready = mbar_wait(b_free, (fold_count - 1) & 1, kSiteProducer, abort_flag);
+          if (ready && fold_count > 0) ready = mbar_wait(b_free, (fold_count - 1) & 1, kSiteProducer, abort_flag);
           if (ready) ready = mbar_wait(raw_full, fold_count & 1, kSiteProducer, abort_flag);
         }
         if (__shfl_sync(0xffffffffu, ready ? 1 : 0, 0) == 0) break;
@@ -323,7 +432,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         ++fold_count;
       }
-      if (lane == 0) {
+      if (SRC != kSlab2 && lane == 0) {
         const int group = n & 1;
         const int j = n >> 1;
         const int sidx = j % C::kStages;

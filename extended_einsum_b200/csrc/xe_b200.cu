@@ -127,6 +127,24 @@ bool encode_gather_map(CUtensorMap* map, const float* base, int64_t rows, int64_
   return r == CUDA_SUCCESS;
 }
 
+// Tensor map of a state table (folds, states, k) for whole-fold slabs: boxes of 32 k x all
+// states (at most 256), 128-byte swizzle.
+bool encode_slab_map(CUtensorMap* map, const float* base, int64_t folds, int64_t states, int64_t k, int64_t s_state,
+                     int64_t s_fold) {
+  PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+  if (!encode || !aligned16(base) || states > 256 || s_state <= 0 || s_fold <= 0 || (s_state * 4) % 16 != 0 ||
+      (s_fold * 4) % 16 != 0)
+    return false;
+  cuuint64_t dims[3] = {(cuuint64_t)k, (cuuint64_t)states, (cuuint64_t)folds};
+  cuuint64_t strides[2] = {(cuuint64_t)(s_state * 4), (cuuint64_t)(s_fold * 4)};
+  cuuint32_t box[3] = {32, (cuuint32_t)states, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 // Tensor map of the raw B operand (batch, k, n): MN-major (n contiguous) boxes
 // of BN n x 32 k, K-major (k contiguous) boxes of 32 k x BN n; unswizzled.
 bool encode_b_map(CUtensorMap* map, const float* base, int64_t batch, int64_t k, int64_t n, int64_t s_k, int64_t s_n,
@@ -310,6 +328,26 @@ bool encode_c_map(CUtensorMap* map, float* base, int64_t batch, int64_t m, int64
   return r == CUDA_SUCCESS;
 }
 
+template <int SRC>
+xe_status launch_cp_layer_t(const xe::cp::Params& cp, const CUtensorMap& ma, const CUtensorMap& ma2,
+                            const CUtensorMap& mb, const CUtensorMap& mc, cudaStream_t s) {
+  constexpr int smem = xe::cp::Cfg<SRC>::kSmemBytes;
+  auto kernel = xe::cp::cp_layer_kernel<SRC>;
+  static std::atomic<uint32_t> attribute_set{0};
+  cudaError_t e = prepare_kernel(kernel, smem, attribute_set);
+  if (e != cudaSuccess) return fail(XE_ERR_CUDA, "xe_logspace_gemm: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  const int grid = (int)std::min<int64_t>(cp.num_tiles, current_device_sms());
+  kernel<<<grid, xe::cp::kThreads, smem, s>>>(cp, ma, ma2, mb, mc);
+  return check_launch("xe_logspace_gemm");
+}
+
+xe_status launch_cp_layer(const xe::cp::Params& cp, int src, const CUtensorMap& ma, const CUtensorMap& ma2,
+                          const CUtensorMap& mb, const CUtensorMap& mc, cudaStream_t s) {
+  if (src == xe::cp::kSlab2) return launch_cp_layer_t<xe::cp::kSlab2>(cp, ma, ma2, mb, mc, s);
+  if (src == xe::cp::kDense2) return launch_cp_layer_t<xe::cp::kDense2>(cp, ma, ma2, mb, mc, s);
+  return launch_cp_layer_t<xe::cp::kDense>(cp, ma, ma2, mb, mc, s);
+}
+
 // The circuit's CP sum layer (K = N = 64, log A with its shifts computed in the kernel,
 // linear K-major B staged by TMA, contiguous output, at least 4 tiles per fold) runs on
 // its own kernel (cp_layer.cuh), which gives the same results as lse_gemm_kernel.
@@ -329,16 +367,9 @@ xe_status try_cp_layer(const Params& q, const GemmPlan& g, bool a_linear, bool b
   cp.tiles_m = q.tiles_m;
   cp.num_tiles = q.batch * q.tiles_m;
   cp.shift_min = q.shift_min;
-  const bool pair = g.asrc == kATma2;
-  const int smem = pair ? xe::cp::Cfg<true>::kSmemBytes : xe::cp::Cfg<false>::kSmemBytes;
-  auto kernel = pair ? xe::cp::cp_layer_kernel<true> : xe::cp::cp_layer_kernel<false>;
-  static std::atomic<uint32_t> attribute_set[2];
-  cudaError_t e = prepare_kernel(kernel, smem, attribute_set[pair ? 1 : 0]);
-  if (e != cudaSuccess) return fail(XE_ERR_CUDA, "xe_logspace_gemm: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-  const int grid = (int)std::min<int64_t>(cp.num_tiles, current_device_sms());
-  kernel<<<grid, xe::cp::kThreads, smem, s>>>(cp, g.ma, g.ma2, g.mb, mc);
+  const int src = g.asrc == kATma2 ? xe::cp::kDense2 : xe::cp::kDense;
   launched = true;
-  return check_launch("xe_logspace_gemm");
+  return launch_cp_layer(cp, src, g.ma, g.ma2, g.mb, mc, s);
 }
 
 xe_status launch_gemm(const Params& p, const GemmPlan& g, bool a_linear, bool bk, cudaStream_t s) {
@@ -689,6 +720,28 @@ xe_status gather_gemm(const char* who, const float* table, int64_t t_sf, int64_t
     shift_b = static_cast<float*>(workspace);
     st = shift_impl(b, nullptr, b_sb, b_sn, b_sk, folds, n, k, shift_mode == XE_SHIFT_MAX, shift_b, s);
     if (st != XE_OK) return st;
+  }
+  // the second CP sum layer of a circuit over a state table: the CP-layer kernel with the
+  // two folds' table slabs in shared memory (same results as the general kernel below)
+  if (pair > 0 && k == xe::cp::kK && n == xe::cp::kN && b_linear && b_sk == 1 && b_sn != 1 && c_sn == 1 &&
+      states <= 256 && (batch + xe::gemm::kBM - 1) / xe::gemm::kBM >= 4 && env_int("XE_GEMM_NO_CP_LAYER", 0) == 0) {
+    CUtensorMap slab{}, mw{}, mc{};
+    if (encode_slab_map(&slab, table, folds + pair, states, k, t_ss, t_sf) &&
+        encode_b_map(&mw, b, folds, k, n, b_sk, b_sn, b_sb, true, xe::cp::kN) &&
+        encode_c_map(&mc, c, folds, batch, n, c_sm, c_sb)) {
+      xe::cp::Params cp{};
+      cp.folds = (int)folds;
+      cp.M = (int)batch;
+      cp.tiles_m = (int)((batch + xe::gemm::kBM - 1) / xe::gemm::kBM);
+      cp.num_tiles = cp.folds * cp.tiles_m;
+      cp.shift_min = shift_mode == XE_SHIFT_MIN ? 1 : 0;
+      cp.pixels = pixels;
+      cp.var = var_of_fold;
+      cp.pixel_stride = pixel_stride;
+      cp.states = (int)states;
+      cp.pair = (int)pair;
+      return launch_cp_layer(cp, xe::cp::kSlab2, slab, slab, mw, mc, s);
+    }
   }
   // the A rows are gathered per thread (global loads), their shifts computed in the kernel
   GemmPlan plan = plan_gemm(table, nullptr, t_sf, t_ss, 1, false, b, b_sb, b_sk, b_sn, folds, batch, n, k, true);

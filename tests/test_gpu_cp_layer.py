@@ -76,3 +76,39 @@ def test_cp_layer_strided_output_falls_back(monkeypatch):
     ops.logspace_gemm(y[:folds], b, a2=y[folds:], b_linear=True, out=out)
     ref = _run(y, w, folds, True, "max", monkeypatch, general=False)
     assert torch.equal(out, ref)
+
+
+def _pair_inputs(folds, states, batch, seed):
+    g = torch.Generator().manual_seed(seed)
+    variables = 2 * folds + 3
+    table = (torch.randn(2 * folds, states, 64, generator=g) - 4.0).cuda()
+    pixels = torch.randint(states, (batch, variables), generator=g, dtype=torch.uint8).cuda()
+    var = torch.randperm(variables, generator=g)[: 2 * folds].to(torch.int32).cuda()
+    w = torch.softmax(torch.randn(folds, 64, 64, generator=g), dim=2).cuda()
+    return table, pixels, var, w.permute(0, 2, 1)
+
+
+@pytest.mark.parametrize(
+    "folds,states,batch,mode",
+    [(16, 256, 1000, "max"), (5, 7, 600, "max"), (300, 256, 512, "max"), (3, 100, 2049, "min"), (1, 256, 8192, "max")],
+)
+def test_slab_pair_layer_equals_general_kernel(folds, states, batch, mode, monkeypatch):
+    """The state-table pair layer with the slabs in shared memory == the gathered general kernel, bit for bit."""
+    table, pixels, var, b = _pair_inputs(folds, states, batch, seed=folds + states + batch)
+    monkeypatch.delenv("XE_GEMM_NO_CP_LAYER", raising=False)
+    ours = ops.logspace_gemm_gather_pair(table, pixels, var, b, b_linear=True, shift=mode).cpu().numpy()
+    monkeypatch.setenv("XE_GEMM_NO_CP_LAYER", "1")
+    general = ops.logspace_gemm_gather_pair(table, pixels, var, b, b_linear=True, shift=mode).cpu().numpy()
+    assert np.array_equal(ours, general, equal_nan=True)
+    assert ops.device_status() == 0
+
+
+def test_slab_pair_layer_reports_out_of_range_pixels(monkeypatch):
+    monkeypatch.delenv("XE_GEMM_NO_CP_LAYER", raising=False)
+    table, pixels, var, b = _pair_inputs(4, 10, 600, seed=3)
+    pixels[17, int(var[2])] = 250  # no such state
+    assert ops.device_status() == 0
+    ops.logspace_gemm_gather_pair(table, pixels, var, b, b_linear=True)
+    status = ops.device_status(clear=True)
+    assert status >> 16 == 1 and status & 0xFFFF == 33  # XE_ERR_INVALID_ARGUMENT, the gathered-row site
+    assert ops.device_status() == 0
