@@ -36,6 +36,18 @@
 namespace xe {
 namespace cp {
 
+#ifdef XE_TRACE_TILES
+// Per-tile event times (clock64) of CTA 0's first 64 tiles, trace builds only.
+constexpr int kTraceTiles = 64, kTraceEvents = 16;
+__device__ long long g_trace[kTraceTiles * kTraceEvents];
+#define XE_CP_TRACE(n, ev)                                                                                          \
+  do {                                                                                                              \
+    if (blockIdx.x == 0 && (int)(n) < ::xe::cp::kTraceTiles) ::xe::cp::g_trace[(n) * ::xe::cp::kTraceEvents + (ev)] = clock64(); \
+  } while (0)
+#else
+#define XE_CP_TRACE(n, ev)
+#endif
+
 using namespace gemm;
 constexpr int kK = 64;
 constexpr int kN = 64;
@@ -179,25 +191,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       s1 = m < p.M ? (int)__ldg(p.pixels + (int64_t)m * p.pixel_stride + v1) : 0;
       s2 = m < p.M ? (int)__ldg(p.pixels + (int64_t)m * p.pixel_stride + v2) : 0;
     };
-    if (SRC == kSlab2 && first + group < last) load_pixels(first + group, px1, px2);
-    for (int i = first + group, j = 0; i < last && ok; i += 2, ++j) {
+    // The row of local tile j (tile i of the CTA) in registers, and its extreme (the shift);
+    // false if a wait gave up.  Releases the staging slot (dense sources) once every value has
+    // been used.
+    auto load_row = [&](int i, int j, float (&x)[64], float& shift) -> bool {
       const int bb = fold_of(i);
       const int mt = i - bb * p.tiles_m;
       const bool valid = mt * kBM + r < p.M;
-      // -------- the row, in registers, and its extreme
-      float x[64];
       const int sidx = j % C::kStages;
       if (SRC == kSlab2) {
         const int g = bb - fold0;
-        while (ok && acquired <= g) {
+        bool fine = true;
+        while (fine && acquired <= g) {
           while (released < acquired) {  // folds before `acquired` are done with
             mbar_arrive(slab_empty);
             ++released;
           }
-          ok = mbar_wait(slab_full, acquired & 1, kSiteAStaged, abort_flag);
+          fine = mbar_wait(slab_full, acquired & 1, kSiteAStaged, abort_flag);
           ++acquired;
         }
-        if (!ok) break;
+        if (!fine) return false;
         int s1 = px1, s2 = px2;
         if (i + 2 < last) load_pixels(i + 2, px1, px2);
         if (s1 >= p.states || s2 >= p.states) {
@@ -225,10 +238,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       } else {
         const uint32_t u = j / C::kStages;
-        if (!mbar_wait(&a_full[group * C::kStages + sidx], u & 1, kSiteAStaged, abort_flag)) {
-          ok = false;
-          break;
-        }
+        if (!mbar_wait(&a_full[group * C::kStages + sidx], u & 1, kSiteAStaged, abort_flag)) return false;
         const uint32_t stage = smem_base + C::kOffA + (group * C::kStages + sidx) * C::kStageBytes;
 #pragma unroll
         for (int kb = 0; kb < 2; ++kb) {
@@ -250,21 +260,43 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      float e = is_min ? INFINITY : -INFINITY;
+      // four independent chains (max / min are exact: the order does not change the result)
+      float e0 = is_min ? INFINITY : -INFINITY, e1 = e0, e2 = e0, e3 = e0;
 #pragma unroll
-      for (int k = 0; k < 64; ++k) e = extreme(e, x[k], is_min);
-      const float shift = valid ? e : 0.0f;
+      for (int k = 0; k < 64; k += 4) {
+        e0 = extreme(e0, x[k], is_min);
+        e1 = extreme(e1, x[k + 1], is_min);
+        e2 = extreme(e2, x[k + 2], is_min);
+        e3 = extreme(e3, x[k + 3], is_min);
+      }
+      const float e = extreme(extreme(e0, e1, is_min), extreme(e2, e3, is_min), is_min);
+      shift = valid ? e : 0.0f;
       // every value of the row has been used: the slot may be refilled
       if (SRC != kSlab2) mbar_arrive(&a_empty[group * C::kStages + sidx]);
-      // -------- exp / split into this group's A columns (free: the previous tile's
-      // epilogue waited for its MMAs)
+      return true;
+    };
+    if (SRC == kSlab2 && first + group < last) load_pixels(first + group, px1, px2);
+    float x[64], shift = 0.0f;
+    if (first + group < last) ok = load_row(first + group, 0, x, shift);
+    // Pipelined (kPipelined): the transform of tile j, then the row of tile j+1 while tile j's
+    // products run, then tile j's epilogue; otherwise the row of tile j+1 follows the epilogue
+    // (one staging slot per group: its next tile is still in flight).  Either way the transform
+    // of tile j+1 (into the A columns tile j's products read) follows the epilogue of tile j,
+    // which waited for those products.
+    constexpr bool kPipelined = C::kStages > 1 || SRC == kSlab2;
+    for (int i = first + group, j = 0; i < last && ok; i += 2, ++j) {
+      const int bb = fold_of(i);
+      const int mt = i - bb * p.tiles_m;
+      const float tile_shift = shift;
+      if (r == 0) XE_CP_TRACE(i - first, 0);
+      // -------- exp / split into this group's A columns
 #pragma unroll
       for (int kb = 0; kb < 2; ++kb) {
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           float hi[16], lo[16];
 #pragma unroll
-          for (int t = 0; t < 16; ++t) split_rn(exp_shifted(x[32 * kb + 16 * h + t], shift), hi[t], lo[t]);
+          for (int t = 0; t < 16; ++t) split_rn(exp_shifted(x[32 * kb + 16 * h + t], tile_shift), hi[t], lo[t]);
           tmem_st16(tg + 64 * kb + 16 * h, hi);
           tmem_st16(tg + 64 * kb + 32 + 16 * h, lo);
         }
@@ -273,27 +305,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&a_ready[group]);
+      if (r == 0) XE_CP_TRACE(i - first, 1);
+      // -------- the group's next row while this tile's products run
+      if (kPipelined && i + 2 < last && !load_row(i + 2, j + 1, x, shift)) ok = false;
+      if (r == 0) XE_CP_TRACE(i - first, 2);
       // -------- epilogue
       if (!mbar_wait_warp(&acc_full[group], j & 1, kSiteDrainChunk, abort_flag)) {
         ok = false;
         break;
       }
       tc_fence_after();
+      if (r == 0) XE_CP_TRACE(i - first, 3);
 #pragma unroll 1
       for (int sl = 0; sl < 2; ++sl) {
-        float out[32];
+        float out[32], w[32];
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          float v[16], w[16];
-          tmem_ld16(tg + kTmemMain + 32 * sl + 16 * h, v);
-          tmem_ld16(tg + kTmemCorr + 32 * sl + 16 * h, w);
-          tmem_wait_ld();
+          tmem_ld16(tg + kTmemMain + 32 * sl + 16 * h, out + 16 * h);
+          tmem_ld16(tg + kTmemCorr + 32 * sl + 16 * h, w + 16 * h);
+        }
+        tmem_wait_ld();
 #pragma unroll
-          for (int t = 0; t < 16; ++t) {
-            // an overflowed main term carries the result; its correction is NaN
-            const float s = isinf(v[t]) ? v[t] : v[t] + w[t];
-            out[16 * h + t] = fast_log(s) + shift;
-          }
+        for (int t = 0; t < 32; ++t) {
+          // an overflowed main term carries the result; its correction is NaN
+          const float s = isinf(out[t]) ? out[t] : out[t] + w[t];
+          out[t] = fast_log(s) + tile_shift;
         }
         // the previous block's store has read this warp's staging buffer
         if (lane == 0) bulk_wait_read();
@@ -312,6 +348,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       // this tile's accumulator has been read: the MMAs of the group's next tile may
       // overwrite it once its A columns are written (a_ready orders both)
       tc_fence_before();
+      if (r == 0) XE_CP_TRACE(i - first, 4);
+      if (!kPipelined && i + 2 < last && !load_row(i + 2, j + 1, x, shift)) ok = false;
     }
     // kSlab2: release the remaining folds' slabs (this group may have no tile in the last ones)
     if (SRC == kSlab2 && first < last && ok) {
@@ -343,8 +381,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!mbar_wait(b_ready, fold_count & 1, kSiteMmaChunk, abort_flag)) break;
           ++fold_count;
         }
+        XE_CP_TRACE(n, 5);
         if (!mbar_wait(&a_ready[group], j & 1, kSiteMmaFull, abort_flag)) break;
         tc_fence_after();
+        XE_CP_TRACE(n, 6);
         const uint32_t tg = tmem + group * kTmemPerGroup;
         const uint32_t d_main = tg + kTmemMain, d_corr = tg + kTmemCorr;
 #pragma unroll

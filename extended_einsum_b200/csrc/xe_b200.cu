@@ -484,6 +484,18 @@ int xe_device_status(int clear) {
   return v;
 }
 
+#ifdef XE_TRACE_TILES
+// Trace builds only: copies (and clears) the CP-layer kernel's per-tile event times of CTA 0.
+int xe_profile_trace(long long* out, int n) {
+  const int count = n < xe::cp::kTraceTiles * xe::cp::kTraceEvents ? n : xe::cp::kTraceTiles * xe::cp::kTraceEvents;
+  if (cudaDeviceSynchronize() != cudaSuccess) return -1;
+  if (cudaMemcpyFromSymbol(out, xe::cp::g_trace, count * sizeof(long long)) != cudaSuccess) return -1;
+  static long long zero[xe::cp::kTraceTiles * xe::cp::kTraceEvents] = {};
+  cudaMemcpyToSymbol(xe::cp::g_trace, zero, sizeof(zero));
+  return count;
+}
+#endif
+
 #ifdef XE_PROFILE
 // Profiling builds only: copies (and optionally clears) the per-site wait-cycle counters.
 int xe_profile_wait_cycles(unsigned long long* out, int n, int clear) {
