@@ -334,6 +334,30 @@ def run_ours(args, rank: int, world: int, device: torch.device, dist_on: bool) -
     big_value = world * 2.0 * 8192**3 / (big_ms * 1e-3) / 1e12
     del big_a, big_b
 
+    from extended_einsum_b200 import ops
+
+    # the Tucker layer 'bfi,bfj,foij->bfo' (b=512, f=2048, i=j=o=32), linear softmax weights
+    tgen = torch.Generator(device=device).manual_seed(2 + 1000 * rank)
+    t_l = torch.randn(512, 2048, 32, device=device, generator=tgen) - 3.0
+    t_r = torch.randn(512, 2048, 32, device=device, generator=tgen) - 3.0
+    t_w = ops.softmax(torch.randn(2048, 32, 32, 32, device=device, generator=tgen), (2, 3))
+    tucker_ms = time_region(lambda record: ops.logspace_tucker(t_l, t_r, t_w), 8, 3, dist_on) / 8
+    tucker_value = world * 2.0 * 512 * 2048 * 32**3 / (tucker_ms * 1e-3) / 1e12
+    del t_l, t_r, t_w
+    # row softmax of a (65536, 32768) matrix, 2 N(0,1)
+    s_x = 2.0 * torch.randn(65536, 32768, device=device, generator=tgen)
+    softmax_ms = time_region(lambda record: ops.softmax(s_x, 1), 5, 3, dist_on) / 5
+    softmax_gbs = 2 * s_x.numel() * 4 / (softmax_ms * 1e-3) / 1e9
+    del s_x
+    torch.cuda.empty_cache()
+    # the 32768^3 contraction (per GPU, weak), log(U(0,1)) values; 0.5 s per step
+    huge_a = torch.log(torch.rand(1, 32768, 32768, device=device, generator=tgen))
+    huge_b = torch.log(torch.rand(1, 32768, 32768, device=device, generator=tgen))
+    huge_ms = time_region(large_matmul_step(huge_a, huge_b), 2, 1, dist_on) / 2
+    huge_value = world * 2.0 * 32768**3 / (huge_ms * 1e-3) / 1e12
+    del huge_a, huge_b
+    torch.cuda.empty_cache()
+
     # secondary: the folded circuit, batch-sharded
     circ = Circuit(device, rank, args.circuit_batch)
 
@@ -379,6 +403,21 @@ def run_ours(args, rank: int, world: int, device: torch.device, dist_on: bool) -
             "metric": "log-space einsum TFLOP/s, 'ik,kj->ij' 8192^3 per GPU", "value": round(big_value, 2), "unit": "TFLOP/s",
             "ms_per_step": round(big_ms, 3), "frac_of_split_tf32_peak": round(big_value / world / (peaks["bf16_tflops"] / 6.0), 4),
             "workload": "A, B = log(U(0,1)) 8192x8192 fp32, logspace_max, shift passes + contraction kernel",
+        },
+        "tucker": {
+            "metric": "log-space Tucker layer TFLOP/s", "value": round(tucker_value, 2), "unit": "TFLOP/s",
+            "ms_per_step": round(tucker_ms, 4), "frac_of_split_tf32_peak": round(tucker_value / world / (peaks["bf16_tflops"] / 6.0), 4),
+            "workload": "'bfi,bfj,foij->bfo' b=512 f=2048 i=j=o=32, l, r = N(-3,1), w = softmax of N(0,1) logits over (i,j), logspace_max",
+        },
+        "softmax": {
+            "metric": "softmax GB/s (one read and one write of the matrix)", "value": round(softmax_gbs, 1), "unit": "GB/s",
+            "ms_per_step": round(softmax_ms, 4), "hbm_frac": round(softmax_gbs / world / peaks["hbm_gbs"], 4),
+            "workload": "row softmax of a (65536, 32768) fp32 matrix of 2 N(0,1) values",
+        },
+        "large_32768": {
+            "metric": "log-space einsum TFLOP/s, 'ik,kj->ij' 32768^3 per GPU", "value": round(huge_value, 2), "unit": "TFLOP/s",
+            "ms_per_step": round(huge_ms, 2), "frac_of_split_tf32_peak": round(huge_value / world / (peaks["bf16_tflops"] / 6.0), 4),
+            "workload": "A, B = log(U(0,1)) 32768x32768 fp32, logspace_max, shift passes + contraction kernel, 1 warm-up + 2 steps",
         },
         "scaled_sum": {
             "metric": "log-space einsum TFLOP/s, scaled_sum mode", "value": round(scaled_value, 3), "unit": "TFLOP/s",

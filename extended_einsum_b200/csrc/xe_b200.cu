@@ -16,6 +16,7 @@
 #include "../../include/xe_b200.h"
 #include "lse_gemm.cuh"
 #include "cp_layer.cuh"
+#include "tucker_layer.cuh"
 #include "pointwise.cuh"
 #include "tucker.cuh"
 
@@ -1019,6 +1020,48 @@ static xe_status xe_tucker_impl(const float* l, const float* r, const float* w, 
   if (!aligned16(l) || !aligned16(r) || !aligned16(w) || !aligned16(y))
     return fail(XE_ERR_INVALID_ARGUMENT, "xe_logspace_tucker: operands must be 16-byte aligned");
   if (batch == 0 || folds == 0 || o_dim == 0) return XE_OK;
+  // I = J = O = 32: the two-stage kernel (tucker_layer.cuh); XE_GEMM_NO_CP_LAYER=1 selects the general one
+  if (i_dim == xe::tk::kDim && j_dim == xe::tk::kDim && o_dim == xe::tk::kDim && env_int("XE_GEMM_NO_CP_LAYER", 0) == 0) {
+    PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+    CUtensorMap ml{}, mr{}, mw{}, my{};
+    bool maps = encode != nullptr;
+    auto rows_map = [&](CUtensorMap* map, const float* base, int box_rows) {
+      // (batch, folds, 32) contiguous: boxes of 32 x 1 fold x box_rows rows, 128-byte swizzle
+      cuuint64_t dims[3] = {32, (cuuint64_t)folds, (cuuint64_t)batch};
+      cuuint64_t strides[2] = {32 * 4, (cuuint64_t)(folds * 32 * 4)};
+      cuuint32_t box[3] = {32, 1, (cuuint32_t)box_rows};
+      cuuint32_t estr[3] = {1, 1, 1};
+      return encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    };
+    if (maps) maps = rows_map(&ml, l, xe::gemm::kBM) && rows_map(&mr, r, xe::gemm::kBM) && rows_map(&my, y, 32);
+    if (maps) {
+      // w (folds, 32 o, 32 i, 32 j): per fold 1024 (o,i) rows of 32 j; chunks of 64 rows
+      cuuint64_t dims[3] = {32, 1024, (cuuint64_t)folds};
+      cuuint64_t strides[2] = {32 * 4, 1024 * 32 * 4};
+      cuuint32_t box[3] = {32, xe::tk::kChunkN, 1};
+      cuuint32_t estr[3] = {1, 1, 1};
+      maps = encode(&mw, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(w), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    }
+    if (maps) {
+      xe::tk::Params tp{};
+      tp.rows = (int)batch;
+      tp.folds = (int)folds;
+      tp.tiles_m = (int)((batch + xe::gemm::kBM - 1) / xe::gemm::kBM);
+      tp.num_tiles = tp.folds * tp.tiles_m;
+      tp.shift_min = shift_mode == XE_SHIFT_MIN;
+      static std::atomic<uint32_t> attribute_set{0};
+      cudaError_t e = prepare_kernel(xe::tk::tucker_layer_kernel, xe::tk::Cfg::kSmemBytes, attribute_set);
+      if (e != cudaSuccess)
+        return fail(XE_ERR_CUDA, "xe_logspace_tucker: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+      const int grid = (int)std::min<int64_t>(tp.num_tiles, current_device_sms());
+      xe::tk::tucker_layer_kernel<<<grid, xe::tk::kThreads, xe::tk::Cfg::kSmemBytes, stream>>>(tp, ml, mr, mw, my);
+      return check_launch("xe_logspace_tucker");
+    }
+  }
   Params p{};
   // the weights are the linear, K-major B operand of a batched contraction over folds
   p.b = w;

@@ -56,3 +56,21 @@ def test_tucker_rejects_unsupported_shapes():
 
 def test_no_device_wait_timed_out():
     assert ops.device_status() == 0
+
+
+@pytest.mark.parametrize("b,f,mode", [(300, 7, "max"), (128, 150, "min"), (1000, 3, "max")])
+def test_tucker_layer_kernel_matches_general_kernel(b, f, mode, monkeypatch):
+    """I = J = O = 32 runs the two-stage kernel (j contracted first on the tensor cores, i in
+    the epilogue); the general kernel contracts (i, j) at once.  Both against each other
+    and the oracle, with a row of -inf and rows past a 128-row tile."""
+    left, right, w = _inputs(b, f, 32, 32, 32, seed=b + f)
+    left[5, 1] = -float("inf")
+    monkeypatch.delenv("XE_GEMM_NO_CP_LAYER", raising=False)
+    ours = ops.logspace_tucker(left.cuda(), right.cuda(), w.cuda(), shift=mode).cpu().numpy()
+    monkeypatch.setenv("XE_GEMM_NO_CP_LAYER", "1")
+    general = ops.logspace_tucker(left.cuda(), right.cuda(), w.cuda(), shift=mode).cpu().numpy()
+    with np.errstate(invalid="ignore", divide="ignore"):
+        expected = oracle.logspace_tucker(left.double().numpy(), right.double().numpy(), w.double().numpy(), mode)
+    log_close(ours, expected)
+    log_close(ours, general)
+    assert ops.device_status() == 0
