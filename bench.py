@@ -408,6 +408,8 @@ def run_ours(args, rank: int, world: int, device: torch.device, dist_on: bool) -
             "metric": "log-space Tucker layer TFLOP/s", "value": round(tucker_value, 2), "unit": "TFLOP/s",
             "ms_per_step": round(tucker_ms, 4), "frac_of_split_tf32_peak": round(tucker_value / world / (peaks["bf16_tflops"] / 6.0), 4),
             "workload": "'bfi,bfj,foij->bfo' b=512 f=2048 i=j=o=32, l, r = N(-3,1), w = softmax of N(0,1) logits over (i,j), logspace_max",
+            "flops_basis": "2*b*f*o*i*j, the fused (i,j) form; the kernel contracts j first on the tensor cores and i in "
+                           "its epilogue, executing half of that as tensor work",
         },
         "softmax": {
             "metric": "softmax GB/s (one read and one write of the matrix)", "value": round(softmax_gbs, 1), "unit": "GB/s",
