@@ -216,6 +216,93 @@ __global__ void __launch_bounds__(kThreads == 32 ? 256 : kThreads)
   }
 }
 
+// Row softmax for 16384 < len <= 32768 (16-byte aligned rows): persistent CTAs of 1024
+// threads, one row in registers (8 float4 per thread, the element mapping and arithmetic of
+// softmax_rows_reg<1024, 8>, so the results are identical) while a bulk copy brings the
+// CTA's next row into shared memory.  softmax_rows_reg holds one row per SM with its load
+// latency exposed; here the next row's transfer overlaps the reductions and stores.
+template <int kQ>
+__global__ void __launch_bounds__(1024, 1)
+    softmax_rows_prefetch(const float* __restrict__ x, float* __restrict__ y, int64_t rows, int64_t len, int log_out) {
+  constexpr int kThreads = 1024;
+  extern __shared__ __align__(16) uint8_t row_buf[];  // len floats
+  __shared__ float scratch[32];
+  __shared__ uint64_t full;
+  __shared__ int abort_flag;
+  const int tid = threadIdx.x;
+  const uint32_t buf = smem_u32(row_buf);
+  const uint32_t bytes = (uint32_t)(len * 4);
+  // the row's bulk copy, in pieces of at most 32 KB (16-byte multiples)
+  auto fetch = [&](int64_t row) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(&full)), "r"(bytes) : "memory");
+    for (uint32_t off = 0; off < bytes; off += 32768) {
+      const uint32_t piece = bytes - off < 32768 ? bytes - off : 32768;
+      asm volatile(
+          "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(buf + off),
+          "l"(x + row * len + off / 4), "r"(piece), "r"(smem_u32(&full))
+          : "memory");
+    }
+  };
+  if (tid == 0) {
+    mbar_init(&full, 1);
+    abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  __syncthreads();
+  if (tid == 0 && (int64_t)blockIdx.x < rows) fetch(blockIdx.x);
+  uint32_t phase = 0;
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x, phase ^= 1) {
+    if (!mbar_wait(&full, phase, kSiteSoftmax, &abort_flag)) break;
+    float4 v[kQ];
+    float m = -INFINITY;
+#pragma unroll
+    for (int q = 0; q < kQ; ++q) {
+      const int64_t i = 4 * ((int64_t)q * kThreads + tid);
+      if (i < len) {
+        asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
+                     : "=f"(v[q].x), "=f"(v[q].y), "=f"(v[q].z), "=f"(v[q].w)
+                     : "r"(buf + (uint32_t)(i * 4)));
+      } else {
+        v[q] = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+      }
+      m = nan_extreme<true>(m, nan_extreme<true>(nan_extreme<true>(v[q].x, v[q].y), nan_extreme<true>(v[q].z, v[q].w)));
+    }
+    m = block_reduce<kThreads, true>(m, scratch);  // its barriers also order every read of the buffer
+    if (tid == 0 && row + gridDim.x < rows) {
+      fence_proxy_async_smem();
+      fetch(row + gridDim.x);
+    }
+    float s = 0.0f;
+#pragma unroll
+    for (int q = 0; q < kQ; ++q) {
+      const int64_t i = 4 * ((int64_t)q * kThreads + tid);
+      const float ex = (i < len) ? expf(v[q].x - m) : 0.0f;
+      const float ey = (i + 1 < len) ? expf(v[q].y - m) : 0.0f;
+      const float ez = (i + 2 < len) ? expf(v[q].z - m) : 0.0f;
+      const float ew = (i + 3 < len) ? expf(v[q].w - m) : 0.0f;
+      s += (ex + ey) + (ez + ew);
+    }
+    __syncthreads();
+    s = block_reduce<kThreads, false>(s, scratch);
+    const float inv = 1.0f / s;
+    const float lse = m + logf(s);
+    float* py = y + row * len;
+#pragma unroll
+    for (int q = 0; q < kQ; ++q) {
+      const int64_t i = 4 * ((int64_t)q * kThreads + tid);
+      float4 o;
+      if (log_out) {
+        o = make_float4(v[q].x - lse, v[q].y - lse, v[q].z - lse, v[q].w - lse);
+      } else {
+        o = make_float4(expf(v[q].x - m) * inv, expf(v[q].y - m) * inv, expf(v[q].z - m) * inv,
+                        expf(v[q].w - m) * inv);
+      }
+      if (i < len) stg_v4(py + i, o);
+    }
+    __syncthreads();  // scratch is reused by the next row's reductions
+  }
+}
+
 // Softmax of rows too long for registers: one block per row, three streaming
 // passes (max, sum, write).
 __global__ void __launch_bounds__(1024) softmax_rows_stream(const float* __restrict__ x, float* __restrict__ y,

@@ -854,7 +854,15 @@ xe_status xe_softmax(const float* x, float* y, int64_t outer, int64_t axis_len, 
   else if (len <= 1024) XE_SOFTMAX_WARP(8);
   else if (len <= 4096) XE_SOFTMAX_BLOCK(256, 4);
   else if (len <= 16384) XE_SOFTMAX_BLOCK(1024, 4);
-  else if (len <= 32768) XE_SOFTMAX_BLOCK(1024, 8);
+  else if (len <= 32768 && vec && env_int("XE_SOFTMAX_NO_PREFETCH", 0) == 0) {
+    // one row in registers while the next one streams into shared memory
+    const int smem = (int)(len * 4);
+    static std::atomic<uint32_t> attribute_set{0};
+    cudaError_t e = prepare_kernel(xe::softmax_rows_prefetch<8>, 32768 * 4, attribute_set);  // the largest row
+    if (e != cudaSuccess) return fail(XE_ERR_CUDA, "xe_softmax: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    const int grid = (int)std::min<int64_t>(rows, current_device_sms());
+    xe::softmax_rows_prefetch<8><<<grid, 1024, smem, s>>>(x, y, rows, len, lo);
+  } else if (len <= 32768) XE_SOFTMAX_BLOCK(1024, 8);
   else if (len <= 65536) XE_SOFTMAX_BLOCK(1024, 16);
   else xe::softmax_rows_stream<<<(unsigned)rows, 1024, 0, s>>>(x, y, len, lo);
 #undef XE_SOFTMAX_WARP

@@ -37,6 +37,7 @@ enum WaitSite : int {
   kSiteDrainShift = 14,
   kSiteProducer = 15,
   kNumSites = 16,
+  kSiteSoftmax = 16,  // the prefetching row softmax (not among the wait-time counters)
 };
 
 #ifdef XE_PROFILE

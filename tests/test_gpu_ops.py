@@ -38,6 +38,26 @@ def test_softmax_wide_rows_configuration():
     np.testing.assert_allclose(y.sum(axis=1), 1.0, rtol=1e-5)
 
 
+@pytest.mark.parametrize("rows,cols", [(300, 20000), (1000, 32768), (3, 16388)])
+def test_prefetching_row_softmax_equals_register_softmax(rows, cols, monkeypatch):
+    """Rows of 16K-32K columns take the kernel that streams the next row into shared memory;
+    it runs the register-resident kernel's arithmetic, so both agree bit for bit, with -inf
+    and NaN rows included."""
+    gen = torch.Generator().manual_seed(rows + cols)
+    x = 2.0 * torch.randn(rows, cols, generator=gen)
+    x[1, :] = -float("inf")
+    x[2, 7] = float("nan")
+    x = x.cuda()
+    for log_output in (False, True):
+        monkeypatch.delenv("XE_SOFTMAX_NO_PREFETCH", raising=False)
+        ours = ops.softmax(x, 1, log_output=log_output).cpu().numpy()
+        monkeypatch.setenv("XE_SOFTMAX_NO_PREFETCH", "1")
+        reg = ops.softmax(x, 1, log_output=log_output).cpu().numpy()
+        assert np.array_equal(ours, reg, equal_nan=True)
+    monkeypatch.delenv("XE_SOFTMAX_NO_PREFETCH", raising=False)
+    assert ops.device_status() == 0
+
+
 def test_log_add_broadcast_and_quotient():
     gen = torch.Generator().manual_seed(3)
     a = torch.randn(4, 1, 6, generator=gen)
