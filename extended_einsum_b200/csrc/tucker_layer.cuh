@@ -7,8 +7,8 @@
 // w linear (a softmax of the layer's logits).  The contraction runs in two
 // stages, j first (the path torch.einsum takes for the three operands):
 //
-//   T[b,(o,i)] = sum_j er[b,j] w[f,o,i,j]     tensor cores: M = 128 rows b, N = 64
-//                                             (two o) per chunk, K = 32 j, split-TF32
+//   T[b,(o,i)] = sum_j er[b,j] w[f,o,i,j]     tensor cores: M = 128 rows b, N = 128
+//                                             (four o) per chunk, K = 32 j, split-TF32
 //                                             (hi*hi + hi*lo + lo*hi: 96 products per
 //                                             output, accumulated in fp32)
 //   y[b,o]     = sum_i el[b,i] T[b,(o,i)]     fp32 FMAs in the epilogue
@@ -16,12 +16,12 @@
 // with el = exp(l - sl), er = exp(r - sr).  That is half the tensor work of the
 // fused (i,j) product, and the A operand (er) is 32 values per row instead of
 // 1024.  Per 128-row tile of fold f the weights w[f] stream through shared memory
-// in 16 chunks of 64 (o,i) rows x 32 j, split into TF32 hi / lo as they arrive.
+// in 8 chunks of 128 (o,i) rows x 32 j, split into TF32 hi / lo as they arrive.
 //
 // Warps 0-3 and 4-7: two row groups owning alternate tiles of the CTA's
-// contiguous range (scan, exp, A operand in TMEM, epilogue), each with a
-// double-buffered accumulator, so that the products of a chunk overlap the
-// epilogue of the previous one; warps 8-11: TF32 split of the weight chunks;
+// contiguous range (scan, exp, A operand in TMEM, epilogue), each with one
+// accumulator: while a group drains a chunk, the other group's products run;
+// warps 8-11: TF32 split of the weight chunks;
 // warp 12: TMEM allocation and MMA issue (the two tiles' chunks interleaved);
 // warp 13: TMA loads.
 #pragma once
@@ -33,16 +33,16 @@ namespace tk {
 
 using namespace gemm;
 constexpr int kDim = 32;                        // I = J = O
-constexpr int kChunkN = 64;                     // (o,i) rows per chunk: two o
-constexpr int kChunks = kDim * kDim / kChunkN;  // 16 per tile
+constexpr int kChunkN = 128;                    // (o,i) rows per chunk: four o
+constexpr int kChunks = kDim * kDim / kChunkN;  // 8 per tile
 constexpr int kThreads = 448;
 constexpr int kLoWarp0 = 8, kMmaWarp = 12, kProducerWarp = 13;
 constexpr int kRowBytes = kBM * kDim * 4;    // 16 KB: 128 rows x 32, 128-byte swizzle
-constexpr int kWBytes = kChunkN * kDim * 4;  // 8 KB: 64 (o,i) rows x 32 j
-constexpr int kWStages = 8;
+constexpr int kWBytes = kChunkN * kDim * 4;  // 16 KB: 128 (o,i) rows x 32 j
+constexpr int kWStages = 4;
 constexpr int kOutBytes = 32 * kDim * 4;  // per row warp: 32 rows x 32 o
-// TMEM of a row group (256 columns each): er hi [0,32), er lo [32,64), two accumulator
-// buffers [64,128) and [128,192)
+// TMEM of a row group (256 columns each): er hi [0,32), er lo [32,64), the accumulator
+// [64,192)
 constexpr uint32_t kTmemGroup = 256, kTmemAcc = 64;
 
 struct Cfg {
@@ -74,9 +74,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* w_ready = w_full + kWStages;   // [kWStages]
   uint64_t* w_empty = w_ready + kWStages;  // [kWStages]
   uint64_t* a_ready = w_empty + kWStages;  // [group]
-  uint64_t* acc_full = a_ready + 2;        // [group][buffer]
-  uint64_t* acc_empty = acc_full + 4;      // [group][buffer]
-  uint64_t* drain = acc_empty + 4;
+  uint64_t* acc_full = a_ready + 2;        // [group]
+  uint64_t* acc_empty = acc_full + 2;      // [group]
+  uint64_t* drain = acc_empty + 2;
   uint32_t* tmem_slot = (uint32_t*)(drain + 1);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
@@ -88,7 +88,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&lr_empty[g], 128);
       mbar_init(&a_ready[g], 4);
     }
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
       mbar_init(&acc_empty[i], 4);
     }
@@ -171,37 +171,40 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
 #pragma unroll 1
       for (int c = 0; c < kChunks; ++c, ++gc) {
-        const uint32_t buf = gc & 1;
-        if (!mbar_wait_warp(&acc_full[group * 2 + buf], (gc >> 1) & 1, kSiteDrainChunk, abort_flag)) {
+        if (!mbar_wait_warp(&acc_full[group], gc & 1, kSiteDrainChunk, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        if (c == 0 || c == 8) XE_CP_TRACE(r == 0 ? n : 1 << 20, c == 0 ? 8 : 9);
-        float t0[kDim], t1[kDim];
-        tmem_ld32(tg + lane_bits + kTmemAcc + 64 * buf, t0);
-        tmem_ld32(tg + lane_bits + kTmemAcc + 64 * buf + kDim, t1);
-        tmem_wait_ld();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&acc_empty[group * 2 + buf]);  // the buffer has been read
-        float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f, b0 = 0.0f, b1 = 0.0f, b2 = 0.0f, b3 = 0.0f;
+        float y[4];
 #pragma unroll
-        for (int i = 0; i < kDim; i += 4) {
-          a0 = fmaf(el[i], t0[i], a0);
-          a1 = fmaf(el[i + 1], t0[i + 1], a1);
-          a2 = fmaf(el[i + 2], t0[i + 2], a2);
-          a3 = fmaf(el[i + 3], t0[i + 3], a3);
-          b0 = fmaf(el[i], t1[i], b0);
-          b1 = fmaf(el[i + 1], t1[i + 1], b1);
-          b2 = fmaf(el[i + 2], t1[i + 2], b2);
-          b3 = fmaf(el[i + 3], t1[i + 3], b3);
+        for (int h = 0; h < 2; ++h) {  // two o at a time
+          float t0[kDim], t1[kDim];
+          tmem_ld32(tg + lane_bits + kTmemAcc + 64 * h, t0);
+          tmem_ld32(tg + lane_bits + kTmemAcc + 64 * h + kDim, t1);
+          tmem_wait_ld();
+          if (h == 1) {  // the accumulator has been read
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[group]);
+          }
+          float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f, b0 = 0.0f, b1 = 0.0f, b2 = 0.0f, b3 = 0.0f;
+#pragma unroll
+          for (int i = 0; i < kDim; i += 4) {
+            a0 = fmaf(el[i], t0[i], a0);
+            a1 = fmaf(el[i + 1], t0[i + 1], a1);
+            a2 = fmaf(el[i + 2], t0[i + 2], a2);
+            a3 = fmaf(el[i + 3], t0[i + 3], a3);
+            b0 = fmaf(el[i], t1[i], b0);
+            b1 = fmaf(el[i + 1], t1[i + 1], b1);
+            b2 = fmaf(el[i + 2], t1[i + 2], b2);
+            b3 = fmaf(el[i + 3], t1[i + 3], b3);
+          }
+          y[2 * h] = (a0 + a1) + (a2 + a3);
+          y[2 * h + 1] = (b0 + b1) + (b2 + b3);
         }
-        const float y0 = (a0 + a1) + (a2 + a3), y1 = (b0 + b1) + (b2 + b3);
-        // columns 2c, 2c+1: half of the 16-byte chunk c / 2 (swizzled by the row)
-        asm volatile("st.shared.v2.f32 [%0], {%1, %2};" ::"r"(yrow + (((c >> 1) ^ (lane & 7)) << 4) + (c & 1) * 8),
-                     "f"(y0), "f"(y1)
-                     : "memory");
+        // columns 4c .. 4c+3: the 16-byte chunk c (swizzled by the row)
+        sts_v4(yrow + ((c ^ (lane & 7)) << 4), make_float4(y[0], y[1], y[2], y[3]));
       }
       if (!ok) break;
       XE_CP_TRACE(r == 0 ? n : 1 << 20, 1);
@@ -232,7 +235,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (tt == 0 && (gw % (2 * kChunks) == 0 || gw % (2 * kChunks) == 16)) XE_CP_TRACE(2 * (gw / (2 * kChunks)), gw % (2 * kChunks) == 0 ? 6 : 7);
       const uint32_t hi = smem_base + C::kOffW + s * 2 * kWBytes, lo = hi + kWBytes;
 #pragma unroll
-      for (int k = 0; k < kWBytes / 16 / 128; ++k) {  // 4 chunks of 16 bytes per thread
+      for (int k = 0; k < kWBytes / 16 / 128; ++k) {  // 8 chunks of 16 bytes per thread
         const uint32_t off = (uint32_t)(tt + 128 * k) * 16;
         const float4 v = lds_v4(hi + off);
         float4 h, l;
@@ -261,15 +264,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         for (int c = 0; c < kChunks && ok; ++c) {
           for (int g = 0; g < groups; ++g, ++gw) {
-            const uint32_t s = gw % kWStages, buf = gcg[g] & 1;
+            const uint32_t s = gw % kWStages;
             if (!mbar_wait(&w_ready[s], (gw / kWStages) & 1, kSiteMmaFull, abort_flag) ||
-                !mbar_wait(&acc_empty[g * 2 + buf], ((gcg[g] >> 1) & 1) ^ 1, kSiteMmaChunk, abort_flag)) {
+                !mbar_wait(&acc_empty[g], (gcg[g] & 1) ^ 1, kSiteMmaChunk, abort_flag)) {
               ok = false;
               break;
             }
             tc_fence_after();
             const uint32_t tg = tmem + g * kTmemGroup;
-            const uint32_t d = tg + kTmemAcc + 64 * buf;
+            const uint32_t d = tg + kTmemAcc;
             const uint32_t b_hi = smem_base + C::kOffW + s * 2 * kWBytes, b_lo = b_hi + kWBytes;
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
@@ -279,7 +282,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               umma_tf32_ts(d, tg + kk * 8, dbl, idesc, 1);
               umma_tf32_ts(d, tg + 32 + kk * 8, dbh, idesc, 1);
             }
-            umma_commit(&acc_full[g * 2 + buf]);
+            umma_commit(&acc_full[g]);
             umma_commit(&w_empty[s]);
             if (c == 0 || c == 8) XE_CP_TRACE(n0 + g, c == 0 ? 2 : 3);
             ++gcg[g];
