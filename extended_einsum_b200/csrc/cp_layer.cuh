@@ -36,17 +36,7 @@
 namespace xe {
 namespace cp {
 
-#ifdef XE_TRACE_TILES
-// Per-tile event times (clock64) of CTA 0's first 64 tiles, trace builds only.
-constexpr int kTraceTiles = 64, kTraceEvents = 16;
-__device__ long long g_trace[kTraceTiles * kTraceEvents];
-#define XE_CP_TRACE(n, ev)                                                                                          \
-  do {                                                                                                              \
-    if (blockIdx.x == 0 && (int)(n) < ::xe::cp::kTraceTiles) ::xe::cp::g_trace[(n) * ::xe::cp::kTraceEvents + (ev)] = clock64(); \
-  } while (0)
-#else
-#define XE_CP_TRACE(n, ev)
-#endif
+#define XE_CP_TRACE(n, ev) XE_TILE_TRACE(n, ev)
 
 using namespace gemm;
 constexpr int kK = 64;

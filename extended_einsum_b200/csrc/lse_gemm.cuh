@@ -854,6 +854,7 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
           mbar_arrive(&full[s]);
           if (release >= 0) mbar_arrive(&a_empty[release]);
         }
+        if (r == 0 && (kb == 0 || kb == 8)) XE_TILE_TRACE(tl, kb == 0 ? 2 : 3);
         if ((ASRC == kALdg || preloaded) && kb + 1 < p.num_kb) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) cur[j] = nxt[j];
@@ -905,6 +906,7 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
           mbar_arrive(&full[s]);
           if (release >= 0) mbar_arrive(&b_empty[release]);
         }
+        if (t == 0 && (kb == 0 || kb == 8)) XE_TILE_TRACE(it / p.num_kb, kb == 0 ? 4 : 5);
         if (BSRC != kBTma && more) {
 #pragma unroll
           for (int i = 0; i < BT::kQ; ++i) cur[i] = nxt[i];
@@ -942,11 +944,13 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
           }
           const uint32_t s = it % kStages;
           const uint32_t ph = (it / kStages) & 1;
+          if (kb == 0) XE_TILE_TRACE(tl, 12);
           if (!mbar_wait(&full[s], ph, kSiteMmaFull, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
+          if (kb == 0) XE_TILE_TRACE(tl, 13);
           const uint32_t a_hi = tmem + C::kTmemA + 64 * s, a_lo = a_hi + 32;
           const uint32_t b_hi = smem_base + C::kOffB + s * C::kStageBytes, b_lo = b_hi + C::kBTile;
 #pragma unroll
@@ -962,6 +966,7 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
             umma_commit(&chunk_full[gc & 1]);
             ++gc;
           }
+          if (kb == 0 || kb == 8 || kb == p.num_kb - 1) XE_TILE_TRACE(tl, kb == 0 ? 6 : kb == 8 ? 7 : 8);
         }
       }
       // All issued MMAs must finish before TMEM is released.
@@ -1018,12 +1023,14 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&chunk_empty[cb]);
+        if (r == 0 && c == 0) XE_TILE_TRACE(tl, 9);
       }
       if (!ok) break;
       const bool direct = chunks == 1;
       const uint32_t dcb = gc & 1;  // the last (or only) chunk
       if (!mbar_wait_warp(&chunk_full[dcb], (gc >> 1) & 1, kSiteDrainChunk, abort_flag)) break;
       tc_fence_after();
+      if (r == 0) XE_TILE_TRACE(tl, 10);
       ++gc;
       // -------- epilogue from shared memory, overlapping the next tile's MMAs
       XE_SEGMENT_BEGIN(seg_ep);
@@ -1131,6 +1138,7 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
         }
         XE_SEGMENT_END(seg_e4, 11);
       }
+      if (r == 0) XE_TILE_TRACE(tl, 11);
     }
   } else if (a_gathered(ASRC)) {
     // ------------------------------------------------------------ gather producer (whole warp)
@@ -1238,6 +1246,7 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
           mbar_expect_tx(&a_full[sidx], C::kAStageBytes);
           tma_load_3d(dst, &tmap_a, kb * kBK, mt * kBM, bb, &a_full[sidx]);
           if (ASRC == kATma2) tma_load_3d(dst + kATileBytes, &tmap_a2, kb * kBK, mt * kBM, bb, &a_full[sidx]);
+          if (kb == 0 || kb == 8) XE_TILE_TRACE(ait / p.num_kb, kb == 0 ? 0 : 1);
           ++ait;
         }
         if (BSRC == kBTma) {

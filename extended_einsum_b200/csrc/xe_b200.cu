@@ -488,11 +488,11 @@ int xe_device_status(int clear) {
 #ifdef XE_TRACE_TILES
 // Trace builds only: copies (and clears) the CP-layer kernel's per-tile event times of CTA 0.
 int xe_profile_trace(long long* out, int n) {
-  const int count = n < xe::cp::kTraceTiles * xe::cp::kTraceEvents ? n : xe::cp::kTraceTiles * xe::cp::kTraceEvents;
+  const int count = n < xe::kTraceTiles * xe::kTraceEvents ? n : xe::kTraceTiles * xe::kTraceEvents;
   if (cudaDeviceSynchronize() != cudaSuccess) return -1;
-  if (cudaMemcpyFromSymbol(out, xe::cp::g_trace, count * sizeof(long long)) != cudaSuccess) return -1;
-  static long long zero[xe::cp::kTraceTiles * xe::cp::kTraceEvents] = {};
-  cudaMemcpyToSymbol(xe::cp::g_trace, zero, sizeof(zero));
+  if (cudaMemcpyFromSymbol(out, xe::g_trace, count * sizeof(long long)) != cudaSuccess) return -1;
+  static long long zero[xe::kTraceTiles * xe::kTraceEvents] = {};
+  cudaMemcpyToSymbol(xe::g_trace, zero, sizeof(zero));
   return count;
 }
 #endif

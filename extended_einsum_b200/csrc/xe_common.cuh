@@ -52,6 +52,18 @@ __device__ unsigned long long g_segment_cycles[kNumSites];
 #define XE_SEGMENT_END(name, idx)
 #endif
 
+#ifdef XE_TRACE_TILES
+// Per-tile event times (clock64) of CTA 0's first 64 tiles, trace builds only.
+constexpr int kTraceTiles = 64, kTraceEvents = 16;
+__device__ long long g_trace[kTraceTiles * kTraceEvents];
+#define XE_TILE_TRACE(n, ev)                                                                                 \
+  do {                                                                                                       \
+    if (blockIdx.x == 0 && (int)(n) < ::xe::kTraceTiles) ::xe::g_trace[(n) * ::xe::kTraceEvents + (ev)] = clock64(); \
+  } while (0)
+#else
+#define XE_TILE_TRACE(n, ev)
+#endif
+
 // About two seconds: far above any legitimate wait in these kernels.
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;
 
