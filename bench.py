@@ -18,8 +18,14 @@ scaling) with no data-path collective; the circuit gathers its per-sample
 log-likelihoods with one all_gather per step.  Times are CUDA-event times,
 the max over ranks.
 
-``--impl reference`` times the reference's CPU path (its torch executor call
-sequence, oracle/torch_port.py) on the host cores, on rank 0 only.
+``--impl reference`` times the reference package itself (extended_einsum,
+installed unmodified into baseline/_ref by baseline/install_reference.sh) on
+the host cores, rank 0 only, on the same workload: its public
+``TensorExpression.materialize('logspace_max')``, which on torch compiles the
+translated program with torch.compile (backends/torch.py:141-150; the one-time
+compile is excluded), and beside it the eager ``run_program`` of the same
+backend program (demo/cirkit.py:428-435).  The repo line's ``cpu_baseline``
+is that same arm, run as a CUDA-free child process.
 """
 
 from __future__ import annotations
@@ -38,6 +44,7 @@ import numpy as np
 import torch
 
 ROOT = Path(__file__).resolve().parent
+REFERENCE_PACKAGE = ROOT / "baseline" / "_ref"
 sys.path.insert(0, str(ROOT))
 
 SPLIT_TF32_NOTE = "split-TF32 (3 TF32 products per multiply-add): peak = measured bf16 / 2 (TF32 rate) / 3"
@@ -147,10 +154,11 @@ class LogspaceBmm:
     def flops_per_step(self) -> float:
         return 2.0 * self.batch * self.m * self.n * self.k
 
-    def config(self) -> dict:
+    @classmethod
+    def config(cls) -> dict:
         return {
             "workload": "logspace einsum 'bik,bkj->bij' b=128 i=k=j=512, fp32 N(0,8^2) log-values seed 1, logspace_max",
-            "global_batch": self.batch, "seq_len": None, "parallelism": None,
+            "global_batch": cls.batch, "seq_len": None, "parallelism": None,
             "l2": "inputs (268 MB) larger than L2 (126 MB); no flush",
         }
 
@@ -207,26 +215,6 @@ class LogspaceBmm:
             "peak_basis": f"{SPLIT_TF32_NOTE} ({peaks['basis']})", "kernel_ms": round(kernel_ms, 4),
         }
 
-    @staticmethod
-    def cpu_sample(threads_budget_s: float = 10.0) -> dict:
-        """The reference's torch CPU path on a sample of 4 of the 128 batches, repeated for ~10 s."""
-        from oracle import torch_port
-
-        gen = torch.Generator().manual_seed(1)
-        a = 8.0 * torch.randn(4, 512, 512, generator=gen)
-        b = 8.0 * torch.randn(4, 512, 512, generator=gen)
-        torch_port.logspace_bmm(a, b)
-        t0 = time.perf_counter()
-        reps = 0
-        while time.perf_counter() - t0 < threads_budget_s:
-            torch_port.logspace_bmm(a, b)
-            reps += 1
-        dt = (time.perf_counter() - t0) / reps
-        return {
-            "value": round(2.0 * 4 * 512**3 / dt / 1e12, 5), "unit": "TFLOP/s", "cores": torch.get_num_threads(),
-            "kind": "port", "sample": f"4 of 128 batches of 512^3 per call, {reps} calls, torch CPU executor sequence (oracle/torch_port.py)",
-        }
-
 
 class Circuit:
     """32x32 quad-tree CP circuit, K=64, 256 states, batch 8192 per GPU, log-likelihood output."""
@@ -279,6 +267,47 @@ class Circuit:
     def launches_per_step(self) -> int:
         levels = len(self.circuit.fold_counts)
         return 2 + 2 * levels + 2
+
+
+class LoweredCircuit:
+    """The same 32x32 circuit as the reference's own folded program, run through lower() / run_program.
+
+    The program is the one demo/cirkit.py:466-479 builds: the demo's expression, folded by the
+    reference's FoldSameShapedOperations and OptimizeContractionPaths (reference package from
+    baseline/_ref).  Its data input is the (variables, batch, K) categorical probabilities that the
+    demo gathers outside xe (demo/cirkit.py:525-527); here seeded softmax values stand in for them,
+    resident on the device.  lower() fuses each level's Hadamard product into the next sum layer.
+    """
+
+    def __init__(self, device: torch.device, rank: int, batch: int) -> None:
+        if str(REFERENCE_PACKAGE) not in sys.path:
+            sys.path.insert(0, str(REFERENCE_PACKAGE))
+        import extended_einsum as xe
+
+        import extended_einsum_b200 as xb
+        from extended_einsum_b200.circuit import demo_circuit_inputs, demo_circuit_program
+
+        self.batch = batch
+        program, data_input = demo_circuit_program(xe, 32, 32, 64, batch)
+        gen = torch.Generator(device=device).manual_seed(3 + 1000 * rank)
+        self.inputs = demo_circuit_inputs(program, data_input, gen, device)
+        self.lowered = xb.lower(program)
+        self.run = xb.run_program
+        self.launches = sum(1 for c in self.lowered.backend_calls if getattr(c, "fn", None) is not None and
+                            getattr(getattr(c, "fn"), "__name__", "") != "<lambda>")
+
+    def step(self, record: bool) -> torch.Tensor:
+        return self.run(self.lowered, self.inputs)
+
+    @staticmethod
+    def hbm_bytes_per_sample(variables: int = 1024, units: int = 64) -> int:
+        """Layer-by-layer bytes per sample: the data rows read once, each level written once and read
+        once by the next (its Hadamard product fused), the root's two rows read, one value written."""
+        folds, f = 0, variables // 2
+        while f >= 2:
+            folds += f
+            f //= 2
+        return 4 * units * (2 * variables + 3 * folds + 2) + 4
 
 
 # ---------------------------------------------------------------------------
@@ -397,6 +426,27 @@ def run_ours(args, rank: int, world: int, device: torch.device, dist_on: bool) -
     del circ
     torch.cuda.empty_cache()
 
+    # the reference's own folded circuit program through lower() / run_program (the drop-in path)
+    lowered_line = None
+    if (REFERENCE_PACKAGE / "extended_einsum").is_dir():
+        low = LoweredCircuit(device, rank, args.circuit_batch)
+        l_steps = max(3, args.steps // 4)
+        l_ms = time_region(low.step, l_steps, 3, dist_on) / l_steps
+        l_value = world * low.batch / (l_ms * 1e-3)
+        l_bytes = LoweredCircuit.hbm_bytes_per_sample()
+        lowered_line = {
+            "metric": "circuit samples/s through lower()", "value": round(l_value, 1), "unit": "samples/s",
+            "ms_per_step": round(l_ms, 4),
+            "workload": f"the reference's folded program of the same circuit (its FoldSameShapedOperations + "
+                        f"OptimizeContractionPaths), batch {low.batch} per GPU, data input (1024, batch, 64) "
+                        "categorical probabilities resident, run_program of the lowered program, eager",
+            "hbm_bytes_per_sample": l_bytes,
+            "hbm_frac": round(l_bytes * l_value / world / 1e9 / peaks["hbm_gbs"], 4),
+            "kernel_calls_per_step": low.launches,
+        }
+        del low
+        torch.cuda.empty_cache()
+
     if rank != 0:
         return None
     line = {
@@ -420,6 +470,7 @@ def run_ours(args, rank: int, world: int, device: torch.device, dist_on: bool) -
             "tflops_algorithmic": round(flops_sample * c_value / world / 1e12, 2),
             "e2e_samples_per_s": round(world * args.circuit_batch / (c_e2e_ms * 1e-3), 1),
         },
+        "circuit_lowered": lowered_line,
         "large_8192": {
             "metric": "log-space einsum TFLOP/s, 'ik,kj->ij' 8192^3 per GPU", "value": round(big_value, 2), "unit": "TFLOP/s",
             "ms_per_step": round(big_ms, 3), "frac_of_split_tf32_peak": round(big_value / world / (peaks["bf16_tflops"] / 6.0), 4),
@@ -448,38 +499,126 @@ def run_ours(args, rank: int, world: int, device: torch.device, dist_on: bool) -
         },
     }
     if world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = LogspaceBmm.cpu_sample()
+        line["cpu_baseline"] = cpu_baseline(args)
     return line
 
 
+def cpu_baseline(args) -> dict:
+    """The reference arm below, run as a child process that never touches CUDA, with the same steps."""
+    import subprocess
+
+    env = {k: v for k, v in os.environ.items() if k not in ("OMP_NUM_THREADS", "MKL_NUM_THREADS")}
+    cmd = [sys.executable, str(Path(__file__).resolve()), "--impl", "reference", "--steps", str(args.steps), "--warmup", str(args.warmup)]
+    out = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=1800)
+    lines = [ln for ln in out.stdout.splitlines() if ln.startswith("{")]
+    if out.returncode != 0 or not lines:
+        return {"value": None, "unit": "TFLOP/s", "cores": None, "kind": "reference",
+                "sample": f"reference arm failed (rc {out.returncode}): {out.stderr.strip().splitlines()[-1:] }"}
+    ref = json.loads(lines[-1])
+    base = dict(ref["cpu_baseline"])
+    base["eager"] = ref.get("eager")
+    return base
+
+
+class ReferenceCPU:
+    """The reference package's own CPU path on the headline workload (128 x 512^3, N(0, 8^2), seed 1).
+
+    ``materialize`` is the reference's public call (interface/tensor_expression.py:104-117): extract
+    the program, translate it with TorchBackendFunctions, compile it with TorchCompiler
+    (torch.compile, backends/torch.py:141-150) and run it.  Later steps call the compiled
+    ``_backend_code`` again, as a user re-running the materialized expression would; the compile is
+    timed once and reported apart.  ``eager`` runs the same backend program through ``run_program``
+    (backend_translation/runtime.py:9-21), the demo's path without --torch-compile.
+    """
+
+    def __init__(self) -> None:
+        if not (REFERENCE_PACKAGE / "extended_einsum").is_dir():
+            raise RuntimeError("the reference package is not installed in baseline/_ref (run baseline/install_reference.sh)")
+        sys.path.insert(0, str(REFERENCE_PACKAGE))
+        import extended_einsum as xe
+        from extended_einsum.backend_translation.runtime import run_program
+        from extended_einsum.backend_translation.translate import translate_to_backend_program
+        from extended_einsum.backends.torch import TorchBackendFunctions
+
+        gen = torch.Generator().manual_seed(1)
+        a = 8.0 * torch.randn(LogspaceBmm.batch, LogspaceBmm.m, LogspaceBmm.k, generator=gen)
+        b = 8.0 * torch.randn(LogspaceBmm.batch, LogspaceBmm.k, LogspaceBmm.n, generator=gen)
+        self.expr = xe.log(xe.einsum("bik,bkj->bij", xe.exp(xe.array(a)), xe.exp(xe.array(b))))
+        program, arguments = xe.extract_program(self.expr, "logspace_max")
+        self.inputs = [arg.backend_array for arg in arguments]
+        backend_program = translate_to_backend_program(program, TorchBackendFunctions())
+        self.backend_calls = len(backend_program.backend_calls)
+        self.eager = lambda: run_program(backend_program, self.inputs)
+        self.compile_s = None
+
+    def compiled(self):
+        import torch._inductor.config as inductor_config
+
+        # the image's CXX wrapper (/opt/gcc) lacks libgomp's specs, which inductor's OpenMP
+        # CPU kernels need; the system g++ has them
+        if os.path.exists("/usr/bin/g++"):
+            inductor_config.cpp.cxx = (None, "/usr/bin/g++")
+        t0 = time.perf_counter()
+        self.expr.materialize("logspace_max")
+        self.compile_s = time.perf_counter() - t0
+        code = self.expr._backend_code
+        inputs = [arg.backend_array for arg in self.expr._input_arguments]
+        return lambda: code(inputs)
+
+
+def time_cpu_steps(fn, steps: int, warmup: int, warm_s: float = 5.0) -> float:
+    """Seconds per step over exactly `steps` calls, after `warmup` calls and at least `warm_s` s of calls.
+
+    The first seconds of a fresh process run slower (the allocator's first large blocks are
+    fresh pages), so warm-up runs until both bounds are met."""
+    t0 = time.perf_counter()
+    n = 0
+    while n < warmup or time.perf_counter() - t0 < warm_s:
+        fn()
+        n += 1
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        fn()
+    return (time.perf_counter() - t0) / steps
+
+
 def run_reference(args, rank: int) -> dict | None:
-    """The reference's CPU path (torch executor sequence) on the host cores, rank 0 only."""
+    """The reference package's CPU path on the host cores, rank 0 only (same config as the repo line)."""
     if rank != 0:
         return None
-    from oracle import torch_port
-
     # every host thread this process may run on (the affinity set, not the machine's count)
     torch.set_num_threads(len(os.sched_getaffinity(0)) or 1)
-    gen = torch.Generator().manual_seed(1)
-    sample_batches = 4
-    a = 8.0 * torch.randn(sample_batches, 512, 512, generator=gen)
-    b = 8.0 * torch.randn(sample_batches, 512, 512, generator=gen)
-    for _ in range(args.warmup):
-        torch_port.logspace_bmm(a, b)
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        torch_port.logspace_bmm(a, b)
-    dt = (time.perf_counter() - t0) / args.steps
-    value = 2.0 * sample_batches * 512**3 / dt / 1e12
-    sample = f"{sample_batches} of the 128 batches of 512^3 per step (the per-batch work is identical), torch CPU executor sequence (oracle/torch_port.py)"
-    return {
-        "impl": "reference", "metric": LogspaceBmm.metric, "value": round(value, 5), "unit": "TFLOP/s",
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3),
+    flops = 2.0 * LogspaceBmm.batch * LogspaceBmm.m * LogspaceBmm.n * LogspaceBmm.k
+    ref = ReferenceCPU()
+    kind, note = "compiled", None
+    try:
+        step = ref.compiled()
+    except Exception as exc:  # noqa: BLE001 - torch.compile unusable on this host: the eager path is the anchor
+        kind, note, step = "eager", f"torch.compile failed ({type(exc).__name__}); eager run_program is the anchor", ref.eager
+    dt = time_cpu_steps(step, args.steps, args.warmup)
+    value = flops / dt / 1e12
+    eager_dt = dt if kind == "eager" else time_cpu_steps(ref.eager, max(3, args.steps // 2), 3)
+    eager = {"value": round(flops / eager_dt / 1e12, 5), "unit": "TFLOP/s", "ms_per_step": round(eager_dt * 1e3, 2),
+             "path": f"run_program of the translated backend program ({ref.backend_calls} torch calls)"}
+    sample = (f"the whole workload per step (128 x 512^3), reference package from baseline/_ref, "
+              f"{'materialize(): torch.compile of the translated program, compile excluded' if kind == 'compiled' else 'eager run_program'}")
+    cores = torch.get_num_threads()
+    world = args.gpus
+    config = {**LogspaceBmm.config(), "parallelism": f"batch-sharded x{world} (weak)"}
+    line = {
+        "impl": "reference", "metric": LogspaceBmm.metric, "value": round(value, 5), "unit": LogspaceBmm.unit,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "logspace einsum 'bik,bkj->bij' b=128 i=k=j=512, fp32 N(0,8^2) log-values seed 1, logspace_max"},
-        "cpu_baseline": {"value": round(value, 5), "unit": "TFLOP/s", "cores": torch.get_num_threads(), "kind": "port", "sample": sample},
+        "config": config,
+        "cpu_baseline": {"value": round(value, 5), "unit": "TFLOP/s", "cores": cores, "kind": "reference", "sample": sample,
+                         "path": kind, "host_cpus": os.cpu_count(),
+                         "compile_s": None if ref.compile_s is None else round(ref.compile_s, 1)},
+        "eager": eager,
         "e2e": {"value": round(value, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if note:
+        line["note"] = note
+    return line
 
 
 def main() -> None:

@@ -110,4 +110,3 @@ def disable() -> None:
 
     reference.TensorExpression.materialize = _ORIGINAL_MATERIALIZE
     _ORIGINAL_MATERIALIZE = None
-STABLE_MODES = ("logspace_max", "logspace_min", "scaled_sum", "scaled_max", "scaled_min")

@@ -34,6 +34,7 @@ contiguous halves [0, F/2) and [F/2, F) of level l's output.
 
 from __future__ import annotations
 
+import importlib
 import math
 from dataclasses import dataclass
 
@@ -185,3 +186,51 @@ class CircuitForward:
         b_root = w_root.t().unsqueeze(0)  # (1, K, 1)
         ll = ops.logspace_gemm(y[0:1], b_root, a2=y[1:2], b_linear=True, shift=self.shift)
         return ll[0]
+
+
+def demo_circuit_program(xe, height: int, width: int, units: int, batch: int, stability_mode: str = "logspace_max"):
+    """The demo's folded CP quad-tree circuit program, built and folded by the reference package ``xe``.
+
+    The expression is the one demo/cirkit.py:131-210 builds from a cirkit quad-tree CP circuit
+    (cirkit is not needed): leaf v is ``xe.select(data, v)`` of the (variables, batch, units)
+    categorical probabilities, every sum layer is 'ab,cb->ac' with softmax(Parameter) weights over
+    its input units, the two children of a region are joined by the Hadamard product 'ab,ab->ab'
+    (the pairing of quad_tree_leaf_order), and the root sum has one output unit under ``xe.log``.
+    It is folded as demo/cirkit.py:478-479 folds it: FoldSameShapedOperations, then
+    OptimizeContractionPaths (preprocess.py).  Returns the folded RichProgram and the index of its
+    data input; every other input is a packed parameter.
+    """
+    tensor_expression = importlib.import_module(xe.__name__ + ".interface.tensor_expression")
+    preprocess = importlib.import_module(xe.__name__ + ".preprocess")
+    parameter = tensor_expression.Parameter
+    variables = height * width
+    data = xe.array(torch.empty((variables, batch, units), dtype=torch.float32))
+
+    def sum_layer(child, outputs: int = units):
+        weights = xe.softmax(parameter(xe.array(torch.empty((outputs, units), dtype=torch.float32))), axis=1)
+        return xe.einsum("ab,cb->ac", child, weights)
+
+    level = [sum_layer(xe.select(data, v)) for v in quad_tree_leaf_order(height, width)]
+    while len(level) > 2:
+        half = len(level) // 2
+        level = [sum_layer(xe.einsum("ab,ab->ab", level[i], level[i + half])) for i in range(half)]
+    root = sum_layer(xe.einsum("ab,ab->ab", level[0], level[1]), outputs=1)
+    program, _ = xe.extract_program(xe.log(root), stability_mode=stability_mode)
+    folded = preprocess.FoldSameShapedOperations.apply_with_metadata(program)
+    folded_program = preprocess.OptimizeContractionPaths.apply(folded.program)
+    data_inputs = [i for i in range(folded_program.n_inputs) if i not in folded_program.parameter_indices]
+    if len(data_inputs) != 1:
+        raise ValueError(f"expected one data input in the folded circuit, found {len(data_inputs)}")
+    return folded_program, data_inputs[0]
+
+
+def demo_circuit_inputs(program, data_input: int, generator: torch.Generator, device: torch.device | str = "cpu"):
+    """Seeded inputs of a demo_circuit_program: the data input holds categorical probabilities
+    (softmax over the units of N(0, 1) logits, a stand-in for the gathered state rows), every
+    parameter N(0, 1) logits, as the demo initialises them (demo/cirkit.py:511-518)."""
+    inputs = []
+    for i in range(program.n_inputs):
+        shape = tuple(program.shapes[i])
+        values = torch.randn(shape, generator=generator, device=generator.device)
+        inputs.append((torch.softmax(values, dim=-1) if i == data_input else values).to(device))
+    return inputs

@@ -13,6 +13,10 @@ same arithmetic is one launch:
 * 'bfi,bfj,foij->bfo'    -> xe_logspace_tucker (the fused Tucker layer,
                             preprocess.py:1095-1106)
 * contraction-free       -> xe_log_add (translate.py:706-718)
+* a Hadamard product of two log operands feeding a two-operand contraction
+  (the folded circuit's 'cab,cab->cab' -> 'dac,dbc->dab')
+                         -> xe_logspace_gemm with the second factor as the
+                            fused addend of A
 
 Grouped labels are flattened with ``reshape``, which is a view for the
 layouts that reach this path; a layout that cannot be viewed is copied.
@@ -113,7 +117,28 @@ def _reduce(labels: str, output_string: str, x: torch.Tensor, linear: bool, shif
     return y.reshape([sizes[label] for label in output_string])
 
 
-def _binary(input_strings, output_string, operands, linear, shift, sizes) -> torch.Tensor:
+def logspace_einsum_hadamard(
+    format_string: str, b_linear: bool, shift: str, a: torch.Tensor, a2: torch.Tensor, b: torch.Tensor
+) -> torch.Tensor:
+    """The log-space einsum of (a + a2) and b, where a + a2 is a log-domain Hadamard product.
+
+    ``a`` and ``a2`` carry the first operand's labels; the kernel adds them in
+    fp32 before the row shift (the addend ``a2`` of xe_logspace_gemm), which
+    is the separate log add (translate.py:706-718) followed by the contraction
+    (:686-750) without the intermediate tensor.  Operands whose grouped views
+    differ in strides are added first.
+    """
+    input_strings, output_string = parse_format_string(format_string)
+    _check_labels(input_strings, output_string)
+    sizes = _sizes(input_strings, (a, b))
+    if a2.shape != a.shape:
+        raise ValueError(f"einsum: Hadamard factors of shapes {tuple(a.shape)} and {tuple(a2.shape)}")
+    if a.stride() != a2.stride():
+        return _binary(input_strings, output_string, (ops.log_add(a, a2), b), (False, b_linear), shift, sizes)
+    return _binary(input_strings, output_string, (a, b), (False, b_linear), shift, sizes, a2=a2)
+
+
+def _binary(input_strings, output_string, operands, linear, shift, sizes, a2: torch.Tensor | None = None) -> torch.Tensor:
     la, lb = input_strings
     batch = "".join(label for label in output_string if label in la and label in lb)
     m_labels = "".join(label for label in output_string if label in la and label not in lb)
@@ -126,7 +151,11 @@ def _binary(input_strings, output_string, operands, linear, shift, sizes) -> tor
         )
     a = _group(operands[0], la, [batch, m_labels, k_labels], sizes)
     b = _group(operands[1], lb, [batch, k_labels, n_labels], sizes)
-    c = ops.logspace_gemm(a, b, a_linear=linear[0], b_linear=linear[1], shift=shift)
+    if a2 is not None:
+        a2 = _group(a2, la, [batch, m_labels, k_labels], sizes)
+        if a2.stride() != a.stride():  # one of the two views had to be copied
+            a, a2 = ops.log_add(a, a2), None
+    c = ops.logspace_gemm(a, b, a2=a2, a_linear=linear[0], b_linear=linear[1], shift=shift)
     grouped = batch + m_labels + n_labels
     c = c.reshape([sizes[label] for label in grouped])
     return c.permute([grouped.index(label) for label in output_string])

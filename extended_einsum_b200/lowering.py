@@ -11,12 +11,22 @@ generic backend calls per stable einsum, this lowering appends one call into
 libxe_b200.so (contraction.py), so a BackendProgram here is a short list of kernel
 launches.
 
+One pattern of the folded circuits is fused across instructions: a
+Hadamard product of two log-domain values with identical labels (the folded
+'cab,cab->cab' over the two slice halves of the previous level, or 'ab,ab->ab'
+over two selects at the root; translate.py:706-718 lowers it to a log add)
+whose only consumer is a two-operand contraction becomes the fused addend
+(``a2``) of that contraction, so the product is never written to memory.
+The arithmetic is unchanged: the kernel adds the two values in fp32 before
+the row shift, as the separate log add would.
+
 The result is a ``BackendProgram`` with the reference's structure
 (backend.py:81-85) that ``run_program`` (runtime.py:9-21) executes.
 """
 
 from __future__ import annotations
 
+from collections import Counter
 from collections.abc import Callable, Sequence
 from dataclasses import dataclass, field
 from functools import partial
@@ -109,6 +119,14 @@ class _LogspaceLowering:
         self.builder = _Builder(program.n_inputs)
         self.positions: dict[tuple[int, str], int] = {(i, "raw"): i for i in range(program.n_inputs)}
         self.parameter_derived = parameter_derived_ssa_ids(program)
+        # Hadamard products held back to be fused into their consumer: ssa -> (log position, log position)
+        self.deferred: dict[int, tuple[int, int]] = {}
+        self.uses = Counter(a for instruction in program.instructions for a in instruction.argument_ssa_ids)
+        self.uses[program.output_ssa] += 1
+        self.consumer: dict[int, Any] = {}
+        for instruction in program.instructions:
+            for a in instruction.argument_ssa_ids:
+                self.consumer[a] = instruction
 
     def run(self) -> BackendProgram:
         for index, instruction in enumerate(self.program.instructions):
@@ -126,8 +144,29 @@ class _LogspaceLowering:
 
     def _log(self, ssa: int) -> int:
         if (ssa, "logspace") not in self.positions:
-            self.positions[ssa, "logspace"] = self.builder.append(ops.log, (self.positions[ssa, "raw"],))
+            if ssa in self.deferred:
+                # a held-back Hadamard product whose consumer could not take it fused
+                self.positions[ssa, "logspace"] = self.builder.append(ops.log_add, self.deferred.pop(ssa))
+            else:
+                self.positions[ssa, "logspace"] = self.builder.append(ops.log, (self.positions[ssa, "raw"],))
         return self.positions[ssa, "logspace"]
+
+    def _defer_hadamard(self, format_string: str, args: tuple[int, ...], result: int) -> bool:
+        """Holds back a log-space Hadamard product whose single consumer is a binary contraction."""
+        input_strings, output_string = parse_format_string(format_string)
+        if len(args) != 2 or input_strings[0] != output_string or input_strings[1] != output_string:
+            return False
+        if any(a in self.parameter_derived for a in args) or result in self.parameter_derived:
+            return False
+        if self.uses[result] != 1 or result == self.program.output_ssa or result not in self.consumer:
+            return False
+        consumer = self.consumer[result]
+        if consumer.operator.name != "einsum" or len(consumer.argument_ssa_ids) != 2 or consumer.argument_ssa_ids.count(result) != 1:
+            return False
+        if is_contraction_free_einsum(consumer.operator.format_string):
+            return False
+        self.deferred[result] = (self._log(args[0]), self._log(args[1]))
+        return True
 
     def _instruction(self, instruction: Any, result: int) -> None:
         op = instruction.operator
@@ -156,7 +195,8 @@ class _LogspaceLowering:
             fn = partial(_take, axis=op.axis)
             self.positions[result, "logspace"] = b.append(fn, (self._log(args[0]), self._raw(args[1])))
         elif name == "einsum":
-            self._einsum(op.format_string, args, result)
+            if not self._defer_hadamard(op.format_string, args, result):
+                self._einsum(op.format_string, args, result)
         else:
             raise NotImplementedError(f"The operator {name} has no logspace backend translation.")
 
@@ -168,6 +208,18 @@ class _LogspaceLowering:
         if is_contraction_free_einsum(format_string) and not any(linear):
             fn = partial(_contraction.log_broadcast_product, format_string)
             self.positions[result, "logspace"] = self.builder.append(fn, tuple(self._log(a) for a in args))
+            return
+        fused = [i for i, a in enumerate(args) if a in self.deferred and not linear[i]]
+        if len(args) == 2 and fused:
+            # the held-back Hadamard product becomes the fused addend of this contraction's first operand
+            i = fused[0]
+            other = 1 - i
+            b_position = self._raw(args[other]) if linear[other] else self._log(args[other])
+            a_position, a2_position = self.deferred.pop(args[i])
+            _, output_string = parse_format_string(format_string)
+            fmt = f"{input_strings[i]},{input_strings[other]}->{output_string}"
+            fn = partial(_contraction.logspace_einsum_hadamard, fmt, linear[other], self.shift)
+            self.positions[result, "logspace"] = self.builder.append(fn, (a_position, a2_position, b_position))
             return
         positions = tuple(self._raw(a) if lin else self._log(a) for a, lin in zip(args, linear))
         fn = partial(_contraction.logspace_einsum, format_string, linear, self.shift)

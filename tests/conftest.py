@@ -1,6 +1,8 @@
 from __future__ import annotations
 
+import importlib
 import json
+import os
 import sys
 from pathlib import Path
 
@@ -12,6 +14,10 @@ if str(REPO_ROOT) not in sys.path:
     sys.path.insert(0, str(REPO_ROOT))
 
 GOLDEN_DIR = Path(__file__).resolve().parent / "golden"
+
+# the reference package (extended_einsum, pure Python), installed unmodified by
+# baseline/install_reference.sh; XE_REFERENCE_PACKAGE points elsewhere
+REFERENCE_PACKAGE = Path(os.environ.get("XE_REFERENCE_PACKAGE", REPO_ROOT / "baseline" / "_ref"))
 
 # fp32 log-domain tolerance: 1e-5 absolute, plus two fp32 ulps of the
 # reference value (below 1e-5 for |value| < 40; the fp32 representation of
@@ -27,6 +33,20 @@ def pytest_configure(config: pytest.Config) -> None:
 def pytest_collection_modifyitems(config: pytest.Config, items: list[pytest.Item]) -> None:
     # keep GPU tests ordered after CPU tests inside a module-agnostic run
     items.sort(key=lambda item: ("gpu" in item.keywords, item.fspath.basename.startswith("test_zz")))
+
+
+def import_reference():
+    """Imports the reference package from REFERENCE_PACKAGE; skips the test when it is not installed."""
+    if not (REFERENCE_PACKAGE / "extended_einsum").is_dir():
+        pytest.skip(f"reference package not installed in {REFERENCE_PACKAGE} (baseline/install_reference.sh)")
+    if str(REFERENCE_PACKAGE) not in sys.path:
+        sys.path.insert(0, str(REFERENCE_PACKAGE))
+    return importlib.import_module("extended_einsum")
+
+
+@pytest.fixture(scope="session")
+def reference_xe():
+    return import_reference()
 
 
 @pytest.fixture(scope="session")

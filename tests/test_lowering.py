@@ -70,15 +70,34 @@ def test_run_program_checks_input_count():
 
 
 def test_circuit_program_lowering(golden_programs):
+    from extended_einsum_b200.contraction import logspace_einsum_hadamard
+
     program = build_program(golden_programs["circuit_4x4"], "logspace_max")
     lowered = xb.lower(program)
-    # one log of the raw categorical data input; per level: softmax + fused CP einsum,
-    # plus 2 slices + 1 log-add for levels >= 1; top: 2 selects, 1 log-add, softmax,
-    # root einsum.  The reference's translation of the same program has 63 calls.
+    # one log of the raw categorical data input; level 0: softmax + CP einsum; each level >= 1:
+    # softmax, 2 slice views and one CP einsum with the Hadamard product of the halves fused
+    # as its addend; top: 2 select views, softmax and the root einsum with the root product
+    # fused.  The reference's translation of the same program has 63 calls.
     levels = 4
-    assert len(lowered.backend_calls) == 1 + 2 + 5 * (levels - 1) + 5
+    assert len(lowered.backend_calls) == 1 + 2 + 4 * (levels - 1) + 4
     names = [getattr(f, "func", f) for f in _fns(lowered)]
     assert names.count(xb.ops.log) == 1 and xb.ops.exp not in names
+    assert xb.ops.log_add not in names
+    assert names.count(logspace_einsum_hadamard) == levels  # levels 1..3 and the root
+
+
+def test_hadamard_with_two_consumers_is_not_fused():
+    """A product read twice is computed once (as the reference computes it) and not fused."""
+    from extended_einsum_b200.contraction import log_broadcast_product, logspace_einsum_hadamard
+
+    instructions = [
+        fe.RichInstruction(fe.OperatorEinsum("ab,ab->ab"), (0, 1)),
+        fe.RichInstruction(fe.OperatorEinsum("ab,cb->ac"), (3, 2)),
+        fe.RichInstruction(fe.OperatorEinsum("ab,ac->bc"), (3, 4)),
+    ]
+    program = fe.dense_program(instructions, 3, "logspace_max")
+    names = [getattr(f, "func", f) for f in _fns(xb.lower(program))]
+    assert logspace_einsum_hadamard not in names and names.count(log_broadcast_product) == 1
 
 
 def test_quad_tree_leaf_order_is_a_permutation():
@@ -108,17 +127,10 @@ def test_circuit_cost_model():
     assert c.hbm_bytes_per_sample() == 4 * 64 * (1024 + 3 * (512 + 256 + 128 + 64 + 32 + 16 + 8 + 4 + 2)) + 4 * (2 * 64 + 1) + 1024
 
 
-REFERENCE_SRC = Path("/root/reference/src")
+def test_front_end_matches_reference_extract_program(reference_xe):
+    ref = reference_xe
+    from extended_einsum.interface.tensor_expression import Parameter as RefParameter
 
-
-@pytest.mark.skipif(not REFERENCE_SRC.exists(), reason="reference source tree not present")
-def test_front_end_matches_reference_extract_program():
-    sys.path.insert(0, str(REFERENCE_SRC))
-    try:
-        import extended_einsum as ref
-        from extended_einsum.interface.tensor_expression import Parameter as RefParameter
-    finally:
-        sys.path.remove(str(REFERENCE_SRC))
     x = torch.zeros(4, 6, 8)
     w = torch.zeros(4, 5, 8)
     ours, _ = xb.extract_program(xb.log(xb.einsum("dac,dbc->dab", xb.exp(xb.array(x)), xb.softmax(xb.Parameter(xb.array(w)), axis=2))), "logspace_max")
