@@ -279,7 +279,8 @@ class LoweredCircuit:
     resident on the device.  lower() fuses each level's Hadamard product into the next sum layer.
     """
 
-    def __init__(self, device: torch.device, rank: int, batch: int) -> None:
+    def __init__(self, device: torch.device, rank: int, batch: int, layer: str = "cp", side: int = 32,
+                 units: int = 64) -> None:
         if str(REFERENCE_PACKAGE) not in sys.path:
             sys.path.insert(0, str(REFERENCE_PACKAGE))
         import extended_einsum as xe
@@ -288,7 +289,7 @@ class LoweredCircuit:
         from extended_einsum_b200.circuit import demo_circuit_inputs, demo_circuit_program
 
         self.batch = batch
-        program, data_input = demo_circuit_program(xe, 32, 32, 64, batch)
+        program, data_input = demo_circuit_program(xe, side, side, units, batch, layer=layer)
         gen = torch.Generator(device=device).manual_seed(3 + 1000 * rank)
         self.inputs = demo_circuit_inputs(program, data_input, gen, device)
         self.lowered = xb.lower(program)
@@ -298,6 +299,15 @@ class LoweredCircuit:
 
     def step(self, record: bool) -> torch.Tensor:
         return self.run(self.lowered, self.inputs)
+
+    @staticmethod
+    def tucker_flops_per_sample(variables: int, units: int) -> int:
+        """2*O*I*J per layer fold (the fused (i,j) form), every level, the root's one output."""
+        folds, f = 0, variables // 2
+        while f >= 2:
+            folds += f
+            f //= 2
+        return 2 * units**3 * folds + 2 * units * units
 
     @staticmethod
     def hbm_bytes_per_sample(variables: int = 1024, units: int = 64) -> int:
@@ -445,6 +455,23 @@ def run_ours(args, rank: int, world: int, device: torch.device, dist_on: bool) -
             "kernel_calls_per_step": low.launches,
         }
         del low
+        torch.cuda.empty_cache()
+        # the reference's folded Tucker circuit (--sum-product-layer tucker) over a 64x64 grid, K=32:
+        # its first layer is the Tucker configuration b=512, f=2048, i=j=o=32
+        tk = LoweredCircuit(device, rank, 512, layer="tucker", side=64, units=32)
+        t_steps = max(3, args.steps // 4)
+        t_ms = time_region(tk.step, t_steps, 3, dist_on) / t_steps
+        t_flops = LoweredCircuit.tucker_flops_per_sample(4096, 32)
+        lowered_line["tucker_circuit"] = {
+            "metric": "Tucker circuit samples/s through lower()", "value": round(world * tk.batch / (t_ms * 1e-3), 1),
+            "unit": "samples/s", "ms_per_step": round(t_ms, 4),
+            "workload": "the reference's folded 64x64 quad-tree Tucker circuit (Kronecker + sum layers fused by "
+                        "OptimizeContractionPaths into 'acde,abd,abe->abc'), K=32, batch 512 per GPU, data resident",
+            "tflops_algorithmic": round(t_flops * tk.batch / (t_ms * 1e-3) / 1e12, 2),
+            "frac_of_split_tf32_peak": round(t_flops * tk.batch / (t_ms * 1e-3) / 1e12 / (peaks["bf16_tflops"] / 6.0), 4),
+            "kernel_calls_per_step": tk.launches,
+        }
+        del tk
         torch.cuda.empty_cache()
 
     if rank != 0:

@@ -49,6 +49,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "xe_version": (ctypes.c_int, []),
     "xe_last_error_string": (ctypes.c_char_p, []),
     "xe_device_status": (ctypes.c_int, [ctypes.c_int]),
+    "xe_set_wait_timeout_ns": (_c_i32, [ctypes.c_uint64]),
+    "xe_wait_probe": (_c_i32, [_c_i32, _c_ptr]),
+    "xe_categorical_scatter_add": (
+        _c_i32, [_c_ptr, _c_ptr, _c_i64, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_ptr],
+    ),
     "xe_logspace_gemm_workspace_size": (_c_size, [_c_i64, _c_i64, _c_i64, _c_i64, _c_i32, _c_i32]),
     "xe_logspace_gemm": (
         _c_i32,
@@ -101,6 +106,14 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "xe_logspace_tucker": (
         _c_i32,
         [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i32, _c_ptr],
+    ),
+    "xe_logspace_tucker_strided": (
+        _c_i32,
+        [
+            _c_ptr, _c_i64, _c_i64, _c_ptr, _c_i64, _c_i64,  # l, strides, r, strides
+            _c_ptr, _c_ptr, _c_i64, _c_i64,  # w, y, strides
+            _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i32, _c_ptr,  # batch, folds, I, J, O, shift, stream
+        ],
     ),
     "xe_logspace_gemm_gather": (
         _c_i32,

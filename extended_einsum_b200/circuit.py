@@ -22,10 +22,10 @@ and the whole sequence can be captured in one CUDA graph.
 A row of the first layer depends on the sample only through the pixel value of
 its variable, so its output for sample b is row pixels[b, var[f]] of the state
 table, computed by the same kernel on the same row: the values are those of the
-per-sample layer.  For batches smaller than half the states, and when the
-level parameters need gradients, the first layer runs per sample instead
-(the categorical gather fused into it, xe_logspace_gemm_gather, or the
-differentiable gather + contraction).
+per-sample layer.  For batches smaller than half the states the first layer
+runs per sample instead, with the categorical gather fused into it
+(xe_logspace_gemm_gather).  Every step is differentiable: the backward of a
+fused gather scatters its row gradients back into the table.
 
 Layout in HBM (fp32, contiguous): level output (F, B, K) with the batch
 inner to the fold, so that the two Hadamard halves of level l+1 are the two
@@ -157,20 +157,13 @@ class CircuitForward:
 
     def __call__(self, pixels: torch.Tensor) -> torch.Tensor:
         """Log-likelihoods (B, 1) of uint8 pixels (B, variables)."""
-        if ops._needs_grad(self.categorical):
-            raise NotImplementedError("CircuitForward: no backward for the categorical input table on this path")
         table = ops.softmax(self.categorical, 1, log_output=True)
-        # the fused first layers have no backward: with gradients the gather runs on its own
-        differentiable = ops._needs_grad(*self.levels, self.root)
-        state_table = not differentiable and self.circuit.uses_state_table(pixels.shape[0])
+        state_table = self.circuit.uses_state_table(pixels.shape[0])
         y = None
         for level, logits in enumerate(self.levels):
             w = ops.softmax(logits, 2)  # (F, O, K) linear weights
             b_op = w.permute(0, 2, 1)  # (F, K, O), k contiguous
-            if level == 0 and differentiable:
-                x = ops.categorical_gather(table, pixels, self.var_of_fold)
-                y = ops.logspace_gemm(x, b_op, b_linear=True, shift=self.shift)
-            elif level == 0 and state_table:
+            if level == 0 and state_table:
                 # the first sum layer for every state of each variable: (F0, states, K)
                 y = ops.logspace_gemm(table, b_op, b_linear=True, shift=self.shift)
             elif level == 0:
@@ -188,18 +181,25 @@ class CircuitForward:
         return ll[0]
 
 
-def demo_circuit_program(xe, height: int, width: int, units: int, batch: int, stability_mode: str = "logspace_max"):
-    """The demo's folded CP quad-tree circuit program, built and folded by the reference package ``xe``.
+def demo_circuit_program(xe, height: int, width: int, units: int, batch: int, stability_mode: str = "logspace_max",
+                         layer: str = "cp"):
+    """The demo's folded quad-tree circuit program, built and folded by the reference package ``xe``.
 
-    The expression is the one demo/cirkit.py:131-210 builds from a cirkit quad-tree CP circuit
+    The expression is the one demo/cirkit.py:131-210 builds from a cirkit quad-tree circuit
     (cirkit is not needed): leaf v is ``xe.select(data, v)`` of the (variables, batch, units)
-    categorical probabilities, every sum layer is 'ab,cb->ac' with softmax(Parameter) weights over
-    its input units, the two children of a region are joined by the Hadamard product 'ab,ab->ab'
-    (the pairing of quad_tree_leaf_order), and the root sum has one output unit under ``xe.log``.
+    categorical probabilities, and the root has one output unit under ``xe.log``.  The two children
+    of a region (the pairing of quad_tree_leaf_order) are joined
+    * ``layer="cp"`` (--sum-product-layer cp): by the Hadamard product 'ab,ab->ab' of their sum
+      layers 'ab,cb->ac', softmax(Parameter) weights over the input units;
+    * ``layer="tucker"`` (--sum-product-layer tucker): by the Kronecker product 'ab,ac->abc'
+      followed by the sum layer 'abc,dbc->ad' over the unit pairs, weights softmaxed over both.
     It is folded as demo/cirkit.py:478-479 folds it: FoldSameShapedOperations, then
-    OptimizeContractionPaths (preprocess.py).  Returns the folded RichProgram and the index of its
-    data input; every other input is a packed parameter.
+    OptimizeContractionPaths (preprocess.py), which fuses each Kronecker product into its sum
+    layer ('acde,abd,abe->abc').  Returns the folded RichProgram and the index of its data input;
+    every other input is a packed parameter.
     """
+    if layer not in ("cp", "tucker"):
+        raise ValueError(f"unknown sum-product layer {layer!r}; expected 'cp' or 'tucker'")
     tensor_expression = importlib.import_module(xe.__name__ + ".interface.tensor_expression")
     preprocess = importlib.import_module(xe.__name__ + ".preprocess")
     parameter = tensor_expression.Parameter
@@ -210,11 +210,22 @@ def demo_circuit_program(xe, height: int, width: int, units: int, batch: int, st
         weights = xe.softmax(parameter(xe.array(torch.empty((outputs, units), dtype=torch.float32))), axis=1)
         return xe.einsum("ab,cb->ac", child, weights)
 
-    level = [sum_layer(xe.select(data, v)) for v in quad_tree_leaf_order(height, width)]
-    while len(level) > 2:
-        half = len(level) // 2
-        level = [sum_layer(xe.einsum("ab,ab->ab", level[i], level[i + half])) for i in range(half)]
-    root = sum_layer(xe.einsum("ab,ab->ab", level[0], level[1]), outputs=1)
+    def tucker_layer(left, right, outputs: int = units):
+        weights = xe.softmax(parameter(xe.array(torch.empty((outputs, units, units), dtype=torch.float32))), axis=(1, 2))
+        return xe.einsum("abc,dbc->ad", xe.einsum("ab,ac->abc", left, right), weights)
+
+    if layer == "cp":
+        level = [sum_layer(xe.select(data, v)) for v in quad_tree_leaf_order(height, width)]
+        while len(level) > 2:
+            half = len(level) // 2
+            level = [sum_layer(xe.einsum("ab,ab->ab", level[i], level[i + half])) for i in range(half)]
+        root = sum_layer(xe.einsum("ab,ab->ab", level[0], level[1]), outputs=1)
+    else:
+        level = [xe.select(data, v) for v in quad_tree_leaf_order(height, width)]
+        while len(level) > 2:
+            half = len(level) // 2
+            level = [tucker_layer(level[i], level[i + half]) for i in range(half)]
+        root = tucker_layer(level[0], level[1], outputs=1)
     program, _ = xe.extract_program(xe.log(root), stability_mode=stability_mode)
     folded = preprocess.FoldSameShapedOperations.apply_with_metadata(program)
     folded_program = preprocess.OptimizeContractionPaths.apply(folded.program)

@@ -10,8 +10,10 @@ same arithmetic is one launch:
                             batch (both operands and output), M (first operand
                             and output), N (second operand and output) and K
                             (both operands, not output)
-* 'bfi,bfj,foij->bfo'    -> xe_logspace_tucker (the fused Tucker layer,
-                            preprocess.py:1095-1106)
+* 'bfi,bfj,foij->bfo'    -> xe_logspace_tucker_strided (the fused Tucker layer,
+                            preprocess.py:1095-1106), also in the folded
+                            circuits' fold-major form 'acde,abd,abe->abc' and
+                            their root 'bcd,ac,ad->ab'
 * contraction-free       -> xe_log_add (translate.py:706-718)
 * a Hadamard product of two log operands feeding a two-operand contraction
   (the folded circuit's 'cab,cab->cab' -> 'dac,dbc->dab')
@@ -90,7 +92,6 @@ def logspace_einsum(
         raise ValueError(f"The einsum format string has {len(input_strings)} inputs, but the instruction has {len(operands)} arguments.")
     _check_labels(input_strings, output_string)
     sizes = _sizes(input_strings, operands)
-    out_shape = [sizes[label] for label in output_string]
     if len(operands) == 1:
         return _reduce(input_strings[0], output_string, operands[0], linear[0], shift, sizes)
     if len(operands) == 2:
@@ -98,8 +99,7 @@ def logspace_einsum(
     if len(operands) == 3:
         tucker = _match_tucker(input_strings, output_string, linear)
         if tucker is not None:
-            left, right, weights = (operands[i] for i in tucker)
-            return _tucker(input_strings, output_string, tucker, left, right, weights, shift, sizes, out_shape)
+            return _tucker(tucker, operands, shift)
     raise NotImplementedError(
         f"einsum {format_string!r} with {len(operands)} operands has no fused log-space kernel on this path"
     )
@@ -162,29 +162,57 @@ def _binary(input_strings, output_string, operands, linear, shift, sizes, a2: to
 
 
 def _match_tucker(input_strings, output_string, linear):
-    """Index order (left, right, weights) if the einsum is a Tucker layer 'bfi,bfj,foij->bfo'."""
+    """(left, right, weights, fold_first, has_fold) operand roles if the einsum is a Tucker layer.
+
+    Three forms reach this path: the layer as written, 'bfi,bfj,foij->bfo' (batch-major); the
+    folded circuits' layer after FoldSameShapedOperations and OptimizeContractionPaths
+    (preprocess.py:1095-1106, 1310-1393), 'acde,abd,abe->abc' with the fold label first; and their
+    root, 'bcd,ac,ad->ab', a single layer without a fold label.  The weights are the operand with
+    the o, i, j labels (linear[w] must be set when ``linear`` is given); left and right end in i
+    and j and share their leading labels with the output, which ends in o.
+    """
     for w in range(3):
-        if not linear[w]:
+        if linear is not None and not linear[w]:
             continue
         others = [i for i in range(3) if i != w]
-        if linear[others[0]] or linear[others[1]]:
+        if linear is not None and (linear[others[0]] or linear[others[1]]):
             continue
         l_lab, r_lab, w_lab = input_strings[others[0]], input_strings[others[1]], input_strings[w]
-        if len(l_lab) != 3 or len(r_lab) != 3 or len(w_lab) != 4 or len(output_string) != 3:
-            continue
-        b, f, i = l_lab
-        b2, f2, j = r_lab
-        o = next((x for x in output_string if x not in (b, f)), None)
-        if (b, f) != (b2, f2) or o is None or output_string != b + f + o:
-            continue
-        if w_lab != f + o + i + j:
-            continue
-        return (others[0], others[1], w)
+        if len(w_lab) == 4 and len(l_lab) == 3 and len(r_lab) == 3 and len(output_string) == 3:
+            f, o, i, j = w_lab
+            lead = l_lab[:2]
+            b = lead.replace(f, "")
+            if f not in lead or len(b) != 1 or len({b, f, o, i, j}) != 5:
+                continue
+            if l_lab != lead + i or r_lab != lead + j or output_string != lead + o:
+                continue
+            return others[0], others[1], w, lead[0] == f, True
+        if len(w_lab) == 3 and len(l_lab) == 2 and len(r_lab) == 2 and len(output_string) == 2:
+            o, i, j = w_lab
+            b = l_lab[0]
+            if len({b, o, i, j}) != 4 or l_lab != b + i or r_lab != b + j or output_string != b + o:
+                continue
+            return others[0], others[1], w, False, False
     return None
 
 
-def _tucker(input_strings, output_string, order, left, right, weights, shift, sizes, out_shape) -> torch.Tensor:
-    return ops.logspace_tucker(left, right, weights, shift=shift)
+def _tucker(match, operands, shift: str) -> torch.Tensor:
+    """The matched Tucker layer on xe_logspace_tucker_strided, in the layout the einsum names."""
+    l_idx, r_idx, w_idx, fold_first, has_fold = match
+    left, right, weights = operands[l_idx], operands[r_idx], operands[w_idx]
+    if not has_fold:
+        y = ops.logspace_tucker(left.unsqueeze(1), right.unsqueeze(1), weights.unsqueeze(0), shift=shift)
+        return y[:, 0, :]
+    if not fold_first:
+        return ops.logspace_tucker(left, right, weights, shift=shift)
+    # fold-major (F, B, I) operands and output, addressed as (B, F, I) views
+    lt, rt = left.transpose(0, 1), right.transpose(0, 1)
+    if ops._needs_grad(left, right, weights):
+        return ops.logspace_tucker(lt, rt, weights, shift=shift).transpose(0, 1)
+    folds, batch, o_dim = weights.shape[0], left.shape[1], weights.shape[1]
+    out = torch.empty((folds, batch, o_dim), device=left.device, dtype=torch.float32)
+    ops.logspace_tucker(lt, rt, weights, shift=shift, out=out.transpose(0, 1))
+    return out
 
 
 # ---------------------------------------------------------------------------
@@ -216,11 +244,10 @@ def linear_einsum(format_string: str, *operands: torch.Tensor) -> torch.Tensor:
     if len(operands) == 2:
         return _linear_binary(input_strings, output_string, operands, sizes)
     if len(operands) == 3:
-        tucker = _match_tucker(input_strings, output_string, (False, False, True))
+        tucker = _match_tucker(input_strings, output_string, None)
         if tucker is not None:
-            left, right, weights = (operands[i] for i in tucker)
-            logits = ops.logspace_tucker(ops.log(left), ops.log(right), weights, shift="max")
-            return ops.exp(logits)
+            logs = [operand if i == tucker[2] else ops.log(operand) for i, operand in enumerate(operands)]
+            return ops.exp(_tucker(tucker, logs, "max"))
     raise NotImplementedError(f"einsum {format_string!r} with {len(operands)} operands has no fused kernel on this path")
 
 

@@ -120,6 +120,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* slab_empty = slab_full + 1;
   uint32_t* tmem_slot = (uint32_t*)(slab_empty + 1);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+  // the barriers the producer armed, drained at wind-down after an abort
+  ArmedCopies* a_copies = (ArmedCopies*)(tmem_slot + 2);
+  ArmedCopies* raw_copies = a_copies + 1;
+  ArmedCopies* slab_copies = a_copies + 2;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -139,6 +143,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(slab_full, 1);
     mbar_init(slab_empty, 256);
     *abort_flag = 0;
+    *a_copies = *raw_copies = *slab_copies = ArmedCopies{0u, 0u};
     fence_mbarrier_init();
   }
   if (warp == kMmaWarp) tmem_alloc<512>(tmem_slot);
@@ -197,7 +202,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_arrive(slab_empty);
             ++released;
           }
-          fine = mbar_wait(slab_full, acquired & 1, kSiteAStaged, abort_flag);
+          fine = mbar_wait_warp(slab_full, acquired & 1, kSiteAStaged, abort_flag);
           ++acquired;
         }
         if (!fine) return false;
@@ -228,7 +233,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       } else {
         const uint32_t u = j / C::kStages;
-        if (!mbar_wait(&a_full[group * C::kStages + sidx], u & 1, kSiteAStaged, abort_flag)) return false;
+        if (!mbar_wait_warp(&a_full[group * C::kStages + sidx], u & 1, kSiteAStaged, abort_flag)) return false;
         const uint32_t stage = smem_base + C::kOffA + (group * C::kStages + sidx) * C::kStageBytes;
 #pragma unroll
         for (int kb = 0; kb < 2; ++kb) {
@@ -349,7 +354,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive(slab_empty);
           ++released;
         }
-        ok = mbar_wait(slab_full, acquired & 1, kSiteAStaged, abort_flag);
+        ok = mbar_wait_warp(slab_full, acquired & 1, kSiteAStaged, abort_flag);
         ++acquired;
       }
       while (released < acquired) {
@@ -403,9 +408,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ TMA loads, weight split
     bool ok = true;
     int fold_count = 0;
+    uint32_t raw_arms = 0;
     // the first fold's raw weights
     if (lane == 0 && first < last) {
       mbar_expect_tx(raw_full, kBBytes);
+      raw_copies->note(0, raw_arms++);
       const int f = fold_of(first);
       tma_load_3d(smem_base + C::kOffBRaw, &tmap_w, 0, 0, f, raw_full);
       tma_load_3d(smem_base + C::kOffBRaw + kBKBlock, &tmap_w, 32, 0, f, raw_full);
@@ -419,6 +426,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (fold_count > 0) ready = mbar_wait(slab_empty, (fold_count - 1) & 1, kSiteProducer, abort_flag);
           if (ready) {
             mbar_expect_tx(slab_full, 4 * p.states * 128);
+            slab_copies->note(0, fold_count);
 #pragma unroll
             for (int h = 0; h < 2; ++h)
 #pragma unroll
@@ -456,6 +464,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           while (next < last && fold_of(next) == bb) ++next;
           if (next < last) {
             mbar_expect_tx(raw_full, kBBytes);
+            raw_copies->note(0, raw_arms++);
             tma_load_3d(smem_base + C::kOffBRaw, &tmap_w, 0, 0, fold_of(next), raw_full);
             tma_load_3d(smem_base + C::kOffBRaw + kBKBlock, &tmap_w, 32, 0, fold_of(next), raw_full);
           }
@@ -474,6 +483,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int mt = i - bb * p.tiles_m;
           const uint32_t dst = smem_base + C::kOffA + slot * C::kStageBytes;
           mbar_expect_tx(&a_full[slot], C::kStageBytes);
+          a_copies->note(slot, u);
           tma_load_3d(dst, &tmap_a, 0, mt * kBM, bb, &a_full[slot]);
           tma_load_3d(dst + kAKBlock, &tmap_a, 32, mt * kBM, bb, &a_full[slot]);
           if (PAIR) {
@@ -488,6 +498,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  if (*abort_flag) {  // uniform: every thread has passed its last wait
+    a_copies->drain(a_full, abort_flag);
+    raw_copies->drain(raw_full, abort_flag);
+    slab_copies->drain(slab_full, abort_flag);
+    __syncthreads();
+  }
   tc_fence_after();
   if (warp == kMmaWarp) tmem_dealloc<512>(tmem);
 }

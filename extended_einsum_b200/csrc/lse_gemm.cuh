@@ -94,6 +94,7 @@ struct Params {
   const float* tl;
   const float* tr;
   int t_folds, t_i;
+  int64_t t_l_sb, t_l_sf, t_r_sb, t_r_sf;  // element strides of l and r over (batch row, fold); units contiguous
 };
 
 __host__ __device__ constexpr int pow2_at_least(int x) {
@@ -371,9 +372,9 @@ struct ARow {
   __device__ void tucker_row(const Params& p, int bb, int m, bool want_er) {
     valid = m < p.M;
     const bool is_min = p.shift_min != 0;
-    const int64_t r = (int64_t)(valid ? m : 0) * p.t_folds + bb;
-    lrow = p.tl + r * p.t_i;
-    const float* rrow = p.tr + r * kTJ;
+    const int64_t row = valid ? m : 0;
+    lrow = p.tl + row * p.t_l_sb + bb * p.t_l_sf;
+    const float* rrow = p.tr + row * p.t_r_sb + bb * p.t_r_sf;
     float e1 = is_min ? INFINITY : -INFINITY, e2 = e1;
 #pragma unroll 4
     for (int i = 0; i < p.t_i; i += 4) {
@@ -664,6 +665,9 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
   uint64_t* drain = b_empty + 4;                // [1], teardown
   uint32_t* tmem_slot = (uint32_t*)(drain + 1);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+  // the A / B ring barriers the producer armed, drained at wind-down after an abort
+  ArmedCopies* a_copies = (ArmedCopies*)(tmem_slot + 2);
+  ArmedCopies* b_copies = a_copies + 1;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -688,6 +692,7 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
     for (int c = 0; c < C::kCorrBufs; ++c) mbar_init(&corr_empty[c], kDrainWarps);
     mbar_init(drain, 1);
     *abort_flag = 0;
+    *a_copies = *b_copies = ArmedCopies{0u, 0u};
     fence_mbarrier_init();
   }
   if (warp == kMmaWarp) tmem_alloc<C::kTmemCols>(tmem_slot);
@@ -732,7 +737,7 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
             for (int kb = 0; kb < p.num_kb; ++kb) {
               const uint32_t sidx = (ait + kb) % C::kAStages;
               if (!mbar_wait(&a_full[sidx], ((ait + kb) / C::kAStages) & 1, kSiteAStaged, abort_flag)) {
-                ok = false;
+                ok = false;  // per lane: the vote after the scan makes it warp-uniform
                 break;
               }
               const int kvalid = p.K - kb * kBK;
@@ -762,7 +767,7 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
               }
             }
             XE_SEGMENT_END(seg_scan, 6);
-            if (!ok) break;
+            // a lane whose wait ran out (ok false) goes on to the vote at the shift slot below
             if (keep) {
               __syncwarp();
               if (lane == 0)
@@ -795,7 +800,10 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
       // -------- publish the row shifts for the epilogue
       {
         const uint32_t slot = tl & 1;
-        if (!mbar_wait(&shift_empty[slot], ((tl >> 1) & 1) ^ 1, kSiteAShiftSlot, abort_flag)) break;
+        if (!mbar_wait_warp(&shift_empty[slot], ((tl >> 1) & 1) ^ 1, kSiteAShiftSlot, abort_flag, ok)) {
+          ok = false;
+          break;
+        }
         shifts[(slot * 2 + 0) * kBM + r] = s1;
         shifts[(slot * 2 + 1) * kBM + r] = s2;
         __syncwarp();
@@ -809,12 +817,11 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
         // a shared-memory load may still be in flight when the next instruction issues, and the
         // producer's TMA would overwrite the slot.
         int release = -1;
+        // per lane, voted on below; after an abort the loads read a stage nobody consumes
+        bool staged = true;
         if (ASRC != kALdg && !preloaded) {
           const uint32_t sidx = ait % C::kAStages;
-          if (!mbar_wait(&a_full[sidx], (ait / C::kAStages) & 1, kSiteAStaged, abort_flag)) {
-            ok = false;
-            break;
-          }
+          staged = mbar_wait(&a_full[sidx], (ait / C::kAStages) & 1, kSiteAStaged, abort_flag);
           load_staged_row<ASRC>(smem_base + C::kOffA + sidx * C::kAStageBytes, r, a.valid, p.K - kb * kBK, fill,
                                 cur);
           release = (int)sidx;
@@ -825,7 +832,7 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
         XE_SEGMENT_END(seg_load, 1);
         const uint32_t s = it % kStages;
         const uint32_t ph = (it / kStages) & 1;
-        if (!mbar_wait_warp(&empty[s], ph ^ 1, kSiteAStage, abort_flag)) {
+        if (!mbar_wait_warp(&empty[s], ph ^ 1, kSiteAStage, abort_flag, staged)) {
           ok = false;
           break;
         }
@@ -878,12 +885,11 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
       for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
         const bool more = kb + 1 < p.num_kb;
         int release = -1;
+        // per lane, voted on below; after an abort the loads read a stage nobody consumes
+        bool staged = true;
         if (BSRC == kBTma) {
           const uint32_t sidx = bit % C::kBRawStages;
-          if (!mbar_wait(&b_full[sidx], (bit / C::kBRawStages) & 1, kSiteBStage, abort_flag)) {
-            ok = false;
-            break;
-          }
+          staged = mbar_wait(&b_full[sidx], (bit / C::kBRawStages) & 1, kSiteBStage, abort_flag);
           bt.load_staged(p, smem_base + C::kOffBRaw + sidx * C::kBRawBytes, n0, kb * kBK, t, cur);
           release = (int)sidx;  // released after the values are used (see the A rows)
           ++bit;
@@ -892,10 +898,8 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
         }
         const uint32_t s = it % kStages;
         const uint32_t ph = (it / kStages) & 1;
-        if (!mbar_wait(&empty[s], ph ^ 1, kSiteBStage, abort_flag)) {
-          ok = false;
-          break;
-        }
+        // per lane; after an abort the stores below only write this CTA's own stage
+        const bool ready = mbar_wait(&empty[s], ph ^ 1, kSiteBStage, abort_flag) && staged;
         const uint32_t st = smem_base + C::kOffB + s * C::kStageBytes;
         XE_SEGMENT_BEGIN(seg_b);
         bt.store(p, st, st + C::kBTile, t, cur);
@@ -905,6 +909,12 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
         if (lane == 0) {
           mbar_arrive(&full[s]);
           if (release >= 0) mbar_arrive(&b_empty[release]);
+        }
+        // a timeout seen by any lane ends the warp's loop for all of them; voted after the arrival
+        // (after an abort it only hands on a stage that nobody uses), off the tensor core's path
+        if (!__all_sync(0xffffffffu, ready)) {
+          ok = false;
+          break;
         }
         if (t == 0 && (kb == 0 || kb == 8)) XE_TILE_TRACE(it / p.num_kb, kb == 0 ? 4 : 5);
         if (BSRC != kBTma && more) {
@@ -1035,10 +1045,10 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
       // -------- epilogue from shared memory, overlapping the next tile's MMAs
       XE_SEGMENT_BEGIN(seg_ep);
       const uint32_t slot = tl & 1;
-      if (!mbar_wait(&shift_full[slot], (tl >> 1) & 1, kSiteDrainShift, abort_flag)) break;
+      const bool shifted = mbar_wait(&shift_full[slot], (tl >> 1) & 1, kSiteDrainShift, abort_flag);
       const float s1 = shifts[(slot * 2 + 0) * kBM + r];
       const float s2 = shifts[(slot * 2 + 1) * kBM + r];
-      __syncwarp();
+      if (!__all_sync(0xffffffffu, shifted)) break;  // the warp's reconvergence, and a timeout seen by all lanes
       if (lane == 0) mbar_arrive(&shift_empty[slot]);
       // column shifts of a log-domain B, copied into this warp's own slice of shared memory
       float* cshift = p.shift_b ? (float*)(smem + C::kOffColShift) + (group * 4 + q) * BN : nullptr;
@@ -1198,7 +1208,10 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
         bool armed = true;
         if (lane == 0) {
           armed = mbar_wait(&a_empty[sidx], ((ait / C::kAStages) & 1) ^ 1, kSiteProducer, abort_flag);
-          if (armed) mbar_expect_tx(&a_full[sidx], C::kAStageBytes);
+          if (armed) {
+            mbar_expect_tx(&a_full[sidx], C::kAStageBytes);
+            a_copies->note(sidx, ait / C::kAStages);
+          }
         }
         if (__shfl_sync(0xffffffffu, armed ? 1 : 0, 0) == 0) {  // the warp leaves together
           ok = false;
@@ -1217,6 +1230,7 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
           } else {
             const uint32_t bdst = smem_base + C::kOffBRaw + bidx * C::kBRawBytes;
             mbar_expect_tx(&b_full[bidx], C::kBRawBytes);
+            b_copies->note(bidx, bit / C::kBRawStages);
             if (B_KMAJ)
               tma_load_3d(bdst, &tmap_b, kb * kBK, nt * BN, bb, &b_full[bidx]);
             else
@@ -1244,6 +1258,7 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
           }
           const uint32_t dst = smem_base + C::kOffA + sidx * C::kAStageBytes;
           mbar_expect_tx(&a_full[sidx], C::kAStageBytes);
+          a_copies->note(sidx, ait / C::kAStages);
           tma_load_3d(dst, &tmap_a, kb * kBK, mt * kBM, bb, &a_full[sidx]);
           if (ASRC == kATma2) tma_load_3d(dst + kATileBytes, &tmap_a2, kb * kBK, mt * kBM, bb, &a_full[sidx]);
           if (kb == 0 || kb == 8) XE_TILE_TRACE(ait / p.num_kb, kb == 0 ? 0 : 1);
@@ -1257,6 +1272,7 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
           }
           const uint32_t dst = smem_base + C::kOffBRaw + sidx * C::kBRawBytes;
           mbar_expect_tx(&b_full[sidx], C::kBRawBytes);
+          b_copies->note(sidx, bit / C::kBRawStages);
           if (B_KMAJ)
             tma_load_3d(dst, &tmap_b, kb * kBK, nt * BN, bb, &b_full[sidx]);
           else
@@ -1269,6 +1285,11 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  if (*abort_flag) {  // uniform: every thread has passed its last wait
+    a_copies->drain(a_full, abort_flag);
+    b_copies->drain(b_full, abort_flag);
+    __syncthreads();
+  }
   tc_fence_after();
   if (warp == kMmaWarp) tmem_dealloc<C::kTmemCols>(tmem);
 }

@@ -232,9 +232,12 @@ __global__ void __launch_bounds__(1024, 1)
   const int tid = threadIdx.x;
   const uint32_t buf = smem_u32(row_buf);
   const uint32_t bytes = (uint32_t)(len * 4);
+  ArmedCopies copies{0u, 0u};  // thread 0's last row copy, drained after an abort
+  uint32_t fetches = 0;
   // the row's bulk copy, in pieces of at most 32 KB (16-byte multiples)
   auto fetch = [&](int64_t row) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(&full)), "r"(bytes) : "memory");
+    copies.note(0, fetches++);
     for (uint32_t off = 0; off < bytes; off += 32768) {
       const uint32_t piece = bytes - off < 32768 ? bytes - off : 32768;
       asm volatile(
@@ -252,7 +255,8 @@ __global__ void __launch_bounds__(1024, 1)
   if (tid == 0 && (int64_t)blockIdx.x < rows) fetch(blockIdx.x);
   uint32_t phase = 0;
   for (int64_t row = blockIdx.x; row < rows; row += gridDim.x, phase ^= 1) {
-    if (!mbar_wait(&full, phase, kSiteSoftmax, &abort_flag)) break;
+    // the block leaves together (block barriers follow) if any thread's wait ran out
+    if (!__syncthreads_and(mbar_wait(&full, phase, kSiteSoftmax, &abort_flag))) break;
     float4 v[kQ];
     float m = -INFINITY;
 #pragma unroll
@@ -301,6 +305,8 @@ __global__ void __launch_bounds__(1024, 1)
     }
     __syncthreads();  // scratch is reused by the next row's reductions
   }
+  // after an abort the next row's copy may still be landing in this CTA's shared memory
+  if (*(volatile int*)&abort_flag && tid == 0) copies.drain(&full, &abort_flag);
 }
 
 // Softmax of rows too long for registers: one block per row, three streaming
@@ -431,6 +437,75 @@ __global__ void __launch_bounds__(256) categorical_gather1(const float* __restri
       s = states - 1;
     }
     y[g] = __ldg(table + (f * states + s) * units + u);
+  }
+}
+
+// Backward of the categorical gather: dt[f + off, pixels[b, var[f + off]], :] += g[f, b, :].
+// One CTA per (fold, slice of the batch): the fold's (states, units) slice is accumulated in
+// shared memory (one warp per sample row, lanes over the units), then added to global memory
+// once.  g is (folds, batch, units) contiguous.  Bad indices are clamped and reported as in the
+// forward gather.
+__device__ __forceinline__ int64_t scatter_variable(const int32_t* var_of_fold, int64_t fold, int64_t ps) {
+  int64_t v = var_of_fold ? (int64_t)__ldg(var_of_fold + fold) : fold;
+  if (v < 0 || v >= ps) {
+    record_bad_index(kSiteGatherState);
+    v = 0;
+  }
+  return v;
+}
+
+__device__ __forceinline__ int64_t scatter_state(const uint8_t* pixels, int64_t b, int64_t ps, int64_t v, int64_t states) {
+  int64_t s = (int64_t)__ldg(pixels + b * ps + v);
+  if (s >= states) {
+    record_bad_index(kSiteGatherState);
+    s = states - 1;
+  }
+  return s;
+}
+
+__global__ void __launch_bounds__(256) categorical_scatter_smem(const float* __restrict__ g,
+                                                                const uint8_t* __restrict__ pixels, int64_t ps,
+                                                                const int32_t* __restrict__ var_of_fold,
+                                                                float* __restrict__ dt, int64_t states, int64_t units,
+                                                                int64_t batch, int64_t off, int64_t b_chunk) {
+  extern __shared__ float acc[];  // states * units
+  const int64_t f = blockIdx.x;
+  const int64_t slice = states * units;
+  for (int64_t i = threadIdx.x; i < slice; i += blockDim.x) acc[i] = 0.0f;
+  __syncthreads();
+  const int64_t v = scatter_variable(var_of_fold, f + off, ps);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t b0 = (int64_t)blockIdx.y * b_chunk;
+  const int64_t b1 = b0 + b_chunk < batch ? b0 + b_chunk : batch;
+  for (int64_t b = b0 + warp; b < b1; b += blockDim.x >> 5) {
+    const int64_t st = scatter_state(pixels, b, ps, v, states);
+    const float* row = g + (f * batch + b) * units;
+    float* dst = acc + st * units;
+    for (int64_t u = lane; u < units; u += 32) atomicAdd(dst + u, __ldg(row + u));
+  }
+  __syncthreads();
+  float* out = dt + (f + off) * slice;
+  for (int64_t i = threadIdx.x; i < slice; i += blockDim.x) {
+    const float a = acc[i];
+    if (a != 0.0f) atomicAdd(out + i, a);
+  }
+}
+
+// The same with global atomics only, for a (states, units) slice larger than shared memory.
+__global__ void __launch_bounds__(256) categorical_scatter_global(const float* __restrict__ g,
+                                                                  const uint8_t* __restrict__ pixels, int64_t ps,
+                                                                  const int32_t* __restrict__ var_of_fold,
+                                                                  float* __restrict__ dt, int64_t folds,
+                                                                  int64_t states, int64_t units, int64_t batch,
+                                                                  int64_t off) {
+  const int64_t total = folds * batch * units;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t u = i % units;
+    const int64_t row = i / units;
+    const int64_t f = row / batch, b = row - f * batch;
+    const int64_t v = scatter_variable(var_of_fold, f + off, ps);
+    const int64_t st = scatter_state(pixels, b, ps, v, states);
+    atomicAdd(dt + ((f + off) * states + st) * units + u, __ldg(g + i));
   }
 }
 

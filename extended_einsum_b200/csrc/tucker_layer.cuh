@@ -79,6 +79,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* drain = acc_empty + 2;
   uint32_t* tmem_slot = (uint32_t*)(drain + 1);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+  // the barriers the producer armed, drained at wind-down after an abort
+  ArmedCopies* lr_copies = (ArmedCopies*)(tmem_slot + 2);
+  ArmedCopies* w_copies = lr_copies + 1;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -99,6 +102,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
+    *lr_copies = *w_copies = ArmedCopies{0u, 0u};
     fence_mbarrier_init();
   }
   if (warp == kMmaWarp) tmem_alloc<512>(tmem_slot);
@@ -128,7 +132,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int f = tile / p.tiles_m;
       const int mt = tile - f * p.tiles_m;
       const bool valid = mt * kBM + r < p.rows;
-      if (!mbar_wait(&lr_full[group], j & 1, kSiteAStaged, abort_flag)) break;
+      if (!mbar_wait_warp(&lr_full[group], j & 1, kSiteAStaged, abort_flag)) break;
       XE_CP_TRACE(r == 0 ? n : 1 << 20, 0);
       float lv[kDim], rv[kDim];
       const uint32_t lrow = smem_base + C::kOffLR + group * 2 * kRowBytes + r * 128;
@@ -231,7 +235,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int total = count * kChunks;           // every tile's chunks, in ring order
     for (int gw = 0; gw < total; ++gw) {
       const uint32_t s = gw % kWStages;
-      if (!mbar_wait(&w_full[s], (gw / kWStages) & 1, kSiteAStage, abort_flag)) break;
+      if (!mbar_wait_warp(&w_full[s], (gw / kWStages) & 1, kSiteAStage, abort_flag)) break;
       if (tt == 0 && (gw % (2 * kChunks) == 0 || gw % (2 * kChunks) == 16)) XE_CP_TRACE(2 * (gw / (2 * kChunks)), gw % (2 * kChunks) == 0 ? 6 : 7);
       const uint32_t hi = smem_base + C::kOffW + s * 2 * kWBytes, lo = hi + kWBytes;
 #pragma unroll
@@ -306,6 +310,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait(&lr_empty[g], (j & 1) ^ 1, kSiteProducer, abort_flag)) return false;
       const uint32_t dst = smem_base + C::kOffLR + g * 2 * kRowBytes;
       mbar_expect_tx(&lr_full[g], 2 * kRowBytes);
+      lr_copies->note(g, j);
       tma_load_3d(dst, &tmap_l, 0, f, mt * kBM, &lr_full[g]);
       tma_load_3d(dst + kRowBytes, &tmap_r, 0, f, mt * kBM, &lr_full[g]);
       return true;
@@ -325,6 +330,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int f = (first + n0 + g) / p.tiles_m;
           if (c == 0 || c == 8) XE_CP_TRACE(n0 + g, c == 0 ? 4 : 5);
           mbar_expect_tx(&w_full[s], kWBytes);
+          w_copies->note(s, gw / kWStages);
           tma_load_3d(smem_base + C::kOffW + s * 2 * kWBytes, &tmap_w, 0, c * kChunkN, f, &w_full[s]);
         }
       }
@@ -334,6 +340,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  if (*abort_flag) {  // uniform: every thread has passed its last wait
+    lr_copies->drain(lr_full, abort_flag);
+    w_copies->drain(w_full, abort_flag);
+    __syncthreads();
+  }
   tc_fence_after();
   if (warp == kMmaWarp) tmem_dealloc<512>(tmem);
 }

@@ -18,7 +18,6 @@
 #include "cp_layer.cuh"
 #include "tucker_layer.cuh"
 #include "pointwise.cuh"
-#include "tucker.cuh"
 
 namespace {
 
@@ -460,9 +459,54 @@ bool make_nd(const int64_t* shape, const int64_t* as, const int64_t* bs, int ndi
 
 }  // namespace
 
+// The log-space Tucker layer 'bfi,bfj,foij->bfo' (defined after the C entry points).
+static xe_status xe_tucker_impl(const float* l, int64_t l_sb, int64_t l_sf, const float* r, int64_t r_sb,
+                                int64_t r_sf, const float* w, float* y, int64_t y_sb, int64_t y_sf, int64_t batch,
+                                int64_t folds, int64_t i_dim, int64_t j_dim, int64_t o_dim, int32_t shift_mode,
+                                cudaStream_t stream);
+
+namespace xe {
+// The bounded-wait test kernel (xe_wait_probe): warp 0 waits on a barrier expecting one
+// arrival; with `complete` set, warp 1 arrives after a bounded delay, otherwise nothing
+// arrives and the wait runs out after g_wait_timeout_ns.
+__global__ void wait_probe_kernel(int complete) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    mbar_wait(&bar, 0, kSiteWaitProbe, &abort_flag);
+  } else if (threadIdx.x == 32 && complete) {
+    const long long t0 = clock64();
+    while (clock64() - t0 < 20000) {
+    }
+    mbar_arrive(&bar);
+  }
+}
+}  // namespace xe
+
 extern "C" {
 
 int xe_version(void) { return 100; }
+
+xe_status xe_set_wait_timeout_ns(uint64_t ns) {
+  const uint64_t value = ns == 0 ? xe::kWaitTimeoutNs : ns;
+  if (value < 1000ull || value > 60000000000ull)
+    return fail(XE_ERR_INVALID_ARGUMENT, "xe_set_wait_timeout_ns: %llu ns is outside [1 us, 60 s]",
+                (unsigned long long)ns);
+  const cudaError_t e = cudaMemcpyToSymbol(xe::g_wait_timeout_ns, &value, sizeof(value));
+  if (e != cudaSuccess) return fail(XE_ERR_CUDA, "xe_set_wait_timeout_ns: %s", cudaGetErrorString(e));
+  return XE_OK;
+}
+
+xe_status xe_wait_probe(int complete, void* stream) {
+  xe::wait_probe_kernel<<<1, 64, 0, as_stream(stream)>>>(complete);
+  return check_launch("xe_wait_probe");
+}
 
 const char* xe_last_error_string(void) { return g_last_error.c_str(); }
 
@@ -914,6 +958,43 @@ xe_status xe_categorical_gather(const float* table, const uint8_t* pixels, int64
   return check_launch("xe_categorical_gather");
 }
 
+xe_status xe_categorical_scatter_add(const float* grad, const uint8_t* pixels, int64_t pixel_stride,
+                                     const int32_t* var_of_fold, float* table_grad, int64_t folds, int64_t states,
+                                     int64_t units, int64_t batch, int64_t fold_offset, void* stream) {
+  if (!grad || !pixels || !table_grad) return fail(XE_ERR_INVALID_ARGUMENT, "xe_categorical_scatter_add: null pointer");
+  if (folds < 0 || states <= 0 || units < 0 || batch < 0 || fold_offset < 0 || pixel_stride <= 0)
+    return fail(XE_ERR_INVALID_ARGUMENT, "xe_categorical_scatter_add: invalid extents");
+  if (states > 256)
+    return fail(XE_ERR_INVALID_ARGUMENT, "xe_categorical_scatter_add: uint8 pixels address at most 256 states");
+  if (folds == 0 || units == 0 || batch == 0) return XE_OK;
+  cudaStream_t s = as_stream(stream);
+  const int64_t smem = states * units * (int64_t)sizeof(float);
+  if (smem <= 96 * 1024) {
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && !attr_set[dev]) {
+      const cudaError_t e =
+          cudaFuncSetAttribute(xe::categorical_scatter_smem, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+      if (e != cudaSuccess)
+        return fail(XE_ERR_CUDA, "xe_categorical_scatter_add: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+      attr_set[dev] = true;
+    }
+    // at least two CTAs per SM: the batch is split into chunks when there are few folds
+    const int64_t target = 2 * (int64_t)current_device_sms();
+    const int64_t chunks = std::max<int64_t>(1, std::min<int64_t>(batch, (target + folds - 1) / folds));
+    const int64_t b_chunk = (batch + chunks - 1) / chunks;
+    dim3 grid((unsigned)folds, (unsigned)((batch + b_chunk - 1) / b_chunk));
+    xe::categorical_scatter_smem<<<grid, 256, (size_t)smem, s>>>(grad, pixels, pixel_stride, var_of_fold, table_grad,
+                                                                  states, units, batch, fold_offset, b_chunk);
+  } else {
+    const int64_t total = folds * batch * units;
+    xe::categorical_scatter_global<<<(unsigned)grid_for(total, 256, current_device_sms() * 8), 256, 0, s>>>(
+        grad, pixels, pixel_stride, var_of_fold, table_grad, folds, states, units, batch, fold_offset);
+  }
+  return check_launch("xe_categorical_scatter_add");
+}
+
 xe_status xe_logspace_reduce(const float* x, int64_t sb, int64_t sr, int64_t sk, int64_t batch, int64_t rows, int64_t k,
                              int32_t shift_mode, float* y, void* stream) {
   if (!x || !y) return fail(XE_ERR_INVALID_ARGUMENT, "xe_logspace_reduce: null pointer");
@@ -987,7 +1068,16 @@ xe_status xe_unary(const float* x, float* y, int64_t n, int32_t op, void* stream
 
 xe_status xe_logspace_tucker(const float* l, const float* r, const float* w, float* y, int64_t batch, int64_t folds,
                              int64_t i_dim, int64_t j_dim, int64_t o_dim, int32_t shift_mode, void* stream) {
-  return xe_tucker_impl(l, r, w, y, batch, folds, i_dim, j_dim, o_dim, shift_mode, as_stream(stream));
+  return xe_tucker_impl(l, folds * i_dim, i_dim, r, folds * j_dim, j_dim, w, y, folds * o_dim, o_dim, batch, folds, i_dim,
+                        j_dim, o_dim, shift_mode, as_stream(stream));
+}
+
+xe_status xe_logspace_tucker_strided(const float* l, int64_t l_sb, int64_t l_sf, const float* r, int64_t r_sb,
+                                     int64_t r_sf, const float* w, float* y, int64_t y_sb, int64_t y_sf, int64_t batch,
+                                     int64_t folds, int64_t i_dim, int64_t j_dim, int64_t o_dim, int32_t shift_mode,
+                                     void* stream) {
+  return xe_tucker_impl(l, l_sb, l_sf, r, r_sb, r_sf, w, y, y_sb, y_sf, batch, folds, i_dim, j_dim, o_dim, shift_mode,
+                        as_stream(stream));
 }
 
 }  // extern "C"
@@ -1013,11 +1103,20 @@ xe_status launch_tucker(const Params& p, cudaStream_t s) {
 #undef XE_TUCKER_BN
 }
 
-static xe_status xe_tucker_impl(const float* l, const float* r, const float* w, float* y, int64_t batch, int64_t folds,
-                                int64_t i_dim, int64_t j_dim, int64_t o_dim, int32_t shift_mode, cudaStream_t stream) {
+static xe_status xe_tucker_impl(const float* l, int64_t l_sb, int64_t l_sf, const float* r, int64_t r_sb,
+                                int64_t r_sf, const float* w, float* y, int64_t y_sb, int64_t y_sf, int64_t batch,
+                                int64_t folds, int64_t i_dim, int64_t j_dim, int64_t o_dim, int32_t shift_mode,
+                                cudaStream_t stream) {
   if (!l || !r || !w || !y) return fail(XE_ERR_INVALID_ARGUMENT, "xe_logspace_tucker: null pointer");
   if (batch < 0 || folds < 0 || i_dim <= 0 || j_dim <= 0 || o_dim < 0)
     return fail(XE_ERR_INVALID_ARGUMENT, "xe_logspace_tucker: invalid extents");
+  // l and r rows are loaded as 16-byte vectors or through tensor maps: each starts on 16 bytes
+  for (const int64_t stride : {l_sb, l_sf, r_sb, r_sf})
+    if (stride < 0 || stride % 4 != 0)
+      return fail(XE_ERR_INVALID_ARGUMENT, "xe_logspace_tucker: l and r row strides must be non-negative multiples of 4");
+  if (y_sb < 0 || y_sf < 0) return fail(XE_ERR_INVALID_ARGUMENT, "xe_logspace_tucker: negative output strides");
+  // output rows of 16-byte multiples: the Tucker kernel's tensor-map stores and vector stores
+  const bool y_rows16 = y_sb % 4 == 0 && y_sf % 4 == 0;
   if (shift_mode != XE_SHIFT_MAX && shift_mode != XE_SHIFT_MIN)
     return fail(XE_ERR_INVALID_ARGUMENT, "xe_logspace_tucker: unknown shift mode %d", shift_mode);
   if ((j_dim != 32 && j_dim != 64) || i_dim % 8 != 0)
@@ -1025,25 +1124,29 @@ static xe_status xe_tucker_impl(const float* l, const float* r, const float* w, 
                 (long long)i_dim, (long long)j_dim);
   if (batch > INT32_MAX || folds > INT32_MAX || i_dim * j_dim > INT32_MAX || o_dim > INT32_MAX)
     return fail(XE_ERR_NOT_SUPPORTED, "xe_logspace_tucker: extents above 2^31-1 are not supported");
-  if (!aligned16(l) || !aligned16(r) || !aligned16(w) || !aligned16(y))
+  if (!aligned16(l) || !aligned16(r) || !aligned16(w))
     return fail(XE_ERR_INVALID_ARGUMENT, "xe_logspace_tucker: operands must be 16-byte aligned");
   if (batch == 0 || folds == 0 || o_dim == 0) return XE_OK;
   // I = J = O = 32: the two-stage kernel (tucker_layer.cuh); XE_GEMM_NO_CP_LAYER=1 selects the general one
-  if (i_dim == xe::tk::kDim && j_dim == xe::tk::kDim && o_dim == xe::tk::kDim && env_int("XE_GEMM_NO_CP_LAYER", 0) == 0) {
+  if (i_dim == xe::tk::kDim && j_dim == xe::tk::kDim && o_dim == xe::tk::kDim && y_rows16 && aligned16(y) &&
+      env_int("XE_GEMM_NO_CP_LAYER", 0) == 0) {
     PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
     CUtensorMap ml{}, mr{}, mw{}, my{};
     bool maps = encode != nullptr;
-    auto rows_map = [&](CUtensorMap* map, const float* base, int box_rows) {
-      // (batch, folds, 32) contiguous: boxes of 32 x 1 fold x box_rows rows, 128-byte swizzle
+    auto rows_map = [&](CUtensorMap* map, const float* base, int box_rows, int64_t s_b, int64_t s_f) {
+      // (batch, folds, 32) with 32 contiguous units per row: boxes of 32 x 1 fold x box_rows rows,
+      // 128-byte swizzle
       cuuint64_t dims[3] = {32, (cuuint64_t)folds, (cuuint64_t)batch};
-      cuuint64_t strides[2] = {32 * 4, (cuuint64_t)(folds * 32 * 4)};
+      cuuint64_t strides[2] = {(cuuint64_t)(s_f * 4), (cuuint64_t)(s_b * 4)};
       cuuint32_t box[3] = {32, 1, (cuuint32_t)box_rows};
       cuuint32_t estr[3] = {1, 1, 1};
       return encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box, estr,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
     };
-    if (maps) maps = rows_map(&ml, l, xe::gemm::kBM) && rows_map(&mr, r, xe::gemm::kBM) && rows_map(&my, y, 32);
+    if (maps)
+      maps = rows_map(&ml, l, xe::gemm::kBM, l_sb, l_sf) && rows_map(&mr, r, xe::gemm::kBM, r_sb, r_sf) &&
+             rows_map(&my, y, 32, y_sb, y_sf);
     if (maps) {
       // w (folds, 32 o, 32 i, 32 j): per fold 1024 (o,i) rows of 32 j; chunks of 64 rows
       cuuint64_t dims[3] = {32, 1024, (cuuint64_t)folds};
@@ -1077,18 +1180,22 @@ static xe_status xe_tucker_impl(const float* l, const float* r, const float* w, 
   p.b_sk = 1;
   p.b_sn = i_dim * j_dim;
   p.c = y;
-  p.c_sb = o_dim;
-  p.c_sm = folds * o_dim;
+  p.c_sb = y_sf;
+  p.c_sm = y_sb;
   p.c_sn = 1;
   p.batch = (int)folds;
   p.M = (int)batch;
   p.N = (int)o_dim;
   p.K = (int)(i_dim * j_dim);
-  p.c_vec = (o_dim % 4 == 0) ? 1 : 0;
+  p.c_vec = (o_dim % 4 == 0 && y_rows16 && aligned16(y)) ? 1 : 0;
   p.tl = l;
   p.tr = r;
   p.t_folds = (int)folds;
   p.t_i = (int)i_dim;
+  p.t_l_sb = l_sb;
+  p.t_l_sf = l_sf;
+  p.t_r_sb = r_sb;
+  p.t_r_sf = r_sf;
   p.shift_min = shift_mode == XE_SHIFT_MIN;
   return j_dim == 32 ? launch_tucker<32>(p, stream) : launch_tucker<64>(p, stream);
 }

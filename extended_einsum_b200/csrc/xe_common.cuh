@@ -37,7 +37,9 @@ enum WaitSite : int {
   kSiteDrainShift = 14,
   kSiteProducer = 15,
   kNumSites = 16,
-  kSiteSoftmax = 16,  // the prefetching row softmax (not among the wait-time counters)
+  kSiteSoftmax = 16,      // the prefetching row softmax (not among the wait-time counters)
+  kSiteWaitProbe = 17,    // xe_wait_probe, the test kernel whose barrier may never complete
+  kSiteDrainCopies = 18,  // wind-down: bulk copies still landing in shared memory
 };
 
 #ifdef XE_PROFILE
@@ -66,6 +68,12 @@ __device__ long long g_trace[kTraceTiles * kTraceEvents];
 
 // About two seconds: far above any legitimate wait in these kernels.
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;
+
+// The limit of the ordinary waits, per device (xe_set_wait_timeout_ns; kWaitTimeoutNs by default).
+// Waits that guard the release of resources (tensor-core work or bulk copies still in flight
+// when a CTA winds down) keep the fixed kWaitTimeoutNs, so that a short limit never frees TMEM
+// or shared memory under an operation that has not finished.
+__constant__ uint64_t g_wait_timeout_ns = kWaitTimeoutNs;
 
 __device__ __forceinline__ void record_timeout(int site) {
   atomicCAS(&g_device_status, 0, (XE_ERR_DEVICE_TIMEOUT << 16) | site);
@@ -134,6 +142,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int si
 #else
   if (mbar_try_wait(addr, parity)) return true;
 #endif
+  const uint64_t limit = honor_abort ? g_wait_timeout_ns : uint64_t(kWaitTimeoutNs);
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(addr, parity)) {
@@ -144,7 +153,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int si
     }
     if ((i & 255u) == 0) {
       if (honor_abort && *abort) return false;
-      if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+      if (globaltimer_ns() - t0 > limit) {
         *abort = 1;
         record_timeout(site);
         return false;
@@ -153,12 +162,39 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int si
   }
 }
 
+// The ring barriers a producer thread armed last (arrive.expect_tx + bulk copies), with the
+// phase parity of that arming.  A CTA that winds down after an abort drains them before it
+// exits: a bulk copy must not land in shared memory that the CTA no longer owns.  One bit per
+// barrier of a ring of at most 32.  Kept in shared memory beside the abort flag (cleared with
+// it), so that no role carries it in registers.
+struct ArmedCopies {
+  uint32_t armed, parity;
+
+  __device__ __forceinline__ void note(int slot, uint32_t phase) {
+    const uint32_t bit = 1u << slot;
+    armed |= bit;
+    parity = (parity & ~bit) | ((phase & 1u) << slot);
+  }
+
+  // Waits (fixed limit) until the last armed phase of each noted barrier has completed.
+  __device__ __forceinline__ void drain(uint64_t* bars, volatile int* abort) const {
+    for (uint32_t m = armed; m != 0u; m &= m - 1u) {
+      const int slot = __ffs(m) - 1;
+      mbar_wait(&bars[slot], (parity >> slot) & 1u, kSiteDrainCopies, abort, /*honor_abort=*/false);
+    }
+  }
+};
+
 // A wait by every lane of a warp whose next steps are warp-collective
 // (tcgen05.ld / tcgen05.st are .sync.aligned): the lanes leave the spin loop at
 // different times, so the warp is reconverged here, and a timeout seen by any
-// lane is seen by all of them.
-__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int site, volatile int* abort) {
-  const bool ok = mbar_wait(bar, parity, site, abort);
+// lane is seen by all of them.  `pre_ok` carries the outcome of an earlier
+// per-lane wait of the same step into this vote (a lane whose earlier wait ran
+// out does not wait again: it set the abort flag, which ends the others' waits),
+// so that a step takes one vote however many barriers it waits on.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int site, volatile int* abort,
+                                               bool pre_ok = true) {
+  const bool ok = pre_ok && mbar_wait(bar, parity, site, abort);
   return __all_sync(0xffffffffu, ok);
 }
 

@@ -255,8 +255,13 @@ def log_add(a: torch.Tensor, b: torch.Tensor, *, negate_b: bool = False) -> torc
 
 
 def log_add_exp(a: torch.Tensor, b: torch.Tensor, *, subtract: bool = False, shift: str = "max") -> torch.Tensor:
-    """y = log(exp(a - m) +/- exp(b - m)) + m with the scalar m = extreme of a and b."""
-    _no_backward("log_add_exp", a, b)
+    """y = log(exp(a - m) +/- exp(b - m)) + m with the scalar m = extreme of a and b.
+
+    Differentiable (autograd.LogAddExp, m detached) when an operand requires grad."""
+    if _needs_grad(a, b):
+        from .autograd import LogAddExp
+
+        return LogAddExp.apply(a, b, subtract, shift)
     device = _check_tensors("log_add_exp", a, b)
     a = a.contiguous()
     b = b.contiguous()
@@ -308,8 +313,13 @@ def log(x: torch.Tensor) -> torch.Tensor:
 def categorical_gather(
     log_table: torch.Tensor, pixels: torch.Tensor, var_of_fold: torch.Tensor | None = None
 ) -> torch.Tensor:
-    """y[f,b,:] = log_table[f, pixels[b, var_of_fold[f]], :] for uint8 pixels (batch, variables)."""
-    _no_backward("categorical_gather", log_table)
+    """y[f,b,:] = log_table[f, pixels[b, var_of_fold[f]], :] for uint8 pixels (batch, variables).
+
+    Differentiable in the table (autograd.CategoricalGather: a scatter-add)."""
+    if _needs_grad(log_table):
+        from .autograd import CategoricalGather
+
+        return CategoricalGather.apply(log_table, pixels, var_of_fold)
     device = _check_tensors("categorical_gather", log_table)
     if pixels.device != device or pixels.dtype != torch.uint8 or pixels.dim() != 2:
         raise ValueError("categorical_gather: pixels must be a (batch, variables) uint8 tensor on the table's device")
@@ -331,6 +341,44 @@ def categorical_gather(
     )
     _lib.check(status, "xe_categorical_gather")
     return y
+
+
+def categorical_scatter_add(
+    grad: torch.Tensor,
+    pixels: torch.Tensor,
+    var_of_fold: torch.Tensor | None,
+    table_grad: torch.Tensor,
+    *,
+    fold_offset: int = 0,
+) -> torch.Tensor:
+    """table_grad[f + off, pixels[b, var[f + off]], :] += grad[f, b, :] (xe_categorical_scatter_add), in place.
+
+    The backward of categorical_gather: ``grad`` is (folds, batch, units), ``table_grad`` a
+    contiguous (>= off + folds, states, units) accumulator."""
+    device = _check_tensors("categorical_scatter_add", grad, table_grad)
+    if pixels.device != device or pixels.dtype != torch.uint8 or pixels.dim() != 2:
+        raise ValueError("categorical_scatter_add: pixels must be a (batch, variables) uint8 tensor on the table's device")
+    if pixels.stride(1) != 1:
+        pixels = pixels.contiguous()
+    if grad.dim() != 3 or table_grad.dim() != 3 or not table_grad.is_contiguous():
+        raise ValueError("categorical_scatter_add: expected a (folds, batch, units) gradient and a contiguous table")
+    folds, batch, units = grad.shape
+    table_folds, states, table_units = table_grad.shape
+    if table_units != units or table_folds < fold_offset + folds or pixels.shape[0] != batch:
+        raise ValueError("categorical_scatter_add: incompatible shapes")
+    if var_of_fold is not None:
+        if var_of_fold.dtype != torch.int32 or var_of_fold.device != device or var_of_fold.numel() < fold_offset + folds:
+            raise ValueError("categorical_scatter_add: var_of_fold must be int32 with an entry per table fold")
+        var_of_fold = var_of_fold.contiguous()
+    elif pixels.shape[1] < fold_offset + folds:
+        raise ValueError("categorical_scatter_add: fewer pixel variables than table folds")
+    grad = grad.contiguous()
+    status = _lib.load().xe_categorical_scatter_add(
+        grad.data_ptr(), pixels.data_ptr(), pixels.stride(0), _ptr(var_of_fold), table_grad.data_ptr(),
+        folds, states, units, batch, fold_offset, _stream(device),
+    )
+    _lib.check(status, "xe_categorical_scatter_add")
+    return table_grad
 
 
 def logspace_gemm_gather(
@@ -375,7 +423,10 @@ def logspace_gemm_gather_pair(
 
 
 def _gather_gemm(name, log_table, pixels, var_of_fold, b, fold_offset, b_linear, shift):
-    _no_backward(name, log_table, b)
+    if _needs_grad(log_table, b):
+        from .autograd import LogspaceGemmGather
+
+        return LogspaceGemmGather.apply(log_table, pixels, var_of_fold, b, b_linear, shift, fold_offset > 0)
     device = _check_tensors(name, log_table, b)
     if pixels.device != device or pixels.dtype != torch.uint8 or pixels.dim() != 2:
         raise ValueError(f"{name}: pixels must be a (batch, variables) uint8 tensor on the table's device")
@@ -415,11 +466,27 @@ def _gather_gemm(name, log_table, pixels, var_of_fold, b, fold_offset, b_linear,
 
 
 def logspace_tucker(
-    left: torch.Tensor, right: torch.Tensor, weights: torch.Tensor, *, shift: str = "max"
+    left: torch.Tensor,
+    right: torch.Tensor,
+    weights: torch.Tensor,
+    *,
+    shift: str = "max",
+    out: torch.Tensor | None = None,
 ) -> torch.Tensor:
-    """y[b,f,o] = log(sum_ij exp(l-sl) exp(r-sr) w[f,o,i,j]) + sl + sr (xe_logspace_tucker)."""
+    """y[b,f,o] = log(sum_ij exp(l-sl) exp(r-sr) w[f,o,i,j]) + sl + sr (xe_logspace_tucker_strided).
+
+    ``left`` (B, F, I) and ``right`` (B, F, J) may be any views whose unit axis is contiguous and
+    whose batch and fold strides are multiples of 4 elements (the fold-major (F, B, I) tensors of a
+    folded circuit, permuted, qualify); other layouts are copied.  ``out`` (B, F, O) may be any
+    view with contiguous units.
+    ``weights`` is (F, O, I, J).  Differentiable (autograd.LogspaceTucker, shifts detached) when an
+    operand requires grad."""
+    if out is None and _needs_grad(left, right, weights):
+        from .autograd import LogspaceTucker
+
+        return LogspaceTucker.apply(left, right, weights, shift)
     _no_backward("logspace_tucker", left, right, weights)
-    device = _check_tensors("logspace_tucker", left, right, weights)
+    device = _check_tensors("logspace_tucker", left, right, weights, *([out] if out is not None else []))
     if left.dim() != 3 or right.dim() != 3 or weights.dim() != 4:
         raise ValueError("logspace_tucker: expected (B,F,I), (B,F,J) and (F,O,I,J) tensors")
     batch, folds, i_dim = left.shape
@@ -427,14 +494,23 @@ def logspace_tucker(
     o_dim = weights.shape[1]
     if right.shape[:2] != (batch, folds) or weights.shape != (folds, o_dim, i_dim, j_dim):
         raise ValueError("logspace_tucker: incompatible shapes")
-    left, right, weights = left.contiguous(), right.contiguous(), weights.contiguous()
-    y = torch.empty((batch, folds, o_dim), device=device, dtype=torch.float32)
-    status = _lib.load().xe_logspace_tucker(
-        left.data_ptr(), right.data_ptr(), weights.data_ptr(), y.data_ptr(), batch, folds, i_dim, j_dim, o_dim,
+
+    def rows(t: torch.Tensor) -> torch.Tensor:
+        ok = t.stride(2) == 1 and t.stride(0) % 4 == 0 and t.stride(1) % 4 == 0 and t.data_ptr() % 16 == 0
+        return t if ok else t.contiguous()
+
+    left, right, weights = rows(left), rows(right), weights.contiguous()
+    if out is None:
+        out = torch.empty((batch, folds, o_dim), device=device, dtype=torch.float32)
+    elif out.shape != (batch, folds, o_dim) or out.stride(2) != 1 or min(out.stride()) < 0:
+        raise ValueError("logspace_tucker: out must be a (B, F, O) view with contiguous units")
+    status = _lib.load().xe_logspace_tucker_strided(
+        left.data_ptr(), left.stride(0), left.stride(1), right.data_ptr(), right.stride(0), right.stride(1),
+        weights.data_ptr(), out.data_ptr(), out.stride(0), out.stride(1), batch, folds, i_dim, j_dim, o_dim,
         _shift(shift), _stream(device),
     )
     _lib.check(status, "xe_logspace_tucker")
-    return y
+    return out
 
 
 # ---------------------------------------------------------------------------
@@ -560,3 +636,12 @@ def elementwise(op: str, a: torch.Tensor, b: torch.Tensor, c: torch.Tensor | Non
 def device_status(clear: bool = True) -> int:
     """The device-side status word (non-zero after a bounded wait ran out)."""
     return int(_lib.load().xe_device_status(int(clear)))
+
+
+def set_wait_timeout_ns(ns: int) -> None:
+    """Limit of the kernels' bounded waits on the current device, in ns (0 restores the 2 s default).
+
+    Waits for the work already queued first, so that no running kernel sees the change."""
+    if torch.cuda.is_available():
+        torch.cuda.synchronize()
+    _lib.check(_lib.load().xe_set_wait_timeout_ns(int(ns)), "xe_set_wait_timeout_ns")

@@ -51,6 +51,23 @@ const char* xe_last_error_string(void);
  * Synchronises the current device. */
 int xe_device_status(int clear);
 
+/* Limit of the kernels' ordinary bounded waits on the current device, in
+ * nanoseconds (2 s by default; 0 restores the default).  Waits that guard the
+ * release of resources when a CTA winds down keep the 2 s limit.  The value
+ * lives in device memory and applies to every later launch on the device.
+ * No counterpart in the reference, whose executor has no device waits: this
+ * is the knob a caller (and the failure tests) uses to bound a stuck launch.
+ * XE_ERR_INVALID_ARGUMENT for a limit below 1 us or above 60 s. */
+xe_status xe_set_wait_timeout_ns(uint64_t ns);
+
+/* Test kernel of the bounded waits, stream-ordered: one CTA whose first warp
+ * waits on a barrier that expects one arrival.  complete != 0: a second warp
+ * arrives after a short bounded delay and the wait ends normally.
+ * complete == 0: nothing arrives, the wait runs out after the limit above, and
+ * xe_device_status() then reports (XE_ERR_DEVICE_TIMEOUT << 16) | 17.
+ * No counterpart in the reference (test infrastructure for the device status). */
+xe_status xe_wait_probe(int complete, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Log-space batched contraction (the GEMM-shaped stable einsum).
  *
@@ -189,6 +206,18 @@ xe_status xe_categorical_gather(const float* table, const uint8_t* pixels, int64
                                 const int32_t* var_of_fold, float* y, int64_t folds, int64_t states,
                                 int64_t units, int64_t batch, void* stream);
 
+/* Backward of the categorical gather (and of the gathers fused into the first
+ * two circuit layers): table_grad[f + fold_offset, pixels[b, v], :] += grad[f, b, :]
+ * with v = var_of_fold[f + fold_offset] (or f + fold_offset when null), for
+ * f < folds.  grad is (folds, batch, units) contiguous; table_grad holds at least
+ * fold_offset + folds folds of (states, units) and is accumulated into.  The
+ * reference differentiates the demo's gather probabilities[pixel_range, batch.T]
+ * (demo/cirkit.py:525-527) through torch indexing, whose backward is this
+ * scatter-add.  Bad indices are clamped and reported as in xe_categorical_gather. */
+xe_status xe_categorical_scatter_add(const float* grad, const uint8_t* pixels, int64_t pixel_stride,
+                                     const int32_t* var_of_fold, float* table_grad, int64_t folds, int64_t states,
+                                     int64_t units, int64_t batch, int64_t fold_offset, void* stream);
+
 /* The first sum layer of a circuit over categorical input units, with the
  * gather fused into the contraction (replaces xe_categorical_gather followed
  * by xe_logspace_gemm on its output; demo/cirkit.py:525-527 feeding the
@@ -241,6 +270,18 @@ xe_status xe_logspace_gemm_gather_pair(const float* table, int64_t t_sf, int64_t
 xe_status xe_logspace_tucker(const float* l, const float* r, const float* w, float* y, int64_t batch,
                              int64_t folds, int64_t i_dim, int64_t j_dim, int64_t o_dim, int32_t shift_mode,
                              void* stream);
+
+/* The same layer over strided rows: l[b, f, :], r[b, f, :] and y[b, f, :] start at
+ * b * x_sb + f * x_sf (element strides; for l and r non-negative multiples of 4) with
+ * the units contiguous; w is (F, O, I, J) contiguous.  The folded Tucker circuits of the
+ * reference (FoldSameShapedOperations + OptimizeContractionPaths,
+ * preprocess.py:1095-1106, 1310-1393) carry their folds first:
+ * 'acde,abd,abe->abc' over (F, B, I) slices of the previous layer's (F, B, O)
+ * output, which these strides address without a copy. */
+xe_status xe_logspace_tucker_strided(const float* l, int64_t l_sb, int64_t l_sf, const float* r, int64_t r_sb,
+                                     int64_t r_sf, const float* w, float* y, int64_t y_sb, int64_t y_sf, int64_t batch,
+                                     int64_t folds, int64_t i_dim, int64_t j_dim, int64_t o_dim, int32_t shift_mode,
+                                     void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* Scaled stability modes (scaled_sum / scaled_max / scaled_min,

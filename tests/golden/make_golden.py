@@ -36,7 +36,8 @@ import torch
 OUT_DIR = Path(__file__).resolve().parent
 ALL_MODES = ("logspace_max", "logspace_min", "scaled_sum", "scaled_max", "scaled_min")
 # programs whose gradients (of sum(out * w), fixed w) are recorded, logspace_max, fp64
-GRAD_PROGRAMS = ("matmul_logu", "batched_n64", "cp_layer", "softmax_rows")
+GRAD_PROGRAMS = ("matmul_logu", "batched_n64", "cp_layer", "softmax_rows", "tucker", "tucker_two_levels", "mixing_layer",
+                 "agreement_add", "circuit_4x4")
 
 
 def main(reference_root: str) -> None:

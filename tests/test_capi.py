@@ -80,3 +80,10 @@ def test_status_maps_to_reference_exceptions():
     with pytest.raises(RuntimeError):
         _lib.check(_lib.XE_ERR_DEVICE_TIMEOUT, "x")
     _lib.check(_lib.XE_OK, "x")
+
+
+def test_wait_limit_range_is_checked_before_the_device():
+    lib = _lib.load()
+    assert lib.xe_set_wait_timeout_ns(999) == _lib.XE_ERR_INVALID_ARGUMENT
+    assert "outside" in _lib.last_error()
+    assert lib.xe_set_wait_timeout_ns(60_000_000_001) == _lib.XE_ERR_INVALID_ARGUMENT

@@ -97,13 +97,98 @@ def test_logspace_reduce_backward():
 
 
 def test_no_backward_is_loud():
-    a = torch.randn(2, 4, 8, device="cuda", requires_grad=True)
-    w = torch.rand(2, 8, 8, device="cuda")
+    """The scaled modes' glue has no backward on this path."""
+    a = torch.rand(2, 4, 8, device="cuda", requires_grad=True)
     with pytest.raises(NotImplementedError):
-        ops.logspace_tucker(a, a, w.reshape(2, 1, 8, 8).expand(2, 1, 8, 8).contiguous())
+        ops.scaled_gemm(a, a.transpose(1, 2))
 
 
-@pytest.mark.parametrize("name", ["matmul_logu", "batched_n64", "cp_layer", "softmax_rows"])
+@pytest.mark.parametrize("shape", [(200, 3, 32, 32, 32), (50, 2, 8, 32, 5)], ids=["tucker-kernel", "general-kernel"])
+@pytest.mark.parametrize("shift", ["max", "min"])
+def test_logspace_tucker_backward(shape, shift):
+    """y = log sum_ij exp(l_i + r_j) w_oij, with the shifts detached (translate.py:727-740)."""
+    b, f, i, j, o = shape
+    g = torch.Generator().manual_seed(9)
+    left = torch.randn(b, f, i, generator=g) - 3.0
+    right = torch.randn(b, f, j, generator=g) - 3.0
+    w = torch.softmax(torch.randn(f, o, i * j, generator=g), dim=2).reshape(f, o, i, j)
+    up = torch.randn(b, f, o, generator=g)
+    ld, rd, wd = _leaf(left, "cuda"), _leaf(right, "cuda"), _leaf(w, "cuda")
+    (ops.logspace_tucker(ld, rd, wd, shift=shift) * up.cuda()).sum().backward()
+    lr, rr, wr = _leaf(left.double()), _leaf(right.double()), _leaf(w.double())
+    yr = torch.logsumexp((lr[:, :, None, :, None] + rr[:, :, None, None, :] + torch.log(wr)[None]).flatten(3), dim=3)
+    (yr * up.double()).sum().backward()
+    _close(ld.grad, lr.grad)
+    _close(rd.grad, rr.grad)
+    _close(wd.grad, wr.grad)
+
+
+@pytest.mark.parametrize("subtract", [False, True])
+@pytest.mark.parametrize("shift", ["max", "min"])
+def test_log_add_exp_backward(subtract, shift):
+    """y = log(exp(a) +/- exp(b)) with a scalar shift m detached (translate.py:647-664, 774-789)."""
+    g = torch.Generator().manual_seed(12)
+    b = torch.randn(5, 8, generator=g)
+    a = torch.randn(6, 1, 8, generator=g)
+    if subtract:  # every broadcast pair with a > b, so that the difference is positive
+        a = a.abs() + b.max() + 0.5
+    up = torch.randn(6, 5, 8, generator=g)
+    ad, bd = _leaf(a, "cuda"), _leaf(b, "cuda")
+    (ops.log_add_exp(ad, bd, subtract=subtract, shift=shift) * up.cuda()).sum().backward()
+    ar, br = _leaf(a.double()), _leaf(b.double())
+    yr = torch.log(torch.exp(ar) - torch.exp(br)) if subtract else torch.logaddexp(ar, br)
+    (yr * up.double()).sum().backward()
+    _close(ad.grad, ar.grad)
+    _close(bd.grad, br.grad)
+
+
+def _gather_inputs(folds, states, units, batch, variables, seed):
+    g = torch.Generator().manual_seed(seed)
+    table = torch.log_softmax(torch.randn(folds, states, units, generator=g), dim=1)
+    pixels = torch.randint(states, (batch, variables), generator=g, dtype=torch.uint8)
+    var = torch.randperm(variables, generator=g)[:folds].to(torch.int32)
+    return table, pixels, var
+
+
+def _gather_ref(table, pixels, var):
+    return table[torch.arange(table.shape[0])[:, None], pixels[:, var.long()].T.long()]
+
+
+def test_categorical_gather_backward():
+    table, pixels, var = _gather_inputs(6, 20, 16, 50, 8, 13)
+    up = torch.randn(6, 50, 16)
+    td = _leaf(table, "cuda")
+    (ops.categorical_gather(td, pixels.cuda(), var.cuda()) * up.cuda()).sum().backward()
+    tr = _leaf(table.double())
+    (_gather_ref(tr, pixels, var) * up.double()).sum().backward()
+    _close(td.grad, tr.grad)
+
+
+@pytest.mark.parametrize("pair", [False, True], ids=["gather", "state-table-pair"])
+@pytest.mark.parametrize("batch", [300, 1030])
+def test_fused_gather_layer_backward(pair, batch):
+    """The first circuit layers with the gather fused, against the gather, the Hadamard sum and
+    the log-space contraction written out in fp64."""
+    folds, states, units = 4, 32, 64
+    table, pixels, var = _gather_inputs(2 * folds if pair else folds, states, units, batch, 16, 21 + pair)
+    g = torch.Generator().manual_seed(3)
+    w = torch.softmax(torch.randn(folds, units, units, generator=g), dim=2)  # (F, O, K)
+    up = torch.randn(folds, batch, units, generator=g)
+    td, wd = _leaf(table, "cuda"), _leaf(w, "cuda")
+    fused = ops.logspace_gemm_gather_pair if pair else ops.logspace_gemm_gather
+    (fused(td, pixels.cuda(), var.cuda(), wd.permute(0, 2, 1), b_linear=True) * up.cuda()).sum().backward()
+    tr, wr = _leaf(table.double()), _leaf(w.double())
+    rows = _gather_ref(tr, pixels, var)
+    a = rows[:folds] + rows[folds:] if pair else rows
+    yr = torch.logsumexp(a[:, :, None, :] + torch.log(wr)[:, None, :, :], dim=3)
+    (yr * up.double()).sum().backward()
+    _close(td.grad, tr.grad, rtol=5e-5, atol=2e-6)
+    _close(wd.grad, wr.grad, rtol=5e-5, atol=2e-6)
+    assert ops.device_status() == 0
+
+
+@pytest.mark.parametrize("name", ["matmul_logu", "batched_n64", "cp_layer", "softmax_rows", "tucker", "tucker_two_levels",
+                                  "mixing_layer", "agreement_add", "circuit_4x4"])
 def test_materialize_gradients_match_reference(golden, golden_programs, name):
     spec = golden_programs[name]
     if f"{name}/logspace_max/grad0" not in golden:
@@ -137,7 +222,11 @@ def _torch_circuit_ll(cat_logits, pixels, var_of_fold, level_logits, root_logits
     return torch.logsumexp(h[:, None, :] + logw_root[None, :, :], dim=2)  # (B, 1)
 
 
-def test_circuit_gradients_of_the_sum_layers(golden, golden_programs):
+@pytest.mark.parametrize("batch_from", ["golden", "per-sample"])
+def test_circuit_gradients(golden, golden_programs, batch_from):
+    """Every parameter of the circuit, the categorical logits included, through the fused first
+    layers (state table + gathered pairs for the golden batch; the fused per-sample gather for a
+    batch below half the states)."""
     from extended_einsum_b200.circuit import CircuitForward, QuadTreeCircuit
 
     name = "circuit_4x4"
@@ -148,15 +237,21 @@ def test_circuit_gradients_of_the_sum_layers(golden, golden_programs):
     lv = [torch.from_numpy(golden[f"{name}/in{1 + l}"]) for l in range(levels)]
     root = torch.from_numpy(golden[f"{name}/in{1 + levels}"])
     pixels = torch.from_numpy(golden[f"{name}/pixels"])
+    if batch_from == "per-sample":
+        pixels = pixels[:5]
     var = torch.from_numpy(golden[f"{name}/var_of_fold"])
+    circuit = QuadTreeCircuit(c["height"], c["width"], c["units"], c["states"])
+    assert circuit.uses_state_table(pixels.shape[0]) == (batch_from == "golden")
+    cat_d = _leaf(cat, "cuda")
     lv_d = [_leaf(t, "cuda") for t in lv]
     root_d = _leaf(root, "cuda")
-    circuit = QuadTreeCircuit(c["height"], c["width"], c["units"], c["states"])
-    forward = CircuitForward(circuit, {"categorical": cat.cuda(), "levels": lv_d, "root": root_d, "var_of_fold": var.cuda()})
+    forward = CircuitForward(circuit, {"categorical": cat_d, "levels": lv_d, "root": root_d, "var_of_fold": var.cuda()})
     forward(pixels.cuda()).sum().backward()
+    cat_r = _leaf(cat.double())
     lv_r = [_leaf(t.double()) for t in lv]
     root_r = _leaf(root.double())
-    _torch_circuit_ll(cat.double(), pixels, var.long(), lv_r, root_r).sum().backward()
+    _torch_circuit_ll(cat_r, pixels, var.long(), lv_r, root_r).sum().backward()
+    _close(cat_d.grad, cat_r.grad, rtol=1e-4, atol=1e-5)
     for ours, ref in zip(lv_d, lv_r):
         _close(ours.grad, ref.grad, rtol=1e-4, atol=1e-5)
     _close(root_d.grad, root_r.grad, rtol=1e-4, atol=1e-5)

@@ -128,19 +128,22 @@ def test_matmul_materialize_is_one_kernel_call(enabled):
     assert len(expr._backend_program.backend_calls) == 1
 
 
-@pytest.mark.parametrize("shape", [(4, 4, 8, 40), (8, 8, 16, 300), (8, 8, 64, 1024)])
+@pytest.mark.parametrize("layer,shape", [("cp", (4, 4, 8, 40)), ("cp", (8, 8, 16, 300)), ("cp", (8, 8, 64, 1024)),
+                                         ("tucker", (4, 4, 32, 40)), ("tucker", (8, 8, 32, 300))])
 @pytest.mark.parametrize("mode", ["logspace_max", "logspace_min"])
-def test_reference_folded_circuit_through_lower(reference_xe, shape, mode):
+def test_reference_folded_circuit_through_lower(reference_xe, layer, shape, mode):
     """The reference's folded circuit program (its own folding passes) lowered with the Hadamard
-    products fused into the sum layers, against the reference's torch executor of that program."""
-    from extended_einsum_b200.contraction import logspace_einsum_hadamard
+    products fused into the sum layers (CP) or the fused Tucker layers on the Tucker kernel in their
+    fold-major form, against the reference's torch executor of that program."""
+    from extended_einsum_b200.contraction import logspace_einsum, logspace_einsum_hadamard
 
     xe = reference_xe
     h, w, units, batch = shape
-    program, data_input = demo_circuit_program(xe, h, w, units, batch, stability_mode=mode)
+    program, data_input = demo_circuit_program(xe, h, w, units, batch, stability_mode=mode, layer=layer)
     inputs = demo_circuit_inputs(program, data_input, torch.Generator().manual_seed(h * w + units))
     lowered = xb.lower(program)
-    fused = [c for c in lowered.backend_calls if getattr(getattr(c, "fn", None), "func", None) is logspace_einsum_hadamard]
+    fused_kind = logspace_einsum_hadamard if layer == "cp" else logspace_einsum
+    fused = [c for c in lowered.backend_calls if getattr(getattr(c, "fn", None), "func", None) is fused_kind]
     assert len(fused) == int(np.log2(h * w))
     ours = xb.run_program(lowered, [t.to(DEVICE) for t in inputs]).cpu().numpy()
     assert ours.shape == (batch, 1)
@@ -171,3 +174,24 @@ def test_reference_circuit_materialize_unfolded(enabled):
     out = expr.materialize(stability_mode="logspace_max").backend_array
     program, arguments = xe.extract_program(expr, "logspace_max")
     circuit_close(xe, program, [a.backend_array for a in arguments], out.cpu().numpy())
+
+
+@pytest.mark.parametrize("layer,units", [("cp", 16), ("tucker", 32)])
+def test_reference_folded_circuit_gradients_through_lower(reference_xe, layer, units):
+    """Gradients of the summed log-likelihood with respect to every input of the reference's folded
+    circuit program (data and packed parameters) through the lowered program, against the
+    reference's torch executor of the same program in fp64 (shifts detached as it detaches them)."""
+    from extended_einsum.backend_translation.runtime import run_program as reference_run
+    from extended_einsum.backend_translation.translate import translate_to_backend_program
+    from extended_einsum.backends.torch import TorchBackendFunctions
+
+    program, data_input = demo_circuit_program(reference_xe, 4, 4, units, 50, layer=layer)
+    inputs = demo_circuit_inputs(program, data_input, torch.Generator().manual_seed(17))
+    ours = [t.to(DEVICE).requires_grad_(True) for t in inputs]
+    xb.run_program(xb.lower(program), ours).sum().backward()
+    ref = [t.double().requires_grad_(True) for t in inputs]
+    reference_run(translate_to_backend_program(program, TorchBackendFunctions()), ref).sum().backward()
+    for mine, theirs in zip(ours, ref):
+        expected = theirs.grad.numpy()
+        scale = max(float(np.abs(expected).max()), 1.0)
+        np.testing.assert_allclose(mine.grad.double().cpu().numpy(), expected, rtol=1e-4, atol=1e-5 * scale)

@@ -167,3 +167,24 @@ def test_unknown_stability_mode_is_not_implemented():
     program = fe.dense_program([fe.RichInstruction(fe.OperatorExp(), (0,))], 1, "unstable")
     with pytest.raises(NotImplementedError):
         xb.lower(program)
+
+
+@pytest.mark.parametrize("layer", ["cp", "tucker"])
+def test_reference_folded_circuits_lower_without_generic_glue(reference_xe, layer):
+    """The reference's own folded circuit programs (its folding passes) lower to one kernel call per
+    layer: no log add for the Hadamard products, and the fused Tucker layers in their fold-major
+    form ('acde,abd,abe->abc') and the root's form ('bcd,ac,ad->ab') on the Tucker kernel."""
+    from extended_einsum_b200.circuit import demo_circuit_program
+    from extended_einsum_b200.contraction import log_broadcast_product, logspace_einsum, logspace_einsum_hadamard
+
+    program, data_input = demo_circuit_program(reference_xe, 8, 8, 32, 7, layer=layer)
+    lowered = xb.lower(program)
+    names = [getattr(f, "func", f) for f in _fns(lowered)]
+    assert log_broadcast_product not in names and xb.ops.log_add not in names
+    levels = 6
+    if layer == "cp":
+        assert names.count(logspace_einsum_hadamard) == levels
+    else:
+        formats = [f.args[0] for f in _fns(lowered) if getattr(f, "func", None) is logspace_einsum]
+        assert len(formats) == levels
+        assert all(f.replace(" ", "") in ("acde,abd,abe->abc", "bcd,ac,ad->ab") for f in formats), formats
