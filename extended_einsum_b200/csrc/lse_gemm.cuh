@@ -1058,6 +1058,36 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
         __syncwarp();
       }
       XE_SEGMENT_END(seg_ep, 7);
+      // The tile's TMEM columns (the last chunk and the correction) are read out first, summed
+      // with the running sum of the earlier chunks into `running`, and released at once: the next
+      // tile's MMAs (its correction buffer is this one when there is a single one) then run while
+      // this tile's logs and copy-out do.  Same sums in the same order as the one-pass form below.
+      const bool two_pass = !split && C::kRunningBytes > 0;
+      if (two_pass) {
+#pragma unroll 1
+        for (int sl = 0; sl < BN / 32; ++sl) {
+          float* run = running + sl * 32 * kBM + r;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            float v[16], w[16];
+            tmem_ld16(tmem + lane_bits + C::kTmemMain + dcb * BN + sl * 32 + 16 * h, v);
+            tmem_ld16(tmem + lane_bits + C::kTmemCorr + (tl % C::kCorrBufs) * BN + sl * 32 + 16 * h, w);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const float t = direct ? v[j] : run[(16 * h + j) * kBM] + v[j];
+              // an overflowed main term carries the result; its correction is NaN
+              run[(16 * h + j) * kBM] = isinf(t) ? t : t + w[j];
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&chunk_empty[dcb]);
+          mbar_arrive(&corr_empty[tl % C::kCorrBufs]);
+        }
+      }
       float* cbase = p.c + (int64_t)bb * p.c_sb;
 #pragma unroll 1
       for (int sl = 0; sl < BN / 32; ++sl) {
@@ -1074,7 +1104,10 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           float out[16];
-          {
+          if (two_pass) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) out[j] = run[(16 * h + j) * kBM];
+          } else {
             // the last chunk (plus the running sum of the earlier ones) and the correction
             float v[16], w[16];
             tmem_ld16(tmem + lane_bits + C::kTmemMain + dcb * BN + sl * 32 + 16 * h, v);
