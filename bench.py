@@ -7,7 +7,8 @@ One JSON line on rank 0.  Default workload (the headline metric): the batched
 log-space contraction 'bik,bkj->bij', b=128, i=k=j=512, fp32 log-values drawn
 N(0, 8^2) from seed 1, logspace_max mode — "log-space einsum TFLOP/s" over
 algorithmic FLOPs (2*b*i*j*k per step).  A step is one pass of the hot path
-over the whole batch: the shift pre-pass and the fused contraction kernel.
+over the whole batch: the row-shift pass over A, the preparation of B (its
+column shifts, exp and TF32 split, once) and the fused contraction kernel.
 The line also carries the folded-circuit throughput (samples/s) of the 32x32
 quad-tree circuit, batch 8192 per GPU (--circuit-batch), as `secondary`, and
 the same contraction materialized in the scaled_sum mode as `scaled_sum`.
@@ -148,7 +149,8 @@ class LogspaceBmm:
         self.b = self.b_host.to(device)
         self.out_host = torch.empty(self.batch, self.m, self.n).pin_memory()
         self.device = device
-        self.kernel_events: list[tuple[torch.cuda.Event, torch.cuda.Event]] = []
+        self.kernel_events: list[tuple[torch.cuda.Event, ...]] = []
+        self.prepared_events: list[tuple[torch.cuda.Event, ...]] = []
 
     @property
     def flops_per_step(self) -> float:
@@ -163,20 +165,65 @@ class LogspaceBmm:
         }
 
     def step(self, record: bool) -> None:
+        """The row shifts of A, the column shifts of B, the contraction kernel: the three launches
+        xe_logspace_gemm makes for this shape (four row tiles of A: B is transformed in the kernel)."""
         from extended_einsum_b200 import ops
 
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)] if record else None
+        if record:
+            ev[0].record()
         sa = ops.logspace_shift(self.a, shift="max")
+        if record:
+            ev[1].record()
         sb = ops.logspace_shift(self.b.transpose(1, 2), shift="max")
         if record:
-            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s.record()
+            ev[2].record()
         ops.logspace_gemm_shifted(self.a, self.b, sa, sb)
         if record:
-            e.record()
-            self.kernel_events.append((s, e))
+            ev[3].record()
+            self.kernel_events.append(tuple(ev))
+
+    def step_prepared(self, record: bool) -> None:
+        """The same contraction with B prepared once (xe_logspace_b_prepare: column shifts, exp and
+        TF32 split laid out as the kernel's stages), the path xe_logspace_gemm takes from 8 row tiles."""
+        from extended_einsum_b200 import ops
+
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)] if record else None
+        if record:
+            ev[0].record()
+        sa = ops.logspace_shift(self.a, shift="max")
+        if record:
+            ev[1].record()
+        prepared = ops.PreparedB(self.b, shift="max")
+        if record:
+            ev[2].record()
+        ops.logspace_gemm_prepared(self.a, prepared, sa)
+        if record:
+            ev[3].record()
+            self.prepared_events.append(tuple(ev))
 
     def kernel_ms(self) -> float:
-        return statistics.mean(s.elapsed_time(e) for s, e in self.kernel_events)
+        return statistics.mean(ev[2].elapsed_time(ev[3]) for ev in self.kernel_events)
+
+    @staticmethod
+    def _breakdown(events, names) -> dict:
+        return {name: round(statistics.mean(ev[i].elapsed_time(ev[i + 1]) for ev in events), 4)
+                for i, name in enumerate(names)}
+
+    def breakdown_ms(self) -> dict:
+        """Mean device time of each of the step's three launches."""
+        return self._breakdown(self.kernel_events, ("shift_a", "shift_b", "contraction"))
+
+    def prepared_line(self, ms_per_step: float, peaks: dict) -> dict:
+        parts = self._breakdown(self.prepared_events, ("shift_a", "prepare_b", "contraction"))
+        achieved = self.flops_per_step / (parts["contraction"] * 1e-3) / 1e12
+        return {
+            "metric": "log-space einsum TFLOP/s with B prepared", "value": round(self.flops_per_step / (ms_per_step * 1e-3) / 1e12, 3),
+            "unit": "TFLOP/s", "ms_per_step": round(ms_per_step, 5), "step_breakdown_ms": parts,
+            "kernel_frac_of_split_tf32_peak": round(achieved / (peaks["bf16_tflops"] / 6.0), 4),
+            "workload": "the headline contraction as row shifts of A + xe_logspace_b_prepare + xe_logspace_gemm_prepared: "
+                        "the kernel runs faster, the preparation pass costs more than it saves at 4 row tiles",
+        }
 
     def e2e_step(self) -> None:
         """Public API with host buffers: the batch streamed through H2D, the kernels and D2H in 16 chunks.
@@ -357,88 +404,160 @@ def large_matmul_step(a: torch.Tensor, b: torch.Tensor):
 
 
 def run_ours(args, rank: int, world: int, device: torch.device, dist_on: bool) -> dict | None:
+    """Every workload of the line (``--only`` selects one: a profiling run, not the bench line)."""
     from extended_einsum_b200 import _lib
     from extended_einsum_b200 import distributed as xd
+    from extended_einsum_b200 import ops
 
     _lib.load()
     peaks = measured_peaks()
-    work = LogspaceBmm(device, rank)
-    # the headline (device-resident) measurement
-    sampler = ClockSampler(device.index or 0)
-    with sampler:
-        ms = time_region(work.step, args.steps, args.warmup, dist_on)
-    kernel_ms = work.kernel_ms()
-    if dist_on:
-        t = torch.tensor([kernel_ms], device="cuda")
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        kernel_ms = float(t.item())
-    ms_per_step = ms / args.steps
-    value = world * work.flops_per_step / (ms_per_step * 1e-3) / 1e12
-    # end to end through the public API with host buffers
-    e2e_steps = max(5, args.steps // 4)
-    e2e_ms = time_region(lambda record: work.e2e_step(), e2e_steps, 3, dist_on) / e2e_steps
-    e2e_value = world * work.flops_per_step / (e2e_ms * 1e-3) / 1e12
-    h2d, d2h = work.e2e_bytes
 
-    # the same contraction in the scaled_sum mode (device-resident inputs, lowered program)
-    scaled_ms = time_region(lambda record: work.scaled_step(), max(3, args.steps // 2), 3, dist_on) / max(3, args.steps // 2)
-    scaled_value = world * work.flops_per_step / (scaled_ms * 1e-3) / 1e12
+    def want(name: str) -> bool:
+        return args.only in (None, name)
 
-    # the 8192^3 contraction (per GPU, weak), log(U(0,1)) values
-    gen = torch.Generator(device=device).manual_seed(4 + 1000 * rank)
-    big_a = torch.log(torch.rand(1, 8192, 8192, device=device, generator=gen))
-    big_b = torch.log(torch.rand(1, 8192, 8192, device=device, generator=gen))
-    big_ms = time_region(large_matmul_step(big_a, big_b), 5, 3, dist_on) / 5
-    big_value = world * 2.0 * 8192**3 / (big_ms * 1e-3) / 1e12
-    del big_a, big_b
-
-    from extended_einsum_b200 import ops
-
-    # the Tucker layer 'bfi,bfj,foij->bfo' (b=512, f=2048, i=j=o=32), linear softmax weights
-    tgen = torch.Generator(device=device).manual_seed(2 + 1000 * rank)
-    t_l = torch.randn(512, 2048, 32, device=device, generator=tgen) - 3.0
-    t_r = torch.randn(512, 2048, 32, device=device, generator=tgen) - 3.0
-    t_w = ops.softmax(torch.randn(2048, 32, 32, 32, device=device, generator=tgen), (2, 3))
-    tucker_ms = time_region(lambda record: ops.logspace_tucker(t_l, t_r, t_w), 8, 3, dist_on) / 8
-    tucker_value = world * 2.0 * 512 * 2048 * 32**3 / (tucker_ms * 1e-3) / 1e12
-    del t_l, t_r, t_w
-    # row softmax of a (65536, 32768) matrix, 2 N(0,1)
-    s_x = 2.0 * torch.randn(65536, 32768, device=device, generator=tgen)
-    softmax_ms = time_region(lambda record: ops.softmax(s_x, 1), 5, 3, dist_on) / 5
-    softmax_gbs = 2 * s_x.numel() * 4 / (softmax_ms * 1e-3) / 1e9
-    del s_x
-    torch.cuda.empty_cache()
-    # the 32768^3 contraction (per GPU, weak), log(U(0,1)) values; 0.5 s per step
-    huge_a = torch.log(torch.rand(1, 32768, 32768, device=device, generator=tgen))
-    huge_b = torch.log(torch.rand(1, 32768, 32768, device=device, generator=tgen))
-    huge_ms = time_region(large_matmul_step(huge_a, huge_b), 2, 1, dist_on) / 2
-    huge_value = world * 2.0 * 32768**3 / (huge_ms * 1e-3) / 1e12
-    del huge_a, huge_b
-    torch.cuda.empty_cache()
-
-    # secondary: the folded circuit, batch-sharded
-    circ = Circuit(device, rank, args.circuit_batch)
-    circ.capture()
-
-    def circuit_step(record: bool) -> None:
-        ll = circ.step()
+    line: dict = {}
+    if want("headline"):
+        work = LogspaceBmm(device, rank)
+        # the headline (device-resident) measurement
+        sampler = ClockSampler(device.index or 0)
+        with sampler:
+            ms = time_region(work.step, args.steps, args.warmup, dist_on)
+        kernel_ms = work.kernel_ms()
         if dist_on:
-            # batch-sharded: the per-sample log-likelihoods of all ranks, in rank order
-            xd.gather_rows(ll, world * circ.batch)
-
-    c_steps = max(3, args.steps // 2)
-    c_ms = time_region(circuit_step, c_steps, max(3, args.warmup), dist_on) / c_steps
-    c_e2e_ms = time_region(lambda record: circ.e2e_step(), max(3, c_steps // 2), 2, dist_on) / max(3, c_steps // 2)
-    flops_sample = circ.circuit.flops_per_sample()
-    state_table = circ.circuit.uses_state_table(circ.batch)
-    bytes_sample = circ.circuit.hbm_bytes_per_sample(state_table)
-    c_value = world * circ.batch / (c_ms * 1e-3)
-    del circ
+            t = torch.tensor([kernel_ms], device="cuda")
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            kernel_ms = float(t.item())
+        ms_per_step = ms / args.steps
+        value = world * work.flops_per_step / (ms_per_step * 1e-3) / 1e12
+        line.update({
+            "metric": work.metric, "value": round(value, 3), "unit": work.unit, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32 (split-TF32 tensor-core products, fp32 accumulation)", "data": "synthetic",
+            "config": {**work.config(), "parallelism": f"batch-sharded x{world} (weak)"},
+            "gpu_launches": work.launches_per_step * args.steps,
+            "roofline": work.roofline(kernel_ms, peaks, profiled_traffic()),
+            "step_breakdown_ms": work.breakdown_ms(),
+            "clocks": sampler.report(),
+        })
+        p_ms = time_region(work.step_prepared, args.steps, args.warmup, dist_on) / args.steps
+        line["prepared_b"] = work.prepared_line(p_ms, peaks)
+    if want("e2e"):
+        work = work if want("headline") else LogspaceBmm(device, rank)
+        # end to end through the public API with host buffers
+        e2e_steps = max(5, args.steps // 4)
+        e2e_ms = time_region(lambda record: work.e2e_step(), e2e_steps, 3, dist_on) / e2e_steps
+        h2d, d2h = work.e2e_bytes
+        line["e2e"] = {"value": round(world * work.flops_per_step / (e2e_ms * 1e-3) / 1e12, 3), "unit": work.unit,
+                       "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+    if want("scaled"):
+        work = work if (want("headline") or want("e2e")) else LogspaceBmm(device, rank)
+        # the same contraction in the scaled_sum mode (device-resident inputs, lowered program)
+        steps = max(3, args.steps // 2)
+        scaled_ms = time_region(lambda record: work.scaled_step(), steps, 3, dist_on) / steps
+        line["scaled_sum"] = {
+            "metric": "log-space einsum TFLOP/s, scaled_sum mode",
+            "value": round(world * work.flops_per_step / (scaled_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+            "ms_per_step": round(scaled_ms, 4), "workload": "the headline contraction materialized in scaled_sum",
+        }
+    work = None
     torch.cuda.empty_cache()
+
+    if want("large"):
+        # the 8192^3 contraction (per GPU, weak), log(U(0,1)) values
+        gen = torch.Generator(device=device).manual_seed(4 + 1000 * rank)
+        big_a = torch.log(torch.rand(1, 8192, 8192, device=device, generator=gen))
+        big_b = torch.log(torch.rand(1, 8192, 8192, device=device, generator=gen))
+        big_ms = time_region(large_matmul_step(big_a, big_b), 5, 3, dist_on) / 5
+        big_value = world * 2.0 * 8192**3 / (big_ms * 1e-3) / 1e12
+        del big_a, big_b
+        line["large_8192"] = {
+            "metric": "log-space einsum TFLOP/s, 'ik,kj->ij' 8192^3 per GPU", "value": round(big_value, 2), "unit": "TFLOP/s",
+            "ms_per_step": round(big_ms, 3), "frac_of_split_tf32_peak": round(big_value / world / (peaks["bf16_tflops"] / 6.0), 4),
+            "workload": "A, B = log(U(0,1)) 8192x8192 fp32, logspace_max, xe_logspace_gemm (row shifts, B prepared, kernel)",
+        }
+        torch.cuda.empty_cache()
+
+    tgen = torch.Generator(device=device).manual_seed(2 + 1000 * rank)
+    if want("tucker"):
+        # the Tucker layer 'bfi,bfj,foij->bfo' (b=512, f=2048, i=j=o=32), linear softmax weights
+        t_l = torch.randn(512, 2048, 32, device=device, generator=tgen) - 3.0
+        t_r = torch.randn(512, 2048, 32, device=device, generator=tgen) - 3.0
+        t_w = ops.softmax(torch.randn(2048, 32, 32, 32, device=device, generator=tgen), (2, 3))
+        tucker_ms = time_region(lambda record: ops.logspace_tucker(t_l, t_r, t_w), 8, 3, dist_on) / 8
+        tucker_value = world * 2.0 * 512 * 2048 * 32**3 / (tucker_ms * 1e-3) / 1e12
+        del t_l, t_r, t_w
+        line["tucker"] = {
+            "metric": "log-space Tucker layer TFLOP/s", "value": round(tucker_value, 2), "unit": "TFLOP/s",
+            "ms_per_step": round(tucker_ms, 4), "frac_of_split_tf32_peak": round(tucker_value / world / (peaks["bf16_tflops"] / 6.0), 4),
+            "workload": "'bfi,bfj,foij->bfo' b=512 f=2048 i=j=o=32, l, r = N(-3,1), w = softmax of N(0,1) logits over (i,j), logspace_max",
+            "flops_basis": "2*b*f*o*i*j, the fused (i,j) form; the kernel contracts j first on the tensor cores and i in "
+                           "its epilogue, executing half of that as tensor work",
+        }
+    if want("softmax"):
+        # row softmax of a (65536, 32768) matrix, 2 N(0,1)
+        s_x = 2.0 * torch.randn(65536, 32768, device=device, generator=tgen)
+        softmax_ms = time_region(lambda record: ops.softmax(s_x, 1), 5, 3, dist_on) / 5
+        softmax_gbs = 2 * s_x.numel() * 4 / (softmax_ms * 1e-3) / 1e9
+        del s_x
+        torch.cuda.empty_cache()
+        line["softmax"] = {
+            "metric": "softmax GB/s (one read and one write of the matrix)", "value": round(world * softmax_gbs, 1), "unit": "GB/s",
+            "ms_per_step": round(softmax_ms, 4), "hbm_frac": round(softmax_gbs / peaks["hbm_gbs"], 4),
+            "workload": "row softmax of a (65536, 32768) fp32 matrix of 2 N(0,1) values",
+        }
+    if want("huge"):
+        # the 32768^3 contraction (per GPU, weak), log(U(0,1)) values; 0.5 s per step
+        huge_a = torch.log(torch.rand(1, 32768, 32768, device=device, generator=tgen))
+        huge_b = torch.log(torch.rand(1, 32768, 32768, device=device, generator=tgen))
+        huge_ms = time_region(large_matmul_step(huge_a, huge_b), 2, 1, dist_on) / 2
+        huge_value = world * 2.0 * 32768**3 / (huge_ms * 1e-3) / 1e12
+        del huge_a, huge_b
+        torch.cuda.empty_cache()
+        line["large_32768"] = {
+            "metric": "log-space einsum TFLOP/s, 'ik,kj->ij' 32768^3 per GPU", "value": round(huge_value, 2), "unit": "TFLOP/s",
+            "ms_per_step": round(huge_ms, 2),
+            "frac_of_split_tf32_peak": round(huge_value / world / (peaks["bf16_tflops"] / 6.0), 4),
+            "frac_of_sustained_split_tf32_peak": round(
+                huge_value / world / (peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]) / 6.0), 4),
+            "workload": "A, B = log(U(0,1)) 32768x32768 fp32, logspace_max, xe_logspace_gemm, 1 warm-up + 2 steps "
+                        "(a 0.5 s step: the sustained peak is its denominator)",
+        }
+
+    if want("circuit"):
+        # secondary: the folded circuit, batch-sharded
+        circ = Circuit(device, rank, args.circuit_batch)
+        circ.capture()
+
+        def circuit_step(record: bool) -> None:
+            ll = circ.step()
+            if dist_on:
+                # batch-sharded: the per-sample log-likelihoods of all ranks, in rank order
+                xd.gather_rows(ll, world * circ.batch)
+
+        c_steps = max(3, args.steps // 2)
+        c_ms = time_region(circuit_step, c_steps, max(3, args.warmup), dist_on) / c_steps
+        c_e2e_ms = time_region(lambda record: circ.e2e_step(), max(3, c_steps // 2), 2, dist_on) / max(3, c_steps // 2)
+        flops_sample = circ.circuit.flops_per_sample()
+        state_table = circ.circuit.uses_state_table(circ.batch)
+        bytes_sample = circ.circuit.hbm_bytes_per_sample(state_table)
+        c_value = world * circ.batch / (c_ms * 1e-3)
+        del circ
+        torch.cuda.empty_cache()
+        line["secondary"] = {
+            "metric": "circuit samples/s", "value": round(c_value, 1), "unit": "samples/s",
+            "workload": f"folded 32x32 quad-tree CP circuit, K=64, 256 states, batch {args.circuit_batch} per GPU, uint8 pixels seed 3, "
+                        "each step a replay of the forward pass captured as one CUDA graph",
+            "first_layer": "state table (F0 x 256 rows) + gathered Hadamard pairs" if state_table else "per sample, gather fused",
+            "hbm_bytes_per_sample": bytes_sample,
+            "ms_per_step": round(c_ms, 4),
+            "hbm_frac": round(bytes_sample * c_value / world / 1e9 / peaks["hbm_gbs"], 4),
+            "hbm_gbs_algorithmic": round(bytes_sample * c_value / world / 1e9, 1),
+            "tflops_algorithmic": round(flops_sample * c_value / world / 1e12, 2),
+            "e2e_samples_per_s": round(world * args.circuit_batch / (c_e2e_ms * 1e-3), 1),
+        }
 
     # the reference's own folded circuit program through lower() / run_program (the drop-in path)
-    lowered_line = None
-    if (REFERENCE_PACKAGE / "extended_einsum").is_dir():
+    if want("lowered") and (REFERENCE_PACKAGE / "extended_einsum").is_dir():
         low = LoweredCircuit(device, rank, args.circuit_batch)
         l_steps = max(3, args.steps // 4)
         l_ms = time_region(low.step, l_steps, 3, dist_on) / l_steps
@@ -473,59 +592,13 @@ def run_ours(args, rank: int, world: int, device: torch.device, dist_on: bool) -
         }
         del tk
         torch.cuda.empty_cache()
+        line["circuit_lowered"] = lowered_line
 
     if rank != 0:
         return None
-    line = {
-        "metric": work.metric, "value": round(value, 3), "unit": work.unit, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32 (split-TF32 tensor-core products, fp32 accumulation)", "data": "synthetic",
-        "config": {**work.config(), "parallelism": f"batch-sharded x{world} (weak)"},
-        "gpu_launches": work.launches_per_step * args.steps,
-        "roofline": work.roofline(kernel_ms, peaks, profiled_traffic()),
-        "e2e": {"value": round(e2e_value, 3), "unit": work.unit, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-        "clocks": sampler.report(),
-        "secondary": {
-            "metric": "circuit samples/s", "value": round(c_value, 1), "unit": "samples/s",
-            "workload": f"folded 32x32 quad-tree CP circuit, K=64, 256 states, batch {args.circuit_batch} per GPU, uint8 pixels seed 3, "
-                        "each step a replay of the forward pass captured as one CUDA graph",
-            "first_layer": "state table (F0 x 256 rows) + gathered Hadamard pairs" if state_table else "per sample, gather fused",
-            "hbm_bytes_per_sample": bytes_sample,
-            "ms_per_step": round(c_ms, 4),
-            "hbm_frac": round(bytes_sample * c_value / world / 1e9 / peaks["hbm_gbs"], 4),
-            "hbm_gbs_algorithmic": round(bytes_sample * c_value / world / 1e9, 1),
-            "tflops_algorithmic": round(flops_sample * c_value / world / 1e12, 2),
-            "e2e_samples_per_s": round(world * args.circuit_batch / (c_e2e_ms * 1e-3), 1),
-        },
-        "circuit_lowered": lowered_line,
-        "large_8192": {
-            "metric": "log-space einsum TFLOP/s, 'ik,kj->ij' 8192^3 per GPU", "value": round(big_value, 2), "unit": "TFLOP/s",
-            "ms_per_step": round(big_ms, 3), "frac_of_split_tf32_peak": round(big_value / world / (peaks["bf16_tflops"] / 6.0), 4),
-            "workload": "A, B = log(U(0,1)) 8192x8192 fp32, logspace_max, shift passes + contraction kernel",
-        },
-        "tucker": {
-            "metric": "log-space Tucker layer TFLOP/s", "value": round(tucker_value, 2), "unit": "TFLOP/s",
-            "ms_per_step": round(tucker_ms, 4), "frac_of_split_tf32_peak": round(tucker_value / world / (peaks["bf16_tflops"] / 6.0), 4),
-            "workload": "'bfi,bfj,foij->bfo' b=512 f=2048 i=j=o=32, l, r = N(-3,1), w = softmax of N(0,1) logits over (i,j), logspace_max",
-            "flops_basis": "2*b*f*o*i*j, the fused (i,j) form; the kernel contracts j first on the tensor cores and i in "
-                           "its epilogue, executing half of that as tensor work",
-        },
-        "softmax": {
-            "metric": "softmax GB/s (one read and one write of the matrix)", "value": round(world * softmax_gbs, 1), "unit": "GB/s",
-            "ms_per_step": round(softmax_ms, 4), "hbm_frac": round(softmax_gbs / peaks["hbm_gbs"], 4),
-            "workload": "row softmax of a (65536, 32768) fp32 matrix of 2 N(0,1) values",
-        },
-        "large_32768": {
-            "metric": "log-space einsum TFLOP/s, 'ik,kj->ij' 32768^3 per GPU", "value": round(huge_value, 2), "unit": "TFLOP/s",
-            "ms_per_step": round(huge_ms, 2), "frac_of_split_tf32_peak": round(huge_value / world / (peaks["bf16_tflops"] / 6.0), 4),
-            "workload": "A, B = log(U(0,1)) 32768x32768 fp32, logspace_max, shift passes + contraction kernel, 1 warm-up + 2 steps",
-        },
-        "scaled_sum": {
-            "metric": "log-space einsum TFLOP/s, scaled_sum mode", "value": round(scaled_value, 3), "unit": "TFLOP/s",
-            "ms_per_step": round(scaled_ms, 4), "workload": "the headline contraction materialized in scaled_sum",
-        },
-    }
-    if world == 1 and not args.no_cpu_baseline:
+    if args.only is not None:
+        line = {"only": args.only, **line}
+    elif world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args)
     return line
 
@@ -656,6 +729,9 @@ def main() -> None:
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--circuit-batch", type=int, default=8192, help="circuit samples per GPU (default 8192)")
+    parser.add_argument("--only", choices=["headline", "e2e", "scaled", "large", "tucker", "softmax", "huge", "circuit",
+                                           "lowered"], default=None,
+                        help="run one workload alone (profiling; the line then carries that workload only)")
     args = parser.parse_args()
     if args.warmup < 3:
         parser.error("--warmup must be at least 3")

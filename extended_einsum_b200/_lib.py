@@ -84,6 +84,25 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
             _c_i64, _c_i64, _c_i64, _c_i64, _c_ptr,  # batch, m, n, k, stream
         ],
     ),
+    "xe_logspace_b_prepared_size": (_c_size, [_c_i64, _c_i64, _c_i64]),
+    "xe_logspace_gemm_workspace_size_prepared": (_c_size, [_c_i64, _c_i64, _c_i64, _c_i64, _c_i32, _c_i32]),
+    "xe_logspace_b_prepare": (
+        _c_i32,
+        [
+            _c_ptr, _c_i64, _c_i64, _c_i64, _c_i32,  # b, strides, b_linear
+            _c_i64, _c_i64, _c_i64, _c_i32,  # batch, n, k, shift_mode
+            _c_ptr, _c_size, _c_ptr, _c_ptr,  # prepared, bytes, shift_b, stream
+        ],
+    ),
+    "xe_logspace_gemm_prepared": (
+        _c_i32,
+        [
+            _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64, _c_ptr,  # a, a2, strides, shift_a
+            _c_ptr, _c_ptr,  # prepared, shift_b
+            _c_ptr, _c_i64, _c_i64, _c_i64,  # c, strides
+            _c_i64, _c_i64, _c_i64, _c_i64, _c_ptr,  # batch, m, n, k, stream
+        ],
+    ),
     "xe_logspace_shift": (
         _c_i32,
         [_c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i32, _c_ptr, _c_ptr],

@@ -41,6 +41,10 @@ constexpr int kBK = 32;   // k per stage
 constexpr int kAWarps = 4;
 constexpr int kBWarps = 4;
 constexpr int kMmaWarp = kAWarps + kBWarps;  // 8
+// With prepared B the B warps idle, and one of them issues the correction products
+// (hi*lo + lo*hi, their own accumulator) beside the MMA warp's main products, so that the
+// tensor pipe is fed from two instruction streams.
+constexpr int kCorrMmaWarp = kAWarps + 1;  // 5
 constexpr int kDrainWarp0 = kMmaWarp + 1;    // 9..12
 constexpr int kDrainWarps = 4;
 constexpr int kProducerWarp = kDrainWarp0 + kDrainWarps;  // 13
@@ -50,6 +54,8 @@ constexpr int kChunkKB = 8;  // 256 k per main-accumulator chunk
 constexpr int kATileBytes = kBM * kBK * 4;  // one raw A tile (16 KB)
 
 enum AMode : int { kALog = 0, kALinear = 1, kATucker = 2 };
+// What one MMA-issuing thread issues (see mma_issue in lse_gemm_kernel).
+enum MmaRole : int { kMmaAll = 0, kMmaMain = 1, kMmaCorr = 2 };
 // Where the A rows come from: a TMA-filled staging ring (K-major A with
 // 16-byte aligned strides), the same plus a second ring for the fused addend,
 // or per-thread global loads (any layout).
@@ -62,8 +68,10 @@ enum ASource : int { kATma = 0, kATma2 = 1, kALdg = 2, kAGather = 3, kAGather2 =
 __host__ __device__ constexpr bool a_pair(int asrc) { return asrc == kATma2 || asrc == kAGather2; }
 __host__ __device__ constexpr bool a_gathered(int asrc) { return asrc == kAGather || asrc == kAGather2; }
 // Where the raw B tiles come from: a TMA-filled staging ring (16-byte aligned
-// strides), or global loads with or without 16-byte vectors.
-enum BSource : int { kBTma = 0, kBLdgVec = 1, kBLdg = 2 };
+// strides), or global loads with or without 16-byte vectors.  kBPlanes: B was
+// prepared by b_planes_kernel (exp'd, split into TF32 hi / lo, laid out as the
+// MMA's K-major stages), and each stage arrives by one bulk copy; the B warps idle.
+enum BSource : int { kBTma = 0, kBLdgVec = 1, kBLdg = 2, kBPlanes = 3 };
 
 struct Params {
   const float* a;
@@ -75,6 +83,7 @@ struct Params {
   int64_t c_sb, c_sm, c_sn;
   const float* shift_a;  // [batch*M] (log A with K > kInlineShiftK); else nullptr
   const float* shift_b;  // [batch*N] for a log-domain B; nullptr when B is linear
+  const float* b_planes;  // kBPlanes: the prepared B, one kPlaneBlockBytes block per (bb, nt, kb)
   int batch, M, N, K;
   int tiles_m, tiles_n, num_tiles, num_kb;
   int c_vec;      // output rows may be written with 16-byte stores
@@ -109,6 +118,9 @@ struct Cfg {
   static constexpr int kSmemLimit = 232448;
   static constexpr int kBTile = BN * kBK * 4;  // bytes, one of hi/lo (also one raw B tile)
   static constexpr int kStageBytes = 2 * kBTile;
+  // B stages in shared memory: with prepared B they are filled by bulk copies and run deeper
+  // than the two TMEM A stages (the copies' latency is hidden by the ring alone)
+  static constexpr int kBStages = BSRC == kBPlanes ? (a_pair(ASRC) ? 2 : 3) : kStages;
   // the running sum of the accumulation chunks before the last; gathered sources have
   // K <= 128 (one chunk) and need none
   static constexpr int kRunningBytes = a_gathered(ASRC) ? 0 : BN * kBM * 4;
@@ -122,10 +134,14 @@ struct Cfg {
   static constexpr int kOutBytes = kBM * 32 * 4;       // one [128 rows][32 cols] output staging buffer
   static constexpr int kAStageBytes = a_pair(ASRC) ? 2 * kATileBytes : kATileBytes;
   // everything except the two TMA rings and the output staging
-  static constexpr int kFixed = 1024 + kStages * kStageBytes + kRunningBytes + kShiftBytes + kColShiftBytes + 512;
+  static constexpr int kFixed = 1024 + kBStages * kStageBytes + kRunningBytes + kShiftBytes + kColShiftBytes + 512;
   static constexpr int kBRawBytes = BSRC == kBTma ? kBTile : 0;
   static constexpr int kMinRings = (ASRC == kALdg ? 0 : 2 * kAStageBytes) + 2 * kBRawBytes;
-  static constexpr int kOutBufs = (kDrainGroups == 2 || kFixed + kMinRings + 2 * kOutBytes <= kSmemLimit) ? 2 : 1;
+  // With a running-sum buffer and one drain group, each warp stages its output rows in place, in
+  // its own rows' part of the running sums of the slice it copies out (no separate buffer).
+  static constexpr bool kStageInPlace = kRunningBytes > 0 && kDrainGroups == 1;
+  static constexpr int kOutBufs =
+      kStageInPlace ? 0 : (kDrainGroups == 2 || kFixed + kMinRings + 2 * kOutBytes <= kSmemLimit) ? 2 : 1;
   static constexpr int kRingBudget = kSmemLimit - kFixed - kOutBufs * kOutBytes - 1024;
   // up to four stages per ring, A first
   static constexpr int kAStages =
@@ -142,7 +158,7 @@ struct Cfg {
   static constexpr int kCorrBufs = kTmemCorr + 2 * BN <= 512 ? 2 : 1;
   static constexpr int kTmemCols = pow2_at_least(kTmemCorr + kCorrBufs * BN);
   static constexpr int kOffB = 0;
-  static constexpr int kOffA = kOffB + kStages * kStageBytes;
+  static constexpr int kOffA = kOffB + kBStages * kStageBytes;
   static constexpr int kOffBRaw = kOffA + kAStages * kAStageBytes;
   static constexpr int kOffRun = kOffBRaw + kBRawStages * kBRawBytes;
   static constexpr int kOffShift = kOffRun + kRunningBytes;
@@ -261,6 +277,14 @@ __device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap* map
       " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(dst),
       "l"(map), "r"(x), "r"(r0), "r"(r1), "r"(r2), "r"(r3), "r"(smem_u32(bar))
       : "memory");
+}
+
+// Contiguous bulk copy global -> shared memory (16-byte aligned addresses and size), completing
+// on an mbarrier; no multicast.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const float* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
 }
 
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
@@ -638,6 +662,257 @@ struct BTile {
 
 // ---------------------------------------------------------------------------
 
+// ---------------------------------------------------------------------------
+// Prepared B operand.  A B operand is transformed (exp(B - sB), split into TF32 hi / lo) once
+// per (batch, 128-column tile, 32-k block) and written as the 32 KB shared-memory stage that the
+// contraction kernel's MMAs read: the hi tile, then the lo tile, each 128 n-rows x 32 k, K-major
+// with the 128-byte swizzle (kmajor_off).  The kernel then fills a stage with one bulk copy
+// (kBPlanes), which takes the B transform (raw tile in, raw values out, hi / lo in) off the
+// tensor core's shared-memory path and does it once instead of once per 128-row tile of A.
+// Values are bit-identical to the in-kernel transform: same shift, same exp_shifted and
+// split_rn; rows past N and k past K are zeros (exp(-inf), or a linear zero).
+constexpr int kPlaneN = 128;
+constexpr int kPlaneBlockBytes = 2 * kPlaneN * kBK * 4;  // 32 KB
+
+// One CTA (256 threads) per (batch, 128-column tile).  A log-domain B first reduces its columns
+// over k to the shift sB (max.NaN / min.NaN, as the shift pre-pass), written to shift_out.
+// B_KMAJ: element (k, n) at n * b_sn + k (k contiguous); else at k * b_sk + n (n contiguous).
+// Both need 16-byte aligned rows (the host checks the strides, N or K % 4, and the base).
+template <bool B_KMAJ, bool LOG>
+__global__ void __launch_bounds__(256) b_planes_kernel(const float* __restrict__ b, int64_t b_sb, int64_t b_sk,
+                                                       int64_t b_sn, int N, int K, int tiles_n, int shift_min,
+                                                       float* __restrict__ planes, float* __restrict__ shift_out) {
+  __shared__ __align__(1024) uint8_t stage[kPlaneBlockBytes];
+  __shared__ float red[8][kPlaneN];
+  __shared__ float colshift[kPlaneN];
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int nt = blockIdx.x % tiles_n;
+  const int64_t bb = blockIdx.x / tiles_n;
+  const int n0 = nt * kPlaneN;
+  const float* base = b + bb * b_sb;
+  const bool is_min = shift_min != 0;
+  const int num_kb = (K + kBK - 1) / kBK;
+  const float fill = LOG ? -INFINITY : 0.0f;
+
+  // -------- column shifts over all k
+  if (LOG) {
+    if (!B_KMAJ) {
+      const int cq = t & 31, kr = t >> 5;  // columns n0 + 4cq .. +3, k = kr, kr + 8, ...
+      const int n = n0 + 4 * cq;
+      float e[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) e[i] = is_min ? INFINITY : -INFINITY;
+      if (n < N) {  // N % 4 == 0: the quad is whole
+        const float* q = base + n;
+#pragma unroll 4
+        for (int k = kr; k < K; k += 8) {
+          const float4 v = ldg_v4(q + (int64_t)k * b_sk);
+          e[0] = extreme(e[0], v.x, is_min);
+          e[1] = extreme(e[1], v.y, is_min);
+          e[2] = extreme(e[2], v.z, is_min);
+          e[3] = extreme(e[3], v.w, is_min);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) red[kr][4 * cq + i] = e[i];
+      __syncthreads();
+      if (t < kPlaneN) {
+        float x = red[0][t];
+#pragma unroll
+        for (int r = 1; r < 8; ++r) x = extreme(x, red[r][t], is_min);
+        colshift[t] = x;
+        if (n0 + t < N) shift_out[bb * N + n0 + t] = x;
+      }
+    } else {
+      const int nl = t >> 1, half = t & 1;  // row n0 + nl, k quads half, half + 2, ...
+      const int n = n0 + nl;
+      float e = is_min ? INFINITY : -INFINITY;
+      if (n < N) {
+        const float* q = base + (int64_t)n * b_sn;
+#pragma unroll 4
+        for (int k = 4 * half; k < K; k += 8) {  // K % 4 == 0
+          const float4 v = ldg_v4(q + k);
+          e = extreme(extreme(e, v.x, is_min), extreme(v.y, extreme(v.z, v.w, is_min), is_min), is_min);
+        }
+      }
+      e = extreme(e, __shfl_xor_sync(0xffffffffu, e, 1), is_min);
+      if (half == 0) {
+        colshift[nl] = e;
+        if (n < N) shift_out[bb * N + n] = e;
+      }
+    }
+    __syncthreads();
+  }
+
+  // -------- the stages, one 32-k block at a time, assembled in shared memory
+  float* dst_base = planes + ((bb * tiles_n + nt) * (int64_t)num_kb) * (kPlaneBlockBytes / 4);
+  for (int kb = 0; kb < num_kb; ++kb) {
+    const int k0 = kb * kBK;
+    const uint32_t hi = smem_u32(stage), lo = hi + kPlaneBlockBytes / 2;
+    if (!B_KMAJ) {
+      // warp: columns 32 * (warp & 3) .. +31, k 16 * (warp >> 2) .. +15; lane: column quad
+      // lane >> 2, k quad lane & 3.  A 4 x 4 block per thread, transposed into four chunks
+      // (one per column: 4 consecutive k); every store instruction fills the 32 banks 4 times.
+      const int nl0 = 32 * (warp & 3) + 4 * (lane >> 2);
+      const int q = 4 * (warp >> 2) + (lane & 3);  // k quad within the block
+      const int n = n0 + nl0;
+      float v[4][4];  // [k][column]
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int k = k0 + 4 * q + j;
+        if (k < K && n < N) {
+          const float4 x = ldg_v4(base + (int64_t)k * b_sk + n);
+          v[j][0] = x.x;
+          v[j][1] = x.y;
+          v[j][2] = x.z;
+          v[j][3] = x.w;
+        } else {
+          v[j][0] = v[j][1] = v[j][2] = v[j][3] = fill;
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float s = LOG ? colshift[nl0 + i] : 0.0f;
+        float4 h, l;
+        float e0 = LOG ? exp_shifted(v[0][i], s) : v[0][i];
+        float e1 = LOG ? exp_shifted(v[1][i], s) : v[1][i];
+        float e2 = LOG ? exp_shifted(v[2][i], s) : v[2][i];
+        float e3 = LOG ? exp_shifted(v[3][i], s) : v[3][i];
+        if (LOG && n >= N) e0 = e1 = e2 = e3 = 0.0f;  // a column past N (its shift is a fill value)
+        split_rn(e0, h.x, l.x);
+        split_rn(e1, h.y, l.y);
+        split_rn(e2, h.z, l.z);
+        split_rn(e3, h.w, l.w);
+        const uint32_t off = kmajor_off(nl0 + i, q);
+        sts_v4(hi + off, h);
+        sts_v4(lo + off, l);
+      }
+    } else {
+      // warp: rows 16 * warp .. +15, four at a time; lane: row + (lane >> 3), k quad lane & 7
+      const int q = lane & 7;
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const int nl = 16 * warp + 4 * r + (lane >> 3);
+        const int n = n0 + nl, k = k0 + 4 * q;
+        float4 x = make_float4(fill, fill, fill, fill);
+        if (n < N && k < K) x = ldg_v4(base + (int64_t)n * b_sn + k);
+        float4 e = x;
+        if (LOG) {
+          const float s = colshift[nl];
+          e = make_float4(exp_shifted(x.x, s), exp_shifted(x.y, s), exp_shifted(x.z, s), exp_shifted(x.w, s));
+          if (n >= N) e = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        }
+        float4 h, l;
+        split_rn(e.x, h.x, l.x);
+        split_rn(e.y, h.y, l.y);
+        split_rn(e.z, h.z, l.z);
+        split_rn(e.w, h.w, l.w);
+        const uint32_t off = kmajor_off(nl, q);
+        sts_v4(hi + off, h);
+        sts_v4(lo + off, l);
+      }
+    }
+    __syncthreads();  // the block is complete
+    // copy-out: 32 KB contiguous, 16 bytes per thread and instruction
+    float* dst = dst_base + (int64_t)kb * (kPlaneBlockBytes / 4);
+#pragma unroll
+    for (int i = 0; i < kPlaneBlockBytes / (256 * 16); ++i) {
+      const int off = (i * 256 + t) * 16;
+      stg_v4(dst + off / 4, lds_v4(hi + off));
+    }
+    __syncthreads();  // read out before the next block is assembled
+  }
+}
+
+// B with n contiguous and K <= kStripeMaxK: one CTA (256 threads) per (batch, 128-column tile,
+// 32-column quarter) holds its whole column stripe (K x 32 values) in shared memory, so that B is
+// read from HBM once: the stripe is loaded, its column extremes taken (a log-domain B), and the
+// quarter's rows of every stage written (rows 32q .. 32q+31 of a K-major tile are the 4 KB at
+// 4096q of its hi and of its lo part).  Same values as b_planes_kernel.
+constexpr int kStripeMaxK = 512;
+constexpr int kStripePitch = 33;  // floats per stripe row: conflict-free column reads
+__host__ __device__ constexpr int stripe_smem_bytes(int k) {
+  return ((k + kBK - 1) / kBK) * kBK * kStripePitch * 4 + 8 * 32 * 4 + 32 * 4;
+}
+
+template <bool LOG>
+__global__ void __launch_bounds__(256) b_planes_stripe_kernel(const float* __restrict__ b, int64_t b_sb, int64_t b_sk,
+                                                              int N, int K, int tiles_n, int shift_min,
+                                                              float* __restrict__ planes, float* __restrict__ shift_out) {
+  extern __shared__ __align__(16) float stripe[];  // [k_pad][kStripePitch], then red[8][32], colshift[32]
+  const int num_kb = (K + kBK - 1) / kBK;
+  const int k_pad = num_kb * kBK;
+  float* red = stripe + k_pad * kStripePitch;
+  float* colshift = red + 8 * 32;
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int quarter = blockIdx.x & 3;
+  const int nt = (blockIdx.x >> 2) % tiles_n;
+  const int64_t bb = (blockIdx.x >> 2) / tiles_n;
+  const int c0 = nt * kPlaneN + 32 * quarter;  // first column of the stripe
+  const float* base = b + bb * b_sb;
+  const bool is_min = shift_min != 0;
+  const float fill = LOG ? -INFINITY : 0.0f;
+
+  // -------- the stripe: 16-byte loads, lanes 8j .. 8j+7 read row (4 * it + j), 8 rows in flight per thread
+  {
+    const int q4 = lane & 7, rsub = lane >> 3;
+    const int c = c0 + 4 * q4;
+    const bool cv = c < N;  // N % 4 == 0: the quad is whole or absent
+#pragma unroll 8
+    for (int k = 4 * warp + rsub; k < k_pad; k += 32) {
+      float4 v = make_float4(fill, fill, fill, fill);
+      if (cv && k < K) v = ldg_v4(base + (int64_t)k * b_sk + c);
+      float* row = stripe + k * kStripePitch + 4 * q4;
+      row[0] = v.x;
+      row[1] = v.y;
+      row[2] = v.z;
+      row[3] = v.w;
+    }
+  }
+  __syncthreads();
+  // -------- column extremes over k (rows past K hold the fill and do not enter)
+  if (LOG) {
+    float e = is_min ? INFINITY : -INFINITY;
+    for (int k = warp; k < K; k += 8) e = extreme(e, stripe[k * kStripePitch + lane], is_min);
+    red[warp * 32 + lane] = e;
+    __syncthreads();
+    if (t < 32) {
+      float x = red[t];
+#pragma unroll
+      for (int w = 1; w < 8; ++w) x = extreme(x, red[w * 32 + t], is_min);
+      colshift[t] = x;
+      if (c0 + t < N) shift_out[bb * N + c0 + t] = x;
+    }
+    __syncthreads();
+  }
+  // -------- the quarter's rows of every stage: thread t writes chunk (row j = t >> 3, k quad t & 7)
+  const int j = t >> 3, kq = t & 7;
+  const bool col_valid = c0 + j < N;
+  const float s = LOG ? colshift[j] : 0.0f;
+  const int nl = 32 * quarter + j;
+  float* blocks = planes + ((bb * tiles_n + nt) * (int64_t)num_kb) * (kPlaneBlockBytes / 4);
+  const uint32_t off = kmajor_off(nl, kq) / 4;  // floats, within the hi (or lo) tile
+#pragma unroll 4
+  for (int kb = 0; kb < num_kb; ++kb) {
+    const float* src = stripe + (kb * kBK + 4 * kq) * kStripePitch + j;
+    float e[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float x = src[i * kStripePitch];
+      e[i] = LOG ? exp_shifted(x, s) : x;
+      if (!col_valid) e[i] = 0.0f;  // a column past N (its shift is a fill value)
+    }
+    float4 h, l;
+    split_rn(e[0], h.x, l.x);
+    split_rn(e[1], h.y, l.y);
+    split_rn(e[2], h.z, l.z);
+    split_rn(e[3], h.w, l.w);
+    float* blk = blocks + (int64_t)kb * (kPlaneBlockBytes / 4);
+    stg_v4(blk + off, h);
+    stg_v4(blk + kPlaneBlockBytes / 8 + off, l);
+  }
+}
+
 template <int BN, int AMODE, int ASRC, bool B_KMAJ, int BSRC, int TJ>
 __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
     lse_gemm_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtensorMap tmap_a,
@@ -646,6 +921,11 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
   using ARowT = ARow<AMODE, TJ>;
   static_assert(C::kFits, "shared memory configuration");
   static_assert(AMODE != kATucker || ASRC == kALdg, "the Tucker operand is generated from global loads");
+  static_assert(BSRC != kBPlanes || (BN == 128 && B_KMAJ && !a_gathered(ASRC)), "prepared B: 128-column K-major stages");
+  // two MMA issuers with prepared B: the MMA warp (main products) and kCorrMmaWarp (correction
+  // products).  (A second issuer in a warp of its own beside busy B warps measured slower.)
+  constexpr bool kTwoMma = BSRC == kBPlanes;
+  static_assert(!kTwoMma || C::kDrainGroups == 1, "two MMA issuers with one drain group");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   float* running = (float*)(smem + C::kOffRun);    // [BN][128], column-major
@@ -663,7 +943,8 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
   uint64_t* b_full = a_empty + 4;               // [4], TMA transactions
   uint64_t* b_empty = b_full + 4;               // [4], B warps
   uint64_t* drain = b_empty + 4;                // [1], teardown
-  uint32_t* tmem_slot = (uint32_t*)(drain + 1);
+  uint64_t* corr_full = drain + 1;              // [kCorrBufs], the correction MMAs of a tile (two issuers)
+  uint32_t* tmem_slot = (uint32_t*)(corr_full + 2);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
   // the A / B ring barriers the producer armed, drained at wind-down after an abort
   ArmedCopies* a_copies = (ArmedCopies*)(tmem_slot + 2);
@@ -674,8 +955,9 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full[s], kAWarps + kBWarps);
-      mbar_init(&empty[s], 1);
+      // prepared B: the stage's B half comes through b_full / b_empty instead
+      mbar_init(&full[s], BSRC == kBPlanes ? kAWarps : kAWarps + kBWarps);
+      mbar_init(&empty[s], kTwoMma ? 2 : 1);
     }
     for (int c = 0; c < 2; ++c) {
       mbar_init(&chunk_full[c], 1);
@@ -687,10 +969,11 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
       mbar_init(&a_full[s], 1);
       mbar_init(&a_empty[s], kAWarps);
       mbar_init(&b_full[s], 1);
-      mbar_init(&b_empty[s], kBWarps);
+      mbar_init(&b_empty[s], BSRC == kBPlanes ? 2 : kBWarps);  // prepared B: both MMA issuers' commits
     }
     for (int c = 0; c < C::kCorrBufs; ++c) mbar_init(&corr_empty[c], kDrainWarps);
-    mbar_init(drain, 1);
+    mbar_init(drain, kTwoMma ? 2 : 1);
+    for (int c = 0; c < 2; ++c) mbar_init(&corr_full[c], 1);
     *abort_flag = 0;
     *a_copies = *b_copies = ArmedCopies{0u, 0u};
     fence_mbarrier_init();
@@ -701,6 +984,80 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t smem_base = smem_u32(smem);
+
+  // One thread's MMA issue loop.  kMmaAll: per 8-wide k-step main += A_hi*B_hi and
+  // corr += A_hi*B_lo + A_lo*B_hi.  With two issuers, kMmaMain issues the main products (and owns
+  // the chunk hand-over) and kMmaCorr the correction products (its tile hand-over through
+  // corr_full); the stage barriers then count one commit of each.
+  auto mma_issue = [&](int role) {
+    constexpr uint32_t idesc = idesc_tf32(kBM, BN, false, !B_KMAJ);
+    // K-major B advances 32 bytes per 8-element k-step inside the swizzle
+    // row; MN-major B advances two 4-row groups (1024 bytes).
+    constexpr uint32_t b_lbo = B_KMAJ ? 16 : 4096, b_sbo = B_KMAJ ? 1024 : 512, b_step = B_KMAJ ? 32 : 1024;
+    constexpr uint32_t b_lay = B_KMAJ ? kLayoutSW128 : kLayoutSW128Base32B;
+    const bool do_main = role != kMmaCorr, do_corr = role != kMmaMain;
+    uint32_t it = 0, gc = 0, tl = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++tl) {
+      const uint32_t cbuf = tl % C::kCorrBufs;
+      if (do_corr && !mbar_wait(&corr_empty[cbuf], ((tl / C::kCorrBufs) & 1) ^ 1, kSiteMmaCorr, abort_flag)) {
+        ok = false;
+        break;
+      }
+      const uint32_t d_corr = tmem + C::kTmemCorr + cbuf * BN;
+      uint32_t d_main = 0;
+      for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+        const int kc = kb % kChunkKB;
+        if (do_main && kc == 0) {
+          const uint32_t cb = gc & 1;
+          if (!mbar_wait(&chunk_empty[cb], ((gc >> 1) & 1) ^ 1, kSiteMmaChunk, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          d_main = tmem + C::kTmemMain + cb * BN;
+        }
+        const uint32_t s = it % kStages;
+        const uint32_t ph = (it / kStages) & 1;
+        if (kb == 0) XE_TILE_TRACE(tl, 12);
+        if (!mbar_wait(&full[s], ph, kSiteMmaFull, abort_flag)) {
+          ok = false;
+          break;
+        }
+        // prepared B: its own deeper ring of bulk-copied stages
+        const uint32_t bs = BSRC == kBPlanes ? it % C::kBStages : s;
+        if (BSRC == kBPlanes && !mbar_wait(&b_full[bs], (it / C::kBStages) & 1, kSiteMmaFull, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (kb == 0) XE_TILE_TRACE(tl, 13);
+        const uint32_t a_hi = tmem + C::kTmemA + 64 * s, a_lo = a_hi + 32;
+        const uint32_t b_hi = smem_base + C::kOffB + bs * C::kStageBytes, b_lo = b_hi + C::kBTile;
+#pragma unroll
+        for (int kk = 0; kk < kBK / 8; ++kk) {
+          const uint64_t dbh = smem_desc(b_hi + kk * b_step, b_lbo, b_sbo, b_lay);
+          if (do_main) umma_tf32_ts(d_main, a_hi + kk * 8, dbh, idesc, (kc | kk) != 0);
+          if (do_corr) {
+            const uint64_t dbl = smem_desc(b_lo + kk * b_step, b_lbo, b_sbo, b_lay);
+            umma_tf32_ts(d_corr, a_hi + kk * 8, dbl, idesc, (kb | kk) != 0);
+            umma_tf32_ts(d_corr, a_lo + kk * 8, dbh, idesc, 1);
+          }
+        }
+        umma_commit(&empty[s]);
+        if (BSRC == kBPlanes) umma_commit(&b_empty[bs]);
+        if (do_main && (kc == kChunkKB - 1 || kb == p.num_kb - 1)) {
+          umma_commit(&chunk_full[gc & 1]);
+          ++gc;
+        }
+        if (role == kMmaCorr && kb == p.num_kb - 1) umma_commit(&corr_full[cbuf]);
+        if (kb == 0 || kb == 8 || kb == p.num_kb - 1) XE_TILE_TRACE(tl, kb == 0 ? 6 : kb == 8 ? 7 : 8);
+      }
+    }
+    // All issued MMAs must finish before TMEM is released.
+    umma_commit(drain);
+    mbar_wait(drain, 0, kSiteGemmDrain, abort_flag, /*honor_abort=*/false);
+  };
 
   if (warp < kAWarps) {
     // ------------------------------------------------------------ A rows
@@ -870,6 +1227,12 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
     }
   } else if (warp < kAWarps + kBWarps) {
     // ------------------------------------------------------------ B tiles
+    // (with prepared B its stages arrive by bulk copy: warp kCorrMmaWarp issues the correction
+    // products, the others idle)
+    if constexpr (BSRC == kBPlanes) {
+      if (warp == kCorrMmaWarp && lane == 0) mma_issue(kMmaCorr);
+      __syncwarp();
+    } else {
     const int t = threadIdx.x - kAWarps * 32;
     using BT = BTile<BN, B_KMAJ, BSRC>;
     BT bt;
@@ -923,66 +1286,10 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
         }
       }
     }
+    }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issue
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_tf32(kBM, BN, false, !B_KMAJ);
-      // K-major B advances 32 bytes per 8-element k-step inside the swizzle
-      // row; MN-major B advances two 4-row groups (1024 bytes).
-      constexpr uint32_t b_lbo = B_KMAJ ? 16 : 4096, b_sbo = B_KMAJ ? 1024 : 512, b_step = B_KMAJ ? 32 : 1024;
-      constexpr uint32_t b_lay = B_KMAJ ? kLayoutSW128 : kLayoutSW128Base32B;
-      uint32_t it = 0, gc = 0, tl = 0;
-      bool ok = true;
-      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++tl) {
-        const uint32_t cbuf = tl % C::kCorrBufs;
-        if (!mbar_wait(&corr_empty[cbuf], ((tl / C::kCorrBufs) & 1) ^ 1, kSiteMmaCorr, abort_flag)) {
-          ok = false;
-          break;
-        }
-        const uint32_t d_corr = tmem + C::kTmemCorr + cbuf * BN;
-        uint32_t d_main = 0;
-        for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
-          const int kc = kb % kChunkKB;
-          if (kc == 0) {
-            const uint32_t cb = gc & 1;
-            if (!mbar_wait(&chunk_empty[cb], ((gc >> 1) & 1) ^ 1, kSiteMmaChunk, abort_flag)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            d_main = tmem + C::kTmemMain + cb * BN;
-          }
-          const uint32_t s = it % kStages;
-          const uint32_t ph = (it / kStages) & 1;
-          if (kb == 0) XE_TILE_TRACE(tl, 12);
-          if (!mbar_wait(&full[s], ph, kSiteMmaFull, abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          if (kb == 0) XE_TILE_TRACE(tl, 13);
-          const uint32_t a_hi = tmem + C::kTmemA + 64 * s, a_lo = a_hi + 32;
-          const uint32_t b_hi = smem_base + C::kOffB + s * C::kStageBytes, b_lo = b_hi + C::kBTile;
-#pragma unroll
-          for (int kk = 0; kk < kBK / 8; ++kk) {
-            const uint64_t dbh = smem_desc(b_hi + kk * b_step, b_lbo, b_sbo, b_lay);
-            const uint64_t dbl = smem_desc(b_lo + kk * b_step, b_lbo, b_sbo, b_lay);
-            umma_tf32_ts(d_main, a_hi + kk * 8, dbh, idesc, (kc | kk) != 0);
-            umma_tf32_ts(d_corr, a_hi + kk * 8, dbl, idesc, (kb | kk) != 0);
-            umma_tf32_ts(d_corr, a_lo + kk * 8, dbh, idesc, 1);
-          }
-          umma_commit(&empty[s]);
-          if (kc == kChunkKB - 1 || kb == p.num_kb - 1) {
-            umma_commit(&chunk_full[gc & 1]);
-            ++gc;
-          }
-          if (kb == 0 || kb == 8 || kb == p.num_kb - 1) XE_TILE_TRACE(tl, kb == 0 ? 6 : kb == 8 ? 7 : 8);
-        }
-      }
-      // All issued MMAs must finish before TMEM is released.
-      umma_commit(drain);
-      mbar_wait(drain, 0, kSiteGemmDrain, abort_flag, /*honor_abort=*/false);
-    }
+    if (lane == 0) mma_issue(kTwoMma ? kMmaMain : kMmaAll);
     __syncwarp();
   } else if (warp < kProducerWarp || warp > kProducerWarp) {
     // ------------------------------------------------------------ drain + epilogue
@@ -1010,6 +1317,14 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
       decode_tile(p, tile, bb, mt, nt);
       const int m0 = mt * kBM;
       const int n0 = nt * BN;
+      // column shifts of a log-domain B: loaded now, so that their latency passes while the tile's
+      // MMAs run; copied to shared memory in the epilogue
+      float csv[BN / 32];
+#pragma unroll
+      for (int i = 0; i < BN / 32; ++i) {
+        const int c = lane + 32 * i;
+        csv[i] = (p.shift_b && n0 + c < p.N) ? __ldg(p.shift_b + (int64_t)bb * p.N + n0 + c) : 0.0f;
+      }
       // -------- chunks: running[col][row] (+)= main chunk, for all but the last chunk;
       // the epilogue reads the last chunk and the correction straight from TMEM.
       for (int c = 0; c < chunks - 1; ++c, ++gc) {
@@ -1039,30 +1354,42 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
       const bool direct = chunks == 1;
       const uint32_t dcb = gc & 1;  // the last (or only) chunk
       if (!mbar_wait_warp(&chunk_full[dcb], (gc >> 1) & 1, kSiteDrainChunk, abort_flag)) break;
+      // two MMA issuers: the correction products of the tile complete on their own barrier
+      if (kTwoMma && !mbar_wait_warp(&corr_full[tl % C::kCorrBufs], (tl / C::kCorrBufs) & 1, kSiteDrainChunk,
+                                     abort_flag))
+        break;
       tc_fence_after();
       if (r == 0) XE_TILE_TRACE(tl, 10);
       ++gc;
       // -------- epilogue from shared memory, overlapping the next tile's MMAs
-      XE_SEGMENT_BEGIN(seg_ep);
+      // The row shifts (from the A warps) and the column shifts, into this warp's own slice of
+      // shared memory.  With the two-pass form below this comes after the tile's TMEM columns
+      // are released, off the path of the next tile's first MMAs.
       const uint32_t slot = tl & 1;
-      const bool shifted = mbar_wait(&shift_full[slot], (tl >> 1) & 1, kSiteDrainShift, abort_flag);
-      const float s1 = shifts[(slot * 2 + 0) * kBM + r];
-      const float s2 = shifts[(slot * 2 + 1) * kBM + r];
-      if (!__all_sync(0xffffffffu, shifted)) break;  // the warp's reconvergence, and a timeout seen by all lanes
-      if (lane == 0) mbar_arrive(&shift_empty[slot]);
-      // column shifts of a log-domain B, copied into this warp's own slice of shared memory
       float* cshift = p.shift_b ? (float*)(smem + C::kOffColShift) + (group * 4 + q) * BN : nullptr;
-      if (cshift) {
+      float s1 = 0.0f, s2 = 0.0f;
+      auto take_shifts = [&]() -> bool {
+        XE_SEGMENT_BEGIN(seg_ep);
+        const bool shifted = mbar_wait(&shift_full[slot], (tl >> 1) & 1, kSiteDrainShift, abort_flag);
+        s1 = shifts[(slot * 2 + 0) * kBM + r];
+        s2 = shifts[(slot * 2 + 1) * kBM + r];
+        if (!__all_sync(0xffffffffu, shifted)) return false;  // the warp's reconvergence, and a timeout seen by all lanes
+        if (lane == 0) mbar_arrive(&shift_empty[slot]);
+        if (cshift) {
+          __syncwarp();  // the previous tile's reads of cshift are done
 #pragma unroll
-        for (int c = lane; c < BN; c += 32) cshift[c] = (n0 + c < p.N) ? __ldg(p.shift_b + (int64_t)bb * p.N + n0 + c) : 0.0f;
-        __syncwarp();
-      }
-      XE_SEGMENT_END(seg_ep, 7);
+          for (int i = 0; i < BN / 32; ++i) cshift[lane + 32 * i] = csv[i];
+          __syncwarp();
+        }
+        XE_SEGMENT_END(seg_ep, 7);
+        return true;
+      };
       // The tile's TMEM columns (the last chunk and the correction) are read out first, summed
       // with the running sum of the earlier chunks into `running`, and released at once: the next
       // tile's MMAs (its correction buffer is this one when there is a single one) then run while
       // this tile's logs and copy-out do.  Same sums in the same order as the one-pass form below.
       const bool two_pass = !split && C::kRunningBytes > 0;
+      if (!two_pass && !take_shifts()) break;
       if (two_pass) {
 #pragma unroll 1
         for (int sl = 0; sl < BN / 32; ++sl) {
@@ -1087,6 +1414,7 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
           mbar_arrive(&chunk_empty[dcb]);
           mbar_arrive(&corr_empty[tl % C::kCorrBufs]);
         }
+        if (!take_shifts()) break;
       }
       float* cbase = p.c + (int64_t)bb * p.c_sb;
 #pragma unroll 1
@@ -1094,17 +1422,33 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
         const float* run = running + sl * 32 * kBM + r;  // this row's 32 sums of the slice
         // every warp stages and copies out its own 32 rows: warp-level ordering suffices
         if (C::kOutBufs == 1 || split) __syncwarp();  // this buffer's previous copy-out is done
-        // staging buffer as [128 rows][32 cols], 16-byte chunks swizzled by (row & 7)
-        const uint32_t stage = smem_base + C::kOffOutAligned + (ob % C::kOutBufs) * C::kOutBytes;
+        // Staging as [128 rows][32 cols], 16-byte chunks swizzled by (row & 7): row r at
+        // stage + r * 128 in a separate buffer, or, in place, at the 128 bytes that hold the
+        // running sums of column (32 sl + r % 32), rows 32q .. 32q+31 (this warp's own rows):
+        // slice base + (r % 32) * 512 + q * 128.
+        uint32_t stage = 0, srow = 0;
+        float sums[32];  // in place: the whole slice is read before its bytes are reused
+        if constexpr (C::kStageInPlace) {
+          stage = smem_base + C::kOffRun + sl * 32 * kBM * 4;
+          srow = stage + lane * 512 + q * 128;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) sums[j] = run[j * kBM];
+          __syncwarp();
+        } else {
+          stage = smem_base + C::kOffOutAligned + (ob % (C::kOutBufs > 0 ? C::kOutBufs : 1)) * C::kOutBytes;
+          srow = stage + r * 128;
+        }
         if (!split) ++ob;
-        const uint32_t srow = stage + r * 128;
         XE_SEGMENT_BEGIN(seg_e1);
         // 16 columns at a time: sums (TMEM main + correction, or the running sum), log and
         // shifts in the reference's order, staging
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           float out[16];
-          if (two_pass) {
+          if (C::kStageInPlace) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) out[j] = sums[16 * h + j];
+          } else if (two_pass) {
 #pragma unroll
             for (int j = 0; j < 16; ++j) out[j] = run[(16 * h + j) * kBM];
           } else {
@@ -1153,12 +1497,16 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
         // coalesced copy-out: each warp writes 32 rows, 4 rows (512 B) per instruction
         const int chunk = lane & 7;
         const int n = n0 + sl * 32 + 4 * chunk;
+        // byte offset of a staged row of this warp (see the staging layout above)
+        auto row_off = [&](int row) -> uint32_t {
+          return C::kStageInPlace ? (uint32_t)((row & 31) * 512 + q * 128) : (uint32_t)(row * 128);
+        };
         if (p.c_vec && m0 + kBM <= p.M && n0 + sl * 32 + 32 <= p.N) {
           // interior slice: every row and column in bounds, 16-byte stores
 #pragma unroll
           for (int it = 0; it < 8; ++it) {
             const int row = q * 32 + 4 * it + (lane >> 3);
-            stg_v4(cbase + (int64_t)(m0 + row) * p.c_sm + n, lds_v4(stage + row * 128 + ((chunk ^ (row & 7)) << 4)));
+            stg_v4(cbase + (int64_t)(m0 + row) * p.c_sm + n, lds_v4(stage + row_off(row) + ((chunk ^ (row & 7)) << 4)));
           }
           XE_SEGMENT_END(seg_e4, 11);
           continue;
@@ -1168,7 +1516,7 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
           const int row = q * 32 + 4 * it + (lane >> 3);
           const int m = m0 + row;
           if (m >= p.M || n >= p.N) continue;
-          const float4 val = lds_v4(stage + row * 128 + ((chunk ^ (row & 7)) << 4));
+          const float4 val = lds_v4(stage + row_off(row) + ((chunk ^ (row & 7)) << 4));
           float* dst = cbase + (int64_t)m * p.c_sm;
           if (p.c_vec && n + 4 <= p.N) {
             stg_v4(dst + n, val);
@@ -1181,6 +1529,8 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
         }
         XE_SEGMENT_END(seg_e4, 11);
       }
+      // in place: the copy-out's reads come before the next tile's running sums are written
+      if (C::kStageInPlace) __syncwarp();
       if (r == 0) XE_TILE_TRACE(tl, 11);
     }
   } else if (a_gathered(ASRC)) {
@@ -1275,7 +1625,7 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
       }
       XE_SEGMENT_END(seg_prod, 12);
     }
-  } else if ((ASRC != kALdg || BSRC == kBTma) && lane == 0) {
+  } else if ((ASRC != kALdg || BSRC == kBTma || BSRC == kBPlanes) && lane == 0) {
     // ------------------------------------------------------------ TMA producer
     uint32_t ait = 0, bit = 0;
     bool ok = true;
@@ -1310,6 +1660,20 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
             tma_load_3d(dst, &tmap_b, kb * kBK, nt * BN, bb, &b_full[sidx]);
           else
             tma_load_3d(dst, &tmap_b, nt * BN, kb * kBK, bb, &b_full[sidx]);
+          ++bit;
+        }
+        if (BSRC == kBPlanes) {
+          // the prepared stage (hi and lo tiles) of this (bb, nt, kb): one 32 KB bulk copy
+          const uint32_t sidx = bit % C::kBStages;
+          if (!mbar_wait(&b_empty[sidx], ((bit / C::kBStages) & 1) ^ 1, kSiteProducer, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t dst = smem_base + C::kOffB + sidx * C::kStageBytes;
+          mbar_expect_tx(&b_full[sidx], C::kStageBytes);
+          b_copies->note(sidx, bit / C::kBStages);
+          bulk_load(dst, p.b_planes + (((int64_t)bb * p.tiles_n + nt) * p.num_kb + kb) * (C::kStageBytes / 4),
+                    C::kStageBytes, &b_full[sidx]);
           ++bit;
         }
       }

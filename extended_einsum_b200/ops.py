@@ -101,7 +101,8 @@ def logspace_gemm(
     elif out.shape != (batch, m, n):
         raise ValueError(f"logspace_gemm: out has shape {tuple(out.shape)}, expected {(batch, m, n)}")
     lib = _lib.load()
-    ws_bytes = lib.xe_logspace_gemm_workspace_size(batch, m, n, k, int(a_linear), int(b_linear))
+    # room for the prepared B too, where the contraction prepares it (xe_logspace_b_prepare)
+    ws_bytes = lib.xe_logspace_gemm_workspace_size_prepared(batch, m, n, k, int(a_linear), int(b_linear))
     ws = torch.empty(ws_bytes, device=device, dtype=torch.uint8) if ws_bytes else None
     status = lib.xe_logspace_gemm(
         a.data_ptr(), _ptr(a2), a.stride(0), a.stride(1), a.stride(2), int(a_linear),
@@ -142,6 +143,63 @@ def logspace_gemm_shifted(
         batch, m, n, k, _stream(device),
     )
     _lib.check(status, "xe_logspace_gemm_shifted")
+    return out
+
+
+class PreparedB:
+    """A B operand prepared once (xe_logspace_b_prepare) for contractions against several A.
+
+    ``b`` is (batch, K, N) with N or K contiguous; a log-domain B enters as exp(B - shift) with its
+    column shift (max or min over k), a linear one as is.  ``logspace_gemm_prepared`` contracts an A
+    with it; the result equals ``logspace_gemm(a, b, ...)`` bit for bit.
+    """
+
+    def __init__(self, b: torch.Tensor, *, linear: bool = False, shift: str = "max") -> None:
+        _no_backward("PreparedB", b)
+        device = _check_tensors("PreparedB", b)
+        if b.dim() != 3:
+            raise ValueError("PreparedB: expected a (batch, K, N) tensor")
+        batch, k, n = b.shape
+        lib = _lib.load()
+        self.shape = (batch, k, n)
+        self.linear = linear
+        # opaque: the tiled hi / lo stages (a multiple of 32 KB), held as float32
+        self.buffer = torch.empty(lib.xe_logspace_b_prepared_size(batch, n, k) // 4, device=device, dtype=torch.float32)
+        self.shift = None if linear else torch.empty((batch, n), device=device, dtype=torch.float32)
+        status = lib.xe_logspace_b_prepare(
+            b.data_ptr(), b.stride(0), b.stride(1), b.stride(2), int(linear), batch, n, k, _shift(shift),
+            self.buffer.data_ptr(), self.buffer.numel() * 4, _ptr(self.shift), _stream(device),
+        )
+        _lib.check(status, "xe_logspace_b_prepare")
+
+
+def logspace_gemm_prepared(
+    a: torch.Tensor,
+    prepared: PreparedB,
+    shift_a: torch.Tensor | None,
+    *,
+    a2: torch.Tensor | None = None,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """The contraction kernel with a prepared B (xe_logspace_gemm_prepared); shift_a None = linear A."""
+    _no_backward("logspace_gemm_prepared", a)
+    extra = [t for t in (a2, out, shift_a) if t is not None]
+    device = _check_tensors("logspace_gemm_prepared", a, prepared.buffer, *extra)
+    batch, m, k = a.shape
+    if prepared.shape[:2] != (batch, k):
+        raise ValueError(f"logspace_gemm_prepared: A {tuple(a.shape)} does not match the prepared B {prepared.shape}")
+    n = prepared.shape[2]
+    if shift_a is not None and (not shift_a.is_contiguous() or shift_a.numel() != batch * m):
+        raise ValueError("logspace_gemm_prepared: shift_a must be a contiguous (batch, M) vector")
+    if out is None:
+        out = torch.empty((batch, m, n), device=device, dtype=torch.float32)
+    status = _lib.load().xe_logspace_gemm_prepared(
+        a.data_ptr(), _ptr(a2), a.stride(0), a.stride(1), a.stride(2), _ptr(shift_a),
+        prepared.buffer.data_ptr(), _ptr(prepared.shift),
+        out.data_ptr(), out.stride(0), out.stride(1), out.stride(2),
+        batch, m, n, k, _stream(device),
+    )
+    _lib.check(status, "xe_logspace_gemm_prepared")
     return out
 
 

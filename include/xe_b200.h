@@ -140,6 +140,44 @@ xe_status xe_logspace_gemm_shifted(const float* a, const float* a2, int64_t a_sb
                                    float* c, int64_t c_sb, int64_t c_sm, int64_t c_sn,
                                    int64_t batch, int64_t m, int64_t n, int64_t k, void* stream);
 
+/* Prepared B operand.  The same B'[b,k,n] = exp(B - sB) (or a linear B as is)
+ * that xe_logspace_gemm computes per 128-row tile of A, computed once and
+ * stored split into TF32 hi / lo parts in the tiled, swizzled layout of the
+ * contraction kernel's shared-memory stages (an opaque buffer: one 32 KB block
+ * per batch entry, 128-column tile and 32-k block).  The kernel then loads each
+ * stage with one bulk copy and spends no shared-memory bandwidth on B's
+ * transform.  Results are bit-identical to xe_logspace_gemm's.  It replaces,
+ * like xe_logspace_gemm, the per-operand shift / exp part of
+ * _append_logspace_einsum (translate.py:727-740) for the B operand.
+ *
+ * xe_logspace_gemm does this by itself when its workspace holds
+ * xe_logspace_gemm_workspace_size_prepared(...) bytes (B spanning more than
+ * 64 columns, A more than 128 rows, k above 96; otherwise that size equals
+ * xe_logspace_gemm_workspace_size).  A caller that contracts one B against
+ * several A (row blocks of a sharded A) prepares it once with
+ * xe_logspace_b_prepare and calls xe_logspace_gemm_prepared per A.
+ *
+ * xe_logspace_b_prepare: B (b,k,n) at b[b*b_sb + k*b_sk + n*b_sn] with n or k
+ * contiguous, 16-byte aligned rows and that axis a multiple of 4
+ * (XE_ERR_NOT_SUPPORTED otherwise).  A log-domain B (b_linear == 0) also writes
+ * its column shifts sB (batch*n floats, max or min over k) to shift_b.
+ * `prepared` holds xe_logspace_b_prepared_size(batch, n, k) bytes, 16-byte
+ * aligned. */
+size_t xe_logspace_b_prepared_size(int64_t batch, int64_t n, int64_t k);
+size_t xe_logspace_gemm_workspace_size_prepared(int64_t batch, int64_t m, int64_t n, int64_t k,
+                                                int32_t a_linear, int32_t b_linear);
+xe_status xe_logspace_b_prepare(const float* b, int64_t b_sb, int64_t b_sk, int64_t b_sn, int32_t b_linear,
+                                int64_t batch, int64_t n, int64_t k, int32_t shift_mode,
+                                float* prepared, size_t prepared_bytes, float* shift_b, void* stream);
+
+/* The contraction with a prepared B: as xe_logspace_gemm_shifted, with
+ * `shift_a` (batch*m floats, from xe_logspace_shift) for a log-domain A or NULL
+ * for a linear one, and the prepared B with its shift_b (NULL for a linear B). */
+xe_status xe_logspace_gemm_prepared(const float* a, const float* a2, int64_t a_sb, int64_t a_sm, int64_t a_sk,
+                                    const float* shift_a, const float* prepared, const float* shift_b,
+                                    float* c, int64_t c_sb, int64_t c_sm, int64_t c_sn,
+                                    int64_t batch, int64_t m, int64_t n, int64_t k, void* stream);
+
 /* Per-row shift of a strided 3-D operand: out[b*R + r] = max_k (or min_k) of
  * x[b*sb + r*sr + k*sk] (+ x2[...] when x2 is not NULL).  This is the
  * `max(x, axis=reduction_axes, keepdims=True)` call of translate.py:733
