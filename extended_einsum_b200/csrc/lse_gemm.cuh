@@ -674,79 +674,113 @@ struct BTile {
 constexpr int kPlaneN = 128;
 constexpr int kPlaneBlockBytes = 2 * kPlaneN * kBK * 4;  // 32 KB
 
-// One CTA (256 threads) per (batch, 128-column tile).  A log-domain B first reduces its columns
-// over k to the shift sB (max.NaN / min.NaN, as the shift pre-pass), written to shift_out.
-// B_KMAJ: element (k, n) at n * b_sn + k (k contiguous); else at k * b_sk + n (n contiguous).
-// Both need 16-byte aligned rows (the host checks the strides, N or K % 4, and the base).
+// The general preparation (any K; n or k contiguous) runs as two launches, each spread over
+// k: b_col_extreme_kernel reduces a kPrepKRows-row slice of a 128-column tile to per-column
+// partial extremes (max.NaN / min.NaN, as the shift pre-pass), and b_planes_kernel combines the
+// partials of its tile into sB (written by the CTAs of the first k group) and writes the stages of
+// kPrepGroupKB k-blocks.  B_KMAJ: element (k, n) at n * b_sn + k (k contiguous); else at
+// k * b_sk + n (n contiguous).  Both need 16-byte aligned rows (the host checks the strides, N or
+// K % 4, and the base).
+constexpr int kPrepKRows = 1024;  // k rows per partial-extreme CTA
+constexpr int kPrepGroupKB = 8;   // k-blocks per stage-writing CTA
+__host__ __device__ constexpr int prep_ksplit(int k) { return (k + kPrepKRows - 1) / kPrepKRows; }
+
+// partials: [ksplit][batch][tiles_n * 128]
+template <bool B_KMAJ>
+__global__ void __launch_bounds__(256) b_col_extreme_kernel(const float* __restrict__ b, int64_t b_sb, int64_t b_sk,
+                                                            int64_t b_sn, int N, int K, int tiles_n, int batch,
+                                                            int shift_min, float* __restrict__ partials) {
+  __shared__ float red[8][kPlaneN];
+  const int t = threadIdx.x;
+  const int ks = blockIdx.x % prep_ksplit(K);
+  const int rest = blockIdx.x / prep_ksplit(K);
+  const int nt = rest % tiles_n;
+  const int64_t bb = rest / tiles_n;
+  const int n0 = nt * kPlaneN;
+  const int k_lo = ks * kPrepKRows, k_hi = min(K, k_lo + kPrepKRows);
+  const float* base = b + bb * b_sb;
+  const bool is_min = shift_min != 0;
+  float* out = partials + ((int64_t)ks * batch + bb) * (tiles_n * kPlaneN) + n0;
+  if (!B_KMAJ) {
+    const int cq = t & 31, kr = t >> 5;  // columns n0 + 4cq .. +3, k = k_lo + kr, + 8, ...
+    const int n = n0 + 4 * cq;
+    float e[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) e[i] = is_min ? INFINITY : -INFINITY;
+    if (n < N) {  // N % 4 == 0: the quad is whole
+      const float* q = base + n;
+#pragma unroll 8
+      for (int k = k_lo + kr; k < k_hi; k += 8) {
+        const float4 v = ldg_v4(q + (int64_t)k * b_sk);
+        e[0] = extreme(e[0], v.x, is_min);
+        e[1] = extreme(e[1], v.y, is_min);
+        e[2] = extreme(e[2], v.z, is_min);
+        e[3] = extreme(e[3], v.w, is_min);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) red[kr][4 * cq + i] = e[i];
+    __syncthreads();
+    if (t < kPlaneN) {
+      float x = red[0][t];
+#pragma unroll
+      for (int r = 1; r < 8; ++r) x = extreme(x, red[r][t], is_min);
+      out[t] = x;
+    }
+  } else {
+    const int nl = t >> 1, half = t & 1;  // row n0 + nl, k quads half, half + 2, ...
+    const int n = n0 + nl;
+    float e = is_min ? INFINITY : -INFINITY;
+    if (n < N) {
+      const float* q = base + (int64_t)n * b_sn;
+#pragma unroll 8
+      for (int k = k_lo + 4 * half; k < k_hi; k += 8) {  // K % 4 == 0
+        const float4 v = ldg_v4(q + k);
+        e = extreme(extreme(e, v.x, is_min), extreme(v.y, extreme(v.z, v.w, is_min), is_min), is_min);
+      }
+    }
+    e = extreme(e, __shfl_xor_sync(0xffffffffu, e, 1), is_min);
+    if (half == 0) out[nl] = e;
+  }
+}
+
+// One CTA (256 threads) per (batch, 128-column tile, group of kPrepGroupKB k-blocks).
 template <bool B_KMAJ, bool LOG>
 __global__ void __launch_bounds__(256) b_planes_kernel(const float* __restrict__ b, int64_t b_sb, int64_t b_sk,
-                                                       int64_t b_sn, int N, int K, int tiles_n, int shift_min,
+                                                       int64_t b_sn, int N, int K, int tiles_n, int batch,
+                                                       int shift_min, const float* __restrict__ partials,
                                                        float* __restrict__ planes, float* __restrict__ shift_out) {
   __shared__ __align__(1024) uint8_t stage[kPlaneBlockBytes];
-  __shared__ float red[8][kPlaneN];
   __shared__ float colshift[kPlaneN];
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-  const int nt = blockIdx.x % tiles_n;
-  const int64_t bb = blockIdx.x / tiles_n;
+  const int num_kb = (K + kBK - 1) / kBK;
+  const int groups = (num_kb + kPrepGroupKB - 1) / kPrepGroupKB;
+  const int kg = blockIdx.x % groups;
+  const int rest = blockIdx.x / groups;
+  const int nt = rest % tiles_n;
+  const int64_t bb = rest / tiles_n;
   const int n0 = nt * kPlaneN;
   const float* base = b + bb * b_sb;
   const bool is_min = shift_min != 0;
-  const int num_kb = (K + kBK - 1) / kBK;
   const float fill = LOG ? -INFINITY : 0.0f;
 
-  // -------- column shifts over all k
+  // -------- column shifts: the partial extremes of the tile's columns over all k slices
   if (LOG) {
-    if (!B_KMAJ) {
-      const int cq = t & 31, kr = t >> 5;  // columns n0 + 4cq .. +3, k = kr, kr + 8, ...
-      const int n = n0 + 4 * cq;
-      float e[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) e[i] = is_min ? INFINITY : -INFINITY;
-      if (n < N) {  // N % 4 == 0: the quad is whole
-        const float* q = base + n;
-#pragma unroll 4
-        for (int k = kr; k < K; k += 8) {
-          const float4 v = ldg_v4(q + (int64_t)k * b_sk);
-          e[0] = extreme(e[0], v.x, is_min);
-          e[1] = extreme(e[1], v.y, is_min);
-          e[2] = extreme(e[2], v.z, is_min);
-          e[3] = extreme(e[3], v.w, is_min);
-        }
-      }
-#pragma unroll
-      for (int i = 0; i < 4; ++i) red[kr][4 * cq + i] = e[i];
-      __syncthreads();
-      if (t < kPlaneN) {
-        float x = red[0][t];
-#pragma unroll
-        for (int r = 1; r < 8; ++r) x = extreme(x, red[r][t], is_min);
-        colshift[t] = x;
-        if (n0 + t < N) shift_out[bb * N + n0 + t] = x;
-      }
-    } else {
-      const int nl = t >> 1, half = t & 1;  // row n0 + nl, k quads half, half + 2, ...
-      const int n = n0 + nl;
-      float e = is_min ? INFINITY : -INFINITY;
-      if (n < N) {
-        const float* q = base + (int64_t)n * b_sn;
-#pragma unroll 4
-        for (int k = 4 * half; k < K; k += 8) {  // K % 4 == 0
-          const float4 v = ldg_v4(q + k);
-          e = extreme(extreme(e, v.x, is_min), extreme(v.y, extreme(v.z, v.w, is_min), is_min), is_min);
-        }
-      }
-      e = extreme(e, __shfl_xor_sync(0xffffffffu, e, 1), is_min);
-      if (half == 0) {
-        colshift[nl] = e;
-        if (n < N) shift_out[bb * N + n] = e;
-      }
+    if (t < kPlaneN) {
+      const int ksplit = prep_ksplit(K);
+      const float* part = partials + bb * (tiles_n * kPlaneN) + n0 + t;
+      float x = part[0];
+      for (int ks = 1; ks < ksplit; ++ks) x = extreme(x, part[(int64_t)ks * batch * (tiles_n * kPlaneN)], is_min);
+      colshift[t] = x;
+      if (kg == 0 && n0 + t < N) shift_out[bb * N + n0 + t] = x;
     }
     __syncthreads();
   }
 
-  // -------- the stages, one 32-k block at a time, assembled in shared memory
+  // -------- the group's stages, one 32-k block at a time, assembled in shared memory
   float* dst_base = planes + ((bb * tiles_n + nt) * (int64_t)num_kb) * (kPlaneBlockBytes / 4);
-  for (int kb = 0; kb < num_kb; ++kb) {
+  const int kb_end = min(num_kb, (kg + 1) * kPrepGroupKB);
+  for (int kb = kg * kPrepGroupKB; kb < kb_end; ++kb) {
     const int k0 = kb * kBK;
     const uint32_t hi = smem_u32(stage), lo = hi + kPlaneBlockBytes / 2;
     if (!B_KMAJ) {

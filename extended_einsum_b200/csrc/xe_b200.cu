@@ -397,7 +397,17 @@ xe_status launch_gemm_planes(const Params& q, const GemmPlan& g, bool a_linear, 
   return launch_gemm_t<128, kALog, kALdg, true, kBPlanes, 0>(q, g.ma, g.ma2, g.mb, s);
 }
 
+// The prepared B: one kPlaneBlockBytes stage per (batch, 128-column tile, 32-k block), then the
+// partial column extremes of the general preparation ([k slice][batch][tiles_n * 128] floats).
 size_t planes_bytes(int64_t batch, int64_t n, int64_t k) {
+  using namespace xe::gemm;
+  const size_t tiles_n = (size_t)((n + kPlaneN - 1) / kPlaneN);
+  const size_t stages = (size_t)batch * tiles_n * (size_t)((k + kBK - 1) / kBK) * (size_t)kPlaneBlockBytes;
+  const size_t partials = (size_t)prep_ksplit((int)k) * (size_t)batch * tiles_n * kPlaneN * sizeof(float);
+  return stages + round_up(partials);
+}
+
+size_t planes_stage_bytes(int64_t batch, int64_t n, int64_t k) {
   using namespace xe::gemm;
   return (size_t)batch * (size_t)((n + kPlaneN - 1) / kPlaneN) * (size_t)((k + kBK - 1) / kBK) * (size_t)kPlaneBlockBytes;
 }
@@ -452,9 +462,24 @@ xe_status prepare_b(const char* who, const float* b, int64_t b_sb, int64_t b_sk,
                                                          shift_b);
     return check_launch(who);
   }
-  const unsigned g = (unsigned)grid;
-#define XE_PLANES(KM, LOG) \
-  b_planes_kernel<KM, LOG><<<g, 256, 0, s>>>(b, b_sb, b_sk, b_sn, (int)n, (int)k, (int)tiles_n, smin, planes, shift_b)
+  // general preparation: partial column extremes over k slices, then the stages per k group
+  float* partials = planes + planes_stage_bytes(batch, n, k) / sizeof(float);
+  const int64_t ksplit = prep_ksplit((int)k);
+  const int64_t groups = ((k + kBK - 1) / kBK + kPrepGroupKB - 1) / kPrepGroupKB;
+  if (grid * ksplit > INT32_MAX || grid * groups > INT32_MAX) return fail(XE_ERR_NOT_SUPPORTED, "%s: too many B tiles", who);
+  if (!b_linear) {
+    const unsigned g1 = (unsigned)(grid * ksplit);
+    if (lay == 1)
+      b_col_extreme_kernel<false><<<g1, 256, 0, s>>>(b, b_sb, b_sk, b_sn, (int)n, (int)k, (int)tiles_n, (int)batch, smin,
+                                                     partials);
+    else
+      b_col_extreme_kernel<true><<<g1, 256, 0, s>>>(b, b_sb, b_sk, b_sn, (int)n, (int)k, (int)tiles_n, (int)batch, smin,
+                                                    partials);
+  }
+  const unsigned g = (unsigned)(grid * groups);
+#define XE_PLANES(KM, LOG)                                                                                           \
+  b_planes_kernel<KM, LOG><<<g, 256, 0, s>>>(b, b_sb, b_sk, b_sn, (int)n, (int)k, (int)tiles_n, (int)batch, smin, \
+                                             partials, planes, shift_b)
   if (lay == 1) {
     if (b_linear) XE_PLANES(false, false);
     else XE_PLANES(false, true);

@@ -139,4 +139,5 @@ def test_prepare_rejects_bad_arguments():
                                    buf.data_ptr(), 1024, sb.data_ptr(), None)
     assert st == _lib.XE_ERR_INVALID_ARGUMENT and "needed" in _lib.last_error()
     assert ops.device_status() == 0
-    np.testing.assert_equal(lib.xe_logspace_b_prepared_size(2, 129, 33), 2 * 2 * 2 * 32768)
+    # stages (batch x 128-column tiles x 32-k blocks of 32 KB) + the partial column extremes
+    np.testing.assert_equal(lib.xe_logspace_b_prepared_size(2, 129, 33), 2 * 2 * 2 * 32768 + 2 * 256 * 4)
