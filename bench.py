@@ -59,8 +59,9 @@ def measured_peaks() -> dict:
     path = ROOT / "MEASURED_PEAKS.json"
     if path.exists():
         data = json.loads(path.read_text())
-        return {"hbm_gbs": data.get("hbm_gbs", 6650.0), "bf16_tflops": data.get("bf16_tflops", 1590.0), "basis": "of measured"}
-    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "basis": "of fallback"}
+        return {"hbm_gbs": data.get("hbm_gbs", 6650.0), "bf16_tflops": data.get("bf16_tflops", 1590.0),
+                "bf16_tflops_sustained": data.get("bf16_tflops_sustained", 1400.0), "basis": "of measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "basis": "of fallback"}
 
 
 def profiled_traffic() -> dict:
@@ -506,21 +507,41 @@ def run_ours(args, rank: int, world: int, device: torch.device, dist_on: bool) -
             "workload": "row softmax of a (65536, 32768) fp32 matrix of 2 N(0,1) values",
         }
     if want("huge"):
-        # the 32768^3 contraction (per GPU, weak), log(U(0,1)) values; 0.5 s per step
-        huge_a = torch.log(torch.rand(1, 32768, 32768, device=device, generator=tgen))
-        huge_b = torch.log(torch.rand(1, 32768, 32768, device=device, generator=tgen))
-        huge_ms = time_region(large_matmul_step(huge_a, huge_b), 2, 1, dist_on) / 2
-        huge_value = world * 2.0 * 32768**3 / (huge_ms * 1e-3) / 1e12
-        del huge_a, huge_b
+        # the 32768^3 contraction 'ik,kj->ij', log(U(0,1)) values: A row-sharded over the ranks, B
+        # broadcast once from rank 0 (NCCL), every rank contracting its rows with the full B
+        # (strong scaling: the whole contraction is the work at every N)
+        size = 32768
+        lo, hi = xd.shard_bounds(size, rank, world)
+        a_rows = torch.log(torch.rand(hi - lo, size, device=device, generator=tgen))
+        bgen = torch.Generator(device=device).manual_seed(4)
+        b_full = torch.log(torch.rand(size, size, device=device, generator=bgen)) if rank == 0 else None
+        mm = xd.RowShardedMatmul(shift="max")
+        torch.cuda.synchronize()
+        bc0, bc1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        bc0.record()
+        mm.set_b(b_full, (size, size), src=0, device=device)
+        bc1.record()
+        torch.cuda.synchronize()
+        bcast_ms = bc0.elapsed_time(bc1)
+        huge_ms = time_region(lambda record: mm(a_rows, size), 2, 1, dist_on) / 2
+        if dist_on:
+            t = torch.tensor([bcast_ms], device="cuda")
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            bcast_ms = float(t.item())
+        huge_value = 2.0 * size**3 / (huge_ms * 1e-3) / 1e12
+        del a_rows, b_full, mm
         torch.cuda.empty_cache()
         line["large_32768"] = {
-            "metric": "log-space einsum TFLOP/s, 'ik,kj->ij' 32768^3 per GPU", "value": round(huge_value, 2), "unit": "TFLOP/s",
-            "ms_per_step": round(huge_ms, 2),
+            "metric": "log-space einsum TFLOP/s, 'ik,kj->ij' 32768^3, A row-sharded over the GPUs",
+            "value": round(huge_value, 2), "unit": "TFLOP/s", "ms_per_step": round(huge_ms, 2), "scaling": "strong",
             "frac_of_split_tf32_peak": round(huge_value / world / (peaks["bf16_tflops"] / 6.0), 4),
             "frac_of_sustained_split_tf32_peak": round(
                 huge_value / world / (peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]) / 6.0), 4),
-            "workload": "A, B = log(U(0,1)) 32768x32768 fp32, logspace_max, xe_logspace_gemm, 1 warm-up + 2 steps "
-                        "(a 0.5 s step: the sustained peak is its denominator)",
+            "b_broadcast_ms": round(bcast_ms, 2) if world > 1 else None,
+            "workload": f"A, B = log(U(0,1)) 32768x32768 fp32, logspace_max; rank r owns {hi - lo} rows of A, B "
+                        "broadcast once from rank 0 (ncclBroadcast of 4 GiB, timed apart), each step "
+                        "xe_logspace_gemm of the rank's rows (row shifts, B prepared, kernel); 1 warm-up + 2 steps "
+                        "(a long step: the sustained peak is its denominator)",
         }
 
     if want("circuit"):
@@ -554,6 +575,26 @@ def run_ours(args, rank: int, world: int, device: torch.device, dist_on: bool) -
             "hbm_gbs_algorithmic": round(bytes_sample * c_value / world / 1e9, 1),
             "tflops_algorithmic": round(flops_sample * c_value / world / 1e12, 2),
             "e2e_samples_per_s": round(world * args.circuit_batch / (c_e2e_ms * 1e-3), 1),
+        }
+
+    if want("circuit") and world > 1:
+        # the same circuit strong-scaled: one batch of circuit_batch samples sharded over the ranks
+        lo, hi = xd.shard_bounds(args.circuit_batch, rank, world)
+        circ_s = Circuit(device, rank, hi - lo)
+        circ_s.capture()
+
+        def strong_step(record: bool) -> None:
+            xd.gather_rows(circ_s.step(), args.circuit_batch)
+
+        s_steps = max(3, args.steps // 2)
+        s_ms = time_region(strong_step, s_steps, max(3, args.warmup), dist_on) / s_steps
+        del circ_s
+        torch.cuda.empty_cache()
+        line["circuit_strong"] = {
+            "metric": "circuit samples/s, one batch sharded over the GPUs", "value": round(args.circuit_batch / (s_ms * 1e-3), 1),
+            "unit": "samples/s", "ms_per_step": round(s_ms, 4), "scaling": "strong",
+            "workload": f"the folded 32x32 quad-tree CP circuit, {args.circuit_batch} samples in total, "
+                        f"{hi - lo} per rank, log-likelihoods gathered with one all_gather per step",
         }
 
     # the reference's own folded circuit program through lower() / run_program (the drop-in path)
@@ -757,12 +798,12 @@ def main() -> None:
         return
 
     dist_on = world > 1
+    from extended_einsum_b200 import distributed as xd
+
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
     if dist_on:
-        import datetime
-
-        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+        xd.init_distributed("nccl", timeout_s=120.0, device=device, nonblocking=False)
     try:
         line = run_ours(args, rank, world, device, dist_on)
         if line is not None:

@@ -17,7 +17,7 @@
 //                      chunk into an fp32 running sum in smem (round to
 //                      nearest), then log(running + corr) + shifts -> global
 //   producer (13)      one thread: TMA loads of the raw A tiles (and of the
-//                      fused addend) into the staging ring; no multicast
+//                      fused addend) into the staging ring of this CTA alone
 //
 // The tensor core accumulates in fp32 with truncation, a bias that grows
 // linearly with the number of accumulating instructions; the main
@@ -260,7 +260,7 @@ __device__ __forceinline__ void umma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, u
       : "memory");
 }
 
-// 3-D tiled TMA load into shared memory, completing on an mbarrier (no multicast).
+// 3-D tiled TMA load into this CTA's shared memory, completing on an mbarrier.
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
@@ -280,7 +280,7 @@ __device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap* map
 }
 
 // Contiguous bulk copy global -> shared memory (16-byte aligned addresses and size), completing
-// on an mbarrier; no multicast.
+// on an mbarrier; this CTA's shared memory only.
 __device__ __forceinline__ void bulk_load(uint32_t dst, const float* src, uint32_t bytes, uint64_t* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
                "l"(src), "r"(bytes), "r"(smem_u32(bar))
@@ -314,11 +314,21 @@ __device__ __forceinline__ float extreme(float a, float b, bool is_min) {
   return r;
 }
 
+// Tile order within a batch entry: groups of kGroupM row tiles, the row tile fastest inside a
+// group, so that the ~148 tiles in flight at once (one per CTA) share their A row blocks and B
+// column tiles in L2 (about kGroupM CTAs read each B tile at the same time, instead of the one or
+// two of a row-major order, which left a 32768-column B streaming from HBM once per CTA).
+constexpr int kGroupM = 16;
 __device__ __forceinline__ void decode_tile(const Params& p, int tile, int& bb, int& mt, int& nt) {
-  nt = tile % p.tiles_n;
-  const int rest = tile / p.tiles_n;
-  mt = rest % p.tiles_m;
-  bb = rest / p.tiles_m;
+  const int per_batch = p.tiles_m * p.tiles_n;
+  bb = tile / per_batch;
+  const int t = tile - bb * per_batch;
+  const int group = t / (kGroupM * p.tiles_n);
+  const int m0 = group * kGroupM;
+  const int gm = min(kGroupM, p.tiles_m - m0);  // the last group may hold fewer row tiles
+  const int idx = t - group * kGroupM * p.tiles_n;
+  mt = m0 + idx % gm;
+  nt = idx / gm;
 }
 
 // ---------------------------------------------------------------------------

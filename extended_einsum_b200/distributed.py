@@ -22,7 +22,9 @@ CPU ranks.
 
 from __future__ import annotations
 
-from collections.abc import Callable
+import contextlib
+import datetime
+from collections.abc import Callable, Iterator
 
 import torch
 import torch.distributed as dist
@@ -53,7 +55,11 @@ def shard_bounds(total: int, rank: int, world_size: int) -> tuple[int, int]:
 def broadcast_operand(t: torch.Tensor | None, shape: tuple[int, ...], src: int = 0, group=None,
                       device: torch.device | None = None) -> torch.Tensor:
     """The operand ``t`` of rank ``src`` on every rank (ranks other than src pass None)."""
-    rank, _ = world()
+    rank, world_size = world()
+    if world_size == 1:
+        if t is None or tuple(t.shape) != tuple(shape):
+            raise ValueError(f"the source rank must pass the operand of shape {shape}")
+        return t.contiguous()
     if rank == src:
         if t is None or tuple(t.shape) != tuple(shape):
             raise ValueError(f"the source rank must pass the operand of shape {shape}")
@@ -128,3 +134,96 @@ def sharded_circuit_log_likelihood(forward: Callable[[torch.Tensor], torch.Tenso
                                    total_batch: int, group=None) -> torch.Tensor:
     """Log-likelihoods (total_batch, 1) of a batch-sharded circuit: local forward + one gather."""
     return gather_rows(forward(pixels_local), total_batch, group)
+
+
+# ---------------------------------------------------------------------------
+# failure detection between steps
+
+
+def init_distributed(backend: str, timeout_s: float = 60.0, device: torch.device | None = None,
+                     nonblocking: bool = True) -> None:
+    """The default process group, with a short collective timeout.
+
+    For NCCL the communicators are created non-blocking (ncclConfig.blocking = 0):
+    their calls return at once and report errors asynchronously, so that a
+    collective stuck on a dead peer can be aborted from the host
+    (``abort_process_group``) instead of blocking the thread.  NVLS stays as the
+    environment sets it (NCCL_NVLS_ENABLE).  Rendezvous through MASTER_ADDR /
+    MASTER_PORT / RANK / WORLD_SIZE.
+    """
+    options = None
+    if backend == "nccl" and nonblocking:
+        from torch._C._distributed_c10d import ProcessGroupNCCL
+
+        options = ProcessGroupNCCL.Options()
+        options.config.blocking = 0
+    kwargs = {"timeout": datetime.timedelta(seconds=timeout_s)}
+    if device is not None:
+        kwargs["device_id"] = device
+    if options is not None:
+        kwargs["pg_options"] = options
+    dist.init_process_group(backend, **kwargs)
+
+
+def abort_process_group(group=None) -> None:
+    """Ends the process group without waiting for peers: NCCL communicators are aborted
+    (ncclCommAbort through ProcessGroupNCCL), other backends destroyed."""
+    if not (dist.is_available() and dist.is_initialized()):
+        return
+    if dist.get_backend(group) == "nccl":
+        from torch.distributed import distributed_c10d as c10d
+
+        c10d._abort_process_group(group)
+    else:
+        dist.destroy_process_group(group)
+
+
+class PeerFailure(RuntimeError):
+    """Another rank reported a failure (or stopped answering) before this rank's next collective."""
+
+    def __init__(self, rank: int, reason: str) -> None:
+        super().__init__(f"rank {rank} failed: {reason}")
+        self.rank = rank
+        self.reason = reason
+
+
+class PeerMonitor:
+    """Host-side failure detection between steps, through the process group's store.
+
+    A rank that fails inside ``guard()`` records the failure under its rank in
+    the store before the exception propagates; every rank calls ``check()``
+    before it launches the step's kernels and collectives, so the others learn
+    of the failure on the host and leave between steps, with none of their
+    kernels or collectives in flight.  A rank that dies without reporting is
+    caught by the process group's timeout on the next collective instead.
+    """
+
+    def __init__(self, store=None, prefix: str = "xe-peer") -> None:
+        if store is None:
+            from torch.distributed import distributed_c10d as c10d
+
+            store = c10d._get_default_store()
+        self.store = store
+        self.prefix = prefix
+        self.rank, self.world_size = world()
+
+    def _key(self, rank: int) -> str:
+        return f"{self.prefix}/failed/{rank}"
+
+    def report_failure(self, reason: str) -> None:
+        self.store.set(self._key(self.rank), reason[:512])
+
+    def check(self) -> None:
+        """Raises PeerFailure for the first other rank that reported a failure."""
+        for r in range(self.world_size):
+            if r != self.rank and self.store.check([self._key(r)]):
+                raise PeerFailure(r, self.store.get(self._key(r)).decode(errors="replace"))
+
+    @contextlib.contextmanager
+    def guard(self) -> Iterator[None]:
+        """Reports any exception of the block to the peers, then re-raises it."""
+        try:
+            yield
+        except BaseException as exc:
+            self.report_failure(f"{type(exc).__name__}: {exc}")
+            raise

@@ -41,7 +41,8 @@ def _worker(rank: int, world_size: int, port: int, case: str, out_dir: str) -> N
     os.environ["MASTER_PORT"] = str(port)
     import datetime
 
-    dist.init_process_group("gloo", rank=rank, world_size=world_size, timeout=datetime.timedelta(seconds=60))
+    timeout = 5 if case == "peer_vanishes" else 60
+    dist.init_process_group("gloo", rank=rank, world_size=world_size, timeout=datetime.timedelta(seconds=timeout))
     try:
         from extended_einsum_b200 import distributed as xd
 
@@ -69,8 +70,46 @@ def _worker(rank: int, world_size: int, port: int, case: str, out_dir: str) -> N
                 xd.gather_rows(torch.zeros(3, 2), 10)
             except ValueError:
                 torch.save(torch.tensor([1]), Path(out_dir) / f"bad_{rank}.pt")
+        elif case == "peer_raises":
+            # rank 1 fails in its step before the collective; rank 0 learns of it through the
+            # store before it launches the collective, instead of waiting in it
+            monitor = xd.PeerMonitor()
+            dist.barrier()
+            if rank == 1:
+                try:
+                    with monitor.guard():
+                        raise ValueError("bad input on rank 1")
+                except ValueError:
+                    pass
+                dist.barrier()  # the report is in the store before rank 0 checks
+            else:
+                dist.barrier()
+                try:
+                    monitor.check()
+                    dist.all_reduce(torch.ones(4))
+                except xd.PeerFailure as exc:
+                    (Path(out_dir) / "peer_failure.txt").write_text(f"{exc.rank}|{exc.reason}")
+        elif case == "peer_vanishes":
+            # rank 1 leaves between steps without a word; rank 0's next collective ends with an
+            # error after the process group's short timeout instead of hanging
+            dist.barrier()
+            if rank == 0:
+                import time
+
+                t0 = time.monotonic()
+                try:
+                    dist.all_reduce(torch.ones(4))
+                    outcome = "completed"
+                except Exception as exc:  # noqa: BLE001 - gloo raises RuntimeError subclasses
+                    outcome = type(exc).__name__
+                (Path(out_dir) / "vanished.txt").write_text(f"{outcome}|{time.monotonic() - t0:.1f}")
+            return  # no destroy: the peer is gone
     finally:
-        dist.destroy_process_group()
+        if dist.is_initialized():
+            try:
+                dist.destroy_process_group()
+            except Exception:  # noqa: BLE001 - a group whose peer left may not shut down cleanly
+                pass
 
 
 def _spawn(case: str, tmp_path: Path, world_size: int = 2) -> None:
@@ -119,3 +158,30 @@ def test_sharded_circuit_gather_keeps_sample_order(tmp_path):
 def test_gather_rejects_a_shard_of_the_wrong_size(tmp_path):
     _spawn("bad_shard", tmp_path)
     assert (tmp_path / "bad_0.pt").exists() and (tmp_path / "bad_1.pt").exists()
+
+
+def test_a_rank_that_raises_is_reported_before_the_next_collective(tmp_path):
+    _spawn("peer_raises", tmp_path)
+    rank, reason = (tmp_path / "peer_failure.txt").read_text().split("|", 1)
+    assert rank == "1" and "bad input on rank 1" in reason
+
+
+def test_a_rank_that_vanishes_ends_the_next_collective_with_an_error(tmp_path):
+    _spawn("peer_vanishes", tmp_path)
+    outcome, seconds = (tmp_path / "vanished.txt").read_text().split("|")
+    assert outcome != "completed"
+    assert float(seconds) < 30.0
+
+
+def test_init_distributed_builds_nonblocking_nccl_options(monkeypatch):
+    """The NCCL options init_distributed passes (no GPU: the call to torch is intercepted)."""
+    from extended_einsum_b200 import distributed as xd
+
+    seen = {}
+    monkeypatch.setattr(dist, "init_process_group", lambda backend, **kw: seen.update(backend=backend, **kw))
+    xd.init_distributed("nccl", timeout_s=7.0)
+    assert seen["backend"] == "nccl" and seen["pg_options"].config.blocking == 0
+    assert seen["timeout"].total_seconds() == 7.0
+    seen.clear()
+    xd.init_distributed("gloo", timeout_s=3.0)
+    assert "pg_options" not in seen
