@@ -496,7 +496,7 @@ def run_ours(args, rank: int, world: int, device: torch.device, dist_on: bool) -
         }
     if want("softmax"):
         # row softmax of a (65536, 32768) matrix, 2 N(0,1)
-        s_x = 2.0 * torch.randn(65536, 32768, device=device, generator=tgen)
+        s_x = 2.0 * torch.randn(args.softmax_rows, 32768, device=device, generator=tgen)
         softmax_ms = time_region(lambda record: ops.softmax(s_x, 1), 5, 3, dist_on) / 5
         softmax_gbs = 2 * s_x.numel() * 4 / (softmax_ms * 1e-3) / 1e9
         del s_x
@@ -504,7 +504,7 @@ def run_ours(args, rank: int, world: int, device: torch.device, dist_on: bool) -
         line["softmax"] = {
             "metric": "softmax GB/s (one read and one write of the matrix)", "value": round(world * softmax_gbs, 1), "unit": "GB/s",
             "ms_per_step": round(softmax_ms, 4), "hbm_frac": round(softmax_gbs / peaks["hbm_gbs"], 4),
-            "workload": "row softmax of a (65536, 32768) fp32 matrix of 2 N(0,1) values",
+            "workload": f"row softmax of a ({args.softmax_rows}, 32768) fp32 matrix of 2 N(0,1) values",
         }
     if want("huge"):
         # the 32768^3 contraction 'ik,kj->ij', log(U(0,1)) values: A row-sharded over the ranks, B
@@ -770,6 +770,7 @@ def main() -> None:
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--circuit-batch", type=int, default=8192, help="circuit samples per GPU (default 8192)")
+    parser.add_argument("--softmax-rows", type=int, default=65536, help="rows of the softmax workload (default 65536)")
     parser.add_argument("--only", choices=["headline", "e2e", "scaled", "large", "tucker", "softmax", "huge", "circuit",
                                            "lowered"], default=None,
                         help="run one workload alone (profiling; the line then carries that workload only)")
