@@ -216,6 +216,99 @@ __global__ void __launch_bounds__(kThreads == 32 ? 256 : kThreads)
   }
 }
 
+// Short rows (len <= 4 * G <= 64, 16-byte aligned): G lanes per row, one float4 each, so that a
+// warp holds 32 / G rows (the circuit's sum-layer weights are rows of 64).  The arithmetic is
+// softmax_rows_reg<32, 1>'s: the lanes it leaves at -inf add exact zeros to its sums, and its
+// butterfly over 32 lanes combines the G live lanes in this kernel's order, so the results are
+// the same bit for bit.
+template <int G>
+__global__ void __launch_bounds__(256) softmax_rows_group(const float* __restrict__ x, float* __restrict__ y,
+                                                          int64_t rows, int64_t len, int log_out) {
+  static_assert(G >= 1 && G <= 16 && (G & (G - 1)) == 0, "G");
+  const int64_t row = ((int64_t)blockIdx.x * 256 + threadIdx.x) / G;
+  const int lane = threadIdx.x % G;
+  // the lanes of this row's group (groups never straddle a warp)
+  const unsigned gmask = (G == 32 ? 0xffffffffu : ((1u << G) - 1u)) << ((threadIdx.x & 31) / G * G);
+  if (row >= rows) return;  // whole groups leave together
+  const float* px = x + row * len;
+  float* py = y + row * len;
+  const int64_t i = 4 * lane;
+  const float4 v = i < len ? ldg_nc_v4(px + i) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+  float m = nan_extreme<true>(nan_extreme<true>(v.x, v.y), nan_extreme<true>(v.z, v.w));
+#pragma unroll
+  for (int o = G / 2; o > 0; o >>= 1) m = nan_extreme<true>(m, __shfl_xor_sync(gmask, m, o));
+  const float ex = i < len ? expf(v.x - m) : 0.0f;
+  const float ey = i + 1 < len ? expf(v.y - m) : 0.0f;
+  const float ez = i + 2 < len ? expf(v.z - m) : 0.0f;
+  const float ew = i + 3 < len ? expf(v.w - m) : 0.0f;
+  float s = (ex + ey) + (ez + ew);
+#pragma unroll
+  for (int o = G / 2; o > 0; o >>= 1) s += __shfl_xor_sync(gmask, s, o);
+  const float inv = 1.0f / s;
+  const float lse = m + logf(s);
+  if (i < len) {
+    float4 o;
+    if (log_out)
+      o = make_float4(v.x - lse, v.y - lse, v.z - lse, v.w - lse);
+    else
+      o = make_float4(expf(v.x - m) * inv, expf(v.y - m) * inv, expf(v.z - m) * inv, expf(v.w - m) * inv);
+    stg_v4(py + i, o);
+  }
+}
+
+// Softmax over the middle axis of (outer, len, inner) when one outer slice (len x inner values,
+// at most kSlabMaxFloats) fits in shared memory and inner divides 256: one CTA per outer index
+// stages the slice with coalesced 16-byte loads, 256 / inner threads reduce each column
+// (max, then the sum of exp(x - max)), and the outputs leave coalesced.  The categorical input
+// table of a circuit (variables, 256 states, units) normalises over its states this way.
+constexpr int kSlabMaxFloats = 24576;  // 96 KB
+__global__ void __launch_bounds__(256) softmax_slab(const float* __restrict__ x, float* __restrict__ y, int64_t len,
+                                                    int inner, int log_out) {
+  extern __shared__ __align__(16) float slab[];  // [len][inner], then [256] partials, [2][inner] stats
+  float* part = slab + len * inner;
+  float* stat_m = part + 256;
+  float* stat_s = stat_m + inner;
+  const int t = threadIdx.x;
+  const int64_t n = len * inner;  // a multiple of 4
+  const float* px = x + blockIdx.x * n;
+  float* py = y + blockIdx.x * n;
+  for (int64_t i = 4 * t; i < n; i += 1024) *(float4*)(slab + i) = ldg_nc_v4(px + i);
+  __syncthreads();
+  const int c = t % inner, p = t / inner, P = 256 / inner;
+  float m = -INFINITY;
+  for (int64_t a = p; a < len; a += P) m = nan_extreme<true>(m, slab[a * inner + c]);
+  part[t] = m;
+  __syncthreads();
+  if (t < inner) {
+    float mm = part[t];
+    for (int q = 1; q < P; ++q) mm = nan_extreme<true>(mm, part[q * inner + t]);
+    stat_m[t] = mm;
+  }
+  __syncthreads();
+  m = stat_m[c];
+  float sum = 0.0f;
+  for (int64_t a = p; a < len; a += P) sum += expf(slab[a * inner + c] - m);
+  part[t] = sum;
+  __syncthreads();
+  if (t < inner) {
+    float ss = part[t];
+    for (int q = 1; q < P; ++q) ss += part[q * inner + t];
+    stat_s[t] = ss;
+  }
+  __syncthreads();
+  for (int64_t i = 4 * t; i < n; i += 1024) {
+    const float4 v = *(const float4*)(slab + i);
+    const int c0 = (int)(i % inner);  // inner % 4 == 0: the quad lies in one row
+    float r[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float mj = stat_m[c0 + j], sj = stat_s[c0 + j];
+      r[j] = log_out ? r[j] - (mj + logf(sj)) : expf(r[j] - mj) * (1.0f / sj);
+    }
+    stg_v4(py + i, make_float4(r[0], r[1], r[2], r[3]));
+  }
+}
+
 // Row softmax for 16384 < len <= 32768 (16-byte aligned rows): persistent CTAs of 1024
 // threads, one row in registers (8 float4 per thread, the element mapping and arithmetic of
 // softmax_rows_reg<1024, 8>, so the results are identical) while a bulk copy brings the

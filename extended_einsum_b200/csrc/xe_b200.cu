@@ -1070,12 +1070,35 @@ xe_status xe_softmax(const float* x, float* y, int64_t outer, int64_t axis_len, 
   cudaStream_t s = as_stream(stream);
   const int lo = log_output ? 1 : 0;
   if (inner > 1) {
+    if (inner % 4 == 0 && inner <= 256 && 256 % inner == 0 && axis_len * inner <= xe::kSlabMaxFloats &&
+        aligned16(x) && aligned16(y) && outer <= INT32_MAX && env_int("XE_SOFTMAX_NO_SLAB", 0) == 0) {
+      // one outer slice per CTA, staged in shared memory
+      const int smem = (int)((axis_len * inner + 256 + 2 * inner) * sizeof(float));
+      static std::atomic<uint32_t> attribute_set{0};
+      cudaError_t e = prepare_kernel(xe::softmax_slab, (xe::kSlabMaxFloats + 256 + 2 * 256) * (int)sizeof(float),
+                                     attribute_set);
+      if (e != cudaSuccess) return fail(XE_ERR_CUDA, "xe_softmax: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+      xe::softmax_slab<<<(unsigned)outer, 256, smem, s>>>(x, y, axis_len, (int)inner, lo);
+      return check_launch("xe_softmax");
+    }
     const int64_t fibres = outer * inner;
     xe::softmax_strided<<<(unsigned)((fibres + 255) / 256), 256, 0, s>>>(x, y, outer, axis_len, inner, lo);
     return check_launch("xe_softmax");
   }
   const bool vec = aligned16(x) && aligned16(y) && axis_len % 4 == 0;
   const int64_t rows = outer, len = axis_len;
+  if (vec && len <= 64) {
+    // short rows: a group of lanes per row, several rows per warp
+#define XE_SOFTMAX_GROUP(G) \
+  xe::softmax_rows_group<G><<<(unsigned)((rows * G + 255) / 256), 256, 0, s>>>(x, y, rows, len, lo)
+    if (len <= 4) XE_SOFTMAX_GROUP(1);
+    else if (len <= 8) XE_SOFTMAX_GROUP(2);
+    else if (len <= 16) XE_SOFTMAX_GROUP(4);
+    else if (len <= 32) XE_SOFTMAX_GROUP(8);
+    else XE_SOFTMAX_GROUP(16);
+#undef XE_SOFTMAX_GROUP
+    return check_launch("xe_softmax");
+  }
 #define XE_SOFTMAX_WARP(Q)                                                                                   \
   do {                                                                                                       \
     const unsigned blocks = (unsigned)((rows + 7) / 8);                                                      \

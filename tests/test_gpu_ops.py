@@ -17,7 +17,10 @@ pytestmark = pytest.mark.gpu
 @pytest.mark.parametrize(
     "shape,axis",
     [((5, 37), 1), ((300, 1000), 1), ((7, 4096), 1), ((3, 20000), 1), ((2, 40000), 1), ((2, 70000), 1), ((4, 9, 5), 1),
-     ((3, 5, 7), (1, 2)), ((2, 3, 4, 5), (1, 3)), ((64, 64, 64), 2), ((6, 128), 0), ((1, 1), 1), ((9, 33), -1)],
+     ((3, 5, 7), (1, 2)), ((2, 3, 4, 5), (1, 3)), ((64, 64, 64), 2), ((6, 128), 0), ((1, 1), 1), ((9, 33), -1),
+     # rows of at most 64 (lane groups), and middle axes staged per slice in shared memory
+     ((1000, 64), 1), ((50, 20), 1), ((7, 4), 1), ((300, 256, 64), 1), ((5, 256, 4), 1), ((3, 100, 8), 1),
+     ((2, 96, 256), 1)],
 )
 def test_softmax(shape, axis):
     gen = torch.Generator().manual_seed(len(shape) * 100 + shape[0])
@@ -122,3 +125,24 @@ def test_cpu_tensors_are_rejected():
 
 def test_no_device_wait_timed_out():
     assert ops.device_status() == 0
+
+
+@pytest.mark.parametrize("shape", [(6, 256, 64), (40, 64)])
+def test_softmax_minus_inf_and_nan_fibres(shape):
+    """A fibre that is all -inf gives NaN and a NaN propagates through its fibre, as torch does."""
+    gen = torch.Generator().manual_seed(17)
+    x = 2.0 * torch.randn(*shape, generator=gen)
+    if len(shape) == 3:
+        x[0, :, 3] = -float("inf")
+        x[1, 5, 9] = float("nan")
+        axis = 1
+    else:
+        x[0, :] = -float("inf")
+        x[1, 5] = float("nan")
+        axis = 1
+    for log_output in (False, True):
+        ours = ops.softmax(x.cuda(), axis, log_output=log_output).cpu()
+        ref = torch.log_softmax(x.double(), axis) if log_output else torch.softmax(x.double(), axis)
+        assert torch.equal(torch.isnan(ours), torch.isnan(ref))
+        ok = ~torch.isnan(ref)
+        np.testing.assert_allclose(ours[ok].numpy(), ref[ok].numpy(), rtol=2e-6, atol=1e-6 if log_output else 1e-9)
