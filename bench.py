@@ -7,17 +7,20 @@ One JSON line on rank 0.  Default workload (the headline metric): the batched
 log-space contraction 'bik,bkj->bij', b=128, i=k=j=512, fp32 log-values drawn
 N(0, 8^2) from seed 1, logspace_max mode — "log-space einsum TFLOP/s" over
 algorithmic FLOPs (2*b*i*j*k per step).  A step is one pass of the hot path
-over the whole batch: the row-shift pass over A, the preparation of B (its
-column shifts, exp and TF32 split, once) and the fused contraction kernel.
-The line also carries the folded-circuit throughput (samples/s) of the 32x32
-quad-tree circuit, batch 8192 per GPU (--circuit-batch), as `secondary`, and
-the same contraction materialized in the scaled_sum mode as `scaled_sum`.
+over the whole batch: the row-shift pass over A, the column-shift pass over B
+and the fused contraction kernel (the launches xe_logspace_gemm makes for this
+shape); the same step with B prepared once is reported beside it.  The line also
+carries the folded-circuit throughput (samples/s) of the 32x32 quad-tree
+circuit, batch 8192 per GPU (--circuit-batch), as `secondary`, its training
+step, the 8192^3 and 32768^3 contractions, the Tucker layer, the row softmax,
+and the headline expression in the scaled_sum mode.
 
-Multi-GPU (torchrun, one process per GPU, NCCL): the batch is sharded by
-construction — every rank processes its own batch of the same size (weak
-scaling) with no data-path collective; the circuit gathers its per-sample
-log-likelihoods with one all_gather per step.  Times are CUDA-event times,
-the max over ranks.
+Multi-GPU (torchrun, one process per GPU, NCCL): most lines are weak-scaled
+(every rank its own batch, no data-path collective; the circuit gathers its
+per-sample log-likelihoods with one all_gather per step); the 32768^3
+contraction is A row-sharded with B broadcast once, and the circuit is also
+run as one batch sharded over the ranks (strong scaling).  Times are
+CUDA-event times, the max over ranks.
 
 ``--impl reference`` times the reference package itself (extended_einsum,
 installed unmodified into baseline/_ref by baseline/install_reference.sh) on
@@ -317,6 +320,41 @@ class Circuit:
         return 2 + 2 * levels + 2
 
 
+class CircuitTrain:
+    """The demo's training step on the same circuit (demo/cirkit.py:698-708): forward pass,
+    loss = -mean log-likelihood, loss.backward() through the kernels' backward passes, an Adam
+    step on the logits; with several ranks the gradients are averaged with one all_reduce per
+    parameter (data parallel)."""
+
+    def __init__(self, device: torch.device, rank: int, batch: int = 8192) -> None:
+        from extended_einsum_b200.circuit import CircuitForward, QuadTreeCircuit
+
+        self.circuit = QuadTreeCircuit(32, 32, 64, 256)
+        gen = torch.Generator().manual_seed(3)
+        params = self.circuit.init_parameters(gen)
+        self.leaves = [params["categorical"].to(device).requires_grad_(),
+                       *[t.to(device).requires_grad_() for t in params["levels"]],
+                       params["root"].to(device).requires_grad_()]
+        dev = {"categorical": self.leaves[0], "levels": self.leaves[1:-1], "root": self.leaves[-1],
+               "var_of_fold": params["var_of_fold"].to(device)}
+        self.forward = CircuitForward(self.circuit, dev)
+        pixel_gen = torch.Generator().manual_seed(3 + 1000 * rank)
+        self.pixels = torch.randint(256, (batch, self.circuit.variables), generator=pixel_gen, dtype=torch.uint8).to(device)
+        self.batch = batch
+        self.opt = torch.optim.Adam(self.leaves, lr=1e-2)
+
+    def step(self, dist_on: bool) -> None:
+        self.opt.zero_grad(set_to_none=True)
+        loss = -self.forward(self.pixels).mean()
+        loss.backward()
+        if dist_on:
+            world_size = torch.distributed.get_world_size()
+            for p in self.leaves:
+                torch.distributed.all_reduce(p.grad)
+                p.grad.div_(world_size)
+        self.opt.step()
+
+
 class LoweredCircuit:
     """The same 32x32 circuit as the reference's own folded program, run through lower() / run_program.
 
@@ -458,7 +496,9 @@ def run_ours(args, rank: int, world: int, device: torch.device, dist_on: bool) -
         line["scaled_sum"] = {
             "metric": "log-space einsum TFLOP/s, scaled_sum mode",
             "value": round(world * work.flops_per_step / (scaled_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
-            "ms_per_step": round(scaled_ms, 4), "workload": "the headline contraction materialized in scaled_sum",
+            "ms_per_step": round(scaled_ms, 4),
+            "workload": "the headline expression log(einsum(exp(A), exp(B))) materialized in scaled_sum (lowered: "
+                        "one log-space contraction with the exp rule's shifts)",
         }
     work = None
     torch.cuda.empty_cache()
@@ -575,6 +615,21 @@ def run_ours(args, rank: int, world: int, device: torch.device, dist_on: bool) -
             "hbm_gbs_algorithmic": round(bytes_sample * c_value / world / 1e9, 1),
             "tflops_algorithmic": round(flops_sample * c_value / world / 1e12, 2),
             "e2e_samples_per_s": round(world * args.circuit_batch / (c_e2e_ms * 1e-3), 1),
+        }
+
+    if want("circuit"):
+        # the training step (forward, backward, Adam), batch circuit_batch per GPU
+        tr = CircuitTrain(device, rank, args.circuit_batch)
+        tr_steps = max(3, args.steps // 10)
+        tr_ms = time_region(lambda record: tr.step(dist_on), tr_steps, 3, dist_on) / tr_steps
+        del tr
+        torch.cuda.empty_cache()
+        line["circuit_train"] = {
+            "metric": "circuit training samples/s (forward + backward + Adam)", "value": round(world * args.circuit_batch / (tr_ms * 1e-3), 1),
+            "unit": "samples/s", "ms_per_step": round(tr_ms, 3), "scaling": "weak",
+            "workload": f"the folded 32x32 quad-tree CP circuit, batch {args.circuit_batch} per GPU: -mean log-likelihood, "
+                        "loss.backward() through the kernels' backward passes, torch.optim.Adam on the logits"
+                        + ("; gradients averaged with one all_reduce per parameter" if dist_on else ""),
         }
 
     if want("circuit") and world > 1:

@@ -84,6 +84,15 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
             _c_i64, _c_i64, _c_i64, _c_i64, _c_ptr,  # batch, m, n, k, stream
         ],
     ),
+    "xe_logspace_gemm_shifted_strided": (
+        _c_i32,
+        [
+            _c_ptr, _c_i64, _c_i64, _c_i64, _c_ptr, _c_i64, _c_i64,  # a, strides, shift_a, its strides
+            _c_ptr, _c_i64, _c_i64, _c_i64, _c_ptr, _c_i64, _c_i64,  # b, strides, shift_b, its strides
+            _c_ptr, _c_i64, _c_i64, _c_i64,  # c, strides
+            _c_i64, _c_i64, _c_i64, _c_i64, _c_ptr,  # batch, m, n, k, stream
+        ],
+    ),
     "xe_logspace_b_prepared_size": (_c_size, [_c_i64, _c_i64, _c_i64]),
     "xe_logspace_gemm_workspace_size_prepared": (_c_size, [_c_i64, _c_i64, _c_i64, _c_i64, _c_i32, _c_i32]),
     "xe_logspace_b_prepare": (

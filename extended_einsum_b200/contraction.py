@@ -161,6 +161,82 @@ def _binary(input_strings, output_string, operands, linear, shift, sizes, a2: to
     return c.permute([grouped.index(label) for label in output_string])
 
 
+def _scaled_log_plan(format_string: str):
+    """Label plan of ``scaled_log_einsum`` (None when the einsum does not take that path).
+
+    Two operands, at least one contracted label, no label summed within one operand, and for each
+    operand a last label that is either contracted (its exp fibre runs along the contraction: one
+    shift per row of the grouped operand) or the operand's only retained non-batch label (the
+    shift is then one value per batch entry).
+    """
+    input_strings, output_string = parse_format_string(format_string)
+    if len(input_strings) != 2 or len(set(output_string)) != len(output_string):
+        return None
+    la, lb = input_strings
+    if len(set(la)) != len(la) or len(set(lb)) != len(lb) or not la or not lb:
+        return None
+    if any(label not in lb and label not in output_string for label in la) or any(
+        label not in la and label not in output_string for label in lb
+    ):
+        return None
+    batch = "".join(label for label in output_string if label in la and label in lb)
+    m_labels = "".join(label for label in output_string if label in la and label not in lb)
+    n_labels = "".join(label for label in output_string if label in lb and label not in la)
+    k_labels = "".join(label for label in la if label in lb and label not in output_string)
+    if not k_labels or any(label not in la and label not in lb for label in output_string):
+        return None
+    kinds = []
+    for labels, own in ((la, m_labels), (lb, n_labels)):
+        last = labels[-1]
+        if last in k_labels:
+            kinds.append("row")
+        elif own == last:
+            kinds.append("batch")
+        else:
+            return None
+    return input_strings, output_string, batch, m_labels, k_labels, n_labels, tuple(kinds)
+
+
+def scaled_log_einsum_supported(format_string: str) -> bool:
+    return _scaled_log_plan(format_string) is not None
+
+
+def scaled_log_einsum(format_string: str, a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """log(einsum(exp(a), exp(b))) as the scaled modes compute it, in one contraction.
+
+    In the scaled modes exp(x) becomes the pair (exp(x - m), m) with m the maximum of x's last-axis
+    fibres (translate.py:410-420); the einsum brings each operand's scale to its maximum over the
+    contracted axes (:329-340), contracts the normalised operands and renormalises the result per
+    fibre; log(n * e^s) = log(n) + s (:421-425).  The norms cancel in the log, so the value is
+    log(sum_k exp(a - sa) exp(b - sb)) + sa + sb with sa (sb) the maximum of a (b) over its
+    contracted labels and its last label: the log-space contraction with those shifts
+    (xe_logspace_gemm_shifted_strided).  ``a`` and ``b`` are the raw (log-domain) arguments of the
+    two exp instructions.
+    """
+    plan = _scaled_log_plan(format_string)
+    if plan is None:
+        raise NotImplementedError(f"einsum {format_string!r} has no fused scaled log contraction on this path")
+    (la, lb), output_string, batch, m_labels, k_labels, n_labels, kinds = plan
+    sizes = _sizes([la, lb], (a, b))
+    ag = _group(a, la, [batch, m_labels, k_labels], sizes)
+    bg = _group(b, lb, [batch, k_labels, n_labels], sizes)
+    nb, m, k = ag.shape
+    n = bg.shape[2]
+    # shift of A: per (batch, row) over k, or per batch over (m, k); strides into a (batch, m) view
+    if kinds[0] == "row":
+        sa, sa_strides = ops.logspace_shift(ag), (m, 1)
+    else:
+        sa, sa_strides = ops.logspace_shift(ag.reshape(nb, 1, m * k)), (1, 0)
+    if kinds[1] == "row":
+        sb, sb_strides = ops.logspace_shift(bg.transpose(1, 2)), (n, 1)
+    else:
+        sb, sb_strides = ops.logspace_shift(bg.reshape(nb, 1, k * n)), (1, 0)
+    c = ops.logspace_gemm_shifted_strided(ag, bg, sa, sa_strides, sb, sb_strides)
+    grouped = batch + m_labels + n_labels
+    c = c.reshape([sizes[label] for label in grouped])
+    return c.permute([grouped.index(label) for label in output_string])
+
+
 def _match_tucker(input_strings, output_string, linear):
     """(left, right, weights, fold_first, has_fold) operand roles if the einsum is a Tucker layer.
 

@@ -84,6 +84,9 @@ struct Params {
   const float* shift_a;  // [batch*M] (log A with K > kInlineShiftK); else nullptr
   const float* shift_b;  // [batch*N] for a log-domain B; nullptr when B is linear
   const float* b_planes;  // kBPlanes: the prepared B, one kPlaneBlockBytes block per (bb, nt, kb)
+  // element strides of the shift vectors: shift_a[bb * sa_sb + m * sa_sm], shift_b[bb * sb_sb + n * sb_sn]
+  // ((M, 1) and (N, 1) for one shift per row / column; a stride 0 repeats one value)
+  int64_t sa_sb, sa_sm, sb_sb, sb_sn;
   int batch, M, N, K;
   int tiles_m, tiles_n, num_tiles, num_kb;
   int c_vec;      // output rows may be written with 16-byte stores
@@ -550,7 +553,7 @@ struct BTile {
 #pragma unroll
     for (int i = 0; i < kS; ++i) {
       const int n = B_KMAJ ? n0 + (t >> 3) + 16 * i : n0 + 4 * (t % kQPR) + i;
-      shift[i] = (p.shift_b && n < p.N) ? __ldg(p.shift_b + (int64_t)bb * p.N + n) : 0.0f;
+      shift[i] = (p.shift_b && n < p.N) ? __ldg(p.shift_b + (int64_t)bb * p.sb_sb + (int64_t)n * p.sb_sn) : 0.0f;
     }
   }
 
@@ -1128,7 +1131,7 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
         a.set_row(p, bb, m);
         if (AMODE == kALog) {
           if (p.shift_a) {
-            a.shift = a.valid ? __ldg(p.shift_a + (int64_t)bb * p.M + m) : 0.0f;
+            a.shift = a.valid ? __ldg(p.shift_a + (int64_t)bb * p.sa_sb + (int64_t)m * p.sa_sm) : 0.0f;
           } else if (ASRC != kALdg) {
             // every k-block of this tile is staged (num_kb <= kAStages): scan them.  A row of
             // at most two k-blocks stays in registers (cur, nxt) and its stages are released here.
@@ -1367,7 +1370,8 @@ __global__ void __launch_bounds__(Cfg<BN, ASRC, BSRC>::kThreads, 1)
 #pragma unroll
       for (int i = 0; i < BN / 32; ++i) {
         const int c = lane + 32 * i;
-        csv[i] = (p.shift_b && n0 + c < p.N) ? __ldg(p.shift_b + (int64_t)bb * p.N + n0 + c) : 0.0f;
+        csv[i] = (p.shift_b && n0 + c < p.N) ? __ldg(p.shift_b + (int64_t)bb * p.sb_sb + (int64_t)(n0 + c) * p.sb_sn)
+                                              : 0.0f;
       }
       // -------- chunks: running[col][row] (+)= main chunk, for all but the last chunk;
       // the epilogue reads the last chunk and the correction straight from TMEM.

@@ -716,7 +716,8 @@ xe_status gemm_launch(const float* a, const float* a2, int64_t a_sb, int64_t a_s
                       const float* shift_a, const float* b, int64_t b_sb, int64_t b_sk, int64_t b_sn,
                       const float* shift_b, float* c, int64_t c_sb, int64_t c_sm, int64_t c_sn, int64_t batch, int64_t m,
                       int64_t n, int64_t k, bool shift_min, const GemmPlan& g, cudaStream_t s,
-                      bool raw_out = false, const GatherA* gather = nullptr, const float* b_planes = nullptr) {
+                      bool raw_out = false, const GatherA* gather = nullptr, const float* b_planes = nullptr,
+                      const int64_t* shift_strides = nullptr) {
   Params p{};
   p.b_planes = b_planes;
   p.a = a;
@@ -734,6 +735,16 @@ xe_status gemm_launch(const float* a, const float* a2, int64_t a_sb, int64_t a_s
   p.c_sn = c_sn;
   p.shift_a = shift_a;
   p.shift_b = shift_b;
+  p.sa_sb = m;
+  p.sa_sm = 1;
+  p.sb_sb = n;
+  p.sb_sn = 1;
+  if (shift_strides) {
+    p.sa_sb = shift_strides[0];
+    p.sa_sm = shift_strides[1];
+    p.sb_sb = shift_strides[2];
+    p.sb_sn = shift_strides[3];
+  }
   p.batch = (int)batch;
   p.M = (int)m;
   p.N = (int)n;
@@ -1005,6 +1016,25 @@ xe_status xe_logspace_gemm_shifted(const float* a, const float* a2, int64_t a_sb
   plan.inline_shift = false;
   return gemm_launch(a, a2, a_sb, a_sm, a_sk, shift_a == nullptr, shift_a, b, b_sb, b_sk, b_sn, shift_b, c, c_sb, c_sm,
                      c_sn, batch, m, n, k, false, plan, as_stream(stream));
+}
+
+xe_status xe_logspace_gemm_shifted_strided(const float* a, int64_t a_sb, int64_t a_sm, int64_t a_sk,
+                                           const float* shift_a, int64_t sa_sb, int64_t sa_sm, const float* b,
+                                           int64_t b_sb, int64_t b_sk, int64_t b_sn, const float* shift_b,
+                                           int64_t sb_sb, int64_t sb_sn, float* c, int64_t c_sb, int64_t c_sm,
+                                           int64_t c_sn, int64_t batch, int64_t m, int64_t n, int64_t k, void* stream) {
+  xe_status st = gemm_check("xe_logspace_gemm_shifted_strided", a, b, c, batch, m, n, k);
+  if (st != XE_OK) return st;
+  if (!shift_a || !shift_b)
+    return fail(XE_ERR_INVALID_ARGUMENT, "xe_logspace_gemm_shifted_strided: both operands are log-domain: shifts required");
+  if (sa_sb < 0 || sa_sm < 0 || sb_sb < 0 || sb_sn < 0)
+    return fail(XE_ERR_INVALID_ARGUMENT, "xe_logspace_gemm_shifted_strided: negative shift stride");
+  if (batch == 0 || m == 0 || n == 0) return XE_OK;
+  GemmPlan plan = plan_gemm(a, nullptr, a_sb, a_sm, a_sk, false, b, b_sb, b_sk, b_sn, batch, m, n, k);
+  plan.inline_shift = false;
+  const int64_t strides[4] = {sa_sb, sa_sm, sb_sb, sb_sn};
+  return gemm_launch(a, nullptr, a_sb, a_sm, a_sk, false, shift_a, b, b_sb, b_sk, b_sn, shift_b, c, c_sb, c_sm, c_sn,
+                     batch, m, n, k, false, plan, as_stream(stream), false, nullptr, nullptr, strides);
 }
 
 size_t xe_logspace_b_prepared_size(int64_t batch, int64_t n, int64_t k) {

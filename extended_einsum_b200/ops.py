@@ -146,6 +146,33 @@ def logspace_gemm_shifted(
     return out
 
 
+def logspace_gemm_shifted_strided(
+    a: torch.Tensor, b: torch.Tensor, shift_a: torch.Tensor, sa_strides: tuple[int, int], shift_b: torch.Tensor,
+    sb_strides: tuple[int, int], *, out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """The contraction of two log-domain operands with caller-chosen shifts
+    (xe_logspace_gemm_shifted_strided): row m of batch entry t is shifted by
+    shift_a[t * sa_strides[0] + m * sa_strides[1]], column n by shift_b[t * sb_strides[0] + n * sb_strides[1]]."""
+    _no_backward("logspace_gemm_shifted_strided", a, b)
+    device = _check_tensors("logspace_gemm_shifted_strided", a, b, shift_a, shift_b, *([out] if out is not None else []))
+    batch, m, k = a.shape
+    n = b.shape[2]
+    if b.shape[:2] != (batch, k):
+        raise ValueError(f"logspace_gemm_shifted_strided: incompatible shapes {tuple(a.shape)} and {tuple(b.shape)}")
+    for s, (st_b, st_r), rows in ((shift_a, sa_strides, m), (shift_b, sb_strides, n)):
+        if not s.is_contiguous() or (batch - 1) * st_b + (rows - 1) * st_r >= s.numel():
+            raise ValueError("logspace_gemm_shifted_strided: a shift vector is shorter than its strides address")
+    if out is None:
+        out = torch.empty((batch, m, n), device=device, dtype=torch.float32)
+    status = _lib.load().xe_logspace_gemm_shifted_strided(
+        a.data_ptr(), a.stride(0), a.stride(1), a.stride(2), shift_a.data_ptr(), sa_strides[0], sa_strides[1],
+        b.data_ptr(), b.stride(0), b.stride(1), b.stride(2), shift_b.data_ptr(), sb_strides[0], sb_strides[1],
+        out.data_ptr(), out.stride(0), out.stride(1), out.stride(2), batch, m, n, k, _stream(device),
+    )
+    _lib.check(status, "xe_logspace_gemm_shifted_strided")
+    return out
+
+
 class PreparedB:
     """A B operand prepared once (xe_logspace_b_prepare) for contractions against several A.
 

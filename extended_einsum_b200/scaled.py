@@ -31,7 +31,7 @@ import numpy as np
 import torch
 
 from . import ops
-from .contraction import linear_einsum
+from .contraction import linear_einsum, scaled_log_einsum, scaled_log_einsum_supported
 from .frontend import is_contraction_free_einsum, normalize_axis, parse_format_string
 
 SCALED_NORMS = {"scaled_sum": "sum", "scaled_max": "max", "scaled_min": "min"}
@@ -144,6 +144,14 @@ class _ScaledLowering:
         self.scale_shapes: dict[int, Shape] = {}
         self.value_shapes: list[Shape] = [tuple(s) for s in program.shapes]
         self.parameter_derived = parameter_derived
+        # exp results whose scaled pair is made only when something asks for it (position of the
+        # raw argument), and log results that a fused contraction already computed
+        self.lazy_exp: dict[int, int] = {}
+        self.fused_log: dict[int, int] = {}
+        self.uses: dict[int, list[int]] = {}
+        for index, instruction in enumerate(program.instructions):
+            for a in instruction.argument_ssa_ids:
+                self.uses.setdefault(a, []).append(program.n_inputs + index)
 
     def run(self):
         for index, instruction in enumerate(self.program.instructions):
@@ -157,9 +165,8 @@ class _ScaledLowering:
     def _raw(self, ssa: int) -> int:
         """raw = normalized * exp(log_scale), at most once (translate.py:164-171)."""
         if (ssa, "raw") not in self.positions:
-            self.positions[ssa, "raw"] = self.b.append(
-                partial(ops.elementwise, "mul_exp"), (self.positions[ssa, "normalized"], self.positions[ssa, "log_scale"])
-            )
+            normalized, log_scale = self._scaled(ssa)
+            self.positions[ssa, "raw"] = self.b.append(partial(ops.elementwise, "mul_exp"), (normalized, log_scale))
         return self.positions[ssa, "raw"]
 
     def _pair(self, normalize: Any, argument: int) -> tuple[int, int]:
@@ -168,6 +175,11 @@ class _ScaledLowering:
 
     def _scaled(self, ssa: int) -> tuple[int, int]:
         """The fibre-normalised pair of a raw value, at most once (translate.py:174-199)."""
+        if (ssa, "normalized") not in self.positions and ssa in self.lazy_exp:
+            # the exp rule (translate.py:410-420), made when first needed
+            normalized, log_scale = self._pair(partial(ops.fiber_normalize, kind="exp"), self.lazy_exp[ssa])
+            self.positions[ssa, "normalized"], self.positions[ssa, "log_scale"] = normalized, log_scale
+            return normalized, log_scale
         if (ssa, "normalized") not in self.positions:
             raw = self.positions[ssa, "raw"]
             normalized, log_scale = self._pair(partial(ops.fiber_normalize, kind=self.norm), raw)
@@ -201,12 +213,15 @@ class _ScaledLowering:
         name = op.name
         b, pos, shapes = self.b, self.positions, self.scale_shapes
         if name == "exp":
-            # translate.py:434-444: the raw argument's fibre maximum becomes the log scale
-            normalized, log_scale = self._pair(partial(ops.fiber_normalize, kind="exp"), self._raw(args[0]))
-            pos[result, "normalized"], pos[result, "log_scale"] = normalized, log_scale
+            # translate.py:410-420: the raw argument's fibre maximum becomes the log scale (the pair
+            # is made when a consumer needs it: a fused contraction takes the raw argument instead)
+            self.lazy_exp[result] = self._raw(args[0])
             shapes[result] = _fiber_scale_shape(self.value_shapes[result])
+        elif name == "log" and args[0] in self.fused_log:
+            # the contraction already produced log(n) + s (scaled_log_einsum)
+            pos[result, "raw"] = self.fused_log[args[0]]
         elif name == "log":
-            # translate.py:445-449: log(n * e^s) = log(n) + s, stored raw
+            # translate.py:421-425: log(n * e^s) = log(n) + s, stored raw
             n, s = self._scaled(args[0])
             pos[result, "raw"] = b.append(partial(ops.elementwise, "log_add"), (n, s))
         elif name == "softmax":
@@ -314,6 +329,27 @@ class _ScaledLowering:
             value_axis = normalize_axis(op.axis, len(self.value_shapes[result]))
             self.scale_shapes[result] = (*source[:scale_axis], self.value_shapes[result][value_axis], *source[scale_axis + 1 :])
 
+    def _fused_log_einsum(self, format_string: str, args: tuple[int, ...], result: int) -> bool:
+        """log(einsum(exp(x), exp(y))) as one log-space contraction (scaled_log_einsum), when both
+        operands are exp results whose pairs nothing has needed yet and the einsum's only consumer is
+        a log: the scaled pair of the product then never exists.  The value is the same function of
+        the inputs; only its rounding differs from the pair-by-pair sequence."""
+        if len(args) != 2 or any(a not in self.lazy_exp or (a, "normalized") in self.positions for a in args):
+            return False
+        if any(a in self.parameter_derived for a in args) or result == self.program.output_ssa:
+            return False
+        consumers = self.uses.get(result, [])
+        if len(consumers) != 1:
+            return False
+        consumer = self.program.instructions[consumers[0] - self.program.n_inputs]
+        if consumer.operator.name != "log" or not scaled_log_einsum_supported(format_string):
+            return False
+        if any(len(self.value_shapes[a]) != len(s) for a, s in zip(args, parse_format_string(format_string)[0])):
+            return False
+        self.fused_log[result] = self.b.append(partial(scaled_log_einsum, format_string),
+                                               (self.lazy_exp[args[0]], self.lazy_exp[args[1]]))
+        return True
+
     def _einsum(self, format_string: str, args: tuple[int, ...], result: int) -> None:
         """_append_scaled_einsum (translate.py:293-394)."""
         input_strings, output_string = parse_format_string(format_string)
@@ -322,6 +358,8 @@ class _ScaledLowering:
         b, pos = self.b, self.positions
         if result in self.parameter_derived:
             pos[result, "raw"] = b.append(partial(linear_einsum, format_string), tuple(self._raw(a) for a in args))
+            return
+        if self._fused_log_einsum(format_string, args, result):
             return
 
         operands: list[int] = []

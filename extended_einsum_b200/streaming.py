@@ -87,6 +87,10 @@ def materialize_streamed(
         in_ready[slot].record(copy_in)
         return views
 
+    # Each chunk's result stays referenced here until the last copy has completed, so no block is
+    # handed to another stream (record_stream would keep the caching allocator from reusing the
+    # blocks of one call in the next, and it then allocates fresh ones for every chunk).
+    results: list[torch.Tensor] = []
     pending = stage(0)
     for i, (lo, hi) in enumerate(bounds):
         views = pending
@@ -106,8 +110,9 @@ def materialize_streamed(
         in_free[i % 2].record(compute)
         done.record(compute)
         copy_out.wait_event(done)
-        result.record_stream(copy_out)
+        results.append(result)
         with torch.cuda.stream(copy_out):
             out[lo:hi].copy_(result.reshape(out[lo:hi].shape), non_blocking=True)
     copy_out.synchronize()
+    results.clear()
     return out

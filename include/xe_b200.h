@@ -140,6 +140,21 @@ xe_status xe_logspace_gemm_shifted(const float* a, const float* a2, int64_t a_sb
                                    float* c, int64_t c_sb, int64_t c_sm, int64_t c_sn,
                                    int64_t batch, int64_t m, int64_t n, int64_t k, void* stream);
 
+/* xe_logspace_gemm_shifted with shift vectors of any element strides: the
+ * shift of row m of batch entry t is shift_a[t*sa_sb + m*sa_sm], that of column
+ * n shift_b[t*sb_sb + n*sb_sn] (a stride of 0 repeats one value).  Both
+ * operands are log-domain.  Any per-row / per-column values are mathematically
+ * valid shifts; this is how the scaled modes' log(einsum(exp(A), exp(B))) runs
+ * as one contraction: the shift of an operand is its exp rule's fibre maximum
+ * (translate.py:410-420) brought to a common value over the contracted axes
+ * (:329-340), and log(n * e^s) = log(n) + s (:421-425) is the kernel's epilogue. */
+xe_status xe_logspace_gemm_shifted_strided(const float* a, int64_t a_sb, int64_t a_sm, int64_t a_sk,
+                                           const float* shift_a, int64_t sa_sb, int64_t sa_sm,
+                                           const float* b, int64_t b_sb, int64_t b_sk, int64_t b_sn,
+                                           const float* shift_b, int64_t sb_sb, int64_t sb_sn,
+                                           float* c, int64_t c_sb, int64_t c_sm, int64_t c_sn,
+                                           int64_t batch, int64_t m, int64_t n, int64_t k, void* stream);
+
 /* Prepared B operand.  The same B'[b,k,n] = exp(B - sB) (or a linear B as is)
  * that xe_logspace_gemm computes per 128-row tile of A, computed once and
  * stored split into TF32 hi / lo parts in the tiled, swizzled layout of the

@@ -152,12 +152,26 @@ def test_scaled_modes_lower_every_golden_program(golden_programs, mode):
         assert len(lowered.backend_calls) == len(lowered.call_arguments)
 
 
-def test_scaled_matmul_uses_one_tensor_core_contraction():
+@pytest.mark.parametrize("mode", ["scaled_sum", "scaled_max", "scaled_min"])
+def test_scaled_log_matmul_is_one_fused_contraction(mode):
+    """log(einsum(exp(A), exp(B))): the pairs of the exp results and of the product are never
+    formed, the whole expression is one log-space contraction with the exp rule's shifts."""
+    from extended_einsum_b200.contraction import scaled_log_einsum
+
+    a = xb.array(torch.zeros(4, 3))
+    b = xb.array(torch.zeros(3, 5))
+    program, _ = xb.extract_program(xb.log(xb.einsum("ik,kj->ij", xb.exp(a), xb.exp(b))), mode)
+    fns = _fns(xb.lower(program))
+    assert len(fns) == 1 and getattr(fns[0], "func", None) is scaled_log_einsum
+
+
+def test_scaled_matmul_without_log_uses_one_tensor_core_contraction():
+    """Without the log the product's pair is the output: the pair-by-pair sequence, one contraction."""
     from extended_einsum_b200.contraction import linear_einsum
 
     a = xb.array(torch.zeros(4, 3))
     b = xb.array(torch.zeros(3, 5))
-    program, _ = xb.extract_program(xb.log(xb.einsum("ik,kj->ij", xb.exp(a), xb.exp(b))), "scaled_sum")
+    program, _ = xb.extract_program(xb.einsum("ik,kj->ij", xb.exp(a), xb.exp(b)), "scaled_sum")
     fns = _fns(xb.lower(program))
     einsums = [f for f in fns if getattr(f, "func", None) is linear_einsum]
     assert len(einsums) == 1 and einsums[0].args == ("ik,kj->ij",)
