@@ -222,15 +222,19 @@ def scaled_log_einsum(format_string: str, a: torch.Tensor, b: torch.Tensor) -> t
     bg = _group(b, lb, [batch, k_labels, n_labels], sizes)
     nb, m, k = ag.shape
     n = bg.shape[2]
-    # shift of A: per (batch, row) over k, or per batch over (m, k); strides into a (batch, m) view
+    # shift of A: per (batch, row) over k, or per batch over (m, k) -- the row maxima, then their
+    # maximum (max is exact: the same value as one pass, with the rows' parallelism); strides
+    # index a (batch, m) view
+    sa = ops.logspace_shift(ag)
     if kinds[0] == "row":
-        sa, sa_strides = ops.logspace_shift(ag), (m, 1)
+        sa_strides = (m, 1)
     else:
-        sa, sa_strides = ops.logspace_shift(ag.reshape(nb, 1, m * k)), (1, 0)
+        sa, sa_strides = ops.logspace_shift(sa.view(nb, 1, m)), (1, 0)
+    sb = ops.logspace_shift(bg.transpose(1, 2))
     if kinds[1] == "row":
-        sb, sb_strides = ops.logspace_shift(bg.transpose(1, 2)), (n, 1)
+        sb_strides = (n, 1)
     else:
-        sb, sb_strides = ops.logspace_shift(bg.reshape(nb, 1, k * n)), (1, 0)
+        sb, sb_strides = ops.logspace_shift(sb.view(nb, 1, n)), (1, 0)
     c = ops.logspace_gemm_shifted_strided(ag, bg, sa, sa_strides, sb, sb_strides)
     grouped = batch + m_labels + n_labels
     c = c.reshape([sizes[label] for label in grouped])
