@@ -144,11 +144,18 @@ class QuadTreeCircuit:
 
 
 class CircuitForward:
-    """Forward pass of a QuadTreeCircuit on the current CUDA device."""
+    """Forward pass of a QuadTreeCircuit on the current CUDA device.
 
-    def __init__(self, circuit: QuadTreeCircuit, parameters: dict[str, object], shift: str = "max") -> None:
+    With gradients enabled and the state table in use (and K = 64), the call is one autograd node
+    whose backward runs the fused layer backward kernels (xe_cp_layer_backward and friends);
+    ``fused_backward=False`` keeps the per-operation backward of each call instead.
+    """
+
+    def __init__(self, circuit: QuadTreeCircuit, parameters: dict[str, object], shift: str = "max",
+                 fused_backward: bool = True) -> None:
         self.circuit = circuit
         self.shift = shift
+        self.fused_backward = fused_backward
         self.categorical = parameters["categorical"]
         self.levels = list(parameters["levels"])
         self.root = parameters["root"]
@@ -157,6 +164,10 @@ class CircuitForward:
 
     def __call__(self, pixels: torch.Tensor) -> torch.Tensor:
         """Log-likelihoods (B, 1) of uint8 pixels (B, variables)."""
+        params = (self.categorical, self.root, *self.levels)
+        if (self.fused_backward and ops._needs_grad(*params) and self.circuit.uses_state_table(pixels.shape[0])
+                and self.circuit.units == 64 and self.circuit.states <= 256):
+            return _CircuitFunction.apply(self, pixels, *params)
         table = ops.softmax(self.categorical, 1, log_output=True)
         state_table = self.circuit.uses_state_table(pixels.shape[0])
         y = None
@@ -179,6 +190,79 @@ class CircuitForward:
         b_root = w_root.t().unsqueeze(0)  # (1, K, 1)
         ll = ops.logspace_gemm(y[0:1], b_root, a2=y[1:2], b_linear=True, shift=self.shift)
         return ll[0]
+
+
+def _softmax_grad(y: torch.Tensor, dy: torch.Tensor, axis: int) -> torch.Tensor:
+    """dx of y = softmax(x) over ``axis``: y (dy - sum(dy y))."""
+    dot = ops.reduce(ops.elementwise("mul", dy, y), (axis,), "sum", keepdims=True)
+    return ops.elementwise("mul", y, ops.elementwise("sub", dy, dot))
+
+
+class _CircuitFunction(torch.autograd.Function):
+    """The state-table forward of CircuitForward as one autograd node.
+
+    Backward, from the root down (the shifts are stop_gradients, translate.py:727-740):
+      root        elementwise: r = G exp(h - ll) for h the sum of the two top halves, dh = r w_root,
+                  dw_root = sum_b r;
+      levels >= 2 xe_cp_layer_backward: dA of both halves and dw from one pass over the layer's
+                  input halves, output and gradient, the gradient of level l's output being
+                  level l+1's dA read for both halves (fold f reads f mod F_{l+1});
+      level 1     xe_cp_layer_backward_gather_pair over the state table, then
+                  xe_state_table_pair_grad: the gradient of the table;
+      level 0     xe_cp_layer_backward over the categorical log-table (M = states);
+      parameters  the softmax / log-softmax backward of the weights and the categorical logits.
+    """
+
+    @staticmethod
+    def forward(ctx, fwd: "CircuitForward", pixels, categorical, root, *levels):
+        shift = fwd.shift
+        table = ops.softmax(categorical, 1, log_output=True)
+        weights = [ops.softmax(logits, 2) for logits in levels]
+        ys = [ops.logspace_gemm(table, weights[0].permute(0, 2, 1), b_linear=True, shift=shift)]
+        ys.append(ops.logspace_gemm_gather_pair(ys[0], pixels, fwd.var_of_fold, weights[1].permute(0, 2, 1),
+                                                b_linear=True, shift=shift))
+        for w in weights[2:]:
+            y = ys[-1]
+            half = y.shape[0] // 2
+            ys.append(ops.logspace_gemm(y[:half], w.permute(0, 2, 1), a2=y[half:], b_linear=True, shift=shift))
+        w_root = ops.softmax(root, 1)
+        b_root = w_root.t().unsqueeze(0)
+        top = ys[-1]
+        ll = ops.logspace_gemm(top[0:1], b_root, a2=top[1:2], b_linear=True, shift=shift)
+        ctx.fwd = fwd
+        ctx.save_for_backward(pixels, table, w_root, ll, *weights, *ys)
+        ctx.n_levels = len(levels)
+        return ll[0]
+
+    @staticmethod
+    def backward(ctx, g_ll):
+        fwd = ctx.fwd
+        shift = fwd.shift
+        saved = ctx.saved_tensors
+        pixels, table, w_root, ll = saved[:4]
+        n = ctx.n_levels
+        weights, ys = saved[4:4 + n], saved[4 + n:]
+        top = ys[-1]
+        # root: ll[b] = log sum_k exp(h[b,k]) w[k] (shifted), h = top[0] + top[1]; with
+        # r[b,k] = g[b] exp(h[b,k] - ll[b]): dh = r * w, dw = sum_b r
+        h = ops.elementwise("add", top[0], top[1])
+        r = ops.elementwise("rescale", g_ll.contiguous(), h, ll[0])
+        d_root = _softmax_grad(w_root, ops.reduce(r, (0,), "sum", keepdims=True), 1)
+        g = ops.elementwise("mul", r, w_root).unsqueeze(0)  # (1, B, K): the gradient of both top halves
+        d_levels = [None] * n
+        for level in range(n - 1, 1, -1):
+            y_in = ys[level - 1]
+            half = y_in.shape[0] // 2
+            g, dw = ops.cp_layer_backward(y_in[:half], ys[level], g, weights[level], a2=y_in[half:], shift=shift)
+            d_levels[level] = _softmax_grad(weights[level], dw, 2)
+        g, dw = ops.cp_layer_backward_gather_pair(ys[0], pixels, fwd.var_of_fold, ys[1], g, weights[1], shift=shift)
+        d_levels[1] = _softmax_grad(weights[1], dw, 2)
+        g = ops.state_table_pair_grad(g, pixels, fwd.var_of_fold, table.shape[1])
+        d_table, dw = ops.cp_layer_backward(table, ys[0], g, weights[0], shift=shift)
+        d_levels[0] = _softmax_grad(weights[0], dw, 2)
+        total = ops.reduce(d_table, (1,), "sum", keepdims=True)
+        d_categorical = ops.elementwise("sub", d_table, ops.elementwise("mul_exp", total, table))
+        return None, None, d_categorical, d_root, *d_levels
 
 
 def demo_circuit_program(xe, height: int, width: int, units: int, batch: int, stability_mode: str = "logspace_max",

@@ -1,0 +1,672 @@
+// cp_backward.cuh — the backward pass of the folded CP sum layer (K = N = 64), and the gradient
+// of the state table read by the second layer of a circuit.
+//
+// The forward (cp_layer.cuh, lse_gemm.cuh) is
+//   Y[f,m,o] = log( sum_k exp(X[f,m,k] - s) w[f,o,k] ) + s,   s = max_k (or min_k) X[f,m,:],
+// with X = A, A + A2 (the folded Hadamard product fused, translate.py:706-718) or the sum of two
+// state-table rows picked by pixel values, and w (F, O, K) the layer's linear weights (the softmax
+// of its logits; the contraction's B operand is w[f]^T).  The reference differentiates its torch
+// executor's calls, in which the shift is a stop_gradient (backend_translation/translate.py:727-740).
+// With G = dL/dY:
+//   A'[m,k] = exp(X[m,k] - s),   V[m,o] = G[m,o] exp(s - Y[m,o])      (V = G / P)
+//   dX[m,k] = A'[m,k] sum_o V[m,o] w[o,k],   dw[o,k] = sum_m V[m,o] A'[m,k],
+// dX being the gradient of A and of A2 alike.  cpb_kernel computes both from one read of X, Y, G:
+//
+//  * a tile is 64 rows of one fold; each CTA takes a contiguous range of tiles and two warp pairs
+//    (warps 0-1 and 2-3, a thread per row) own alternate tiles;
+//  * tiles rotate through three 64 KB stages, so the loads of the next two tiles are in flight
+//    while one is computed; a stage receives the tile's rows of X (two tensors for a pair source),
+//    Y and G by TMA (tile::gather4 for table rows);
+//  * each thread reads its row, forms A' and V, writes V as TF32 hi / lo into its TMEM lane, and
+//    writes the operands of the weight product in place of its own row of the inputs: S (A'^T hi
+//    over A'^T lo, M = 128) and V^T hi / lo (N = 64), MN-major with the tile's rows as K, so that
+//    a thread's k-row is the 128-byte row its inputs came in and no other thread touches it;
+//  * one thread issues dX' = V w with A = V from TMEM (M = 128 lanes, of which the pair's 64 are
+//    its rows; split TF32 over w^T hi / lo, three products per k-step) and the weight product
+//    D_B[(h,k), o] = sum over the tile's rows of S[(h,k), m] (V^T hi + V^T lo)[o, m];
+//  * the pair's epilogue stores dX = dX' * A' from registers; a drain group (warps 4-7, one TMEM
+//    lane quarter each) adds every tile's D_B into fp32 registers, rounding to nearest (the tensor
+//    core's accumulator truncates, so it restarts with every tile), and writes the two halves
+//    h = 0, 1 of its sums to a workspace slot of the fold when its range leaves the fold;
+//  * the load warp splits w^T into TF32 hi / lo from registers that it fills a fold ahead;
+//  * cpb_reduce_kernel adds the slots of each fold in a fixed order, so dw is deterministic.
+//
+// table_grad_pair_kernel: the second layer's X is T[f, x_m] + T[f + pair, x'_m] for a state
+// table T (2F, states, 64) and pixel values x_m, x'_m of the variables of folds f and f + pair;
+// dT[t, s, :] is the sum of dX[f, m, :] over the rows m whose pixel selects state s of table fold
+// t (the backward of the gather).  One CTA per fold f of dX; warp w owns the states s with
+// s % 16 == w and adds its rows in increasing m, so the sums are deterministic.
+#pragma once
+
+#include "cp_layer.cuh"
+
+namespace xe {
+namespace cpb {
+
+using namespace gemm;
+using cp::bulk_commit;
+using cp::bulk_wait_all;
+using cp::bulk_wait_read;
+using cp::tma_store_3d;
+
+// Per-tile event times of CTA 0 (trace builds only): pair warps 0-5, MMA 6-9, loads 10, drain 11-12.
+#define XE_CPB_TRACE(n, ev) XE_TILE_TRACE(n, ev)
+
+constexpr int kRows = 64;  // rows per tile
+constexpr int kThreads = 320;
+constexpr int kDrainWarp0 = 4;
+constexpr int kMmaWarp = 8;
+constexpr int kProducerWarp = 9;
+constexpr int kBlock = 32 * 32 * 4;       // 32 rows x 32 fp32 (4 KB)
+constexpr int kRegion = 8 * kBlock;       // one warp's 32 rows of X1, X2, Y, G (two column halves each)
+constexpr int kStage = 2 * kRegion;       // one tile
+constexpr int kStages = 3;
+constexpr int kWPlane = 2 * 64 * 32 * 4;  // w^T hi or lo: two o-blocks of [64 k][32 o], K-major
+constexpr int kOffStage = 0;
+constexpr int kOffWHi = kOffStage + kStages * kStage;
+constexpr int kOffWLo = kOffWHi + kWPlane;
+constexpr int kOffBar = kOffWLo + kWPlane;
+constexpr int kSmemBytes = 1024 + kOffBar + 256;
+static_assert(kSmemBytes <= 232448, "shared memory");
+// Blocks of a warp's region: the inputs, tensor t (0 X1, 1 X2, 2 Y, 3 G) and column half c at
+// (2t + c) kBlock (128-byte swizzle, K-major: row m at m * 128); once read, the MN-major operands
+// of the weight product in their place (32-element MN blocks of 4 KB, k-row m at m * 128):
+// S (four MN blocks) over X1 / X2, V^T hi (two) over Y, V^T lo over G.
+constexpr int kOffS = 0, kOffVtHi = 4 * kBlock, kOffVtLo = 6 * kBlock;
+// TMEM columns of pair p (base 256 p): V hi, V lo (the A operand of dX'), dX', D_B
+constexpr uint32_t kTmVHi = 0, kTmVLo = 64, kTmDX = 128, kTmDB = 192;
+
+enum Source : int { kDense = 0, kDense2 = 1, kGather2 = 2 };
+
+struct Params {
+  const float* w;  // (folds, 64 o, 64 k)
+  float* dx;       // (folds, M, 64)
+  int folds, M, tiles_m, num_tiles;
+  int g_folds;  // G[f] = g[f % g_folds]: the next layer's dX is the gradient of both halves of its input
+  int shift_min;
+  int pieces;       // workspace slots per fold
+  float* partials;  // [folds][pieces][2][64 o][64 k]
+  // kGather2: X[f,m,:] = T[f, x_m, :] + T[f + pair, x'_m, :], x_m = pixels[m, var[f]]
+  const uint8_t* pixels;
+  const int32_t* var;  // nullptr: variable = table fold
+  int64_t pixel_stride;
+  int states, pair;
+};
+
+// The CTA whose range holds tile t when num_tiles tiles are split into `grid` contiguous ranges
+// [floor(num_tiles c / grid), floor(num_tiles (c + 1) / grid)): the largest c with
+// num_tiles c < (t + 1) grid.
+__host__ __device__ __forceinline__ int cta_of_tile(int64_t t, int64_t num_tiles, int64_t grid) {
+  return (int)(((t + 1) * grid - 1) / num_tiles);
+}
+
+__device__ __forceinline__ void sts_f32(uint32_t addr, float v) {
+  asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+
+__device__ __forceinline__ float lds_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr));
+  return v;
+}
+
+__device__ __forceinline__ float2 lds_v2(uint32_t addr) {
+  float2 v;
+  asm volatile("ld.shared.v2.f32 {%0,%1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr));
+  return v;
+}
+
+// Byte offset of element (row, e) of a K-major [rows][32] fp32 tile, 128-byte swizzle.
+__device__ __forceinline__ uint32_t kmajor_elem(int row, int e) { return kmajor_off(row, e >> 2) + ((e & 3) << 2); }
+
+template <int SRC>
+__global__ void __launch_bounds__(kThreads, 1)
+    cpb_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtensorMap tmap_x1,
+               const __grid_constant__ CUtensorMap tmap_x2, const __grid_constant__ CUtensorMap tmap_y,
+               const __grid_constant__ CUtensorMap tmap_g) {
+  constexpr bool PAIR = SRC != kDense;
+  // bytes landing in a stage per tile: 64 rows x 64 fp32 of X1 (and X2), Y and G
+  constexpr uint32_t kStageTx = (PAIR ? 4 : 3) * kRows * 64 * 4;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  const uint32_t smem_base = smem_u32(smem);
+  uint64_t* bars = (uint64_t*)(smem + kOffBar);
+  uint64_t* stage_full = bars;               // [kStages] the tile's inputs have landed
+  uint64_t* stage_free = bars + kStages;     // [kStages] the weight product has read the stage
+  uint64_t* ready = bars + 2 * kStages;      // [2] the pair's V (TMEM) and S, V^T (stage) written
+  uint64_t* dx_full = ready + 2;             // [2] dX' complete
+  uint64_t* db_full = dx_full + 2;           // [2] D_B complete
+  uint64_t* db_free = db_full + 2;           // [2] D_B drained
+  uint64_t* w_ready = db_free + 2;           // the fold's w^T hi / lo split
+  uint64_t* w_free = w_ready + 1;            // the fold's last dX' product done with them
+  uint64_t* drain = w_free + 1;
+  uint32_t* tmem_slot = (uint32_t*)(drain + 1);
+  volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+  ArmedCopies* stage_copies = (ArmedCopies*)(tmem_slot + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&stage_full[i], 1);
+      mbar_init(&stage_free[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&ready[i], 2);
+      mbar_init(&dx_full[i], 1);
+      mbar_init(&db_full[i], 1);
+      mbar_init(&db_free[i], 4);
+    }
+    mbar_init(w_ready, 1);
+    mbar_init(w_free, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    *stage_copies = ArmedCopies{0u, 0u};
+    fence_mbarrier_init();
+  }
+  if (warp == kMmaWarp) tmem_alloc<512>(tmem_slot);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int first = (int)(((int64_t)p.num_tiles * blockIdx.x) / gridDim.x);
+  const int last = (int)(((int64_t)p.num_tiles * (blockIdx.x + 1)) / gridDim.x);
+
+  if (warp < kDrainWarp0) {
+    // ------------------------------------------------------------ warp pairs (thread = tile row)
+    const int pair = warp >> 1;
+    const int wq = warp & 1;
+    const uint32_t tp = tmem + pair * 256 + ((uint32_t)(warp * 32) << 16);
+    const bool is_min = p.shift_min != 0;
+    const uint32_t roff = lane * 128;
+    bool ok = true;
+    for (int i = first + pair; i < last && ok; i += 2) {
+      const int n = i - first;
+      const int j = n >> 1;
+      const int st = n % kStages;
+      const int f = i / p.tiles_m;
+      const int mt = i - f * p.tiles_m;
+      const int row = mt * kRows + wq * 32 + lane;
+      const bool valid = row < p.M;
+      const uint32_t region = smem_base + kOffStage + st * kStage + wq * kRegion;
+      const bool tr = wq == 0 && lane == 0;
+      if (tr) XE_CPB_TRACE(n, 0);
+      if (!mbar_wait_warp(&stage_full[st], (n / kStages) & 1, kSiteAStaged, abort_flag)) {
+        ok = false;
+        break;
+      }
+      if (tr) XE_CPB_TRACE(n, 1);
+      float a[64];
+#pragma unroll
+      for (int c = 0; c < 2; ++c)
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const uint32_t off = roff + ((q ^ (lane & 7)) << 4);
+          float4 v = lds_v4(region + c * kBlock + off);
+          if (PAIR) {
+            const float4 u = lds_v4(region + (2 + c) * kBlock + off);
+            v.x += u.x;
+            v.y += u.y;
+            v.z += u.z;
+            v.w += u.w;
+          }
+          a[32 * c + 4 * q] = v.x;
+          a[32 * c + 4 * q + 1] = v.y;
+          a[32 * c + 4 * q + 2] = v.z;
+          a[32 * c + 4 * q + 3] = v.w;
+        }
+      float e0 = is_min ? INFINITY : -INFINITY, e1 = e0, e2 = e0, e3 = e0;
+#pragma unroll
+      for (int k = 0; k < 64; k += 4) {
+        e0 = extreme(e0, a[k], is_min);
+        e1 = extreme(e1, a[k + 1], is_min);
+        e2 = extreme(e2, a[k + 2], is_min);
+        e3 = extreme(e3, a[k + 3], is_min);
+      }
+      const float s = valid ? extreme(extreme(e0, e1, is_min), extreme(e2, e3, is_min), is_min) : 0.0f;
+      // A' and its S columns (M = k for hi, 64 + k for lo), in this thread's k-row of blocks 0-3
+      // (its X rows, read above)
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        float4 hi, lo;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) a[4 * q + t] = valid ? exp_shifted(a[4 * q + t], s) : 0.0f;
+        split_rn(a[4 * q], hi.x, lo.x);
+        split_rn(a[4 * q + 1], hi.y, lo.y);
+        split_rn(a[4 * q + 2], hi.z, lo.z);
+        split_rn(a[4 * q + 3], hi.w, lo.w);
+        sts_v4(region + kOffS + mnmajor_off(lane, q), hi);
+        sts_v4(region + kOffS + mnmajor_off(lane, 16 + q), lo);
+      }
+      // V = G exp(s - Y) by column halves: the half's Y and G are read whole before its V^T
+      // chunks (MN block c of V^T hi / lo, this thread's k-row) replace them
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        float v[32];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const uint32_t off = roff + ((q ^ (lane & 7)) << 4);
+          const float4 yv = lds_v4(region + (4 + c) * kBlock + off);
+          const float4 gv = lds_v4(region + (6 + c) * kBlock + off);
+          v[4 * q] = valid ? gv.x * exp_shifted(s, yv.x) : 0.0f;
+          v[4 * q + 1] = valid ? gv.y * exp_shifted(s, yv.y) : 0.0f;
+          v[4 * q + 2] = valid ? gv.z * exp_shifted(s, yv.z) : 0.0f;
+          v[4 * q + 3] = valid ? gv.w * exp_shifted(s, yv.w) : 0.0f;
+        }
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          float hi[16], lo[16];
+#pragma unroll
+          for (int t = 0; t < 16; ++t) split_rn(v[16 * hh + t], hi[t], lo[t]);
+          tmem_st16(tp + kTmVHi + 32 * c + 16 * hh, hi);
+          tmem_st16(tp + kTmVLo + 32 * c + 16 * hh, lo);
+#pragma unroll
+          for (int qq = 0; qq < 4; ++qq) {
+            const int oq = 8 * c + 4 * hh + qq;
+            sts_v4(region + kOffVtHi + mnmajor_off(lane, oq), make_float4(hi[4 * qq], hi[4 * qq + 1], hi[4 * qq + 2], hi[4 * qq + 3]));
+            sts_v4(region + kOffVtLo + mnmajor_off(lane, oq), make_float4(lo[4 * qq], lo[4 * qq + 1], lo[4 * qq + 2], lo[4 * qq + 3]));
+          }
+        }
+      }
+      tmem_wait_st();
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ready[pair]);
+      if (tr) XE_CPB_TRACE(n, 2);
+      // -------- epilogue: dX = dX' * A', this thread's row
+      if (!mbar_wait_warp(&dx_full[pair], j & 1, kSiteDrainChunk, abort_flag)) {
+        ok = false;
+        break;
+      }
+      if (tr) XE_CPB_TRACE(n, 3);
+      tc_fence_after();
+      float* dst = p.dx + ((int64_t)f * p.M + (valid ? row : 0)) * 64;
+#pragma unroll
+      for (int sl = 0; sl < 2; ++sl) {
+        float d[32];
+        tmem_ld16(tp + kTmDX + 32 * sl, d);
+        tmem_ld16(tp + kTmDX + 32 * sl + 16, d + 16);
+        tmem_wait_ld();
+        if (valid) {
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            stg_v4(dst + 32 * sl + 4 * c, make_float4(d[4 * c] * a[32 * sl + 4 * c], d[4 * c + 1] * a[32 * sl + 4 * c + 1],
+                                                      d[4 * c + 2] * a[32 * sl + 4 * c + 2],
+                                                      d[4 * c + 3] * a[32 * sl + 4 * c + 3]));
+        }
+      }
+      // dX' has been read: the pair's next V (and its product) may replace it
+      tc_fence_before();
+      if (tr) XE_CPB_TRACE(n, 4);
+    }
+  } else if (warp < kMmaWarp) {
+    // ------------------------------------------------------------ D_B drain (lane = row (h, k))
+    const int q = warp - kDrainWarp0;
+    const int h = q >> 1;
+    const int k = 32 * (q & 1) + lane;
+    const uint32_t lane_bits = (uint32_t)(q * 32) << 16;
+    float run[64];
+#pragma unroll
+    for (int o = 0; o < 64; ++o) run[o] = 0.0f;
+    int cur = first < last ? first / p.tiles_m : 0;
+    // this CTA's partial sums of fold f into its slot (slot 0 for the fold's first CTA)
+    auto flush = [&](int f) {
+      const int piece = (int)blockIdx.x - cta_of_tile((int64_t)f * p.tiles_m, p.num_tiles, gridDim.x);
+      float* dst = p.partials + (((int64_t)f * p.pieces + piece) * 2 + h) * 4096 + k;
+#pragma unroll
+      for (int o = 0; o < 64; ++o) {
+        dst[o * 64] = run[o];
+        run[o] = 0.0f;
+      }
+    };
+    bool ok = true;
+    for (int i = first, n = 0; i < last; ++i, ++n) {
+      const int pair = n & 1;
+      const int j = n >> 1;
+      const int f = i / p.tiles_m;
+      if (f != cur) {
+        flush(cur);
+        cur = f;
+      }
+      if (!mbar_wait_warp(&db_full[pair], j & 1, kSiteDrainChunk, abort_flag)) {
+        ok = false;
+        break;
+      }
+      if (q == 0 && lane == 0) XE_CPB_TRACE(n, 11);
+      tc_fence_after();
+      const uint32_t t = tmem + pair * 256 + kTmDB + lane_bits;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        float d[32];
+        tmem_ld16(t + 32 * c, d);
+        tmem_ld16(t + 32 * c + 16, d + 16);
+        tmem_wait_ld();
+#pragma unroll
+        for (int o = 0; o < 32; ++o) run[32 * c + o] += d[o];
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&db_free[pair]);
+      if (q == 0 && lane == 0) XE_CPB_TRACE(n, 12);
+    }
+    if (ok && first < last) flush(cur);
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------------------ MMA issue
+    if (lane == 0) {
+      constexpr uint32_t idesc_x = idesc_tf32(kBM, 64, false, false);  // V (TMEM) x w^T (K-major)
+      constexpr uint32_t idesc_w = idesc_tf32(kBM, 64, true, true);    // S x V^T, both MN-major
+      int fold_count = 0;
+      for (int i = first, n = 0; i < last; ++i, ++n) {
+        const int pair = n & 1;
+        const int j = n >> 1;
+        const int st = n % kStages;
+        const int f = i / p.tiles_m;
+        if (i == first || f != (i - 1) / p.tiles_m) {
+          if (!mbar_wait(w_ready, fold_count & 1, kSiteMmaChunk, abort_flag)) break;
+          ++fold_count;
+        }
+        if (!mbar_wait(&ready[pair], j & 1, kSiteMmaFull, abort_flag)) break;
+        XE_CPB_TRACE(n, 6);
+        tc_fence_after();
+        const uint32_t tb = tmem + pair * 256;
+        // dX'[m, k] = sum_o V[m, o] w[o, k]: 8 k-steps over o, hi*hi + hi*lo + lo*hi
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t boff = (kk >> 2) * (64 * 128) + (kk & 3) * 32;
+          const uint64_t dh = smem_desc(smem_base + kOffWHi + boff, 16, 1024, kLayoutSW128);
+          const uint64_t dl = smem_desc(smem_base + kOffWLo + boff, 16, 1024, kLayoutSW128);
+          umma_tf32_ts(tb + kTmDX, tb + kTmVHi + 8 * kk, dh, idesc_x, kk != 0);
+          umma_tf32_ts(tb + kTmDX, tb + kTmVHi + 8 * kk, dl, idesc_x, 1);
+          umma_tf32_ts(tb + kTmDX, tb + kTmVLo + 8 * kk, dh, idesc_x, 1);
+        }
+        umma_commit(&dx_full[pair]);
+        XE_CPB_TRACE(n, 7);
+        // the fold's last tile: its w^T split may be replaced once these products are done
+        if (i + 1 < last && (i + 1) / p.tiles_m != f) umma_commit(w_free);
+        // the weight product, once the previous D_B of the pair is drained: per warp of the pair
+        // (32 rows, MN-major k-rows) four 8-row k-steps of 1 KB
+        if (j > 0 && !mbar_wait(&db_free[pair], (j - 1) & 1, kSiteMmaCorr, abort_flag)) break;
+        XE_CPB_TRACE(n, 8);
+        tc_fence_after();
+        const uint32_t stage = smem_base + kOffStage + st * kStage;
+#pragma unroll
+        for (int w = 0; w < 2; ++w)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint32_t reg = stage + w * kRegion + kk * 1024;
+            const uint64_t da = smem_desc(reg + kOffS, 4096, 512, kLayoutSW128Base32B);
+            const uint64_t dvh = smem_desc(reg + kOffVtHi, 4096, 512, kLayoutSW128Base32B);
+            const uint64_t dvl = smem_desc(reg + kOffVtLo, 4096, 512, kLayoutSW128Base32B);
+            umma_tf32(tb + kTmDB, da, dvh, idesc_w, (w | kk) != 0);
+            umma_tf32(tb + kTmDB, da, dvl, idesc_w, 1);
+          }
+        umma_commit(&stage_free[st]);
+        umma_commit(&db_full[pair]);
+        XE_CPB_TRACE(n, 9);
+      }
+      // All issued MMAs must finish before TMEM is released.
+      umma_commit(drain);
+      mbar_wait(drain, 0, kSiteGemmDrain, abort_flag, /*honor_abort=*/false);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ loads and the weight split
+    // This lane's 32 chunks of w^T: chunk c = lane + 32 i holds (k = c & 63, o = 4 (c >> 6) .. + 3),
+    // read from w (o, k) a fold ahead (coalesced over k), split into w^T hi / lo at the fold's start.
+    float4 wr[32];
+    auto load_w = [&](int f) {
+      const float* wf = p.w + (int64_t)f * 4096;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int kr = lane + 32 * (i & 1), o = 4 * (i >> 1);
+        wr[i] = make_float4(__ldg(wf + o * 64 + kr), __ldg(wf + (o + 1) * 64 + kr), __ldg(wf + (o + 2) * 64 + kr),
+                            __ldg(wf + (o + 3) * 64 + kr));
+      }
+    };
+    if (first < last) load_w(first / p.tiles_m);
+    bool ok = true;
+    int fold_count = 0;
+    for (int i = first, n = 0; i < last && ok; ++i, ++n) {
+      const int f = i / p.tiles_m;
+      const int st = n % kStages;
+      const int mt = i - f * p.tiles_m;
+      bool armed = true;
+      if (lane == 0) {
+        armed = mbar_wait(&stage_free[st], ((n / kStages) & 1) ^ 1, kSiteProducer, abort_flag);
+        if (armed) {
+          XE_CPB_TRACE(n, 10);
+          mbar_expect_tx(&stage_full[st], kStageTx);
+          stage_copies->note(st, n / kStages);
+        }
+      }
+      if (__shfl_sync(0xffffffffu, armed ? 1 : 0, 0) == 0) {  // the warp leaves together
+        ok = false;
+        break;
+      }
+      const uint32_t stage = smem_base + kOffStage + st * kStage;
+      if (SRC == kGather2) {
+        // lane l: table fold f (l < 16) or f + pair, rows 4 (l & 15) .. + 3 of the tile; a row
+        // past M reads its table fold's first row (the pair threads mask it)
+        const int h = lane >> 4, grp = lane & 15;
+        const int64_t tf = (int64_t)f + (int64_t)h * p.pair;
+        int64_t var = p.var ? (int64_t)__ldg(p.var + tf) : tf;
+        if (var < 0 || var >= p.pixel_stride) {
+          record_bad_index(kSiteGemmGatherState);
+          var = 0;
+        }
+        int rows[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const int m = mt * kRows + 4 * grp + t;
+          int sv = m < p.M ? (int)__ldg(p.pixels + (int64_t)m * p.pixel_stride + var) : 0;
+          if (sv >= p.states) {
+            record_bad_index(kSiteGemmGatherState);
+            sv = p.states - 1;
+          }
+          rows[t] = (int)(tf * p.states + sv);
+        }
+        const uint32_t dst = stage + (grp >> 3) * kRegion + (2 * h) * kBlock + (grp & 7) * 512;
+        tma_gather4(dst, &tmap_x1, 0, rows[0], rows[1], rows[2], rows[3], &stage_full[st]);
+        tma_gather4(dst + kBlock, &tmap_x1, 32, rows[0], rows[1], rows[2], rows[3], &stage_full[st]);
+      }
+      if (lane == 0) {
+        const int gz = f % p.g_folds;
+#pragma unroll
+        for (int w = 0; w < 2; ++w) {
+          const uint32_t reg = stage + w * kRegion;
+          const int r0 = mt * kRows + w * 32;
+          if (SRC != kGather2) {
+            tma_load_3d(reg, &tmap_x1, 0, r0, f, &stage_full[st]);
+            tma_load_3d(reg + kBlock, &tmap_x1, 32, r0, f, &stage_full[st]);
+            if (PAIR) {
+              tma_load_3d(reg + 2 * kBlock, &tmap_x2, 0, r0, f, &stage_full[st]);
+              tma_load_3d(reg + 3 * kBlock, &tmap_x2, 32, r0, f, &stage_full[st]);
+            }
+          }
+          tma_load_3d(reg + 4 * kBlock, &tmap_y, 0, r0, f, &stage_full[st]);
+          tma_load_3d(reg + 5 * kBlock, &tmap_y, 32, r0, f, &stage_full[st]);
+          tma_load_3d(reg + 6 * kBlock, &tmap_g, 0, r0, gz, &stage_full[st]);
+          tma_load_3d(reg + 7 * kBlock, &tmap_g, 32, r0, gz, &stage_full[st]);
+        }
+      }
+      __syncwarp();
+      if (i == first || f != (i - 1) / p.tiles_m) {
+        // the fold's first tile: once the previous fold's dX' products are done with w^T, split
+        // this fold's w (in registers) into it, then fetch the next fold's
+        bool wfree = true;
+        if (lane == 0 && fold_count > 0) wfree = mbar_wait(w_free, (fold_count - 1) & 1, kSiteProducer, abort_flag);
+        if (__shfl_sync(0xffffffffu, wfree ? 1 : 0, 0) == 0) {
+          ok = false;
+          break;
+        }
+#pragma unroll
+        for (int i2 = 0; i2 < 32; ++i2) {
+          const int kr = lane + 32 * (i2 & 1), oc = i2 >> 1;
+          float4 hi, lo;
+          split_rn(wr[i2].x, hi.x, lo.x);
+          split_rn(wr[i2].y, hi.y, lo.y);
+          split_rn(wr[i2].z, hi.z, lo.z);
+          split_rn(wr[i2].w, hi.w, lo.w);
+          const uint32_t dst = (oc >> 3) * (64 * 128) + kmajor_off(kr, oc & 7);
+          sts_v4(smem_base + kOffWHi + dst, hi);
+          sts_v4(smem_base + kOffWLo + dst, lo);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(w_ready);
+        if ((f + 1) * p.tiles_m < last) load_w(f + 1);
+        ++fold_count;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (*abort_flag) {  // uniform: every thread has passed its last wait
+    stage_copies->drain(stage_full, abort_flag);
+    __syncthreads();
+  }
+  tc_fence_after();
+  if (warp == kMmaWarp) tmem_dealloc<512>(tmem);
+}
+
+// dw[f] = the sum of fold f's workspace slots (its CTAs in order, each slot's halves h = 0, 1);
+// one thread per 4 consecutive elements.
+__global__ void __launch_bounds__(256) cpb_reduce_kernel(const float* __restrict__ partials, int folds, int pieces,
+                                                         int tiles_m, int num_tiles, int grid, float* __restrict__ dw) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (int64_t)folds * 1024) return;
+  const int f = (int)(idx >> 10);
+  const int e4 = (int)(idx & 1023);
+  const int c0 = cta_of_tile((int64_t)f * tiles_m, num_tiles, grid);
+  const int c1 = cta_of_tile((int64_t)f * tiles_m + tiles_m - 1, num_tiles, grid);
+  float4 s = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  for (int pc = 0; pc <= c1 - c0; ++pc)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(partials + (((int64_t)f * pieces + pc) * 2 + h) * 4096) + e4);
+      s.x += v.x;
+      s.y += v.y;
+      s.z += v.z;
+      s.w += v.w;
+    }
+  reinterpret_cast<float4*>(dw)[idx] = s;
+}
+
+// ---------------------------------------------------------------------------- state-table gradient
+constexpr int kTgWarps = 16;  // consumer warps; warp w owns the states s with s % 16 == w
+constexpr int kTgThreads = (kTgWarps + 1) * 32;
+constexpr int kTgChunk = 64;  // rows of dX per bulk copy (16 KB)
+constexpr int kTgStages = 4;
+constexpr int kTgRing = kTgStages * kTgChunk * 256;
+
+__host__ __device__ constexpr int tg_smem_bytes(int states) { return 2 * states * 256 + kTgRing + 128; }
+
+// Rows reach shared memory in 64-row chunks through a 4-slot ring filled by the last warp.
+__global__ void __launch_bounds__(kTgThreads, 1)
+    table_grad_pair_kernel(const float* __restrict__ dx, int M, const uint8_t* __restrict__ pixels, int64_t ps,
+                           const int32_t* __restrict__ var, int pair, int states, float* __restrict__ dt) {
+  extern __shared__ __align__(16) uint8_t tg_smem[];
+  float* acc = reinterpret_cast<float*>(tg_smem);  // [2][states][64]
+  const uint32_t ring = smem_u32(tg_smem + 2 * states * 256);
+  uint64_t* full = reinterpret_cast<uint64_t*>(tg_smem + 2 * states * 256 + kTgRing);
+  uint64_t* empty = full + kTgStages;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kTgStages);
+  ArmedCopies* copies = reinterpret_cast<ArmedCopies*>(const_cast<int*>(abort_flag) + 1);
+  const int f = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < 2 * states * 16; i += blockDim.x)
+    reinterpret_cast<float4*>(acc)[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kTgStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kTgWarps);
+    }
+    *abort_flag = 0;
+    *copies = ArmedCopies{0u, 0u};
+    fence_mbarrier_init();
+  }
+  __syncthreads();
+  const int chunks = (M + kTgChunk - 1) / kTgChunk;
+  const float* src = dx + (int64_t)f * M * 64;
+  if (warp == kTgWarps) {
+    if (lane == 0) {
+      for (int c = 0; c < chunks; ++c) {
+        const int slot = c % kTgStages;
+        const uint32_t u = c / kTgStages;
+        if (!mbar_wait(&empty[slot], (u & 1) ^ 1, kSiteProducer, abort_flag)) break;
+        const int rows = min(kTgChunk, M - c * kTgChunk);
+        mbar_expect_tx(&full[slot], rows * 256);
+        copies->note(slot, u);
+        bulk_load(ring + slot * (kTgChunk * 256), src + (int64_t)c * kTgChunk * 64, rows * 256, &full[slot]);
+      }
+    }
+  } else {
+    int64_t v1 = var ? (int64_t)__ldg(var + f) : f;
+    int64_t v2 = var ? (int64_t)__ldg(var + f + pair) : (int64_t)f + pair;
+    if (v1 < 0 || v1 >= ps || v2 < 0 || v2 >= ps) {
+      record_bad_index(kSiteGatherState);
+      v1 = v2 = 0;
+    }
+    for (int c = 0; c < chunks; ++c) {
+      const int slot = c % kTgStages;
+      const uint32_t u = c / kTgStages;
+      // the states of rows lane and 32 + lane of the chunk (-1 past M), loaded before the wait
+      int s1[2], s2[2];
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const int m = c * kTgChunk + 32 * hf + lane;
+        s1[hf] = s2[hf] = -1;
+        if (m < M) {
+          s1[hf] = (int)__ldg(pixels + (int64_t)m * ps + v1);
+          s2[hf] = (int)__ldg(pixels + (int64_t)m * ps + v2);
+          if (s1[hf] >= states || s2[hf] >= states) {
+            record_bad_index(kSiteGatherState);
+            s1[hf] = min(s1[hf], states - 1);
+            s2[hf] = min(s2[hf], states - 1);
+          }
+        }
+      }
+      if (!mbar_wait_warp(&full[slot], u & 1, kSiteAStaged, abort_flag)) break;
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const uint32_t rows = ring + slot * (kTgChunk * 256) + hf * (32 * 256) + lane * 8;
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          const int sv = t == 0 ? s1[hf] : s2[hf];
+          float* table = acc + t * states * 64;
+          uint32_t own = __ballot_sync(0xffffffffu, sv >= 0 && (sv & (kTgWarps - 1)) == warp);
+          while (own) {
+            const int b = __ffs(own) - 1;
+            own &= own - 1;
+            const int st = __shfl_sync(0xffffffffu, sv, b);
+            const float2 x = lds_v2(rows + b * 256);
+            float2* d = reinterpret_cast<float2*>(table + st * 64) + lane;
+            float2 y = *d;
+            y.x += x.x;
+            y.y += x.y;
+            *d = y;
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
+    }
+  }
+  __syncthreads();
+  if (*abort_flag) {
+    copies->drain(full, abort_flag);
+    return;
+  }
+  // both table folds' slabs, every state (zero where no row selected it)
+  const int per = states * 16;  // float4 per table fold
+  for (int i = threadIdx.x; i < 2 * per; i += blockDim.x) {
+    const int h = i / per, r = i - h * per;
+    reinterpret_cast<float4*>(dt + ((int64_t)f + (int64_t)h * pair) * states * 64)[r] =
+        reinterpret_cast<const float4*>(acc)[i];
+  }
+}
+
+}  // namespace cpb
+}  // namespace xe

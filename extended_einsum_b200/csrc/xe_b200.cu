@@ -16,6 +16,7 @@
 #include "../../include/xe_b200.h"
 #include "lse_gemm.cuh"
 #include "cp_layer.cuh"
+#include "cp_backward.cuh"
 #include "tucker_layer.cuh"
 #include "pointwise.cuh"
 
@@ -1596,6 +1597,170 @@ xe_status xe_elementwise(int32_t op, const float* a, const int64_t* a_strides, c
     default: launch_elementwise<xe::kOpRescale>(a, b, c, y, sh, total, contig, s); break;
   }
   return check_launch("xe_elementwise");
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------------ CP layer backward
+namespace {
+
+// Tensor map of a contiguous (folds, m, 64) operand: boxes of 32 columns x 32 rows, 128-byte swizzle.
+bool encode_rows_map(CUtensorMap* map, const float* base, int64_t folds, int64_t m) {
+  return encode_c_map(map, const_cast<float*>(base), folds, m, 64, 64, m * 64);
+}
+
+struct CpbGeometry {
+  int64_t tiles_m = 0, num_tiles = 0;
+  int grid = 0, pieces = 0;
+};
+
+// The tiles, the grid (one CTA per SM at most) and the workspace slots per fold: the most CTAs
+// whose tile ranges meet one fold.
+CpbGeometry cpb_geometry(int64_t folds, int64_t m) {
+  using xe::cpb::cta_of_tile;
+  CpbGeometry g;
+  g.tiles_m = (m + xe::cpb::kRows - 1) / xe::cpb::kRows;
+  g.num_tiles = folds * g.tiles_m;
+  if (g.num_tiles == 0) return g;
+  g.grid = (int)std::min<int64_t>(g.num_tiles, current_device_sms());
+  g.pieces = 1;
+  for (int64_t f = 0; f < folds; ++f) {
+    const int c0 = cta_of_tile(f * g.tiles_m, g.num_tiles, g.grid);
+    const int c1 = cta_of_tile(f * g.tiles_m + g.tiles_m - 1, g.num_tiles, g.grid);
+    g.pieces = std::max(g.pieces, c1 - c0 + 1);
+  }
+  return g;
+}
+
+size_t cpb_workspace_bytes(const CpbGeometry& g, int64_t folds) {
+  return g.num_tiles == 0 ? 0 : round_up((size_t)folds * (size_t)g.pieces * 2 * 4096 * sizeof(float));
+}
+
+template <int SRC>
+xe_status launch_cpb_t(const char* who, const xe::cpb::Params& q, const CUtensorMap& mx1, const CUtensorMap& mx2,
+                       const CUtensorMap& my, const CUtensorMap& mg, int grid, cudaStream_t s) {
+  auto kernel = xe::cpb::cpb_kernel<SRC>;
+  static std::atomic<uint32_t> attribute_set{0};
+  cudaError_t e = prepare_kernel(kernel, xe::cpb::kSmemBytes, attribute_set);
+  if (e != cudaSuccess) return fail(XE_ERR_CUDA, "%s: cudaFuncSetAttribute: %s", who, cudaGetErrorString(e));
+  kernel<<<grid, xe::cpb::kThreads, xe::cpb::kSmemBytes, s>>>(q, mx1, mx2, my, mg);
+  return check_launch(who);
+}
+
+// Shared by both entry points: src is xe::cpb::kDense / kDense2 (x1 = A, x2 = A2 or null, both
+// (folds, m, 64)) or kGather2 (x1 = the (table_folds, states, 64) table).
+xe_status cpb_run(const char* who, int src, const float* x1, const float* x2, int64_t table_folds, int64_t states,
+                  const uint8_t* pixels, int64_t pixel_stride, const int32_t* var_of_fold, int64_t fold_offset,
+                  const float* y, const float* g, int64_t g_folds, const float* w, float* dx, float* dw, int64_t folds,
+                  int64_t m, int32_t shift_mode, void* workspace, size_t workspace_bytes, cudaStream_t s) {
+  if (!x1 || !y || !g || !w || !dx || !dw) return fail(XE_ERR_INVALID_ARGUMENT, "%s: null pointer", who);
+  if (folds < 0 || m < 0) return fail(XE_ERR_INVALID_ARGUMENT, "%s: negative extent", who);
+  if (g_folds < 1) return fail(XE_ERR_INVALID_ARGUMENT, "%s: g_folds must be positive", who);
+  if (shift_mode != XE_SHIFT_MAX && shift_mode != XE_SHIFT_MIN)
+    return fail(XE_ERR_INVALID_ARGUMENT, "%s: unknown shift mode %d", who, shift_mode);
+  if (folds == 0) return XE_OK;
+  if (m == 0) {
+    cudaError_t e = cudaMemsetAsync(dw, 0, (size_t)folds * 4096 * sizeof(float), s);
+    if (e != cudaSuccess) return fail(XE_ERR_CUDA, "%s: %s", who, cudaGetErrorString(e));
+    return XE_OK;
+  }
+  const CpbGeometry geo = cpb_geometry(folds, m);
+  if (m > INT32_MAX || geo.num_tiles > INT32_MAX || g_folds > INT32_MAX)
+    return fail(XE_ERR_NOT_SUPPORTED, "%s: too many rows", who);
+  const size_t need = cpb_workspace_bytes(geo, folds);
+  if (workspace_bytes < need || (need > 0 && !workspace))
+    return fail(XE_ERR_INVALID_ARGUMENT, "%s: workspace of %zu bytes, %zu needed", who, workspace_bytes, need);
+  if (!aligned16(w) || !aligned16(dx))
+    return fail(XE_ERR_NOT_SUPPORTED, "%s: operands must be contiguous and 16-byte aligned", who);
+  CUtensorMap mx1{}, mx2{}, my{}, mg{};
+  bool maps = encode_rows_map(&my, y, folds, m) && encode_rows_map(&mg, g, g_folds, m);
+  if (src == xe::cpb::kGather2) {
+    maps = maps && encode_gather_map(&mx1, x1, table_folds * states, 64, 64);
+  } else {
+    maps = maps && encode_rows_map(&mx1, x1, folds, m);
+    if (x2) maps = maps && encode_rows_map(&mx2, x2, folds, m);
+  }
+  if (!maps) return fail(XE_ERR_NOT_SUPPORTED, "%s: operands must be contiguous and 16-byte aligned", who);
+  xe::cpb::Params q{};
+  q.w = w;
+  q.dx = dx;
+  q.folds = (int)folds;
+  q.M = (int)m;
+  q.tiles_m = (int)geo.tiles_m;
+  q.num_tiles = (int)geo.num_tiles;
+  q.g_folds = (int)g_folds;
+  q.shift_min = shift_mode == XE_SHIFT_MIN ? 1 : 0;
+  q.pieces = geo.pieces;
+  q.partials = static_cast<float*>(workspace);
+  q.pixels = pixels;
+  q.var = var_of_fold;
+  q.pixel_stride = pixel_stride;
+  q.states = (int)states;
+  q.pair = (int)fold_offset;
+  xe_status st;
+  if (src == xe::cpb::kGather2) st = launch_cpb_t<xe::cpb::kGather2>(who, q, mx1, mx1, my, mg, geo.grid, s);
+  else if (x2) st = launch_cpb_t<xe::cpb::kDense2>(who, q, mx1, mx2, my, mg, geo.grid, s);
+  else st = launch_cpb_t<xe::cpb::kDense>(who, q, mx1, mx1, my, mg, geo.grid, s);
+  if (st != XE_OK) return st;
+  const int64_t threads = folds * 1024;
+  xe::cpb::cpb_reduce_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(
+      q.partials, q.folds, q.pieces, q.tiles_m, q.num_tiles, geo.grid, dw);
+  return check_launch(who);
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t xe_cp_layer_backward_workspace_size(int64_t folds, int64_t m) {
+  if (folds <= 0 || m <= 0) return 0;
+  return cpb_workspace_bytes(cpb_geometry(folds, m), folds);
+}
+
+xe_status xe_cp_layer_backward(const float* a, const float* a2, const float* y, const float* g, int64_t g_folds,
+                               const float* w, float* da, float* dw, int64_t folds, int64_t m, int32_t shift_mode,
+                               void* workspace, size_t workspace_bytes, void* stream) {
+  return cpb_run("xe_cp_layer_backward", a2 ? xe::cpb::kDense2 : xe::cpb::kDense, a, a2, 0, 0, nullptr, 0, nullptr, 0,
+                 y, g, g_folds, w, da, dw, folds, m, shift_mode, workspace, workspace_bytes, as_stream(stream));
+}
+
+xe_status xe_cp_layer_backward_gather_pair(const float* table, int64_t table_folds, int64_t states,
+                                           const uint8_t* pixels, int64_t pixel_stride, const int32_t* var_of_fold,
+                                           int64_t fold_offset, const float* y, const float* g, int64_t g_folds,
+                                           const float* w, float* da, float* dw, int64_t folds, int64_t m,
+                                           int32_t shift_mode, void* workspace, size_t workspace_bytes, void* stream) {
+  const char* who = "xe_cp_layer_backward_gather_pair";
+  if (!pixels) return fail(XE_ERR_INVALID_ARGUMENT, "%s: null pointer", who);
+  if (states < 1 || fold_offset < 1 || pixel_stride < 1)
+    return fail(XE_ERR_INVALID_ARGUMENT, "%s: states, fold_offset and pixel_stride must be positive", who);
+  if (table_folds < folds + fold_offset)
+    return fail(XE_ERR_INVALID_ARGUMENT, "%s: the table has %lld folds, %lld needed", who, (long long)table_folds,
+                (long long)(folds + fold_offset));
+  if (table_folds * states > INT32_MAX) return fail(XE_ERR_NOT_SUPPORTED, "%s: table too large", who);
+  return cpb_run(who, xe::cpb::kGather2, table, nullptr, table_folds, states, pixels, pixel_stride, var_of_fold,
+                 fold_offset, y, g, g_folds, w, da, dw, folds, m, shift_mode, workspace, workspace_bytes,
+                 as_stream(stream));
+}
+
+xe_status xe_state_table_pair_grad(const float* da, int64_t folds, int64_t m, const uint8_t* pixels,
+                                   int64_t pixel_stride, const int32_t* var_of_fold, int64_t fold_offset,
+                                   int64_t states, float* table_grad, void* stream) {
+  const char* who = "xe_state_table_pair_grad";
+  if (!da || !pixels || !table_grad) return fail(XE_ERR_INVALID_ARGUMENT, "%s: null pointer", who);
+  if (folds < 0 || m < 0) return fail(XE_ERR_INVALID_ARGUMENT, "%s: negative extent", who);
+  if (states < 1 || states > 256 || fold_offset < 1 || pixel_stride < 1)
+    return fail(states > 256 ? XE_ERR_NOT_SUPPORTED : XE_ERR_INVALID_ARGUMENT,
+                "%s: needs 1 <= states <= 256 and positive fold_offset and pixel_stride", who);
+  if (m > INT32_MAX || folds + fold_offset > INT32_MAX) return fail(XE_ERR_NOT_SUPPORTED, "%s: too many rows", who);
+  if (!aligned16(da) || !aligned16(table_grad)) return fail(XE_ERR_NOT_SUPPORTED, "%s: 16-byte aligned buffers", who);
+  if (folds == 0) return XE_OK;
+  const int smem = xe::cpb::tg_smem_bytes((int)states);
+  static std::atomic<uint32_t> attribute_set{0};
+  cudaError_t e = prepare_kernel(xe::cpb::table_grad_pair_kernel, xe::cpb::tg_smem_bytes(256), attribute_set);
+  if (e != cudaSuccess) return fail(XE_ERR_CUDA, "%s: cudaFuncSetAttribute: %s", who, cudaGetErrorString(e));
+  xe::cpb::table_grad_pair_kernel<<<(unsigned)folds, xe::cpb::kTgThreads, smem, as_stream(stream)>>>(
+      da, (int)m, pixels, pixel_stride, var_of_fold, (int)fold_offset, (int)states, table_grad);
+  return check_launch(who);
 }
 
 }  // extern "C"

@@ -550,6 +550,115 @@ def _gather_gemm(name, log_table, pixels, var_of_fold, b, fold_offset, b_linear,
     return out
 
 
+def cp_layer_backward(
+    a: torch.Tensor,
+    y: torch.Tensor,
+    g: torch.Tensor,
+    w: torch.Tensor,
+    *,
+    a2: torch.Tensor | None = None,
+    shift: str = "max",
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Gradients of the folded CP sum layer y = logspace_gemm(a, w.permute(0, 2, 1), a2=a2,
+    b_linear=True) (xe_cp_layer_backward): returns (dA, dw), dA also the gradient of a2.
+
+    a, a2, y are (F, M, 64); g is dL/dy, (F, M, 64) or (F / r, M, 64) with fold f reading
+    g[f % g.shape[0]] (the next layer's dA, the gradient of both halves of its input); w is the
+    (F, 64, 64) linear weights (o, k).  All contiguous float32 on one device.
+    """
+    device = _check_tensors("cp_layer_backward", a, y, g, w, *([a2] if a2 is not None else []))
+    folds, m, _ = _cp_backward_shapes("cp_layer_backward", a, y, g, w)
+    if a2 is not None and (tuple(a2.shape) != tuple(a.shape) or not a2.is_contiguous()):
+        raise ValueError("cp_layer_backward: a2 must be contiguous with a's shape")
+    da = torch.empty_like(y)
+    dw = torch.empty_like(w)
+    lib = _lib.load()
+    ws_bytes = lib.xe_cp_layer_backward_workspace_size(folds, m)
+    ws = torch.empty(ws_bytes, device=device, dtype=torch.uint8) if ws_bytes else None
+    status = lib.xe_cp_layer_backward(a.data_ptr(), _ptr(a2), y.data_ptr(), g.data_ptr(), g.shape[0], w.data_ptr(),
+                                      da.data_ptr(), dw.data_ptr(), folds, m, _shift(shift), _ptr(ws), ws_bytes,
+                                      _stream(device))
+    _lib.check(status, "xe_cp_layer_backward")
+    return da, dw
+
+
+def cp_layer_backward_gather_pair(
+    state_table: torch.Tensor,
+    pixels: torch.Tensor,
+    var_of_fold: torch.Tensor | None,
+    y: torch.Tensor,
+    g: torch.Tensor,
+    w: torch.Tensor,
+    *,
+    shift: str = "max",
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Gradients of y = logspace_gemm_gather_pair(state_table, pixels, var_of_fold, w^T, b_linear=True)
+    (xe_cp_layer_backward_gather_pair): returns (dA, dw), dA (F, batch, 64) the gradient of both
+    gathered rows (state_table_pair_grad turns it into the table's gradient)."""
+    device = _check_tensors("cp_layer_backward_gather_pair", state_table, y, g, w)
+    folds, m, _ = _cp_backward_shapes("cp_layer_backward_gather_pair", y, y, g, w)
+    pixels, var_of_fold = _pair_indices("cp_layer_backward_gather_pair", state_table, pixels, var_of_fold, folds, m,
+                                        device)
+    da = torch.empty_like(y)
+    dw = torch.empty_like(w)
+    lib = _lib.load()
+    ws_bytes = lib.xe_cp_layer_backward_workspace_size(folds, m)
+    ws = torch.empty(ws_bytes, device=device, dtype=torch.uint8) if ws_bytes else None
+    status = lib.xe_cp_layer_backward_gather_pair(
+        state_table.data_ptr(), state_table.shape[0], state_table.shape[1], pixels.data_ptr(), pixels.stride(0),
+        _ptr(var_of_fold), folds, y.data_ptr(), g.data_ptr(), g.shape[0], w.data_ptr(), da.data_ptr(), dw.data_ptr(),
+        folds, m, _shift(shift), _ptr(ws), ws_bytes, _stream(device))
+    _lib.check(status, "xe_cp_layer_backward_gather_pair")
+    return da, dw
+
+
+def state_table_pair_grad(
+    da: torch.Tensor, pixels: torch.Tensor, var_of_fold: torch.Tensor | None, states: int
+) -> torch.Tensor:
+    """The (2F, states, 64) gradient of the state table from dA (F, batch, 64) (xe_state_table_pair_grad):
+    row (t, s) sums dA[t mod F, b] over the samples b whose pixel of variable var[t] is s."""
+    device = _check_tensors("state_table_pair_grad", da)
+    if da.dim() != 3 or not da.is_contiguous():
+        raise ValueError("state_table_pair_grad: dA must be a contiguous (F, batch, units) tensor")
+    folds, m, units = da.shape
+    table = torch.empty((2 * folds, states, units), device=device, dtype=torch.float32)
+    pixels, var_of_fold = _pair_indices("state_table_pair_grad", table, pixels, var_of_fold, folds, m, device)
+    if units != 64:
+        raise NotImplementedError("state_table_pair_grad: 64 units")
+    status = _lib.load().xe_state_table_pair_grad(da.data_ptr(), folds, m, pixels.data_ptr(), pixels.stride(0),
+                                                  _ptr(var_of_fold), folds, states, table.data_ptr(), _stream(device))
+    _lib.check(status, "xe_state_table_pair_grad")
+    return table
+
+
+def _cp_backward_shapes(name, a, y, g, w):
+    for t, what in ((a, "a"), (y, "y"), (g, "g"), (w, "w")):
+        if t.dim() != 3 or not t.is_contiguous():
+            raise ValueError(f"{name}: {what} must be a contiguous 3-d tensor")
+    folds, m, units = y.shape
+    if units != 64 or tuple(w.shape) != (folds, 64, 64):
+        raise NotImplementedError(f"{name}: the CP layer backward takes K = N = 64 (w of shape (F, 64, 64))")
+    if tuple(a.shape) != tuple(y.shape) or g.shape[1:] != y.shape[1:] or g.shape[0] < 1 or folds % g.shape[0]:
+        raise ValueError(f"{name}: incompatible shapes a {tuple(a.shape)}, y {tuple(y.shape)}, g {tuple(g.shape)}")
+    return folds, m, units
+
+
+def _pair_indices(name, table, pixels, var_of_fold, folds, m, device):
+    if pixels.device != device or pixels.dtype != torch.uint8 or pixels.dim() != 2 or pixels.shape[0] != m:
+        raise ValueError(f"{name}: pixels must be a (batch, variables) uint8 tensor on the table's device")
+    if pixels.stride(1) != 1:
+        pixels = pixels.contiguous()
+    if table.dim() != 3 or table.shape[0] != 2 * folds or not table.is_contiguous():
+        raise ValueError(f"{name}: expected a contiguous (2F, states, 64) state table")
+    if var_of_fold is not None:
+        if var_of_fold.dtype != torch.int32 or var_of_fold.device != device or var_of_fold.numel() != 2 * folds:
+            raise ValueError(f"{name}: var_of_fold must be int32 with one entry per table fold")
+        var_of_fold = var_of_fold.contiguous()
+    elif pixels.shape[1] < 2 * folds:
+        raise ValueError(f"{name}: fewer pixel variables than table folds")
+    return pixels, var_of_fold
+
+
 def logspace_tucker(
     left: torch.Tensor,
     right: torch.Tensor,

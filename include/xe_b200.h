@@ -313,6 +313,54 @@ xe_status xe_logspace_gemm_gather_pair(const float* table, int64_t t_sf, int64_t
                                        void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* Backward pass of the folded CP sum layer 'dac,dbc->dab' with K = N = 64
+ * (preprocess.py:1310-1337, lowered by translate.py:686-750): the gradients
+ * that torch autograd gives for the reference's executor calls, in which the
+ * shift is a stop_gradient (translate.py:727-740; backends/torch.py:14-16).
+ * Forward:  Y[f,m,o] = log( sum_k exp(X[f,m,k] - s) w[f,o,k] ) + s,
+ *           X = A (+ A2), s = max_k (or min_k) X[f,m,:],
+ *           w (folds, 64 o, 64 k) the linear weights (the contraction's B
+ *           operand is w[f] transposed).
+ * With G = dL/dY and V = G exp(s - Y):
+ *   dA[f,m,k] = exp(X[f,m,k] - s) sum_o V[f,m,o] w[f,o,k]   (also dA2)
+ *   dw[f,o,k] = sum_m V[f,m,o] exp(X[f,m,k] - s).
+ * A, A2, Y, dA are (folds, m, 64) and G is (g_folds, m, 64), all contiguous
+ * and 16-byte aligned; fold f reads G[f % g_folds] (g_folds = folds / 2 when
+ * G is the next layer's dA, the gradient of both halves of its input).  dw
+ * is (folds, 64, 64) contiguous and written whole, deterministically.
+ * `workspace` must hold xe_cp_layer_backward_workspace_size(folds, m) bytes
+ * (per-CTA partial sums of dw). */
+size_t xe_cp_layer_backward_workspace_size(int64_t folds, int64_t m);
+xe_status xe_cp_layer_backward(const float* a, const float* a2, const float* y, const float* g, int64_t g_folds,
+                               const float* w, float* da, float* dw, int64_t folds, int64_t m, int32_t shift_mode,
+                               void* workspace, size_t workspace_bytes, void* stream);
+
+/* The same for the second layer over a state table (the backward of
+ * xe_logspace_gemm_gather_pair): X[f,m,:] = T[f, x_m, :] + T[f + fold_offset,
+ * x'_m, :], with T the (table_folds, states, 64) contiguous table and x_m,
+ * x'_m the pixels of variables var_of_fold[f], var_of_fold[f + fold_offset]
+ * (NULL: the fold) of sample m.  dA is the gradient of both gathered rows;
+ * xe_state_table_pair_grad scatters it into the table. */
+xe_status xe_cp_layer_backward_gather_pair(const float* table, int64_t table_folds, int64_t states,
+                                           const uint8_t* pixels, int64_t pixel_stride, const int32_t* var_of_fold,
+                                           int64_t fold_offset, const float* y, const float* g, int64_t g_folds,
+                                           const float* w, float* da, float* dw, int64_t folds, int64_t m,
+                                           int32_t shift_mode, void* workspace, size_t workspace_bytes, void* stream);
+
+/* The gradient of the state table from dA (folds, m, 64) contiguous: for each
+ * f < folds, table_grad[f, s, :] is the sum of dA[f, m, :] over the samples m
+ * whose pixel of variable var_of_fold[f] is s, and table_grad[f + fold_offset,
+ * s, :] the same for var_of_fold[f + fold_offset] (the backward of torch
+ * indexing in demo/cirkit.py:525-527 composed with the pair gather).  Those
+ * 2 * folds table folds are written whole (zero for states no sample takes);
+ * table_grad, contiguous (>= folds + fold_offset, states, 64), is not read.
+ * The sums run in sample order, so the result is deterministic.  states <= 256.
+ * Bad pixel values are clamped and reported as in xe_categorical_gather. */
+xe_status xe_state_table_pair_grad(const float* da, int64_t folds, int64_t m, const uint8_t* pixels,
+                                   int64_t pixel_stride, const int32_t* var_of_fold, int64_t fold_offset,
+                                   int64_t states, float* table_grad, void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* Log-space Tucker layer 'bfi,bfj,foij->bfo' (the ternary einsum that
  * OptimizeContractionPaths fuses for Tucker circuits, preprocess.py:1095-1106,
  * lowered by _append_logspace_einsum, translate.py:686-750):

@@ -87,3 +87,24 @@ def test_wait_limit_range_is_checked_before_the_device():
     assert lib.xe_set_wait_timeout_ns(999) == _lib.XE_ERR_INVALID_ARGUMENT
     assert "outside" in _lib.last_error()
     assert lib.xe_set_wait_timeout_ns(60_000_000_001) == _lib.XE_ERR_INVALID_ARGUMENT
+
+
+def test_cp_layer_backward_rejects_bad_arguments_without_launch():
+    lib = _lib.load()
+    ws = lib.xe_cp_layer_backward_workspace_size(4, 100)
+    assert ws > 0 and ws % 256 == 0 and lib.xe_cp_layer_backward_workspace_size(0, 100) == 0
+
+    def call(a=16, y=16, g=16, g_folds=1, w=16, mode=0, folds=2, m=100, ws_bytes=1 << 30):
+        return lib.xe_cp_layer_backward(a, None, y, g, g_folds, w, 16, 16, folds, m, mode, 16, ws_bytes, None)
+
+    assert call(a=None) == _lib.XE_ERR_INVALID_ARGUMENT and "null" in _lib.last_error()
+    assert call(g_folds=0) == _lib.XE_ERR_INVALID_ARGUMENT
+    assert call(mode=3) == _lib.XE_ERR_INVALID_ARGUMENT
+    assert call(m=-1) == _lib.XE_ERR_INVALID_ARGUMENT
+    assert call(ws_bytes=16) == _lib.XE_ERR_INVALID_ARGUMENT and "workspace" in _lib.last_error()
+    # the pair form checks its table and indices first
+    st = lib.xe_cp_layer_backward_gather_pair(16, 3, 256, 16, 8, None, 2, 16, 16, 1, 16, 16, 16, 2, 100, 0, 16,
+                                              1 << 30, None)
+    assert st == _lib.XE_ERR_INVALID_ARGUMENT and "folds" in _lib.last_error()
+    assert lib.xe_state_table_pair_grad(16, 2, 10, 16, 8, None, 2, 300, 16, None) == _lib.XE_ERR_NOT_SUPPORTED
+    assert lib.xe_state_table_pair_grad(None, 2, 10, 16, 8, None, 2, 256, 16, None) == _lib.XE_ERR_INVALID_ARGUMENT

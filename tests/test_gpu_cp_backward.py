@@ -1,0 +1,190 @@
+"""The fused backward of the folded CP sum layer (xe_cp_layer_backward, its state-table form
+xe_cp_layer_backward_gather_pair and xe_state_table_pair_grad) against torch autograd of the same
+formulas in fp64, with the shift a constant (stop_gradient in the reference,
+backend_translation/translate.py:727-740); and the circuit's fused backward against fp64 autograd
+of the folded circuit and against the per-operation backward."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from extended_einsum_b200 import ops
+from test_gpu_autograd import _close, _leaf, _torch_circuit_ll
+
+pytestmark = pytest.mark.gpu
+
+LAYER_RTOL, LAYER_ATOL = 2e-5, 1e-6
+
+
+def _layer_ref(x: torch.Tensor, w: torch.Tensor, shift: str) -> torch.Tensor:
+    """y[f,m,o] = log(sum_k exp(x - s) w[f,o,k]) + s, s the detached row extreme."""
+    s = (x.amax(dim=2, keepdim=True) if shift == "max" else x.amin(dim=2, keepdim=True)).detach()
+    return torch.log(torch.einsum("fmk,fok->fmo", torch.exp(x - s), w)) + s
+
+
+def _weights(folds: int, gen: torch.Generator) -> torch.Tensor:
+    return torch.softmax(torch.randn(folds, 64, 64, generator=gen), dim=2)
+
+
+# (folds, rows): one tile, ragged last tiles, rows below one warp, many tiles per fold
+SHAPES = [(1, 64), (3, 200), (2, 1000), (5, 33), (7, 129)]
+
+
+@pytest.mark.parametrize("shape", SHAPES, ids=[f"F{f}xM{m}" for f, m in SHAPES])
+@pytest.mark.parametrize("pair", [False, True], ids=["A", "A+A2"])
+@pytest.mark.parametrize("shift", ["max", "min"])
+def test_cp_layer_backward_matches_fp64_autograd(shape, pair, shift):
+    folds, m = shape
+    gen = torch.Generator().manual_seed(hash((shape, pair, shift)) % 2**31)
+    a = 2.0 * torch.randn(folds, m, 64, generator=gen)
+    a2 = 2.0 * torch.randn(folds, m, 64, generator=gen) if pair else None
+    w = _weights(folds, gen)
+    g = torch.randn(folds, m, 64, generator=gen)
+    ar, wr = _leaf(a.double()), _leaf(w.double())
+    a2r = _leaf(a2.double()) if pair else None
+    y_ref = _layer_ref(ar + a2r if pair else ar, wr, shift)
+    (y_ref * g.double()).sum().backward()
+
+    ad, wd = a.cuda(), w.cuda()
+    a2d = a2.cuda() if pair else None
+    y = ops.logspace_gemm(ad, wd.permute(0, 2, 1), a2=a2d, b_linear=True, shift=shift)
+    da, dw = ops.cp_layer_backward(ad, y, g.cuda(), wd, a2=a2d, shift=shift)
+    torch.cuda.synchronize()
+    _close(da, ar.grad, rtol=LAYER_RTOL, atol=LAYER_ATOL)
+    if pair:
+        _close(da, a2r.grad, rtol=LAYER_RTOL, atol=LAYER_ATOL)
+    _close(dw, wr.grad, rtol=LAYER_RTOL, atol=LAYER_ATOL)
+    assert ops.device_status() == 0
+
+
+def test_gradient_folds_repeat():
+    """G with half the folds: fold f reads G[f % F/2], the next layer's dA for both halves."""
+    gen = torch.Generator().manual_seed(11)
+    folds, m = 4, 300
+    a, a2 = 2.0 * torch.randn(folds, m, 64, generator=gen), 2.0 * torch.randn(folds, m, 64, generator=gen)
+    w = _weights(folds, gen)
+    g_half = torch.randn(folds // 2, m, 64, generator=gen)
+    ar, a2r, wr = _leaf(a.double()), _leaf(a2.double()), _leaf(w.double())
+    (_layer_ref(ar + a2r, wr, "max") * torch.cat([g_half, g_half]).double()).sum().backward()
+    ad, a2d, wd = a.cuda(), a2.cuda(), w.cuda()
+    y = ops.logspace_gemm(ad, wd.permute(0, 2, 1), a2=a2d, b_linear=True)
+    da, dw = ops.cp_layer_backward(ad, y, g_half.cuda(), wd, a2=a2d)
+    _close(da, ar.grad, rtol=LAYER_RTOL, atol=LAYER_ATOL)
+    _close(dw, wr.grad, rtol=LAYER_RTOL, atol=LAYER_ATOL)
+
+
+def test_minus_inf_entries_and_determinism():
+    """-inf entries of X contribute nothing; a second call gives the same bits (fixed reduction order)."""
+    gen = torch.Generator().manual_seed(12)
+    folds, m = 3, 700
+    a = 2.0 * torch.randn(folds, m, 64, generator=gen)
+    a[0, 5, :40] = -float("inf")
+    a[2, 699, 3] = -float("inf")
+    w = _weights(folds, gen)
+    g = torch.randn(folds, m, 64, generator=gen)
+    ar, wr = _leaf(a.double()), _leaf(w.double())
+    (_layer_ref(ar, wr, "max") * g.double()).sum().backward()
+    ad, wd, gd = a.cuda(), w.cuda(), g.cuda()
+    y = ops.logspace_gemm(ad, wd.permute(0, 2, 1), b_linear=True)
+    da, dw = ops.cp_layer_backward(ad, y, gd, wd)
+    da2, dw2 = ops.cp_layer_backward(ad, y, gd, wd)
+    assert torch.equal(da, da2) and torch.equal(dw, dw2)
+    assert torch.isfinite(da).all()
+    _close(da, ar.grad, rtol=LAYER_RTOL, atol=LAYER_ATOL)
+    _close(dw, wr.grad, rtol=LAYER_RTOL, atol=LAYER_ATOL)
+
+
+def _gather_pair_ref(table, pixels, var, folds):
+    f_idx = torch.arange(folds)[:, None]
+    px = pixels.long()
+    return table[f_idx, px[:, var[:folds]].T] + table[f_idx + folds, px[:, var[folds:]].T]
+
+
+@pytest.mark.parametrize("shift", ["max", "min"])
+@pytest.mark.parametrize("m", [300, 64, 1])
+def test_state_table_pair_backward(shift, m):
+    """dA of the gathered pair layer and its scatter into the (2F, states, 64) table, against fp64."""
+    gen = torch.Generator().manual_seed(13 + m)
+    folds, states, variables = 4, 256, 11
+    table = torch.log_softmax(torch.randn(2 * folds, states, 64, generator=gen), dim=1)
+    pixels = torch.randint(states, (m, variables), generator=gen, dtype=torch.uint8)
+    var = torch.randperm(variables, generator=gen)[: 2 * folds].to(torch.int32)
+    w = _weights(folds, gen)
+    g = torch.randn(folds, m, 64, generator=gen)
+    tr, wr = _leaf(table.double()), _leaf(w.double())
+    (_layer_ref(_gather_pair_ref(tr, pixels, var.long(), folds), wr, shift) * g.double()).sum().backward()
+
+    td, pd, vd, wd = table.cuda(), pixels.cuda(), var.cuda(), w.cuda()
+    y = ops.logspace_gemm_gather_pair(td, pd, vd, wd.permute(0, 2, 1), b_linear=True, shift=shift)
+    da, dw = ops.cp_layer_backward_gather_pair(td, pd, vd, y, g.cuda(), wd, shift=shift)
+    dt = ops.state_table_pair_grad(da, pd, vd, states)
+    dt2 = ops.state_table_pair_grad(da, pd, vd, states)
+    torch.cuda.synchronize()
+    assert torch.equal(dt, dt2)
+    _close(dt, tr.grad, rtol=LAYER_RTOL, atol=LAYER_ATOL)
+    _close(dw, wr.grad, rtol=LAYER_RTOL, atol=LAYER_ATOL)
+    assert ops.device_status() == 0
+
+
+def test_out_of_range_pixels_are_clamped_and_reported():
+    gen = torch.Generator().manual_seed(14)
+    folds, states = 2, 100
+    da = torch.randn(folds, 40, 64, generator=gen).cuda()
+    pixels = torch.randint(states, (40, 4), generator=gen, dtype=torch.uint8)
+    pixels[7, 1] = 250
+    dt = ops.state_table_pair_grad(da, pixels.cuda(), None, states)
+    torch.cuda.synchronize()
+    assert ops.device_status(clear=True) != 0
+    assert torch.isfinite(dt).all()
+    assert ops.device_status() == 0
+
+
+def _circuit_case(batch: int, side: int = 8):
+    from extended_einsum_b200.circuit import QuadTreeCircuit
+
+    circuit = QuadTreeCircuit(side, side, 64, 256)
+    gen = torch.Generator().manual_seed(21)
+    params = circuit.init_parameters(gen)
+    pixels = torch.randint(256, (batch, circuit.variables), generator=gen, dtype=torch.uint8)
+    up = torch.randn(batch, 1, generator=gen)
+    return circuit, params, pixels, up
+
+
+def _circuit_grads(circuit, params, pixels, up, fused: bool):
+    from extended_einsum_b200.circuit import CircuitForward
+
+    leaves = [_leaf(params["categorical"], "cuda"), *[_leaf(t, "cuda") for t in params["levels"]],
+              _leaf(params["root"], "cuda")]
+    dev = {"categorical": leaves[0], "levels": leaves[1:-1], "root": leaves[-1],
+           "var_of_fold": params["var_of_fold"].cuda()}
+    forward = CircuitForward(circuit, dev, fused_backward=fused)
+    (forward(pixels.cuda()) * up.cuda()).sum().backward()
+    return [t.grad for t in leaves]
+
+
+def test_fused_circuit_backward_matches_fp64():
+    circuit, params, pixels, up = _circuit_case(300)
+    assert circuit.uses_state_table(300)
+    ours = _circuit_grads(circuit, params, pixels, up, fused=True)
+    cat_r = _leaf(params["categorical"].double())
+    lv_r = [_leaf(t.double()) for t in params["levels"]]
+    root_r = _leaf(params["root"].double())
+    ll = _torch_circuit_ll(cat_r, pixels, params["var_of_fold"].long(), lv_r, root_r)
+    (ll * up.double()).sum().backward()
+    for got, ref in zip(ours[:-1], [cat_r, *lv_r]):
+        _close(got, ref.grad, rtol=1e-4, atol=1e-5)
+    # The root's gradient is sum_b up_b w_k (posterior_bk / w_k - 1): with random weights the top
+    # units' log-likelihoods (about -350 here) nearly agree, the posteriors differ from w by ~1e-5
+    # and the gradient (~1e-5) is a difference of terms ~1e-2 computed from fp32 log-likelihoods
+    # with ~2e-5 absolute error, which bounds any fp32 evaluation's agreement to ~1e-4.
+    _close(ours[-1], root_r.grad, rtol=1e-4, atol=1e-4)
+    assert ops.device_status() == 0
+
+
+def test_fused_circuit_backward_matches_per_operation_backward():
+    circuit, params, pixels, up = _circuit_case(512)
+    fused = _circuit_grads(circuit, params, pixels, up, fused=True)
+    unfused = _circuit_grads(circuit, params, pixels, up, fused=False)
+    for got, ref in zip(fused, unfused):
+        _close(got, ref, rtol=1e-4, atol=1e-5)
