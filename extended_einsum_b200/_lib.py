@@ -67,14 +67,15 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "xe_cp_layer_backward_gather_pair": (
         _c_i32,
         [
-            _c_ptr, _c_i64, _c_i64, _c_ptr, _c_i64, _c_ptr, _c_i64,  # table, folds, states, pixels, stride, var, offset
+            _c_ptr, _c_i64, _c_i64,  # table, folds, states
+            _c_ptr, _c_i64, _c_i64, _c_i64, _c_ptr, _c_i64,  # pixels, strides, variables, var, offset
             _c_ptr, _c_ptr, _c_i64, _c_ptr,  # y, g, g_folds, w
             _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i32,  # da, dw, folds, m, shift_mode
             _c_ptr, _c_size, _c_ptr,  # workspace, bytes, stream
         ],
     ),
     "xe_state_table_pair_grad": (
-        _c_i32, [_c_ptr, _c_i64, _c_i64, _c_ptr, _c_i64, _c_ptr, _c_i64, _c_i64, _c_ptr, _c_ptr],
+        _c_i32, [_c_ptr, _c_i64, _c_i64, _c_ptr, _c_i64, _c_i64, _c_i64, _c_ptr, _c_i64, _c_i64, _c_ptr, _c_ptr],
     ),
     "xe_logspace_gemm": (
         _c_i32,

@@ -12,15 +12,18 @@
 //   dX[m,k] = A'[m,k] sum_o V[m,o] w[o,k],   dw[o,k] = sum_m V[m,o] A'[m,k],
 // dX being the gradient of A and of A2 alike.  cpb_kernel computes both from one read of X, Y, G:
 //
-//  * a tile is 64 rows of one fold; each CTA takes a contiguous range of tiles and two warp pairs
-//    (warps 0-1 and 2-3, a thread per row) own alternate tiles;
+//  * a tile is 64 rows of one fold; each CTA takes a contiguous range of tiles and two pairs own
+//    alternate tiles: pair p is the 64 TMEM lanes 64p.. (quarters 2p, 2p+1) and the four warps
+//    that reach them, two threads per row (warp w: quarter w & 3, columns 32 (w >> 2) ..+31);
 //  * tiles rotate through three 64 KB stages, so the loads of the next two tiles are in flight
 //    while one is computed; a stage receives the tile's rows of X (two tensors for a pair source),
-//    Y and G by TMA (tile::gather4 for table rows);
-//  * each thread reads its row, forms A' and V, writes V as TF32 hi / lo into its TMEM lane, and
-//    writes the operands of the weight product in place of its own row of the inputs: S (A'^T hi
-//    over A'^T lo, M = 128) and V^T hi / lo (N = 64), MN-major with the tile's rows as K, so that
-//    a thread's k-row is the 128-byte row its inputs came in and no other thread touches it;
+//    Y and G by TMA (table rows by cp.async of 16 bytes, a warp instruction per two rows);
+//  * each thread reads its half row, takes the row extreme with the other half (through a TMEM
+//    column of its own dX' half, free until the pair's next product), forms A' and V, writes V as
+//    TF32 hi / lo into its TMEM lane, and writes the operands of the weight product in place of
+//    its half row of the inputs: S (A'^T hi over A'^T lo, M = 128) and V^T hi / lo (N = 64),
+//    MN-major with the tile's rows as K, so that a thread's k-rows are the 128-byte rows its
+//    inputs came in and no other thread touches them;
 //  * one thread issues dX' = V w with A = V from TMEM (M = 128 lanes, of which the pair's 64 are
 //    its rows; split TF32 over w^T hi / lo, three products per k-step) and the weight product
 //    D_B[(h,k), o] = sum over the tile's rows of S[(h,k), m] (V^T hi + V^T lo)[o, m];
@@ -28,14 +31,14 @@
 //    lane quarter each) adds every tile's D_B into fp32 registers, rounding to nearest (the tensor
 //    core's accumulator truncates, so it restarts with every tile), and writes the two halves
 //    h = 0, 1 of its sums to a workspace slot of the fold when its range leaves the fold;
-//  * the load warp splits w^T into TF32 hi / lo from registers that it fills a fold ahead;
+//  * the load warp splits w^T into TF32 hi / lo at each fold's start;
 //  * cpb_reduce_kernel adds the slots of each fold in a fixed order, so dw is deterministic.
 //
 // table_grad_pair_kernel: the second layer's X is T[f, x_m] + T[f + pair, x'_m] for a state
 // table T (2F, states, 64) and pixel values x_m, x'_m of the variables of folds f and f + pair;
 // dT[t, s, :] is the sum of dX[f, m, :] over the rows m whose pixel selects state s of table fold
-// t (the backward of the gather).  One CTA per fold f of dX; warp w owns the states s with
-// s % 16 == w and adds its rows in increasing m, so the sums are deterministic.
+// t (the backward of the gather).  A CTA takes whole folds f of dX; warp w owns the states s
+// with s % 16 == w, sums their rows in registers in increasing m: the sums are deterministic.
 #pragma once
 
 #include "cp_layer.cuh"
@@ -53,10 +56,11 @@ using cp::tma_store_3d;
 #define XE_CPB_TRACE(n, ev) XE_TILE_TRACE(n, ev)
 
 constexpr int kRows = 64;  // rows per tile
-constexpr int kThreads = 320;
-constexpr int kDrainWarp0 = 4;
-constexpr int kMmaWarp = 8;
-constexpr int kProducerWarp = 9;
+constexpr int kComputeWarps = 8;
+constexpr int kDrainWarp0 = 8;  // 8-11: TMEM lane quarters 0-3
+constexpr int kMmaWarp = 12;
+constexpr int kProducerWarp = 13;
+constexpr int kThreads = (kProducerWarp + 1) * 32;
 constexpr int kBlock = 32 * 32 * 4;       // 32 rows x 32 fp32 (4 KB)
 constexpr int kRegion = 8 * kBlock;       // one warp's 32 rows of X1, X2, Y, G (two column halves each)
 constexpr int kStage = 2 * kRegion;       // one tile
@@ -86,10 +90,12 @@ struct Params {
   int shift_min;
   int pieces;       // workspace slots per fold
   float* partials;  // [folds][pieces][2][64 o][64 k]
-  // kGather2: X[f,m,:] = T[f, x_m, :] + T[f + pair, x'_m, :], x_m = pixels[m, var[f]]
+  // kGather2: X[f,m,:] = T[f, x_m, :] + T[f + pair, x'_m, :], x_m the pixel of sample m and
+  // variable var[f]: pixels[m * px_sm + var[f] * px_sv]
+  const float* table;  // (table folds, states, 64)
   const uint8_t* pixels;
   const int32_t* var;  // nullptr: variable = table fold
-  int64_t pixel_stride;
+  int64_t px_sm, px_sv, variables;
   int states, pair;
 };
 
@@ -116,6 +122,36 @@ __device__ __forceinline__ float2 lds_v2(uint32_t addr) {
   return v;
 }
 
+// One fp32 column of the calling warp's 32 TMEM lanes.
+__device__ __forceinline__ void tmem_st1(uint32_t taddr, float v) {
+  __syncwarp();
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};" ::"r"(taddr), "f"(v) : "memory");
+}
+
+__device__ __forceinline__ float tmem_ld1(uint32_t taddr) {
+  __syncwarp();
+  uint32_t r;
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr) : "memory");
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+  return __uint_as_float(r);
+}
+
+// 16 bytes global -> shared memory through L2 (not L1), asynchronous.
+__device__ __forceinline__ void cp_async_16(uint32_t dst, const float* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+
+// One arrival on `bar` once every cp.async this thread issued before has landed; the arrival is
+// one of the barrier's expected count.
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Barrier `id` (1..15) over `count` threads (whole warps).
+__device__ __forceinline__ void named_barrier_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 // Byte offset of element (row, e) of a K-major [rows][32] fp32 tile, 128-byte swizzle.
 __device__ __forceinline__ uint32_t kmajor_elem(int row, int e) { return kmajor_off(row, e >> 2) + ((e & 3) << 2); }
 
@@ -125,8 +161,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                const __grid_constant__ CUtensorMap tmap_x2, const __grid_constant__ CUtensorMap tmap_y,
                const __grid_constant__ CUtensorMap tmap_g) {
   constexpr bool PAIR = SRC != kDense;
-  // bytes landing in a stage per tile: 64 rows x 64 fp32 of X1 (and X2), Y and G
-  constexpr uint32_t kStageTx = (PAIR ? 4 : 3) * kRows * 64 * 4;
+  // bytes the TMA brings into a stage per tile: 64 rows x 64 fp32 of X1 (and X2; the table rows of
+  // kGather2 come by cp.async, which arrives on the barrier once per load lane), Y and G
+  constexpr uint32_t kStageTx = (SRC == kGather2 ? 2 : PAIR ? 4 : 3) * kRows * 64 * 4;
+  constexpr uint32_t kStageArrivals = SRC == kGather2 ? 33 : 1;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   const uint32_t smem_base = smem_u32(smem);
@@ -148,11 +186,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; ++i) {
-      mbar_init(&stage_full[i], 1);
+      mbar_init(&stage_full[i], kStageArrivals);
       mbar_init(&stage_free[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&ready[i], 2);
+      mbar_init(&ready[i], 4);
       mbar_init(&dx_full[i], 1);
       mbar_init(&db_full[i], 1);
       mbar_init(&db_free[i], 4);
@@ -172,11 +210,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int first = (int)(((int64_t)p.num_tiles * blockIdx.x) / gridDim.x);
   const int last = (int)(((int64_t)p.num_tiles * (blockIdx.x + 1)) / gridDim.x);
 
-  if (warp < kDrainWarp0) {
-    // ------------------------------------------------------------ warp pairs (thread = tile row)
-    const int pair = warp >> 1;
-    const int wq = warp & 1;
-    const uint32_t tp = tmem + pair * 256 + ((uint32_t)(warp * 32) << 16);
+  if (warp < kComputeWarps) {
+    // ------------------------------------------------------------ pairs (two threads per row)
+    const int quarter = warp & 3;
+    const int half = warp >> 2;  // columns 32 half .. 32 half + 31 of the row
+    const int pair = quarter >> 1;
+    const int wq = quarter & 1;
+    const uint32_t tp = tmem + pair * 256 + ((uint32_t)(quarter * 32) << 16);
     const bool is_min = p.shift_min != 0;
     const uint32_t roff = lane * 128;
     bool ok = true;
@@ -189,45 +229,53 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int row = mt * kRows + wq * 32 + lane;
       const bool valid = row < p.M;
       const uint32_t region = smem_base + kOffStage + st * kStage + wq * kRegion;
-      const bool tr = wq == 0 && lane == 0;
+      const bool tr = half == 0 && wq == 0 && lane == 0;
       if (tr) XE_CPB_TRACE(n, 0);
       if (!mbar_wait_warp(&stage_full[st], (n / kStages) & 1, kSiteAStaged, abort_flag)) {
         ok = false;
         break;
       }
       if (tr) XE_CPB_TRACE(n, 1);
-      float a[64];
+      float a[32];
 #pragma unroll
-      for (int c = 0; c < 2; ++c)
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const uint32_t off = roff + ((q ^ (lane & 7)) << 4);
-          float4 v = lds_v4(region + c * kBlock + off);
-          if (PAIR) {
-            const float4 u = lds_v4(region + (2 + c) * kBlock + off);
-            v.x += u.x;
-            v.y += u.y;
-            v.z += u.z;
-            v.w += u.w;
-          }
-          a[32 * c + 4 * q] = v.x;
-          a[32 * c + 4 * q + 1] = v.y;
-          a[32 * c + 4 * q + 2] = v.z;
-          a[32 * c + 4 * q + 3] = v.w;
+      for (int q = 0; q < 8; ++q) {
+        const uint32_t off = roff + ((q ^ (lane & 7)) << 4);
+        float4 v = lds_v4(region + half * kBlock + off);
+        if (PAIR) {
+          const float4 u = lds_v4(region + (2 + half) * kBlock + off);
+          v.x += u.x;
+          v.y += u.y;
+          v.z += u.z;
+          v.w += u.w;
         }
+        a[4 * q] = v.x;
+        a[4 * q + 1] = v.y;
+        a[4 * q + 2] = v.z;
+        a[4 * q + 3] = v.w;
+      }
       float e0 = is_min ? INFINITY : -INFINITY, e1 = e0, e2 = e0, e3 = e0;
 #pragma unroll
-      for (int k = 0; k < 64; k += 4) {
+      for (int k = 0; k < 32; k += 4) {
         e0 = extreme(e0, a[k], is_min);
         e1 = extreme(e1, a[k + 1], is_min);
         e2 = extreme(e2, a[k + 2], is_min);
         e3 = extreme(e3, a[k + 3], is_min);
       }
-      const float s = valid ? extreme(extreme(e0, e1, is_min), extreme(e2, e3, is_min), is_min) : 0.0f;
-      // A' and its S columns (M = k for hi, 64 + k for lo), in this thread's k-row of blocks 0-3
-      // (its X rows, read above)
+      const float e_half = extreme(extreme(e0, e1, is_min), extreme(e2, e3, is_min), is_min);
+      // the row extreme: each half leaves its own in the first column of its dX' half (its own
+      // epilogue has read the previous dX' there; the pair's next product is issued after every
+      // thread of the pair has read the other half's)
+      tmem_st1(tp + kTmDX + 32 * half, e_half);
+      tmem_wait_st();
+      tc_fence_before();
+      named_barrier_sync(1 + pair, 128);
+      tc_fence_after();
+      const float e_other = tmem_ld1(tp + kTmDX + 32 * (1 - half));
+      const float s = valid ? extreme(e_half, e_other, is_min) : 0.0f;
+      // A' and its S columns (M = k for hi, 64 + k for lo), in this thread's k-rows of blocks
+      // half and 2 + half (its X rows, read above)
 #pragma unroll
-      for (int q = 0; q < 16; ++q) {
+      for (int q = 0; q < 8; ++q) {
         float4 hi, lo;
 #pragma unroll
         for (int t = 0; t < 4; ++t) a[4 * q + t] = valid ? exp_shifted(a[4 * q + t], s) : 0.0f;
@@ -235,37 +283,34 @@ __global__ void __launch_bounds__(kThreads, 1)
         split_rn(a[4 * q + 1], hi.y, lo.y);
         split_rn(a[4 * q + 2], hi.z, lo.z);
         split_rn(a[4 * q + 3], hi.w, lo.w);
-        sts_v4(region + kOffS + mnmajor_off(lane, q), hi);
-        sts_v4(region + kOffS + mnmajor_off(lane, 16 + q), lo);
+        sts_v4(region + kOffS + mnmajor_off(lane, 8 * half + q), hi);
+        sts_v4(region + kOffS + mnmajor_off(lane, 16 + 8 * half + q), lo);
       }
-      // V = G exp(s - Y) by column halves: the half's Y and G are read whole before its V^T
-      // chunks (MN block c of V^T hi / lo, this thread's k-row) replace them
+      // V = G exp(s - Y) for this half: its Y and G rows are read whole before its V^T chunks
+      // (MN block `half` of V^T hi / lo, this thread's k-row) replace them
+      float v[32];
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        float v[32];
+      for (int q = 0; q < 8; ++q) {
+        const uint32_t off = roff + ((q ^ (lane & 7)) << 4);
+        const float4 yv = lds_v4(region + (4 + half) * kBlock + off);
+        const float4 gv = lds_v4(region + (6 + half) * kBlock + off);
+        v[4 * q] = valid ? gv.x * exp_shifted(s, yv.x) : 0.0f;
+        v[4 * q + 1] = valid ? gv.y * exp_shifted(s, yv.y) : 0.0f;
+        v[4 * q + 2] = valid ? gv.z * exp_shifted(s, yv.z) : 0.0f;
+        v[4 * q + 3] = valid ? gv.w * exp_shifted(s, yv.w) : 0.0f;
+      }
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const uint32_t off = roff + ((q ^ (lane & 7)) << 4);
-          const float4 yv = lds_v4(region + (4 + c) * kBlock + off);
-          const float4 gv = lds_v4(region + (6 + c) * kBlock + off);
-          v[4 * q] = valid ? gv.x * exp_shifted(s, yv.x) : 0.0f;
-          v[4 * q + 1] = valid ? gv.y * exp_shifted(s, yv.y) : 0.0f;
-          v[4 * q + 2] = valid ? gv.z * exp_shifted(s, yv.z) : 0.0f;
-          v[4 * q + 3] = valid ? gv.w * exp_shifted(s, yv.w) : 0.0f;
-        }
+      for (int hh = 0; hh < 2; ++hh) {
+        float hi[16], lo[16];
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          float hi[16], lo[16];
+        for (int t = 0; t < 16; ++t) split_rn(v[16 * hh + t], hi[t], lo[t]);
+        tmem_st16(tp + kTmVHi + 32 * half + 16 * hh, hi);
+        tmem_st16(tp + kTmVLo + 32 * half + 16 * hh, lo);
 #pragma unroll
-          for (int t = 0; t < 16; ++t) split_rn(v[16 * hh + t], hi[t], lo[t]);
-          tmem_st16(tp + kTmVHi + 32 * c + 16 * hh, hi);
-          tmem_st16(tp + kTmVLo + 32 * c + 16 * hh, lo);
-#pragma unroll
-          for (int qq = 0; qq < 4; ++qq) {
-            const int oq = 8 * c + 4 * hh + qq;
-            sts_v4(region + kOffVtHi + mnmajor_off(lane, oq), make_float4(hi[4 * qq], hi[4 * qq + 1], hi[4 * qq + 2], hi[4 * qq + 3]));
-            sts_v4(region + kOffVtLo + mnmajor_off(lane, oq), make_float4(lo[4 * qq], lo[4 * qq + 1], lo[4 * qq + 2], lo[4 * qq + 3]));
-          }
+        for (int qq = 0; qq < 4; ++qq) {
+          const int oq = 8 * half + 4 * hh + qq;
+          sts_v4(region + kOffVtHi + mnmajor_off(lane, oq), make_float4(hi[4 * qq], hi[4 * qq + 1], hi[4 * qq + 2], hi[4 * qq + 3]));
+          sts_v4(region + kOffVtLo + mnmajor_off(lane, oq), make_float4(lo[4 * qq], lo[4 * qq + 1], lo[4 * qq + 2], lo[4 * qq + 3]));
         }
       }
       tmem_wait_st();
@@ -274,27 +319,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&ready[pair]);
       if (tr) XE_CPB_TRACE(n, 2);
-      // -------- epilogue: dX = dX' * A', this thread's row
+      // -------- epilogue: dX = dX' * A', this thread's half row
       if (!mbar_wait_warp(&dx_full[pair], j & 1, kSiteDrainChunk, abort_flag)) {
         ok = false;
         break;
       }
       if (tr) XE_CPB_TRACE(n, 3);
       tc_fence_after();
-      float* dst = p.dx + ((int64_t)f * p.M + (valid ? row : 0)) * 64;
+      float d[32];
+      tmem_ld16(tp + kTmDX + 32 * half, d);
+      tmem_ld16(tp + kTmDX + 32 * half + 16, d + 16);
+      tmem_wait_ld();
+      if (valid) {
+        float* dst = p.dx + ((int64_t)f * p.M + row) * 64 + 32 * half;
 #pragma unroll
-      for (int sl = 0; sl < 2; ++sl) {
-        float d[32];
-        tmem_ld16(tp + kTmDX + 32 * sl, d);
-        tmem_ld16(tp + kTmDX + 32 * sl + 16, d + 16);
-        tmem_wait_ld();
-        if (valid) {
-#pragma unroll
-          for (int c = 0; c < 8; ++c)
-            stg_v4(dst + 32 * sl + 4 * c, make_float4(d[4 * c] * a[32 * sl + 4 * c], d[4 * c + 1] * a[32 * sl + 4 * c + 1],
-                                                      d[4 * c + 2] * a[32 * sl + 4 * c + 2],
-                                                      d[4 * c + 3] * a[32 * sl + 4 * c + 3]));
-        }
+        for (int c = 0; c < 8; ++c)
+          stg_v4(dst + 4 * c, make_float4(d[4 * c] * a[4 * c], d[4 * c + 1] * a[4 * c + 1], d[4 * c + 2] * a[4 * c + 2],
+                                          d[4 * c + 3] * a[4 * c + 3]));
       }
       // dX' has been read: the pair's next V (and its product) may replace it
       tc_fence_before();
@@ -412,19 +453,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------ loads and the weight split
-    // This lane's 32 chunks of w^T: chunk c = lane + 32 i holds (k = c & 63, o = 4 (c >> 6) .. + 3),
-    // read from w (o, k) a fold ahead (coalesced over k), split into w^T hi / lo at the fold's start.
-    float4 wr[32];
-    auto load_w = [&](int f) {
-      const float* wf = p.w + (int64_t)f * 4096;
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int kr = lane + 32 * (i & 1), o = 4 * (i >> 1);
-        wr[i] = make_float4(__ldg(wf + o * 64 + kr), __ldg(wf + (o + 1) * 64 + kr), __ldg(wf + (o + 2) * 64 + kr),
-                            __ldg(wf + (o + 3) * 64 + kr));
-      }
-    };
-    if (first < last) load_w(first / p.tiles_m);
     bool ok = true;
     int fold_count = 0;
     for (int i = first, n = 0; i < last && ok; ++i, ++n) {
@@ -446,29 +474,40 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const uint32_t stage = smem_base + kOffStage + st * kStage;
       if (SRC == kGather2) {
-        // lane l: table fold f (l < 16) or f + pair, rows 4 (l & 15) .. + 3 of the tile; a row
-        // past M reads its table fold's first row (the pair threads mask it)
-        const int h = lane >> 4, grp = lane & 15;
-        const int64_t tf = (int64_t)f + (int64_t)h * p.pair;
-        int64_t var = p.var ? (int64_t)__ldg(p.var + tf) : tf;
-        if (var < 0 || var >= p.pixel_stride) {
-          record_bad_index(kSiteGemmGatherState);
-          var = 0;
-        }
-        int rows[4];
+        // 128 row copies, rows 0..63 of the tile from table folds f and f + pair (instance i: fold
+        // f + (i >> 6) pair, row i & 63), two per warp instruction: lanes 0-15 and 16-31 each copy one
+        // 256-byte row as sixteen 16-byte cp.async into its swizzled K-major place.  Lane l first
+        // looks up instances l, 32 + l, 64 + l and 96 + l; a row past M copies its fold's first row
+        // (the pair threads mask it).
+        int rowoff[4];
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
-          const int m = mt * kRows + 4 * grp + t;
-          int sv = m < p.M ? (int)__ldg(p.pixels + (int64_t)m * p.pixel_stride + var) : 0;
+          const int inst = 32 * t + lane;
+          const int64_t tf = (int64_t)f + (int64_t)(inst >> 6) * p.pair;
+          int64_t var = p.var ? (int64_t)__ldg(p.var + tf) : tf;
+          if (var < 0 || var >= p.variables) {
+            record_bad_index(kSiteGemmGatherState);
+            var = 0;
+          }
+          const int m = mt * kRows + (inst & 63);
+          int sv = m < p.M ? (int)__ldg(p.pixels + (int64_t)m * p.px_sm + var * p.px_sv) : 0;
           if (sv >= p.states) {
             record_bad_index(kSiteGemmGatherState);
             sv = p.states - 1;
           }
-          rows[t] = (int)(tf * p.states + sv);
+          rowoff[t] = (int)((tf * p.states + sv) * 64);
         }
-        const uint32_t dst = stage + (grp >> 3) * kRegion + (2 * h) * kBlock + (grp & 7) * 512;
-        tma_gather4(dst, &tmap_x1, 0, rows[0], rows[1], rows[2], rows[3], &stage_full[st]);
-        tma_gather4(dst + kBlock, &tmap_x1, 32, rows[0], rows[1], rows[2], rows[3], &stage_full[st]);
+        const int q = lane & 15;
+#pragma unroll
+        for (int it = 0; it < 64; ++it) {
+          const int inst = 2 * it + (lane >> 4);
+          const int off = __shfl_sync(0xffffffffu, rowoff[it >> 4], inst & 31);
+          const int h = inst >> 6, r = inst & 63;
+          const uint32_t dst = stage + (r >> 5) * kRegion + (2 * h + (q >> 3)) * kBlock + (r & 31) * 128 +
+                               (((q & 7) ^ (r & 7)) << 4);
+          cp_async_16(dst, p.table + off + 4 * q);
+        }
+        cp_async_arrive_noinc(&stage_full[st]);
       }
       if (lane == 0) {
         const int gz = f % p.g_folds;
@@ -492,30 +531,49 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       __syncwarp();
       if (i == first || f != (i - 1) / p.tiles_m) {
-        // the fold's first tile: once the previous fold's dX' products are done with w^T, split
-        // this fold's w (in registers) into it, then fetch the next fold's
+        // the fold's first tile: split its w into w^T hi / lo once the previous fold's dX'
+        // products are done with them.  Lane l holds chunks c = l + 32 i: (k = c & 63, o = 4 (c >> 6)
+        // .. + 3), read from w (o, k) in four batches of eight (coalesced over k); the first batch
+        // is in flight during the wait.
+        const float* wf = p.w + (int64_t)f * 4096;
         bool wfree = true;
-        if (lane == 0 && fold_count > 0) wfree = mbar_wait(w_free, (fold_count - 1) & 1, kSiteProducer, abort_flag);
-        if (__shfl_sync(0xffffffffu, wfree ? 1 : 0, 0) == 0) {
+#pragma unroll 1
+        for (int b = 0; b < 4; ++b) {
+          float4 wr[8];
+#pragma unroll
+          for (int t = 0; t < 8; ++t) {
+            const int idx = 8 * b + t;
+            const int kr = lane + 32 * (idx & 1), o = 4 * (idx >> 1);
+            wr[t] = make_float4(__ldg(wf + o * 64 + kr), __ldg(wf + (o + 1) * 64 + kr), __ldg(wf + (o + 2) * 64 + kr),
+                                __ldg(wf + (o + 3) * 64 + kr));
+          }
+          if (b == 0) {
+            if (lane == 0 && fold_count > 0)
+              wfree = mbar_wait(w_free, (fold_count - 1) & 1, kSiteProducer, abort_flag);
+            wfree = __shfl_sync(0xffffffffu, wfree ? 1 : 0, 0) != 0;
+            if (!wfree) break;
+          }
+#pragma unroll
+          for (int t = 0; t < 8; ++t) {
+            const int idx = 8 * b + t;
+            const int kr = lane + 32 * (idx & 1), oc = idx >> 1;
+            float4 hi, lo;
+            split_rn(wr[t].x, hi.x, lo.x);
+            split_rn(wr[t].y, hi.y, lo.y);
+            split_rn(wr[t].z, hi.z, lo.z);
+            split_rn(wr[t].w, hi.w, lo.w);
+            const uint32_t dst = (oc >> 3) * (64 * 128) + kmajor_off(kr, oc & 7);
+            sts_v4(smem_base + kOffWHi + dst, hi);
+            sts_v4(smem_base + kOffWLo + dst, lo);
+          }
+        }
+        if (!wfree) {
           ok = false;
           break;
-        }
-#pragma unroll
-        for (int i2 = 0; i2 < 32; ++i2) {
-          const int kr = lane + 32 * (i2 & 1), oc = i2 >> 1;
-          float4 hi, lo;
-          split_rn(wr[i2].x, hi.x, lo.x);
-          split_rn(wr[i2].y, hi.y, lo.y);
-          split_rn(wr[i2].z, hi.z, lo.z);
-          split_rn(wr[i2].w, hi.w, lo.w);
-          const uint32_t dst = (oc >> 3) * (64 * 128) + kmajor_off(kr, oc & 7);
-          sts_v4(smem_base + kOffWHi + dst, hi);
-          sts_v4(smem_base + kOffWLo + dst, lo);
         }
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(w_ready);
-        if ((f + 1) * p.tiles_m < last) load_w(f + 1);
         ++fold_count;
       }
     }
@@ -560,24 +618,23 @@ constexpr int kTgThreads = (kTgWarps + 1) * 32;
 constexpr int kTgChunk = 64;  // rows of dX per bulk copy (16 KB)
 constexpr int kTgStages = 4;
 constexpr int kTgRing = kTgStages * kTgChunk * 256;
+constexpr int kTgSmemBytes = kTgRing + 128;
 
-__host__ __device__ constexpr int tg_smem_bytes(int states) { return 2 * states * 256 + kTgRing + 128; }
-
-// Rows reach shared memory in 64-row chunks through a 4-slot ring filled by the last warp.
+// A warp's sums live in registers: lane l holds units 2l, 2l+1 of its 16 states of both table
+// folds; a row is added to its state's pair through a switch on the state index (uniform over the
+// warp), in increasing row order.  The pixel values are loaded a chunk ahead.  Rows reach shared memory in 64-row chunks through a 4-slot
+// ring filled by the last warp.  A CTA takes folds blockIdx.x, blockIdx.x + gridDim.x, ...
 __global__ void __launch_bounds__(kTgThreads, 1)
-    table_grad_pair_kernel(const float* __restrict__ dx, int M, const uint8_t* __restrict__ pixels, int64_t ps,
-                           const int32_t* __restrict__ var, int pair, int states, float* __restrict__ dt) {
+    table_grad_pair_kernel(const float* __restrict__ dx, int folds, int M, const uint8_t* __restrict__ pixels,
+                           int64_t px_sm, int64_t px_sv, int64_t variables, const int32_t* __restrict__ var, int pair,
+                           int states, float* __restrict__ dt) {
   extern __shared__ __align__(16) uint8_t tg_smem[];
-  float* acc = reinterpret_cast<float*>(tg_smem);  // [2][states][64]
-  const uint32_t ring = smem_u32(tg_smem + 2 * states * 256);
-  uint64_t* full = reinterpret_cast<uint64_t*>(tg_smem + 2 * states * 256 + kTgRing);
+  const uint32_t ring = smem_u32(tg_smem);
+  uint64_t* full = reinterpret_cast<uint64_t*>(tg_smem + kTgRing);
   uint64_t* empty = full + kTgStages;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kTgStages);
   ArmedCopies* copies = reinterpret_cast<ArmedCopies*>(const_cast<int*>(abort_flag) + 1);
-  const int f = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int i = threadIdx.x; i < 2 * states * 16; i += blockDim.x)
-    reinterpret_cast<float4*>(acc)[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
   if (threadIdx.x == 0) {
     for (int i = 0; i < kTgStages; ++i) {
       mbar_init(&full[i], 1);
@@ -589,83 +646,123 @@ __global__ void __launch_bounds__(kTgThreads, 1)
   }
   __syncthreads();
   const int chunks = (M + kTgChunk - 1) / kTgChunk;
-  const float* src = dx + (int64_t)f * M * 64;
   if (warp == kTgWarps) {
     if (lane == 0) {
-      for (int c = 0; c < chunks; ++c) {
-        const int slot = c % kTgStages;
-        const uint32_t u = c / kTgStages;
-        if (!mbar_wait(&empty[slot], (u & 1) ^ 1, kSiteProducer, abort_flag)) break;
-        const int rows = min(kTgChunk, M - c * kTgChunk);
-        mbar_expect_tx(&full[slot], rows * 256);
-        copies->note(slot, u);
-        bulk_load(ring + slot * (kTgChunk * 256), src + (int64_t)c * kTgChunk * 64, rows * 256, &full[slot]);
+      int c_all = 0;  // chunks over every fold of this CTA, in order
+      for (int f = blockIdx.x; f < folds; f += gridDim.x) {
+        const float* src = dx + (int64_t)f * M * 64;
+        bool fine = true;
+        for (int c = 0; c < chunks; ++c, ++c_all) {
+          const int slot = c_all % kTgStages;
+          const uint32_t u = c_all / kTgStages;
+          if (!mbar_wait(&empty[slot], (u & 1) ^ 1, kSiteProducer, abort_flag)) {
+            fine = false;
+            break;
+          }
+          const int rows = min(kTgChunk, M - c * kTgChunk);
+          XE_CPB_TRACE(c_all, 0);
+          mbar_expect_tx(&full[slot], rows * 256);
+          copies->note(slot, u);
+          bulk_load(ring + slot * (kTgChunk * 256), src + (int64_t)c * kTgChunk * 64, rows * 256, &full[slot]);
+        }
+        if (!fine) break;
       }
     }
   } else {
-    int64_t v1 = var ? (int64_t)__ldg(var + f) : f;
-    int64_t v2 = var ? (int64_t)__ldg(var + f + pair) : (int64_t)f + pair;
-    if (v1 < 0 || v1 >= ps || v2 < 0 || v2 >= ps) {
-      record_bad_index(kSiteGatherState);
-      v1 = v2 = 0;
-    }
-    for (int c = 0; c < chunks; ++c) {
-      const int slot = c % kTgStages;
-      const uint32_t u = c / kTgStages;
-      // the states of rows lane and 32 + lane of the chunk (-1 past M), loaded before the wait
-      int s1[2], s2[2];
+    int c_all = 0;
+    bool fine = true;
+    for (int f = blockIdx.x; f < folds && fine; f += gridDim.x) {
+      int64_t v1 = var ? (int64_t)__ldg(var + f) : f;
+      int64_t v2 = var ? (int64_t)__ldg(var + f + pair) : (int64_t)f + pair;
+      if (v1 < 0 || v1 >= variables || v2 < 0 || v2 >= variables) {
+        record_bad_index(kSiteGatherState);
+        v1 = v2 = 0;
+      }
+      float2 acc[2][16];
 #pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        const int m = c * kTgChunk + 32 * hf + lane;
-        s1[hf] = s2[hf] = -1;
-        if (m < M) {
-          s1[hf] = (int)__ldg(pixels + (int64_t)m * ps + v1);
-          s2[hf] = (int)__ldg(pixels + (int64_t)m * ps + v2);
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int k = 0; k < 16; ++k) acc[t][k] = make_float2(0.0f, 0.0f);
+      // the pixel values of rows lane and 32 + lane of chunk c (-1 past M), loaded a chunk ahead
+      // and checked where they are used
+      const uint8_t* px1 = pixels + v1 * px_sv;
+      const uint8_t* px2 = pixels + v2 * px_sv;
+      auto pixels_of = [&](int c, int (&s1)[2], int (&s2)[2]) {
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          const int m = c * kTgChunk + 32 * hf + lane;
+          const bool in = c < chunks && m < M;
+          s1[hf] = in ? (int)__ldg(px1 + (int64_t)m * px_sm) : -1;
+          s2[hf] = in ? (int)__ldg(px2 + (int64_t)m * px_sm) : -1;
+        }
+      };
+      int n1[2], n2[2];
+      pixels_of(0, n1, n2);
+      for (int c = 0; c < chunks; ++c, ++c_all) {
+        const int slot = c_all % kTgStages;
+        const uint32_t u = c_all / kTgStages;
+        int s1[2] = {n1[0], n1[1]}, s2[2] = {n2[0], n2[1]};
+        pixels_of(c + 1, n1, n2);
+        if (warp == 0 && lane == 0) XE_CPB_TRACE(c_all, 1);
+        if (!mbar_wait_warp(&full[slot], u & 1, kSiteAStaged, abort_flag)) {
+          fine = false;
+          break;
+        }
+        if (warp == 0 && lane == 0) XE_CPB_TRACE(c_all, 2);
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
           if (s1[hf] >= states || s2[hf] >= states) {
             record_bad_index(kSiteGatherState);
             s1[hf] = min(s1[hf], states - 1);
             s2[hf] = min(s2[hf], states - 1);
           }
         }
-      }
-      if (!mbar_wait_warp(&full[slot], u & 1, kSiteAStaged, abort_flag)) break;
 #pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        const uint32_t rows = ring + slot * (kTgChunk * 256) + hf * (32 * 256) + lane * 8;
+        for (int hf = 0; hf < 2; ++hf) {
+          const uint32_t rows = ring + slot * (kTgChunk * 256) + hf * (32 * 256) + lane * 8;
 #pragma unroll
-        for (int t = 0; t < 2; ++t) {
-          const int sv = t == 0 ? s1[hf] : s2[hf];
-          float* table = acc + t * states * 64;
-          uint32_t own = __ballot_sync(0xffffffffu, sv >= 0 && (sv & (kTgWarps - 1)) == warp);
-          while (own) {
-            const int b = __ffs(own) - 1;
-            own &= own - 1;
-            const int st = __shfl_sync(0xffffffffu, sv, b);
-            const float2 x = lds_v2(rows + b * 256);
-            float2* d = reinterpret_cast<float2*>(table + st * 64) + lane;
-            float2 y = *d;
-            y.x += x.x;
-            y.y += x.y;
-            *d = y;
+          for (int t = 0; t < 2; ++t) {
+            const int sv = t == 0 ? s1[hf] : s2[hf];
+            uint32_t own = __ballot_sync(0xffffffffu, sv >= 0 && (sv & (kTgWarps - 1)) == warp);
+            while (own) {
+              const int b = __ffs(own) - 1;
+              own &= own - 1;
+              const int k = __shfl_sync(0xffffffffu, sv, b) >> 4;  // this warp's state index (uniform)
+              const float2 x = lds_v2(rows + b * 256);
+              switch (k) {
+#define XE_TG_ADD(kk)          \
+  case kk:                     \
+    acc[t][kk].x += x.x;       \
+    acc[t][kk].y += x.y;       \
+    break;
+                XE_TG_ADD(0) XE_TG_ADD(1) XE_TG_ADD(2) XE_TG_ADD(3) XE_TG_ADD(4) XE_TG_ADD(5) XE_TG_ADD(6)
+                XE_TG_ADD(7) XE_TG_ADD(8) XE_TG_ADD(9) XE_TG_ADD(10) XE_TG_ADD(11) XE_TG_ADD(12) XE_TG_ADD(13)
+                XE_TG_ADD(14) XE_TG_ADD(15)
+#undef XE_TG_ADD
+                default: break;
+              }
+            }
           }
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+        if (lane == 0) XE_CPB_TRACE(c_all, 3 + (warp & 7));
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[slot]);
+      if (!fine) break;
+      // both table folds' rows of this warp's states (zero where no row selected them)
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        float* base = dt + ((int64_t)f + (int64_t)t * pair) * states * 64;
+#pragma unroll
+        for (int kk = 0; kk < 16; ++kk) {
+          const int st = warp + kTgWarps * kk;
+          if (st < states) reinterpret_cast<float2*>(base + (int64_t)st * 64)[lane] = acc[t][kk];
+        }
+      }
     }
   }
   __syncthreads();
-  if (*abort_flag) {
-    copies->drain(full, abort_flag);
-    return;
-  }
-  // both table folds' slabs, every state (zero where no row selected it)
-  const int per = states * 16;  // float4 per table fold
-  for (int i = threadIdx.x; i < 2 * per; i += blockDim.x) {
-    const int h = i / per, r = i - h * per;
-    reinterpret_cast<float4*>(dt + ((int64_t)f + (int64_t)h * pair) * states * 64)[r] =
-        reinterpret_cast<const float4*>(acc)[i];
-  }
+  if (*abort_flag) copies->drain(full, abort_flag);
 }
 
 }  // namespace cpb

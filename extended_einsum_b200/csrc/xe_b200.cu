@@ -1650,7 +1650,8 @@ xe_status launch_cpb_t(const char* who, const xe::cpb::Params& q, const CUtensor
 // Shared by both entry points: src is xe::cpb::kDense / kDense2 (x1 = A, x2 = A2 or null, both
 // (folds, m, 64)) or kGather2 (x1 = the (table_folds, states, 64) table).
 xe_status cpb_run(const char* who, int src, const float* x1, const float* x2, int64_t table_folds, int64_t states,
-                  const uint8_t* pixels, int64_t pixel_stride, const int32_t* var_of_fold, int64_t fold_offset,
+                  const uint8_t* pixels, int64_t px_sm, int64_t px_sv, int64_t variables, const int32_t* var_of_fold,
+                  int64_t fold_offset,
                   const float* y, const float* g, int64_t g_folds, const float* w, float* dx, float* dw, int64_t folds,
                   int64_t m, int32_t shift_mode, void* workspace, size_t workspace_bytes, cudaStream_t s) {
   if (!x1 || !y || !g || !w || !dx || !dw) return fail(XE_ERR_INVALID_ARGUMENT, "%s: null pointer", who);
@@ -1692,9 +1693,12 @@ xe_status cpb_run(const char* who, int src, const float* x1, const float* x2, in
   q.shift_min = shift_mode == XE_SHIFT_MIN ? 1 : 0;
   q.pieces = geo.pieces;
   q.partials = static_cast<float*>(workspace);
+  q.table = src == xe::cpb::kGather2 ? x1 : nullptr;
   q.pixels = pixels;
   q.var = var_of_fold;
-  q.pixel_stride = pixel_stride;
+  q.px_sm = px_sm;
+  q.px_sv = px_sv;
+  q.variables = variables;
   q.states = (int)states;
   q.pair = (int)fold_offset;
   xe_status st;
@@ -1720,46 +1724,50 @@ size_t xe_cp_layer_backward_workspace_size(int64_t folds, int64_t m) {
 xe_status xe_cp_layer_backward(const float* a, const float* a2, const float* y, const float* g, int64_t g_folds,
                                const float* w, float* da, float* dw, int64_t folds, int64_t m, int32_t shift_mode,
                                void* workspace, size_t workspace_bytes, void* stream) {
-  return cpb_run("xe_cp_layer_backward", a2 ? xe::cpb::kDense2 : xe::cpb::kDense, a, a2, 0, 0, nullptr, 0, nullptr, 0,
+  return cpb_run("xe_cp_layer_backward", a2 ? xe::cpb::kDense2 : xe::cpb::kDense, a, a2, 0, 0, nullptr, 0, 0, 0, nullptr, 0,
                  y, g, g_folds, w, da, dw, folds, m, shift_mode, workspace, workspace_bytes, as_stream(stream));
 }
 
 xe_status xe_cp_layer_backward_gather_pair(const float* table, int64_t table_folds, int64_t states,
-                                           const uint8_t* pixels, int64_t pixel_stride, const int32_t* var_of_fold,
+                                           const uint8_t* pixels, int64_t pixel_sample_stride,
+                                           int64_t pixel_var_stride, int64_t variables, const int32_t* var_of_fold,
                                            int64_t fold_offset, const float* y, const float* g, int64_t g_folds,
                                            const float* w, float* da, float* dw, int64_t folds, int64_t m,
                                            int32_t shift_mode, void* workspace, size_t workspace_bytes, void* stream) {
   const char* who = "xe_cp_layer_backward_gather_pair";
   if (!pixels) return fail(XE_ERR_INVALID_ARGUMENT, "%s: null pointer", who);
-  if (states < 1 || fold_offset < 1 || pixel_stride < 1)
-    return fail(XE_ERR_INVALID_ARGUMENT, "%s: states, fold_offset and pixel_stride must be positive", who);
+  if (states < 1 || fold_offset < 1 || variables < 1 || pixel_sample_stride < 0 || pixel_var_stride < 0)
+    return fail(XE_ERR_INVALID_ARGUMENT, "%s: states, fold_offset and variables must be positive, strides non-negative",
+                who);
   if (table_folds < folds + fold_offset)
     return fail(XE_ERR_INVALID_ARGUMENT, "%s: the table has %lld folds, %lld needed", who, (long long)table_folds,
                 (long long)(folds + fold_offset));
-  if (table_folds * states > INT32_MAX) return fail(XE_ERR_NOT_SUPPORTED, "%s: table too large", who);
-  return cpb_run(who, xe::cpb::kGather2, table, nullptr, table_folds, states, pixels, pixel_stride, var_of_fold,
-                 fold_offset, y, g, g_folds, w, da, dw, folds, m, shift_mode, workspace, workspace_bytes,
+  if (table_folds * states * 64 > INT32_MAX) return fail(XE_ERR_NOT_SUPPORTED, "%s: table too large", who);
+  return cpb_run(who, xe::cpb::kGather2, table, nullptr, table_folds, states, pixels, pixel_sample_stride,
+                 pixel_var_stride, variables, var_of_fold, fold_offset, y, g, g_folds, w, da, dw, folds, m, shift_mode, workspace, workspace_bytes,
                  as_stream(stream));
 }
 
 xe_status xe_state_table_pair_grad(const float* da, int64_t folds, int64_t m, const uint8_t* pixels,
-                                   int64_t pixel_stride, const int32_t* var_of_fold, int64_t fold_offset,
-                                   int64_t states, float* table_grad, void* stream) {
+                                   int64_t pixel_sample_stride, int64_t pixel_var_stride, int64_t variables,
+                                   const int32_t* var_of_fold, int64_t fold_offset, int64_t states,
+                                   float* table_grad, void* stream) {
   const char* who = "xe_state_table_pair_grad";
   if (!da || !pixels || !table_grad) return fail(XE_ERR_INVALID_ARGUMENT, "%s: null pointer", who);
   if (folds < 0 || m < 0) return fail(XE_ERR_INVALID_ARGUMENT, "%s: negative extent", who);
-  if (states < 1 || states > 256 || fold_offset < 1 || pixel_stride < 1)
+  if (states < 1 || states > 256 || fold_offset < 1 || variables < 1 || pixel_sample_stride < 0 || pixel_var_stride < 0)
     return fail(states > 256 ? XE_ERR_NOT_SUPPORTED : XE_ERR_INVALID_ARGUMENT,
-                "%s: needs 1 <= states <= 256 and positive fold_offset and pixel_stride", who);
+                "%s: needs 1 <= states <= 256, positive fold_offset and variables, non-negative strides", who);
   if (m > INT32_MAX || folds + fold_offset > INT32_MAX) return fail(XE_ERR_NOT_SUPPORTED, "%s: too many rows", who);
   if (!aligned16(da) || !aligned16(table_grad)) return fail(XE_ERR_NOT_SUPPORTED, "%s: 16-byte aligned buffers", who);
   if (folds == 0) return XE_OK;
-  const int smem = xe::cpb::tg_smem_bytes((int)states);
   static std::atomic<uint32_t> attribute_set{0};
-  cudaError_t e = prepare_kernel(xe::cpb::table_grad_pair_kernel, xe::cpb::tg_smem_bytes(256), attribute_set);
+  cudaError_t e = prepare_kernel(xe::cpb::table_grad_pair_kernel, xe::cpb::kTgSmemBytes, attribute_set);
   if (e != cudaSuccess) return fail(XE_ERR_CUDA, "%s: cudaFuncSetAttribute: %s", who, cudaGetErrorString(e));
-  xe::cpb::table_grad_pair_kernel<<<(unsigned)folds, xe::cpb::kTgThreads, smem, as_stream(stream)>>>(
-      da, (int)m, pixels, pixel_stride, var_of_fold, (int)fold_offset, (int)states, table_grad);
+  const int grid = (int)std::min<int64_t>(folds, current_device_sms());
+  xe::cpb::table_grad_pair_kernel<<<grid, xe::cpb::kTgThreads, xe::cpb::kTgSmemBytes, as_stream(stream)>>>(
+      da, (int)folds, (int)m, pixels, pixel_sample_stride, pixel_var_stride, variables, var_of_fold, (int)fold_offset,
+      (int)states, table_grad);
   return check_launch(who);
 }
 

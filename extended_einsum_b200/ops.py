@@ -606,8 +606,8 @@ def cp_layer_backward_gather_pair(
     ws = torch.empty(ws_bytes, device=device, dtype=torch.uint8) if ws_bytes else None
     status = lib.xe_cp_layer_backward_gather_pair(
         state_table.data_ptr(), state_table.shape[0], state_table.shape[1], pixels.data_ptr(), pixels.stride(0),
-        _ptr(var_of_fold), folds, y.data_ptr(), g.data_ptr(), g.shape[0], w.data_ptr(), da.data_ptr(), dw.data_ptr(),
-        folds, m, _shift(shift), _ptr(ws), ws_bytes, _stream(device))
+        pixels.stride(1), pixels.shape[1], _ptr(var_of_fold), folds, y.data_ptr(), g.data_ptr(), g.shape[0],
+        w.data_ptr(), da.data_ptr(), dw.data_ptr(), folds, m, _shift(shift), _ptr(ws), ws_bytes, _stream(device))
     _lib.check(status, "xe_cp_layer_backward_gather_pair")
     return da, dw
 
@@ -626,7 +626,8 @@ def state_table_pair_grad(
     if units != 64:
         raise NotImplementedError("state_table_pair_grad: 64 units")
     status = _lib.load().xe_state_table_pair_grad(da.data_ptr(), folds, m, pixels.data_ptr(), pixels.stride(0),
-                                                  _ptr(var_of_fold), folds, states, table.data_ptr(), _stream(device))
+                                                  pixels.stride(1), pixels.shape[1], _ptr(var_of_fold), folds, states,
+                                                  table.data_ptr(), _stream(device))
     _lib.check(status, "xe_state_table_pair_grad")
     return table
 
@@ -646,8 +647,6 @@ def _cp_backward_shapes(name, a, y, g, w):
 def _pair_indices(name, table, pixels, var_of_fold, folds, m, device):
     if pixels.device != device or pixels.dtype != torch.uint8 or pixels.dim() != 2 or pixels.shape[0] != m:
         raise ValueError(f"{name}: pixels must be a (batch, variables) uint8 tensor on the table's device")
-    if pixels.stride(1) != 1:
-        pixels = pixels.contiguous()
     if table.dim() != 3 or table.shape[0] != 2 * folds or not table.is_contiguous():
         raise ValueError(f"{name}: expected a contiguous (2F, states, 64) state table")
     if var_of_fold is not None:

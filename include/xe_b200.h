@@ -339,10 +339,13 @@ xe_status xe_cp_layer_backward(const float* a, const float* a2, const float* y, 
  * xe_logspace_gemm_gather_pair): X[f,m,:] = T[f, x_m, :] + T[f + fold_offset,
  * x'_m, :], with T the (table_folds, states, 64) contiguous table and x_m,
  * x'_m the pixels of variables var_of_fold[f], var_of_fold[f + fold_offset]
- * (NULL: the fold) of sample m.  dA is the gradient of both gathered rows;
- * xe_state_table_pair_grad scatters it into the table. */
+ * (NULL: the fold) of sample m: pixels[m * pixel_sample_stride +
+ * v * pixel_var_stride] for v < variables (a variable-major copy, strides
+ * (1, m), reads one sector per 32 samples).  dA is the gradient of both
+ * gathered rows; xe_state_table_pair_grad scatters it into the table. */
 xe_status xe_cp_layer_backward_gather_pair(const float* table, int64_t table_folds, int64_t states,
-                                           const uint8_t* pixels, int64_t pixel_stride, const int32_t* var_of_fold,
+                                           const uint8_t* pixels, int64_t pixel_sample_stride,
+                                           int64_t pixel_var_stride, int64_t variables, const int32_t* var_of_fold,
                                            int64_t fold_offset, const float* y, const float* g, int64_t g_folds,
                                            const float* w, float* da, float* dw, int64_t folds, int64_t m,
                                            int32_t shift_mode, void* workspace, size_t workspace_bytes, void* stream);
@@ -355,10 +358,12 @@ xe_status xe_cp_layer_backward_gather_pair(const float* table, int64_t table_fol
  * 2 * folds table folds are written whole (zero for states no sample takes);
  * table_grad, contiguous (>= folds + fold_offset, states, 64), is not read.
  * The sums run in sample order, so the result is deterministic.  states <= 256.
- * Bad pixel values are clamped and reported as in xe_categorical_gather. */
+ * Pixels as in xe_cp_layer_backward_gather_pair.  Bad pixel values are clamped
+ * and reported as in xe_categorical_gather. */
 xe_status xe_state_table_pair_grad(const float* da, int64_t folds, int64_t m, const uint8_t* pixels,
-                                   int64_t pixel_stride, const int32_t* var_of_fold, int64_t fold_offset,
-                                   int64_t states, float* table_grad, void* stream);
+                                   int64_t pixel_sample_stride, int64_t pixel_var_stride, int64_t variables,
+                                   const int32_t* var_of_fold, int64_t fold_offset, int64_t states,
+                                   float* table_grad, void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* Log-space Tucker layer 'bfi,bfj,foij->bfo' (the ternary einsum that

@@ -103,8 +103,8 @@ def test_cp_layer_backward_rejects_bad_arguments_without_launch():
     assert call(m=-1) == _lib.XE_ERR_INVALID_ARGUMENT
     assert call(ws_bytes=16) == _lib.XE_ERR_INVALID_ARGUMENT and "workspace" in _lib.last_error()
     # the pair form checks its table and indices first
-    st = lib.xe_cp_layer_backward_gather_pair(16, 3, 256, 16, 8, None, 2, 16, 16, 1, 16, 16, 16, 2, 100, 0, 16,
+    st = lib.xe_cp_layer_backward_gather_pair(16, 3, 256, 16, 8, 1, 8, None, 2, 16, 16, 1, 16, 16, 16, 2, 100, 0, 16,
                                               1 << 30, None)
     assert st == _lib.XE_ERR_INVALID_ARGUMENT and "folds" in _lib.last_error()
-    assert lib.xe_state_table_pair_grad(16, 2, 10, 16, 8, None, 2, 300, 16, None) == _lib.XE_ERR_NOT_SUPPORTED
-    assert lib.xe_state_table_pair_grad(None, 2, 10, 16, 8, None, 2, 256, 16, None) == _lib.XE_ERR_INVALID_ARGUMENT
+    assert lib.xe_state_table_pair_grad(16, 2, 10, 16, 8, 1, 8, None, 2, 300, 16, None) == _lib.XE_ERR_NOT_SUPPORTED
+    assert lib.xe_state_table_pair_grad(None, 2, 10, 16, 8, 1, 8, None, 2, 256, 16, None) == _lib.XE_ERR_INVALID_ARGUMENT

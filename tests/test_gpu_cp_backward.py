@@ -103,7 +103,8 @@ def _gather_pair_ref(table, pixels, var, folds):
 
 @pytest.mark.parametrize("shift", ["max", "min"])
 @pytest.mark.parametrize("m", [300, 64, 1])
-def test_state_table_pair_backward(shift, m):
+@pytest.mark.parametrize("pixel_layout", ["sample-major", "variable-major"])
+def test_state_table_pair_backward(shift, m, pixel_layout):
     """dA of the gathered pair layer and its scatter into the (2F, states, 64) table, against fp64."""
     gen = torch.Generator().manual_seed(13 + m)
     folds, states, variables = 4, 256, 11
@@ -117,6 +118,8 @@ def test_state_table_pair_backward(shift, m):
 
     td, pd, vd, wd = table.cuda(), pixels.cuda(), var.cuda(), w.cuda()
     y = ops.logspace_gemm_gather_pair(td, pd, vd, wd.permute(0, 2, 1), b_linear=True, shift=shift)
+    if pixel_layout == "variable-major":
+        pd = pd.t().contiguous().t()
     da, dw = ops.cp_layer_backward_gather_pair(td, pd, vd, y, g.cuda(), wd, shift=shift)
     dt = ops.state_table_pair_grad(da, pd, vd, states)
     dt2 = ops.state_table_pair_grad(da, pd, vd, states)
