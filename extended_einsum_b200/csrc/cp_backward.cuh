@@ -455,6 +455,31 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ loads and the weight split
     bool ok = true;
     int fold_count = 0;
+    // kGather2: the pixel values of a tile's row copies, looked up a tile ahead (the variables of
+    // a fold once per fold)
+    int pxv[4] = {0, 0, 0, 0};
+    int var_fold = -1;
+    int64_t var0 = 0, var1 = 0;
+    auto lookup = [&](int i2) {
+      const int f2 = i2 / p.tiles_m;
+      const int mt2 = i2 - f2 * p.tiles_m;
+      if (f2 != var_fold) {
+        var_fold = f2;
+        var0 = p.var ? (int64_t)__ldg(p.var + f2) : f2;
+        var1 = p.var ? (int64_t)__ldg(p.var + f2 + p.pair) : (int64_t)f2 + p.pair;
+        if (var0 < 0 || var0 >= p.variables || var1 < 0 || var1 >= p.variables) {
+          record_bad_index(kSiteGemmGatherState);
+          var0 = var1 = 0;
+        }
+      }
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const int inst = 32 * t + lane;
+        const int m = mt2 * kRows + (inst & 63);
+        pxv[t] = m < p.M ? (int)__ldg(p.pixels + (int64_t)m * p.px_sm + ((inst >> 6) ? var1 : var0) * p.px_sv) : 0;
+      }
+    };
+    if (SRC == kGather2 && first < last) lookup(first);
     for (int i = first, n = 0; i < last && ok; ++i, ++n) {
       const int f = i / p.tiles_m;
       const int st = n % kStages;
@@ -476,27 +501,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (SRC == kGather2) {
         // 128 row copies, rows 0..63 of the tile from table folds f and f + pair (instance i: fold
         // f + (i >> 6) pair, row i & 63), two per warp instruction: lanes 0-15 and 16-31 each copy one
-        // 256-byte row as sixteen 16-byte cp.async into its swizzled K-major place.  Lane l first
-        // looks up instances l, 32 + l, 64 + l and 96 + l; a row past M copies its fold's first row
-        // (the pair threads mask it).
+        // 256-byte row as sixteen 16-byte cp.async into its swizzled K-major place.  Lane l holds the
+        // pixel values of instances l, 32 + l, 64 + l and 96 + l, loaded a tile ahead; a row past M
+        // copies its fold's first row (the pair threads mask it).
         int rowoff[4];
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
           const int inst = 32 * t + lane;
-          const int64_t tf = (int64_t)f + (int64_t)(inst >> 6) * p.pair;
-          int64_t var = p.var ? (int64_t)__ldg(p.var + tf) : tf;
-          if (var < 0 || var >= p.variables) {
-            record_bad_index(kSiteGemmGatherState);
-            var = 0;
-          }
-          const int m = mt * kRows + (inst & 63);
-          int sv = m < p.M ? (int)__ldg(p.pixels + (int64_t)m * p.px_sm + var * p.px_sv) : 0;
+          int sv = pxv[t];
           if (sv >= p.states) {
             record_bad_index(kSiteGemmGatherState);
             sv = p.states - 1;
           }
-          rowoff[t] = (int)((tf * p.states + sv) * 64);
+          rowoff[t] = (int)((((int64_t)f + (int64_t)(inst >> 6) * p.pair) * p.states + sv) * 64);
         }
+        if (i + 1 < last) lookup(i + 1);
         const int q = lane & 15;
 #pragma unroll
         for (int it = 0; it < 64; ++it) {
