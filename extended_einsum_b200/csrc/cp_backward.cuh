@@ -19,7 +19,8 @@
 //    while one is computed; a stage receives the tile's rows of X (two tensors for a pair source),
 //    Y and G by TMA (table rows by cp.async of 16 bytes, a warp instruction per two rows);
 //  * each thread reads its half row, takes the row extreme with the other half (through a TMEM
-//    column of its own dX' half, free until the pair's next product), forms A' and V, writes V as
+//    column of its own dX' half, free until the pair's next product, and a bounded mbarrier
+//    phase on which all the pair's threads arrive), forms A' and V, writes V as
 //    TF32 hi / lo into its TMEM lane, and writes the operands of the weight product in place of
 //    its half row of the inputs: S (A'^T hi over A'^T lo, M = 128) and V^T hi / lo (N = 64),
 //    MN-major with the tile's rows as K, so that a thread's k-rows are the 128-byte rows its
@@ -147,11 +148,6 @@ __device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-// Barrier `id` (1..15) over `count` threads (whole warps).
-__device__ __forceinline__ void named_barrier_sync(int id, int count) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
-
 // Byte offset of element (row, e) of a K-major [rows][32] fp32 tile, 128-byte swizzle.
 __device__ __forceinline__ uint32_t kmajor_elem(int row, int e) { return kmajor_off(row, e >> 2) + ((e & 3) << 2); }
 
@@ -178,7 +174,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* w_ready = db_free + 2;           // the fold's w^T hi / lo split
   uint64_t* w_free = w_ready + 1;            // the fold's last dX' product done with them
   uint64_t* drain = w_free + 1;
-  uint32_t* tmem_slot = (uint32_t*)(drain + 1);
+  uint64_t* x_ready = drain + 1;             // [2] both halves' row extremes of the pair's tile written
+  uint32_t* tmem_slot = (uint32_t*)(x_ready + 2);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
   ArmedCopies* stage_copies = (ArmedCopies*)(tmem_slot + 2);
 
@@ -194,6 +191,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&dx_full[i], 1);
       mbar_init(&db_full[i], 1);
       mbar_init(&db_free[i], 4);
+      mbar_init(&x_ready[i], 4 * 32);
     }
     mbar_init(w_ready, 1);
     mbar_init(w_free, 1);
@@ -264,11 +262,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float e_half = extreme(extreme(e0, e1, is_min), extreme(e2, e3, is_min), is_min);
       // the row extreme: each half leaves its own in the first column of its dX' half (its own
       // epilogue has read the previous dX' there; the pair's next product is issued after every
-      // thread of the pair has read the other half's)
+      // thread of the pair has read the other half's); the pair's phase j of x_ready completes
+      // once all 128 threads have written
       tmem_st1(tp + kTmDX + 32 * half, e_half);
       tmem_wait_st();
       tc_fence_before();
-      named_barrier_sync(1 + pair, 128);
+      mbar_arrive(&x_ready[pair]);
+      if (!mbar_wait_warp(&x_ready[pair], j & 1, kSiteAStaged, abort_flag)) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
       const float e_other = tmem_ld1(tp + kTmDX + 32 * (1 - half));
       const float s = valid ? extreme(e_half, e_other, is_min) : 0.0f;
