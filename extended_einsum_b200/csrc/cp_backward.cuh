@@ -53,7 +53,8 @@ using cp::bulk_wait_all;
 using cp::bulk_wait_read;
 using cp::tma_store_3d;
 
-// Per-tile event times of CTA 0 (trace builds only): pair warps 0-5, MMA 6-9, loads 10, drain 11-12.
+// Event times of CTA 0 (trace builds only).  cpb_kernel, per tile: pair warps 0-4, MMA 6-9, loads
+// 10, drain 11-12; table_grad_pair_kernel, per chunk: issue 0, warp 0's wait 1-2, warps 0-7 done 3-10.
 #define XE_CPB_TRACE(n, ev) XE_TILE_TRACE(n, ev)
 
 constexpr int kRows = 64;  // rows per tile
@@ -107,16 +108,6 @@ __host__ __device__ __forceinline__ int cta_of_tile(int64_t t, int64_t num_tiles
   return (int)(((t + 1) * grid - 1) / num_tiles);
 }
 
-__device__ __forceinline__ void sts_f32(uint32_t addr, float v) {
-  asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
-}
-
-__device__ __forceinline__ float lds_f32(uint32_t addr) {
-  float v;
-  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr));
-  return v;
-}
-
 __device__ __forceinline__ float2 lds_v2(uint32_t addr) {
   float2 v;
   asm volatile("ld.shared.v2.f32 {%0,%1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr));
@@ -148,8 +139,6 @@ __device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-// Byte offset of element (row, e) of a K-major [rows][32] fp32 tile, 128-byte swizzle.
-__device__ __forceinline__ uint32_t kmajor_elem(int row, int e) { return kmajor_off(row, e >> 2) + ((e & 3) << 2); }
 
 template <int SRC>
 __global__ void __launch_bounds__(kThreads, 1)
