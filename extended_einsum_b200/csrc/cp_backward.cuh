@@ -39,7 +39,7 @@
 // table T (2F, states, 64) and pixel values x_m, x'_m of the variables of folds f and f + pair;
 // dT[t, s, :] is the sum of dX[f, m, :] over the rows m whose pixel selects state s of table fold
 // t (the backward of the gather).  A CTA takes whole folds f of dX; warp w owns the states s
-// with s % 16 == w, sums their rows in registers in increasing m: the sums are deterministic.
+// with s % 31 == w, sums their rows in registers in increasing m: the sums are deterministic.
 #pragma once
 
 #include "cp_layer.cuh"
@@ -624,15 +624,16 @@ __global__ void __launch_bounds__(256) cpb_reduce_kernel(const float* __restrict
 }
 
 // ---------------------------------------------------------------------------- state-table gradient
-constexpr int kTgWarps = 16;  // consumer warps; warp w owns the states s with s % 16 == w
+constexpr int kTgWarps = 31;  // consumer warps; warp w owns the states s with s % 31 == w
+constexpr int kTgStatesPerWarp = (256 + kTgWarps - 1) / kTgWarps;  // 9
 constexpr int kTgThreads = (kTgWarps + 1) * 32;
 constexpr int kTgChunk = 64;  // rows of dX per bulk copy (16 KB)
 constexpr int kTgStages = 4;
 constexpr int kTgRing = kTgStages * kTgChunk * 256;
 constexpr int kTgSmemBytes = kTgRing + 128;
 
-// A warp's sums live in registers: lane l holds units 2l, 2l+1 of its 16 states of both table
-// folds; a row is added to its state's pair through a switch on the state index (uniform over the
+// A warp's sums live in registers: lane l holds units 2l, 2l+1 of its (at most 9) states of both
+// table folds; a row is added to its state's pair through a switch on the state index (uniform over the
 // warp), in increasing row order.  The pixel values are loaded a chunk ahead.  Rows reach shared memory in 64-row chunks through a 4-slot
 // ring filled by the last warp.  A CTA takes folds blockIdx.x, blockIdx.x + gridDim.x, ...
 __global__ void __launch_bounds__(kTgThreads, 1)
@@ -689,11 +690,11 @@ __global__ void __launch_bounds__(kTgThreads, 1)
         record_bad_index(kSiteGatherState);
         v1 = v2 = 0;
       }
-      float2 acc[2][16];
+      float2 acc[2][kTgStatesPerWarp];
 #pragma unroll
       for (int t = 0; t < 2; ++t)
 #pragma unroll
-        for (int k = 0; k < 16; ++k) acc[t][k] = make_float2(0.0f, 0.0f);
+        for (int k = 0; k < kTgStatesPerWarp; ++k) acc[t][k] = make_float2(0.0f, 0.0f);
       // the pixel values of rows lane and 32 + lane of chunk c (-1 past M), loaded a chunk ahead
       // and checked where they are used
       const uint8_t* px1 = pixels + v1 * px_sv;
@@ -734,11 +735,11 @@ __global__ void __launch_bounds__(kTgThreads, 1)
 #pragma unroll
           for (int t = 0; t < 2; ++t) {
             const int sv = t == 0 ? s1[hf] : s2[hf];
-            uint32_t own = __ballot_sync(0xffffffffu, sv >= 0 && (sv & (kTgWarps - 1)) == warp);
+            uint32_t own = __ballot_sync(0xffffffffu, sv >= 0 && sv % kTgWarps == warp);
             while (own) {
               const int b = __ffs(own) - 1;
               own &= own - 1;
-              const int k = __shfl_sync(0xffffffffu, sv, b) >> 4;  // this warp's state index (uniform)
+              const int k = __shfl_sync(0xffffffffu, sv, b) / kTgWarps;  // this warp's state index (uniform)
               const float2 x = lds_v2(rows + b * 256);
               switch (k) {
 #define XE_TG_ADD(kk)          \
@@ -747,8 +748,7 @@ __global__ void __launch_bounds__(kTgThreads, 1)
     acc[t][kk].y += x.y;       \
     break;
                 XE_TG_ADD(0) XE_TG_ADD(1) XE_TG_ADD(2) XE_TG_ADD(3) XE_TG_ADD(4) XE_TG_ADD(5) XE_TG_ADD(6)
-                XE_TG_ADD(7) XE_TG_ADD(8) XE_TG_ADD(9) XE_TG_ADD(10) XE_TG_ADD(11) XE_TG_ADD(12) XE_TG_ADD(13)
-                XE_TG_ADD(14) XE_TG_ADD(15)
+                XE_TG_ADD(7) XE_TG_ADD(8)
 #undef XE_TG_ADD
                 default: break;
               }
@@ -765,7 +765,7 @@ __global__ void __launch_bounds__(kTgThreads, 1)
       for (int t = 0; t < 2; ++t) {
         float* base = dt + ((int64_t)f + (int64_t)t * pair) * states * 64;
 #pragma unroll
-        for (int kk = 0; kk < 16; ++kk) {
+        for (int kk = 0; kk < kTgStatesPerWarp; ++kk) {
           const int st = warp + kTgWarps * kk;
           if (st < states) reinterpret_cast<float2*>(base + (int64_t)st * 64)[lane] = acc[t][kk];
         }
