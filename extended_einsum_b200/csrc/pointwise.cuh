@@ -923,4 +923,39 @@ __global__ void __launch_bounds__(256) reduce_rows(const float* __restrict__ x, 
   }
 }
 
+// The same reduction when the outputs of a batch entry are contiguous (sr == 1, rows <= 256) and
+// k is strided (a leading axis): one 1024-thread block per batch entry, thread t on column
+// t % rows and on the k-slice t / rows (k = slice, slice + S, ... for S = 1024 / rows slices), so
+// that a warp's loads cover consecutive columns; the S partials of a column are then combined in
+// slice order (deterministic).
+template <int KIND>
+__global__ void __launch_bounds__(1024) reduce_cols(const float* __restrict__ x, int64_t sb, int64_t sk, int64_t rows,
+                                                    int64_t k, float* __restrict__ y) {
+  __shared__ float part[1024];
+  const int64_t bb = blockIdx.x;
+  const int c = (int)(threadIdx.x % rows);
+  const int slice = (int)(threadIdx.x / rows);
+  const int slices = (int)(1024 / rows);
+  float acc = KIND == kFiberSum ? 0.0f : (KIND == kFiberMin ? INFINITY : -INFINITY);
+  if (slice < slices) {
+    const float* px = x + bb * sb + c;
+#pragma unroll 8
+    for (int64_t j = slice; j < k; j += slices) {
+      const float v = __ldg(px + j * sk);
+      if (KIND == kFiberSum) acc += v;
+      else acc = nan_extreme<KIND != kFiberMin>(acc, v);
+    }
+  }
+  part[threadIdx.x] = acc;
+  __syncthreads();
+  if (threadIdx.x < rows) {
+    float r = part[threadIdx.x];
+    for (int s2 = 1; s2 < slices; ++s2) {
+      const float v = part[s2 * rows + threadIdx.x];
+      r = KIND == kFiberSum ? r + v : nan_extreme<KIND != kFiberMin>(r, v);
+    }
+    y[bb * rows + threadIdx.x] = r;
+  }
+}
+
 }  // namespace xe

@@ -1482,6 +1482,12 @@ void launch_fiber(const float* x, const xe::RowIndexer& ri, int64_t rows, int64_
 template <int KIND>
 void launch_reduce(const float* x, int64_t sb, int64_t sr, int64_t sk, int64_t batch, int64_t rows, int64_t k, float* y,
                    cudaStream_t s) {
+  // contiguous outputs, a strided k at least 64 long, one block per batch entry (at least 64 of
+  // them): columns across threads (coalesced loads)
+  if (sr == 1 && rows <= 256 && sk >= rows && k >= 64 && batch >= 64 && batch <= INT32_MAX) {
+    xe::reduce_cols<KIND><<<(unsigned)batch, 1024, 0, s>>>(x, sb, sk, rows, k, y);
+    return;
+  }
   const int64_t blocks = grid_for(batch * rows, 8, (int64_t)current_device_sms() * 16);
   xe::reduce_rows<KIND><<<(unsigned)blocks, 256, 0, s>>>(x, sb, sr, sk, batch, rows, k, y);
 }

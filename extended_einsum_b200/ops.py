@@ -788,12 +788,24 @@ def reduce(x: torch.Tensor, axes: Sequence[int] | None, kind: str, *, keepdims: 
     kept_shape = [x.shape[d] for d in keep]
     rows = math.prod(kept_shape)
     k = math.prod(x.shape[d] for d in axes)
-    view = x.permute(keep + list(axes)).reshape(1, rows, k)
     y = torch.empty(rows, device=device, dtype=torch.float32)
-    status = _lib.load().xe_reduce(
-        view.data_ptr(), view.stride(0), view.stride(1), view.stride(2), 1, rows, k, FIBER_KINDS[kind], y.data_ptr(),
-        _stream(device),
-    )
+    after = math.prod(x.shape[axes[-1] + 1:]) if axes else 1
+    block = bool(axes) and x.is_contiguous() and axes == tuple(range(axes[0], axes[-1] + 1)) and 1 < after <= 256
+    if block and rows == after and k >= 8192 and k % 64 == 0:
+        # one long leading block: 64-row chunks reduced as a batch, then the chunks (two passes in
+        # a fixed order)
+        partial = reduce(x.reshape(k // 64, 64, after), (1,), kind)
+        return reduce(partial, (0,), kind, keepdims=keepdims).reshape(
+            [1 if d in axes else x.shape[d] for d in range(nd)] if keepdims else kept_shape)
+    if block:
+        # a middle (or leading) block of a contiguous tensor: (before, k, after) with the outputs
+        # contiguous, no copy
+        before = rows // after
+        args = (x.data_ptr(), k * after, 1, after, before, after, k)
+    else:
+        view = x.permute(keep + list(axes)).reshape(1, rows, k)
+        args = (view.data_ptr(), view.stride(0), view.stride(1), view.stride(2), 1, rows, k)
+    status = _lib.load().xe_reduce(*args, FIBER_KINDS[kind], y.data_ptr(), _stream(device))
     _lib.check(status, "xe_reduce")
     if keepdims:
         return y.reshape([1 if d in axes else x.shape[d] for d in range(nd)])

@@ -146,3 +146,25 @@ def test_softmax_minus_inf_and_nan_fibres(shape):
         assert torch.equal(torch.isnan(ours), torch.isnan(ref))
         ok = ~torch.isnan(ref)
         np.testing.assert_allclose(ours[ok].numpy(), ref[ok].numpy(), rtol=2e-6, atol=1e-6 if log_output else 1e-9)
+
+
+@pytest.mark.parametrize("shape,axes", [((8192, 64), (0,)), ((1024, 256, 64), (1,)), ((300, 7), (0,)),
+                                        ((5, 70, 3, 9), (1, 2)), ((64, 100), (0,)), ((3, 40, 300), (1,))])
+@pytest.mark.parametrize("kind", ["sum", "max", "min"])
+def test_reduce_leading_and_middle_axes(shape, axes, kind):
+    """xe_reduce over a leading or middle block of axes (contiguous outputs: the column kernel when
+    the reduced length reaches 64 and at most 256 outputs per entry) against torch fp64."""
+    g = torch.Generator().manual_seed(len(shape) + sum(shape))
+    x = torch.randn(*shape, generator=g)
+    if kind == "max":
+        x.view(-1)[17] = float("nan")
+    y = ops.reduce(x.cuda(), axes, kind).cpu()
+    xd = x.double()
+    ref = xd.sum(dim=axes) if kind == "sum" else (xd.amax(dim=axes) if kind == "max" else xd.amin(dim=axes))
+    if kind == "max":
+        # a NaN input propagates to its output (the reference's torch max does the same)
+        nan_out = torch.isnan(ref)
+        assert torch.equal(torch.isnan(y), nan_out)
+        y, ref = y[~nan_out], ref[~nan_out]
+    np.testing.assert_allclose(y.double().numpy(), ref.numpy(), rtol=1e-5, atol=1e-4)
+    assert ops.device_status() == 0
