@@ -74,6 +74,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
             _c_ptr, _c_size, _c_ptr,  # workspace, bytes, stream
         ],
     ),
+    "xe_u8_transpose": (_c_i32, [_c_ptr, _c_i64, _c_i64, _c_i64, _c_ptr, _c_ptr]),
     "xe_state_table_pair_grad": (
         _c_i32, [_c_ptr, _c_i64, _c_i64, _c_ptr, _c_i64, _c_i64, _c_i64, _c_ptr, _c_i64, _c_i64, _c_ptr, _c_ptr],
     ),

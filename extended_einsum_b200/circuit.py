@@ -256,7 +256,7 @@ class _CircuitFunction(torch.autograd.Function):
             g, dw = ops.cp_layer_backward(y_in[:half], ys[level], g, weights[level], a2=y_in[half:], shift=shift)
             d_levels[level] = _softmax_grad(weights[level], dw, 2)
         # the pixels variable-major (strides (1, batch)): 32 samples' values of a variable in one sector
-        pixels_vm = pixels.t().contiguous().t()
+        pixels_vm = ops.variable_major(pixels)
         g, dw = ops.cp_layer_backward_gather_pair(ys[0], pixels_vm, fwd.var_of_fold, ys[1], g, weights[1], shift=shift)
         d_levels[1] = _softmax_grad(weights[1], dw, 2)
         g = ops.state_table_pair_grad(g, pixels_vm, fwd.var_of_fold, table.shape[1])

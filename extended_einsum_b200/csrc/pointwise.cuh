@@ -958,4 +958,24 @@ __global__ void __launch_bounds__(1024) reduce_cols(const float* __restrict__ x,
   }
 }
 
+// y (cols, rows) = x (rows, cols)^T for bytes, x with row stride s_row: 32 x 32 tiles through
+// shared memory, 32 consecutive bytes per warp access on both sides.
+__global__ void __launch_bounds__(256) transpose_u8(const uint8_t* __restrict__ x, int64_t rows, int64_t cols,
+                                                    int64_t s_row, uint8_t* __restrict__ y) {
+  __shared__ uint8_t tile[32][33];
+  const int64_t r0 = (int64_t)blockIdx.y * 32, c0 = (int64_t)blockIdx.x * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t r = r0 + ty + 8 * i, c = c0 + tx;
+    if (r < rows && c < cols) tile[ty + 8 * i][tx] = x[r * s_row + c];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t c = c0 + ty + 8 * i, r = r0 + tx;
+    if (r < rows && c < cols) y[c * rows + r] = tile[tx][ty + 8 * i];
+  }
+}
+
 }  // namespace xe

@@ -1778,3 +1778,17 @@ xe_status xe_state_table_pair_grad(const float* da, int64_t folds, int64_t m, co
 }
 
 }  // extern "C"
+
+extern "C" {
+
+xe_status xe_u8_transpose(const uint8_t* x, int64_t rows, int64_t cols, int64_t row_stride, uint8_t* y, void* stream) {
+  if (!x || !y) return fail(XE_ERR_INVALID_ARGUMENT, "xe_u8_transpose: null pointer");
+  if (rows < 0 || cols < 0 || row_stride < cols) return fail(XE_ERR_INVALID_ARGUMENT, "xe_u8_transpose: bad extents");
+  if (rows == 0 || cols == 0) return XE_OK;
+  const int64_t gx = (cols + 31) / 32, gy = (rows + 31) / 32;
+  if (gx > INT32_MAX || gy > 65535) return fail(XE_ERR_NOT_SUPPORTED, "xe_u8_transpose: too many rows");
+  xe::transpose_u8<<<dim3((unsigned)gx, (unsigned)gy), 256, 0, as_stream(stream)>>>(x, rows, cols, row_stride, y);
+  return check_launch("xe_u8_transpose");
+}
+
+}  // extern "C"

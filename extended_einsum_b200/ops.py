@@ -632,6 +632,20 @@ def state_table_pair_grad(
     return table
 
 
+def variable_major(pixels: torch.Tensor) -> torch.Tensor:
+    """The (batch, variables) uint8 pixels as a (batch, variables) view of a variable-major copy
+    (strides (1, batch)), made by xe_u8_transpose: the layout the state-table backward reads."""
+    device = pixels.device
+    if device.type != "cuda" or pixels.dtype != torch.uint8 or pixels.dim() != 2 or pixels.stride(1) != 1:
+        raise ValueError("variable_major: a CUDA uint8 (batch, variables) tensor with unit column stride")
+    batch, variables = pixels.shape
+    out = torch.empty((variables, batch), device=device, dtype=torch.uint8)
+    status = _lib.load().xe_u8_transpose(pixels.data_ptr(), batch, variables, pixels.stride(0), out.data_ptr(),
+                                         _stream(device))
+    _lib.check(status, "xe_u8_transpose")
+    return out.t()
+
+
 def _cp_backward_shapes(name, a, y, g, w):
     for t, what in ((a, "a"), (y, "y"), (g, "g"), (w, "w")):
         if t.dim() != 3 or not t.is_contiguous():

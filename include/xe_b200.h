@@ -365,6 +365,12 @@ xe_status xe_state_table_pair_grad(const float* da, int64_t folds, int64_t m, co
                                    const int32_t* var_of_fold, int64_t fold_offset, int64_t states,
                                    float* table_grad, void* stream);
 
+/* y (cols, rows), contiguous, = the transpose of the uint8 matrix x (rows,
+ * cols) with row stride row_stride: the pixels variable-major for the
+ * state-table backward above (no counterpart in the reference, whose pixels
+ * stay in torch; glue of this path).  rows <= 65535 * 32. */
+xe_status xe_u8_transpose(const uint8_t* x, int64_t rows, int64_t cols, int64_t row_stride, uint8_t* y, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Log-space Tucker layer 'bfi,bfj,foij->bfo' (the ternary einsum that
  * OptimizeContractionPaths fuses for Tucker circuits, preprocess.py:1095-1106,

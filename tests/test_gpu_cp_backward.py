@@ -191,3 +191,14 @@ def test_fused_circuit_backward_matches_per_operation_backward():
     unfused = _circuit_grads(circuit, params, pixels, up, fused=False)
     for got, ref in zip(fused, unfused):
         _close(got, ref, rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize("shape", [(8192, 1024), (300, 77), (1, 5), (33, 1)])
+def test_variable_major_pixels(shape):
+    gen = torch.Generator().manual_seed(shape[0] + shape[1])
+    pixels = torch.randint(256, shape, generator=gen, dtype=torch.uint8).cuda()
+    vm = ops.variable_major(pixels)
+    assert vm.shape == pixels.shape and vm.stride() == (1, shape[0])
+    assert torch.equal(vm, pixels)
+    wide = torch.randint(256, (shape[0], shape[1] + 9), generator=gen, dtype=torch.uint8).cuda()
+    assert torch.equal(ops.variable_major(wide[:, : shape[1]]), wide[:, : shape[1]])
